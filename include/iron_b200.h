@@ -1,0 +1,115 @@
+/*
+ * iron_b200.h -- C ABI of libiron_b200.so, the B200 (sm_100a) kernels behind the
+ * IRON operator classes.
+ *
+ * Conventions (every entry point):
+ *   - Returns an int status: IRON_OK (0) or a negative iron_status_t. Never throws,
+ *     never aborts, never prints. iron_strerror() names a status.
+ *   - All tensors are device pointers owned by the caller. bf16 values travel as
+ *     uint16_t bit patterns. Shapes are element counts; strides are element counts.
+ *   - `stream` is a cudaStream_t passed as void*; NULL means the legacy default
+ *     stream. Work is enqueued asynchronously; the call returns after launch.
+ *   - Arguments are validated on the host before any launch (null pointers,
+ *     shapes, 16-byte alignment where the kernel uses vector loads). A CUDA launch
+ *     failure is reported as IRON_ERR_CUDA; iron_last_cuda_error() gives the code.
+ *   - The library keeps no state beyond a per-device attribute cache; distinct
+ *     streams may be used from distinct threads.
+ *   - `flags` bit IRON_FLAG_PDL launches the kernel with programmatic dependent
+ *     launch: it may start before the previous kernel on the stream finishes and
+ *     streams its weights before waiting for that kernel. Use it only when the
+ *     weights are not written by the preceding kernel (inference graphs).
+ *
+ * Each entry point names the IRON (reference) interface it replaces as
+ * file:line within the reference project.
+ */
+#ifndef IRON_B200_H
+#define IRON_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  IRON_OK = 0,
+  IRON_ERR_NULL = -1,          /* a required pointer is NULL */
+  IRON_ERR_SHAPE = -2,         /* a size is <= 0, or sizes are inconsistent */
+  IRON_ERR_ALIGN = -3,         /* a pointer or leading dimension is misaligned */
+  IRON_ERR_UNSUPPORTED = -4,   /* a valid request this build does not implement */
+  IRON_ERR_CUDA = -5,          /* a CUDA runtime call failed */
+  IRON_ERR_WORKSPACE = -6,     /* the caller's workspace is too small */
+  IRON_ERR_TIMEOUT = -7,       /* a bounded device-side wait gave up */
+  IRON_ERR_ARG = -8            /* any other invalid argument */
+} iron_status_t;
+
+#define IRON_FLAG_PDL 0x1u
+
+/* GEMV epilogues (applied in fp32 to each output before the bf16 store). */
+#define IRON_EPI_NONE 0
+#define IRON_EPI_GELU 1     /* tanh-approximation GELU */
+
+/* ---- library ------------------------------------------------------------ */
+
+/* Human-readable name of a status code. Never NULL. */
+const char *iron_strerror(int status);
+/* The cudaError_t of the last IRON_ERR_CUDA on this thread (0 if none). */
+int iron_last_cuda_error(void);
+/* ABI version: (major << 16) | minor. */
+int iron_abi_version(void);
+
+/* ---- GEMV (bf16 weights) --------------------------------------------------
+ * Replaces GEMV(M, K, num_batches, epilogue) -- iron/operators/gemv/op.py:22-159,
+ * golden iron/operators/gemv/reference.py:9-11 (C = A @ B).
+ *   For b in [0, num_batches), v in [0, n_vec):
+ *     y[b*y_bstride + v*M + m] = epi( sum_k W[b*w_bstride + m*ldw + k] * x[b*x_bstride + v*K + k] )
+ *                                + (residual ? residual[b*y_bstride + v*M + m] : 0)
+ *   fp32 accumulation, one bf16 rounding per output. num_batches > 1 is IRON's batched
+ *   GEMV (independent matrices); n_vec > 1 is a decode batch sharing one matrix.
+ *   W, x rows must start on 16-byte boundaries (ldw, K multiples of 8).
+ */
+int iron_gemv_bf16(const uint16_t *W, const uint16_t *x, uint16_t *y,
+                   int M, int K, int64_t ldw,
+                   int num_batches, int64_t w_bstride, int64_t x_bstride,
+                   int64_t y_bstride, int n_vec,
+                   const uint16_t *residual, int epilogue, unsigned flags,
+                   void *stream);
+
+/* ---- int4 group-32 GEMV ---------------------------------------------------
+ * The fused Dequant+GEMV of the north star (no single reference op; composes
+ * iron/operators/dequant/op.py:20-81 with iron/operators/gemv/op.py:22-159).
+ *   Wq:     uint8 [N, K/2]; element k of row n is nibble (k&1) of byte n*K/2 + k/2
+ *           (low nibble = even k), a signed two's-complement int4 in [-8, 7].
+ *   scales: bf16 [N, K/32]; one scale per 32 consecutive k of a row.
+ *   x:      bf16 [n_vec, K];  y: bf16 [n_vec, N].
+ *   y[v, n] = sum_k bf16(q[n,k] * scale[n,k/32]) * x[v,k]   (fp32 accumulate)
+ *             + residual[v, n] if residual != NULL.
+ *   K must be a multiple of 128, N a multiple of 16, 1 <= n_vec <= 64.
+ */
+int iron_gemv_int4g32(const uint8_t *Wq, const uint16_t *scales,
+                      const uint16_t *x, uint16_t *y, int N, int K, int n_vec,
+                      const uint16_t *residual, unsigned flags, void *stream);
+
+/* Dequantize the int4g32 GEMV weight format above to bf16 [N, K], bit-exact:
+ * out[n,k] = bf16(q[n,k] * scale[n,k/32]) (the fp32 product rounded once). */
+int iron_dequant_s4g32_rows(const uint8_t *Wq, const uint16_t *scales,
+                            uint16_t *out, int N, int K, void *stream);
+
+/* ---- Dequant (uint4 tiles) ------------------------------------------------
+ * Replaces Dequant(size, ..., tile_size, group_size) -- iron/operators/dequant/op.py:20-81,
+ * golden iron/operators/dequant/reference.py:8-18; payload layout from the packer
+ * iron/operators/dequant/reference.py:68-92.
+ *   payload: per tile of tile_size elements, tile_size/2 code bytes (element 2k = low
+ *   nibble of byte k, unsigned 0..15), then tile_size/group_size bf16 scales (LE).
+ *   out[i] = bf16(code_i * scale_{i/group_size}); size a multiple of tile_size,
+ *   tile_size a multiple of group_size, group_size even.
+ */
+int iron_dequant_u4(const uint8_t *payload, uint16_t *out, int64_t size,
+                    int tile_size, int group_size, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IRON_B200_H */

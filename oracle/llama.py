@@ -1,0 +1,64 @@
+"""Llama-3.2-1B decode block and model, composed from the oracle ops (test oracle).
+
+Follows iron/applications/llama_3.2_1b/llama_cpu.py:170-218 (transformer block:
+RMSNorm -> GQA attention with RoPE and KV-cache append -> residual -> RMSNorm ->
+SwiGLU -> residual) and :221-285 (embedding, 16 blocks, final norm, tied
+lm-head). Intermediates are rounded to bf16 at the same points as the B200
+pipeline stores them, so a kernel-by-kernel comparison is tight; the fp32
+golden (llama_cpu run in fp32) is the accuracy reference.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import ops
+
+BF16 = torch.bfloat16
+
+
+def block_decode(x, k_cache, v_cache, pos, W, angles, n_heads, n_kv, head_dim, eps=1e-5):
+    """One decode step of one block for a batch of sequences.
+
+    x [B, E] bf16; caches [B, n_kv, Lmax, hd] bf16 (updated in place at slot pos[b]);
+    pos [B] ints (tokens already cached); W dict of bf16 weights with keys
+    n1 q k v o n2 g u d (linear weights [out, in]); angles [ctx, hd] table.
+    Returns the block output [B, E] bf16.
+    """
+    B, E = x.shape
+    xn = ops.rms_norm(x, W["n1"], eps)
+    q = ops.gemv_multi(W["q"], xn).view(B, n_heads, head_dim)
+    k = ops.gemv_multi(W["k"], xn).view(B, n_kv, head_dim)
+    v = ops.gemv_multi(W["v"], xn).view(B, n_kv, head_dim)
+    lens = []
+    for b in range(B):
+        p = int(pos[b])
+        ang = angles[p : p + 1].to(BF16)
+        q[b] = ops.rope(q[b], ang)
+        k[b] = ops.rope(k[b], ang)
+        k_cache[b, :, p] = k[b]
+        v_cache[b, :, p] = v[b]
+        lens.append(p + 1)
+    attn = ops.attn_decode(q, k_cache, v_cache, lens).reshape(B, n_heads * head_dim)
+    h = ops.add(x, ops.gemv_multi(W["o"], attn))
+    hn = ops.rms_norm(h, W["n2"], eps)
+    act = ops.swiglu_act(ops.gemv_multi(W["g"], hn), ops.gemv_multi(W["u"], hn))
+    return ops.add(h, ops.gemv_multi(W["d"], act))
+
+
+def block_mlp_half(x, k_cache, v_cache, pos, W, angles, n_heads, n_kv, head_dim, eps=1e-5):
+    """BASELINE config 3's chain: RMSNorm -> QKV -> RoPE -> KV append, then SwiGLU
+    on the normed input. Returns (q_roped [B,Hq,hd], mlp_out [B,E])."""
+    B, E = x.shape
+    xn = ops.rms_norm(x, W["n1"], eps)
+    q = ops.gemv_multi(W["q"], xn).view(B, n_heads, head_dim)
+    k = ops.gemv_multi(W["k"], xn).view(B, n_kv, head_dim)
+    v = ops.gemv_multi(W["v"], xn).view(B, n_kv, head_dim)
+    for b in range(B):
+        p = int(pos[b])
+        ang = angles[p : p + 1].to(BF16)
+        q[b] = ops.rope(q[b], ang)
+        k_cache[b, :, p] = ops.rope(k[b], ang)
+        v_cache[b, :, p] = v[b]
+    act = ops.swiglu_act(ops.gemv_multi(W["g"], xn), ops.gemv_multi(W["u"], xn))
+    return q, ops.gemv_multi(W["d"], act)

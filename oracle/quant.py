@@ -1,0 +1,82 @@
+"""Integer/byte work of the hot path, restated in numpy (test oracle).
+
+- ``dequant_u4_tiles``: IRON Dequant, contract iron/operators/dequant/reference.py:8-18
+  (per tile: tile/2 code bytes, element 2k = low nibble, unsigned; then tile/group
+  bf16 scales; out = bf16(code * scale), the fp32 product rounded once).
+- ``pack_u4_tiles``: the payload layout written by IRON's packer
+  iron/operators/dequant/reference.py:68-92.
+- ``dequant_s4g32`` / ``pack_s4g32``: the int4 group-32 GEMV weight format of the
+  north star (signed int4 in [-8, 7], two per byte along K, low nibble = even k,
+  one bf16 scale per 32 k).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even fp32 -> bf16 bit patterns (NaN stays NaN)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    rounded = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    out = rounded.astype(np.uint16)
+    nan = np.isnan(np.asarray(x, dtype=np.float32))
+    out[nan] = 0x7FC0
+    return out
+
+
+def dequant_u4_tiles(payload: np.ndarray, tile_size: int, group_size: int) -> np.ndarray:
+    """bf16 bits of code * scale for IRON's Dequant payload."""
+    payload = np.asarray(payload, dtype=np.uint8)
+    tile_bytes = tile_size // 2 + 2 * (tile_size // group_size)
+    tiles = payload.reshape(-1, tile_bytes)
+    codes = tiles[:, : tile_size // 2]
+    q = np.stack([codes & 0xF, codes >> 4], axis=-1).reshape(len(tiles), tile_size)
+    sb = tiles[:, tile_size // 2 :].reshape(len(tiles), -1, 2)
+    sbits = sb[..., 0].astype(np.uint16) | (sb[..., 1].astype(np.uint16) << 8)
+    s = np.repeat(bf16_bits_to_f32(sbits), group_size, axis=1)
+    return f32_to_bf16_bits(q.astype(np.float32) * s).reshape(-1)
+
+
+def pack_u4_tiles(codes: np.ndarray, scale_bits: np.ndarray, tile_size: int, group_size: int) -> np.ndarray:
+    """codes: uint8 [size] in 0..15; scale_bits: uint16 [size/group] -> payload bytes."""
+    codes = np.asarray(codes, dtype=np.uint8).reshape(-1, tile_size)
+    sbits = np.asarray(scale_bits, dtype=np.uint16).reshape(len(codes), tile_size // group_size)
+    packed = (codes[:, 0::2] & 0xF) | ((codes[:, 1::2] & 0xF) << 4)
+    sbytes = np.stack([sbits & 0xFF, sbits >> 8], axis=-1).astype(np.uint8).reshape(len(codes), -1)
+    return np.concatenate([packed.astype(np.uint8), sbytes], axis=1).reshape(-1)
+
+
+def pack_s4g32(q: np.ndarray) -> np.ndarray:
+    """q: int [N, K] in [-8, 7] -> uint8 [N, K/2], even k in the low nibble."""
+    u = (np.asarray(q).astype(np.int16) & 0xF).astype(np.uint8)
+    return (u[:, 0::2] | (u[:, 1::2] << 4)).astype(np.uint8)
+
+
+def unpack_s4(codes: np.ndarray) -> np.ndarray:
+    """uint8 [N, K/2] -> int8 [N, K], two's-complement nibbles."""
+    c = np.asarray(codes, dtype=np.uint8)
+    lo = (c & 0xF).astype(np.int8)
+    hi = (c >> 4).astype(np.int8)
+    lo = np.where(lo >= 8, lo - 16, lo)
+    hi = np.where(hi >= 8, hi - 16, hi)
+    return np.stack([lo, hi], axis=-1).reshape(c.shape[0], -1).astype(np.int8)
+
+
+def dequant_s4g32(codes: np.ndarray, scale_bits: np.ndarray, group: int = 32) -> np.ndarray:
+    """bf16 bits [N, K] of bf16(q * scale) for the int4g32 GEMV weights."""
+    q = unpack_s4(codes).astype(np.float32)
+    s = np.repeat(bf16_bits_to_f32(np.asarray(scale_bits, dtype=np.uint16)), group, axis=1)
+    return f32_to_bf16_bits(q * s)
+
+
+def make_s4g32(n: int, k: int, seed: int = 42, smin: float = 0.005, smax: float = 0.02):
+    """BASELINE config-2 weights: q ~ U{-8..7}, scales ~ U[smin, smax] rounded to bf16."""
+    rng = np.random.default_rng(seed)
+    q = rng.integers(-8, 8, size=(n, k), dtype=np.int16)
+    s = rng.uniform(smin, smax, size=(n, k // 32)).astype(np.float32)
+    return pack_s4g32(q), f32_to_bf16_bits(s), q

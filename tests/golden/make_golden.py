@@ -1,0 +1,204 @@
+"""Generate the golden fixtures in tests/golden/ by running IRON's own goldens.
+
+Run from the repository root in a checkout that has the reference next to it:
+
+    python tests/golden/make_golden.py /path/to/IRON
+
+Each IRON golden module (``iron/operators/<op>/reference.py``,
+``iron/applications/llama_3.2_1b/llama_cpu.py``) is loaded by file path and run
+at small, seeded sizes; inputs and outputs are saved as ``<case>.npz`` (bf16 as
+uint16 bit patterns). The fixtures are committed, so tests never need the
+reference at run time.
+
+``iron/operators/dequant/reference.py`` imports ``expand_ref`` from the absent
+third-party package ``mlir_aie`` (pinned ``1.4.4.dev53+gd53582d`` in IRON's
+requirements.txt). Only its packer ``generate_inputs`` is used here, with that
+import satisfied by a stub that refuses to run; the expected output is rebuilt
+from the same seeded quantization steps the packer performs
+(dequant/reference.py:32-64), so the fixture pins both the byte layout and the
+arithmetic.
+"""
+
+from __future__ import annotations
+
+import importlib.util
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+import torch
+
+OUT = Path(__file__).resolve().parent
+
+
+def _load(ref: Path, rel: str, name: str):
+    spec = importlib.util.spec_from_file_location(name, ref / rel)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _np(t):
+    if isinstance(t, torch.Tensor):
+        t = t.detach().contiguous()
+        if t.dtype == torch.bfloat16:
+            return t.view(torch.uint16).numpy().copy()
+        return t.numpy().copy()
+    return np.asarray(t)
+
+
+def _save(name, **arrays):
+    np.savez_compressed(OUT / f"{name}.npz", **{k: _np(v) for k, v in arrays.items()})
+    print("wrote", name)
+
+
+def main(ref: Path):
+    ops = ref / "iron" / "operators"
+
+    g = _load(ref, "iron/operators/gemv/reference.py", "ref_gemv")
+    for M, K in [(128, 128), (64, 256)]:
+        d = g.generate_golden_reference(M=M, K=K)
+        _save(f"gemv_M{M}_K{K}", A=d["A"], B=d["B"], C=d["C"])
+    d = g.generate_golden_reference_batched(M=64, K=128, num_batches=4)
+    _save("gemv_batched_M64_K128_b4", A=d["A"], B=d["B"], C=d["C"])
+    d = g.generate_golden_reference(M=64, K=128)
+    c_gelu = torch.from_numpy(g.gelu_tanh_approx(d["C"].float().numpy()).astype(np.float32))
+    _save("gemv_gelu_M64_K128", A=d["A"], B=d["B"], C=c_gelu.to(torch.bfloat16))
+
+    # Dequant: the packer needs `aie.iron.kernels.datamovement.expand_ref` importable.
+    stub = types.ModuleType("aie.iron.kernels.datamovement")
+
+    def _refuse(*a, **k):
+        raise RuntimeError("expand_ref (mlir_aie) is not available here")
+
+    stub.expand_ref = _refuse
+    for mname in ("aie", "aie.iron", "aie.iron.kernels"):
+        sys.modules.setdefault(mname, types.ModuleType(mname))
+    sys.modules["aie.iron.kernels.datamovement"] = stub
+    dq = _load(ref, "iron/operators/dequant/reference.py", "ref_dequant")
+    for length, tile, group in [(2048, 1024, 32), (4096, 4096, 32), (1024, 256, 32)]:
+        payload = dq.generate_inputs(input_length=length, tile_size=tile, group_size=group)
+        # Same seeded steps as the packer (dequant/reference.py:32-64).
+        torch.manual_seed(42)
+        nt, ns = length // tile, tile // group
+        A = torch.rand(nt * ns, group, dtype=torch.bfloat16) * 3.75
+        r1 = 1 / 3.75
+        scales = r1 + (1 - r1) * torch.rand(nt * ns, dtype=torch.bfloat16)
+        q = torch.quantize_per_channel(
+            A.to(torch.float32), scales=scales.to(torch.float32),
+            zero_points=torch.zeros(nt * ns), axis=0, dtype=torch.quint8,
+        ).int_repr()
+        expected = (q.to(torch.float32) * scales.to(torch.float32)[:, None]).to(torch.bfloat16)
+        _save(f"dequant_{length}_t{tile}_g{group}", payload=payload, codes=q.to(torch.uint8),
+              scales=scales, out=expected.reshape(-1))
+
+    rn = _load(ref, "iron/operators/rms_norm/reference.py", "ref_rms")
+    x, w = rn.generate_inputs(rows=4, cols=256, weighted=True)
+    _save("rms_norm_w_4x256", x=x, w=w, out=rn.reference(x, w=w, weighted=True))
+    (x,) = rn.generate_inputs(rows=2, cols=2048)
+    _save("rms_norm_2x2048", x=x, out=rn.reference(x))
+
+    rp = _load(ref, "iron/operators/rope/reference.py", "ref_rope")
+    for rows, cols, arows in [(32, 128, 8), (32, 64, 1), (64, 128, 32)]:
+        x, ang = rp.generate_inputs(rows=rows, cols=cols, context_len=arows)
+        _save(f"rope_{rows}x{cols}_a{arows}", x=x, angles=ang,
+              out0=rp.reference(x, ang, 0), out1=rp.reference(x, ang, 1))
+
+    sm = _load(ref, "iron/operators/softmax/reference.py", "ref_softmax")
+    x = sm.generate_inputs(rows=16, cols=512)
+    _save("softmax_16x512", x=x, out=sm.reference(x))
+
+    si = _load(ref, "iron/operators/silu/reference.py", "ref_silu")
+    x = si.generate_inputs(2048)
+    _save("silu_2048", x=x, out=si.reference(x))
+    mu = _load(ref, "iron/operators/elementwise_mul/reference.py", "ref_mul")
+    a, b = mu.generate_inputs(2048)
+    _save("mul_2048", a=a, b=b, out=mu.reference(a, b))
+    ad = _load(ref, "iron/operators/elementwise_add/reference.py", "ref_add")
+    a, b = ad.generate_inputs(2048)
+    _save("add_2048", a=a, b=b, out=ad.reference(a, b))
+
+    sw = _load(ref, "iron/operators/swiglu_decode/reference.py", "ref_swiglu")
+    d = sw.generate_golden_reference(M=1, K=256, N=512)
+    _save("swiglu_decode_e256_h512", **{k: v for k, v in d.items()})
+
+    sc = _load(ref, "iron/operators/strided_copy/reference.py", "ref_sc")
+    N_KV, HD = 8, 64
+
+    def kv(seq, slot, ch=1):
+        return dict(input_sizes=[N_KV, HD], input_strides=[HD, 1], input_offset=0,
+                    input_buffer_size=N_KV * HD, output_sizes=[1, N_KV, HD],
+                    output_strides=[0, seq * HD, 1], output_offset=slot * HD,
+                    output_buffer_size=N_KV * seq * HD, num_aie_channels=ch)
+
+    def flat(n, ch=1):
+        return dict(input_sizes=[n], input_strides=[1], input_offset=0, input_buffer_size=n,
+                    output_sizes=[n], output_strides=[1], output_offset=0,
+                    output_buffer_size=n, num_aie_channels=ch)
+
+    cases = {"flat1024": flat(1024), "flat1024_ch4": flat(1024, 4),
+             "kv_slot0": kv(128, 0), "kv_slot5": kv(128, 5), "kv_slot_last": kv(128, 127),
+             "kv_slot5_ch2": kv(128, 5, 2), "kv_slot5_ch4": kv(128, 5, 4),
+             "kv_llama_full": kv(2048, 1000)}
+    import json
+    for cname, kw in cases.items():
+        dd = sc.generate_golden_reference(**kw)
+        _save(f"strided_copy_{cname}", input=dd["input"], output=dd["output"],
+              kwargs=np.frombuffer(json.dumps(kw).encode(), dtype=np.uint8))
+    kw = kv(128, 0)
+    dd = sc.generate_golden_reference(**kw, output_offset_addend=7 * HD, seed=3)
+    _save("strided_copy_kv_addend7", input=dd["input"], output=dd["output"],
+          kwargs=np.frombuffer(json.dumps(dict(kw, output_offset_addend=7 * HD)).encode(), dtype=np.uint8))
+
+    rep = _load(ref, "iron/operators/repeat/reference.py", "ref_repeat")
+    x = rep.generate_inputs(8, 256)
+    _save("repeat_8x256_r4", x=x, out=rep.reference(x, 4))
+    tr = _load(ref, "iron/operators/transpose/reference.py", "ref_tr")
+    x = tr.generate_inputs(64, 32, num_batches=2)
+    _save("transpose_2x64x32", x=x, out=tr.reference(x).contiguous())
+
+    mh = _load(ref, "iron/operators/mha/reference.py", "ref_mha")
+    d = mh.generate_golden_reference(heads=2, S_q=128, S_kv=128, d=64, num_kv_heads=1)
+    _save("mha_h2_kv1_s128", Q=d["Q"], K=d["K"], V=d["V"], O=d["O"])
+    d = mh.generate_golden_reference(heads=4, S_q=100, S_kv=100, d=64, num_kv_heads=2)
+    _save("mha_h4_kv2_s100", Q=d["Q"], K=d["K"], V=d["V"], O=d["O"])
+
+    # Llama decode block at reduced width through llama_cpu's own functions.
+    app = ref / "iron" / "applications" / "llama_3.2_1b"
+    sys.path.insert(0, str(app))
+    harness = _load(ref, "iron/applications/llama_3.2_1b/llama_inference_harness.py", "llama_inference_harness")
+    sys.modules["llama_inference_harness"] = harness
+    lc = _load(ref, "iron/applications/llama_3.2_1b/llama_cpu.py", "ref_llama_cpu")
+    angles = harness.compute_rope_angles(64, 64, 500000.0)
+    _save("rope_angles_hd64_ctx64", angles=angles)
+    torch.manual_seed(7)
+    emb, nh, nkv, hd, hid, past = 256, 4, 2, 64, 512, 9
+    W = {
+        "n1": 1 + 0.02 * torch.randn(emb), "q": 0.02 * torch.randn(nh * hd, emb),
+        "k": 0.02 * torch.randn(nkv * hd, emb), "v": 0.02 * torch.randn(nkv * hd, emb),
+        "o": 0.02 * torch.randn(emb, nh * hd), "n2": 1 + 0.02 * torch.randn(emb),
+        "g": 0.02 * torch.randn(hid, emb), "u": 0.02 * torch.randn(hid, emb),
+        "d": 0.02 * torch.randn(emb, hid),
+    }
+    W = {k: v.to(torch.bfloat16) for k, v in W.items()}
+    x = torch.randn(1, 1, emb).to(torch.bfloat16)
+    kc = torch.randn(1, nkv, past, hd).to(torch.bfloat16)
+    vc = torch.randn(1, nkv, past, hd).to(torch.bfloat16)
+    Wf = {k: v.float() for k, v in W.items()}
+    y, k2, v2 = lc.transformer_block_forward(
+        x.float(), kc.float(), vc.float(), nh, nkv, Wf["n1"], Wf["q"], Wf["k"], Wf["v"],
+        Wf["o"], Wf["n2"], Wf["g"], Wf["u"], Wf["d"], angles.float(), None)
+    _save("llama_block_decode_small", x=x, kc=kc, vc=vc, angles=angles,
+          **{f"W_{k}": v for k, v in W.items()}, y=y.to(torch.bfloat16),
+          k_new=k2.to(torch.bfloat16), v_new=v2.to(torch.bfloat16),
+          dims=np.array([emb, nh, nkv, hd, hid, past]))
+
+
+if __name__ == "__main__":
+    import os
+
+    src = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("IRON_REFERENCE_DIR")
+    if not src:
+        sys.exit("usage: make_golden.py <path to the IRON checkout>")
+    main(Path(src))

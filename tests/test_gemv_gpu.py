@@ -1,0 +1,164 @@
+"""GEMV (bf16 and int4-g32) and Dequant on the B200 against the CPU oracle.
+
+Shapes follow IRON's own tests (iron/operators/gemv/test.py:20-41, :83-98,
+iron/operators/dequant/test.py:13-55) and BASELINE configs 1-2. Tolerances:
+IRON's GEMV bar rel 0.04 / abs 1e-3 (gemv/test.py:69-71) for bf16; the north
+star's rtol 2e-2 / atol 1e-2 for the int4 GEMV; exact for dequantized weights.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_close, bf16, bits, load
+from oracle import ops, quant
+
+pytestmark = pytest.mark.gpu
+
+from iron_b200 import _lib
+from iron_b200.common.test_utils import run_test
+from iron_b200.operators import GEMV, Dequant
+
+
+def _golden_like(M, K, seed=42, b=None):
+    """The input distribution of gemv/reference.py:28-36 (randn * 4, bf16)."""
+    torch.manual_seed(seed)
+    if b is None:
+        return torch.randn(M, K, dtype=torch.bfloat16) * 4, torch.randn(K, dtype=torch.bfloat16) * 4
+    return (torch.randn(b, M, K, dtype=torch.bfloat16) * 4,
+            torch.randn(b, K, dtype=torch.bfloat16) * 4)
+
+
+@pytest.mark.parametrize("name", ["gemv_M128_K128", "gemv_M64_K256"])
+def test_gemv_golden_fixture(name):
+    d = load(name)
+    A, B, C = bf16(d["A"]), bf16(d["B"]), bf16(d["C"])
+    op = GEMV(M=A.shape[0], K=A.shape[1])
+    errors, _, _ = run_test(op, {"matrix": A, "vector": B}, {"output": C}, rel_tol=0.04, abs_tol=1e-3)
+    assert not errors
+
+
+@pytest.mark.parametrize("M,K", [(128, 128), (2048, 8192), (8192, 2048), (512, 2048), (2048, 2048),
+                                 (128256 // 8, 2048), (40, 96), (1026, 64)])
+def test_gemv_bf16_shapes(M, K):
+    A, B = _golden_like(M, K)
+    C = ops.gemv(A, B)
+    errors, lat, bw = run_test(GEMV(M=M, K=K), {"matrix": A, "vector": B}, {"output": C},
+                               rel_tol=0.04, abs_tol=1e-3)
+    assert not errors
+
+
+@pytest.mark.parametrize("M,K,nb", [(256, 128, 4), (256, 128, 100), (448, 64, 192), (64, 1536, 8),
+                                    (1026, 64, 2), (1024, 1024, 2), (512, 64, 32), (2048, 64, 32),
+                                    (64, 2048, 32)])
+def test_gemv_batched(M, K, nb):
+    A, B = _golden_like(M, K, b=nb)
+    C = ops.gemv(A, B)
+    errors, _, _ = run_test(GEMV(M=M, K=K, num_batches=nb),
+                            {"matrix": A.flatten(), "vector": B.flatten()},
+                            {"output": C.flatten()}, rel_tol=0.04, abs_tol=1e-3)
+    assert not errors
+
+
+def test_gemv_gelu_fixture():
+    d = load("gemv_gelu_M64_K128")
+    op = GEMV(M=64, K=128, epilogue="gelu", tile_size_input=16, tile_size_output=16)
+    errors, _, _ = run_test(op, {"matrix": bf16(d["A"]), "vector": bf16(d["B"])},
+                            {"output": bf16(d["C"])}, rel_tol=0.06, abs_tol=2e-2)
+    assert not errors
+
+
+@pytest.mark.parametrize("n_vec", [1, 2, 7, 8, 9, 16, 33, 64])
+def test_gemv_decode_batch(n_vec):
+    torch.manual_seed(n_vec)
+    M, K = 2048, 2048
+    A = (torch.randn(M, K) * 0.02).to(torch.bfloat16)
+    X = torch.randn(n_vec, K).to(torch.bfloat16)
+    op = GEMV(M=M, K=K, n_vec=n_vec)
+    errors, _, _ = run_test(op, {"matrix": A, "vector": X}, {"output": ops.gemv_multi(A, X)},
+                            rel_tol=2e-2, abs_tol=1e-2)
+    assert not errors
+
+
+def test_gemv_residual_epilogue():
+    torch.manual_seed(3)
+    M, K, nv = 2048, 8192, 4
+    A = (torch.randn(M, K) * 0.02).to(torch.bfloat16).cuda()
+    X = torch.randn(nv, K).to(torch.bfloat16).cuda()
+    R = torch.randn(nv, M).to(torch.bfloat16).cuda()
+    Y = torch.empty(nv, M, dtype=torch.bfloat16, device="cuda")
+    op = GEMV(M=M, K=K, n_vec=nv)
+    op._launch(A, X, Y, stream=_lib.current_stream(), residual=R)
+    exp = ops.add(ops.gemv_multi(A.cpu(), X.cpu()), R.cpu())
+    assert_close(Y.cpu(), exp, 2e-2, 1e-2, what="gemv+residual")
+
+
+# ---- int4 group-32 --------------------------------------------------------------
+def _s4_case(N, K, nv, seed=42):
+    codes, sbits, _ = quant.make_s4g32(N, K, seed=seed)
+    torch.manual_seed(seed)
+    X = torch.randn(nv, K).to(torch.bfloat16)
+    W = bf16(quant.dequant_s4g32(codes, sbits))
+    return torch.from_numpy(codes), bf16(sbits), X, W
+
+
+@pytest.mark.parametrize("N,K", [(8192, 2048), (2048, 8192), (16, 128), (512, 2048), (128256 // 4, 2048)])
+def test_dequant_s4g32_rows_bit_exact(N, K):
+    codes, scales, _, W = _s4_case(N, K, 1)
+    out = torch.empty(N, K, dtype=torch.bfloat16, device="cuda")
+    _lib.call("iron_dequant_s4g32_rows", codes.cuda().data_ptr(), scales.cuda().data_ptr(),
+              out.data_ptr(), N, K, _lib.current_stream())
+    np.testing.assert_array_equal(bits(out), bits(W))
+
+
+@pytest.mark.parametrize("N,K,nv", [(8192, 2048, 1), (8192, 2048, 4), (8192, 2048, 8), (16, 128, 1),
+                                    (2048, 8192, 1), (512, 2048, 3), (8192, 2048, 16), (2048, 2048, 64),
+                                    (14336 // 2, 4096, 1)])
+def test_gemv_int4g32(N, K, nv):
+    codes, scales, X, W = _s4_case(N, K, nv)
+    op = GEMV(M=N, K=K, weight_dtype="int4g32", n_vec=nv)
+    vec = X if nv > 1 else X[0]
+    exp = ops.gemv_multi(W, X) if nv > 1 else ops.gemv(W, X[0])
+    errors, _, _ = run_test(op, {"codes": codes, "scales": scales, "vector": vec}, {"output": exp},
+                            rel_tol=2e-2, abs_tol=1e-2)
+    assert not errors
+
+
+def test_gemv_int4g32_residual_and_determinism():
+    N, K, nv = 8192, 2048, 2
+    codes, scales, X, W = _s4_case(N, K, nv, seed=5)
+    R = torch.randn(nv, N).to(torch.bfloat16)
+    c, s, x, r = (t.cuda() for t in (codes, scales, X, R))
+    outs = []
+    for _ in range(3):
+        y = torch.empty(nv, N, dtype=torch.bfloat16, device="cuda")
+        _lib.call("iron_gemv_int4g32", c.data_ptr(), s.data_ptr(), x.data_ptr(), y.data_ptr(),
+                  N, K, nv, r.data_ptr(), 0, _lib.current_stream())
+        outs.append(y.cpu())
+    assert all(torch.equal(outs[0], o) for o in outs[1:]), "int4 GEMV not bitwise deterministic"
+    assert_close(outs[0], ops.add(ops.gemv_multi(W, X), R), 2e-2, 1e-2, what="int4+residual")
+
+
+# ---- Dequant (IRON uint4 tiles) -----------------------------------------------
+@pytest.mark.parametrize("name,tile", [("dequant_2048_t1024_g32", 1024), ("dequant_4096_t4096_g32", 4096),
+                                       ("dequant_1024_t256_g32", 256)])
+def test_dequant_golden_bit_exact(name, tile):
+    d = load(name)
+    size = len(d["out"])
+    op = Dequant(size=size, num_aie_columns=1, num_channels=1, tile_size=tile)
+    errors, _, _ = run_test(op, {"payload": torch.from_numpy(d["payload"])},
+                            {"output": bf16(d["out"])}, rel_tol=0.0, abs_tol=0.0)
+    assert not errors
+
+
+def test_dequant_bench_size_bit_exact():
+    size, tile = 1 << 23, 4096
+    rng = np.random.default_rng(0)
+    codes = rng.integers(0, 16, size=size, dtype=np.uint8)
+    sb = quant.f32_to_bf16_bits(rng.uniform(0.25, 1.0, size=size // 32).astype(np.float32))
+    payload = quant.pack_u4_tiles(codes, sb, tile, 32)
+    exp = quant.dequant_u4_tiles(payload, tile, 32)
+    op = Dequant(size=size, num_aie_columns=8, num_channels=2, tile_size=tile)
+    errors, _, _ = run_test(op, {"payload": torch.from_numpy(payload)}, {"output": bf16(exp)},
+                            rel_tol=0.0, abs_tol=0.0)
+    assert not errors
