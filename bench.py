@@ -218,15 +218,17 @@ def run_ours(args, world, rank, local):
         copies = max(2, -(-3 * L2_BYTES // wl.weight_bytes))
         codes, scales, x, y = _make_int4_device(wl, copies)
         N, K, nv = wl.N, wl.K, wl.n_vec
-        cp, sp_, xp, yp = codes.data_ptr(), scales.data_ptr(), x.data_ptr(), y.data_ptr()
-        cstride, sstride = codes[0].numel(), scales[0].numel() * 2
+        packed = torch.stack([GEMV.pack_int4g32(codes[j], scales[j]) for j in range(copies)])
+        op = GEMV(M=N, K=K, weight_dtype="int4g32", n_vec=nv)
+        ws = op.workspace()
+        pp, xp, yp, wsp, wsn = packed.data_ptr(), x.data_ptr(), y.data_ptr(), ws.data_ptr(), ws.numel()
+        pstride = packed[0].numel()
 
         def launch(i, flags=_lib.IRON_FLAG_PDL):
             j = i % copies
-            return lib.iron_gemv_int4g32(cp + j * cstride, sp_ + j * sstride, xp, yp, N, K, nv,
-                                         None, flags, sp)
+            return lib.iron_gemv_int4g32(pp + j * pstride, xp, yp, N, K, nv, None, wsp, wsn, flags, sp)
 
-        kernel_key = "gemv_s4g32_kernel"
+        kernel_key = "gemv_s4g32_stream_kernel"
     else:
         M, K = 2048, 8192
         wl = Int4Gemv(1)
@@ -365,17 +367,17 @@ def _e2e(args, wl, env):
     if args.workload == "int4_gemv":
         op = GEMV(M=wl.N, K=wl.K, weight_dtype="int4g32", n_vec=wl.n_vec)
         fn = op.get_callable()
-        codes, scales = env["codes"], env["scales"]
+        packed = env["packed"]
         x_host = env["x"].cpu().pin_memory()
         y_host = torch.empty(tuple(env["y"].shape), dtype=torch.bfloat16).pin_memory()
         x_dev = torch.empty_like(env["x"])
         y_dev = torch.empty_like(env["y"])
-        copies = codes.shape[0]
+        copies = packed.shape[0]
 
         def step(i):
             x_dev.copy_(x_host, non_blocking=True)
             j = i % copies
-            fn(codes[j], scales[j], x_dev if wl.n_vec > 1 else x_dev[0], y_dev if wl.n_vec > 1 else y_dev[0])
+            fn(packed[j], x_dev if wl.n_vec > 1 else x_dev[0], y_dev if wl.n_vec > 1 else y_dev[0])
             y_host.copy_(y_dev, non_blocking=True)
     else:
         M, K = env["M"], env["K"]

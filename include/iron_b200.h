@@ -79,21 +79,35 @@ int iron_gemv_bf16(const uint16_t *W, const uint16_t *x, uint16_t *y,
 /* ---- int4 group-32 GEMV ---------------------------------------------------
  * The fused Dequant+GEMV of the north star (no single reference op; composes
  * iron/operators/dequant/op.py:20-81 with iron/operators/gemv/op.py:22-159).
- *   Wq:     uint8 [N, K/2]; element k of row n is nibble (k&1) of byte n*K/2 + k/2
- *           (low nibble = even k), a signed two's-complement int4 in [-8, 7].
- *   scales: bf16 [N, K/32]; one scale per 32 consecutive k of a row.
- *   x:      bf16 [n_vec, K];  y: bf16 [n_vec, N].
- *   y[v, n] = sum_k bf16(q[n,k] * scale[n,k/32]) * x[v,k]   (fp32 accumulate)
- *             + residual[v, n] if residual != NULL.
- *   K must be a multiple of 128, N a multiple of 16, 1 <= n_vec <= 64.
+ * Logical weights: signed two's-complement int4 q[n,k] in [-8, 7] and one bf16
+ * scale per 32 consecutive k of a row; the value is q * scale.
+ *
+ * Natural layout (what a checkpoint holds):
+ *   codes:  uint8 [N, K/2]; element k of row n is nibble (k&1) of byte n*K/2 + k/2
+ *           (low nibble = even k).
+ *   scales: bf16 [N, K/32].
+ * iron_pack_int4g32 repacks both into the GEMV's streaming layout (done once,
+ * like IRON's flm.GEMM pack_B, iron/operators/flm/gemm/op.py:455-473):
+ * (N/16)*(K/128) units of 1152 bytes, unit (t, c) = rows 16t..16t+15, k 128c..128c+127.
  */
-int iron_gemv_int4g32(const uint8_t *Wq, const uint16_t *scales,
-                      const uint16_t *x, uint16_t *y, int N, int K, int n_vec,
-                      const uint16_t *residual, unsigned flags, void *stream);
+int iron_pack_int4g32(const uint8_t *codes, const uint16_t *scales, uint8_t *packed,
+                      int N, int K, void *stream);
+size_t iron_gemv_int4g32_workspace_bytes(int N, int K, int n_vec);
+/*   y[v, n] = sum_k q[n,k] * scale[n,k/32] * x[v,k]  (fp32; one bf16 rounding)
+ *             + residual[v, n] if residual != NULL.
+ *   x: bf16 [n_vec, K]; y: bf16 [n_vec, N]; K % 128 == 0, N % 16 == 0, n_vec <= 64.
+ *   workspace: >= iron_gemv_int4g32_workspace_bytes(N, K, n_vec) bytes, 16-byte
+ *   aligned, zero-filled before its first use; every call leaves it zero-filled
+ *   except word 0, a sticky device error code (IRON_ERR_TIMEOUT after a bounded
+ *   wait gave up). Calls that share a workspace must not overlap on the GPU.
+ */
+int iron_gemv_int4g32(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,
+                      int n_vec, const uint16_t *residual, void *workspace,
+                      size_t workspace_bytes, unsigned flags, void *stream);
 
-/* Dequantize the int4g32 GEMV weight format above to bf16 [N, K], bit-exact:
+/* Dequantize natural-layout int4g32 weights to bf16 [N, K], bit-exact:
  * out[n,k] = bf16(q[n,k] * scale[n,k/32]) (the fp32 product rounded once). */
-int iron_dequant_s4g32_rows(const uint8_t *Wq, const uint16_t *scales,
+int iron_dequant_s4g32_rows(const uint8_t *codes, const uint16_t *scales,
                             uint16_t *out, int N, int K, void *stream);
 
 /* ---- Dequant (uint4 tiles) ------------------------------------------------

@@ -1,4 +1,4 @@
-// GEMV kernels: bf16 weights and signed-int4 group-32 weights.
+// bf16 GEMV kernel, and the exact dequantization of the int4 group-32 format.
 //
 // Both are HBM-bound streams over the weight matrix. A warp owns a 16-row tile
 // and a slice of K; it loads 16-byte pieces of two rows per lane straight into
@@ -216,108 +216,6 @@ gemv_bf16_kernel(const uint16_t *__restrict__ W, const uint16_t *__restrict__ x,
 }
 
 // ---------------------------------------------------------------------------
-// int4 group-32 GEMV. Chunk = 128 k of a 16-row tile: lane (gid, tid) loads the
-// 16 code bytes of group 4c+tid (32 k, one scale) for rows gid and gid+8.
-// Code word j (k 8j..8j+7 of the group) shifted by 4i yields the pair
-// (k 8j+i, k 8j+4+i); pairs (j,0),(j,1) feed one MMA step and (j,2),(j,3) the
-// next. The activations are permuted to the same pairs with PRMT.
-template <int NT, int CS, int U>
-__global__ void __launch_bounds__(kGemvThreads)
-gemv_s4g32_kernel(const uint8_t *__restrict__ Wq, const uint16_t *__restrict__ scales,
-                  const uint16_t *__restrict__ x, uint16_t *__restrict__ y, int N, int K,
-                  int n_vec, const uint16_t *__restrict__ residual) {
-  __shared__ float red[(kGemvWarps + CS) * NT * 4 * 32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int gid = lane >> 2, tid = lane & 3;
-  const int rank = (CS > 1) ? static_cast<int>(blockIdx.x % CS) : 0;
-  const int row0 = blockIdx.y * 16;
-
-  const int chunks = K / 128;
-  const int slices = kGemvWarps * CS;
-  const int per = (chunks + slices - 1) / slices;
-  const int slice = rank * kGemvWarps + warp;
-  const int c_begin = min(chunks, slice * per);
-  const int c_end = min(chunks, c_begin + per);
-
-  const int groups = K / 32;
-  const int row_lo = row0 + gid, row_hi = row_lo + 8;  // N % 16 == 0: always valid
-  const uint8_t *q_lo = Wq + static_cast<int64_t>(row_lo) * (K / 2) + tid * 16;
-  const uint8_t *q_hi = Wq + static_cast<int64_t>(row_hi) * (K / 2) + tid * 16;
-  const uint16_t *s_lo = scales + static_cast<int64_t>(row_lo) * groups + tid;
-  const uint16_t *s_hi = scales + static_cast<int64_t>(row_hi) * groups + tid;
-
-  float acc[NT][4];
-#pragma unroll
-  for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
-
-  uint4 a_lo[U], a_hi[U];
-  uint32_t sc_lo[U], sc_hi[U];
-  auto load = [&](int c0) {
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int c = c0 + u;
-      if (c < c_end) {
-        a_lo[u] = ld_stream_v4(q_lo + c * 64);
-        a_hi[u] = ld_stream_v4(q_hi + c * 64);
-        sc_lo[u] = ld_stream_u16(s_lo + c * 4);
-        sc_hi[u] = ld_stream_u16(s_hi + c * 4);
-      } else {
-        a_lo[u] = a_hi[u] = zero4();
-        sc_lo[u] = sc_hi[u] = 0u;
-      }
-    }
-  };
-  load(c_begin);
-  pdl_wait();
-  for (int c0 = c_begin; c0 < c_end; c0 += U) {
-    uint4 n_lo[U], n_hi[U];
-    uint32_t m_lo[U], m_hi[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      n_lo[u] = a_lo[u]; n_hi[u] = a_hi[u];
-      m_lo[u] = sc_lo[u]; m_hi[u] = sc_hi[u];
-    }
-    if (c0 + U < c_end) load(c0 + U);
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int c = c0 + u;
-      if (c >= c_end) break;
-      const uint32_t s2_lo = m_lo[u] | (m_lo[u] << 16);
-      const uint32_t s2_hi = m_hi[u] | (m_hi[u] << 16);
-      const int kg = (c * 4 + tid) * 32;  // first k of this lane's group
-      const uint32_t wl[4] = {n_lo[u].x, n_lo[u].y, n_lo[u].z, n_lo[u].w};
-      const uint32_t wh[4] = {n_hi[u].x, n_hi[u].y, n_hi[u].z, n_hi[u].w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t pl[4], ph[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          pl[i] = s4x2_dequant(wl[j] >> (4 * i), s2_lo);
-          ph[i] = s4x2_dequant(wh[j] >> (4 * i), s2_hi);
-        }
-        const uint32_t A0[4] = {pl[0], ph[0], pl[1], ph[1]};
-        const uint32_t A1[4] = {pl[2], ph[2], pl[3], ph[3]};
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          const int v = t * 8 + gid;
-          uint4 xb = zero4();
-          if (v < n_vec) xb = ld_act_v4(x + static_cast<int64_t>(v) * K + kg + 8 * j);
-          // xb = x[kg+8j .. +7]; pairs (e0,e4),(e1,e5),(e2,e6),(e3,e7).
-          const uint32_t b0 = prmt(xb.x, xb.z, 0x5410u);
-          const uint32_t b1 = prmt(xb.x, xb.z, 0x7632u);
-          const uint32_t b2 = prmt(xb.y, xb.w, 0x5410u);
-          const uint32_t b3 = prmt(xb.y, xb.w, 0x7632u);
-          mma_bf16_16816(acc[t], A0, b0, b1);
-          mma_bf16_16816(acc[t], A1, b2, b3);
-        }
-      }
-    }
-  }
-  pdl_launch_dependents();
-  gemv_reduce_store<NT, CS>(acc, red, row0, N, n_vec, y, residual, IRON_EPI_NONE);
-}
-
-// ---------------------------------------------------------------------------
 // Exact dequantization of the int4g32 GEMV format to bf16 rows (parity check).
 __global__ void dequant_s4g32_rows_kernel(const uint8_t *__restrict__ Wq,
                                           const uint16_t *__restrict__ scales,
@@ -364,40 +262,6 @@ static int launch_bf16(const uint16_t *W, const uint16_t *x, uint16_t *y, int M,
   cfg.numAttrs = na;
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_bf16_kernel<NT, CS, 4>, W, x, y, M, K, ldw, wb,
                                      xb, yb, n_vec, res, epi);
-  if (e != cudaSuccess) {
-    set_last_cuda_error(e);
-    (void)cudaGetLastError();
-    return IRON_ERR_CUDA;
-  }
-  return IRON_OK;
-}
-
-template <int NT, int CS>
-static int launch_s4(const uint8_t *Wq, const uint16_t *sc, const uint16_t *x, uint16_t *y,
-                     int N, int K, int n_vec, const uint16_t *res, bool pdl, cudaStream_t s) {
-  dim3 grid(CS, N / 16, 1);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(kGemvThreads);
-  cfg.stream = s;
-  cudaLaunchAttribute attr[2];
-  int na = 0;
-  if (CS > 1) {
-    attr[na].id = cudaLaunchAttributeClusterDimension;
-    attr[na].val.clusterDim.x = CS;
-    attr[na].val.clusterDim.y = 1;
-    attr[na].val.clusterDim.z = 1;
-    ++na;
-  }
-  if (pdl) {
-    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[na].val.programmaticStreamSerializationAllowed = 1;
-    ++na;
-  }
-  cfg.attrs = attr;
-  cfg.numAttrs = na;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_s4g32_kernel<NT, CS, 4>, Wq, sc, x, y, N, K,
-                                     n_vec, res);
   if (e != cudaSuccess) {
     set_last_cuda_error(e);
     (void)cudaGetLastError();
@@ -458,24 +322,6 @@ extern "C" int iron_gemv_bf16(const uint16_t *W, const uint16_t *x, uint16_t *y,
                                                W, x, y, M, K, ldw, num_batches, w_bstride,
                                                x_bstride, y_bstride, n_vec, residual,
                                                epilogue, pdl, s))));
-  return st;
-}
-
-extern "C" int iron_gemv_int4g32(const uint8_t *Wq, const uint16_t *scales, const uint16_t *x,
-                                 uint16_t *y, int N, int K, int n_vec,
-                                 const uint16_t *residual, unsigned flags, void *stream) {
-  if (!Wq || !scales || !x || !y) return IRON_ERR_NULL;
-  if (N <= 0 || K <= 0 || n_vec <= 0 || n_vec > 64) return IRON_ERR_SHAPE;
-  if (K % 128 || N % 16 || N / 16 > 65535) return IRON_ERR_SHAPE;
-  if (!aligned16(Wq) || !aligned16(x)) return IRON_ERR_ALIGN;
-  if (reinterpret_cast<uintptr_t>(scales) & 1u) return IRON_ERR_ALIGN;
-  const bool pdl = (flags & IRON_FLAG_PDL) != 0;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int cs = pick_split(N / 16, K / 128);
-  int st = IRON_OK;
-  IRON_DISPATCH_NT(n_vec, IRON_DISPATCH_CS(cs, st = (launch_s4<NT, CS>(
-                                               Wq, scales, x, y, N, K, n_vec, residual, pdl,
-                                               s))));
   return st;
 }
 

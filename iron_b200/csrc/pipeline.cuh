@@ -1,0 +1,77 @@
+// mbarrier + bulk-copy (TMA engine, non-tensor) helpers with bounded waits.
+//
+// Every wait spins a bounded number of times; on exhaustion it returns false and
+// the caller records IRON_ERR_TIMEOUT in the error word and leaves. A wait never
+// runs forever. No copy here uses cluster multicast: every bulk copy reads this
+// GPU's global memory into the issuing CTA's own shared memory.
+#pragma once
+
+#include "common.cuh"
+
+namespace iron {
+
+// ~2^22 polls of try_wait (each may suspend up to an implementation-defined
+// interval) -- seconds at most, far above any legitimate wait here.
+constexpr uint32_t kWaitPolls = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+
+// Make barrier initialisation visible to the async (bulk-copy) proxy.
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+               ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Bounded wait for the phase with the given parity to complete.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  const uint32_t a = smem_addr(bar);
+  for (uint32_t i = 0; i < kWaitPolls; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+// Bulk global -> shared copy of `bytes` (multiple of 16, both addresses 16-byte
+// aligned), completing transaction bytes on `bar`.
+__device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, uint32_t bytes,
+                                         uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_addr(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Named barrier among `threads` threads (id 1..15; id 0 is __syncthreads).
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Sticky error word in device memory (0 = ok).
+__device__ __forceinline__ void raise_error(int *err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+}  // namespace iron

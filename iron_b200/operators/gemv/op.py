@@ -7,8 +7,9 @@ IRON validates them and otherwise ignored: the CUDA kernel picks its own tiling.
 
 Two optional fields extend the operator without changing existing calls:
 ``weight_dtype="int4g32"`` selects the fused int4-unpack + group-scale GEMV
-(buffers: packed codes, scales, vector, output) and ``n_vec`` multiplies one
-matrix by ``n_vec`` vectors (a decode batch).
+(buffers: packed weights, vector, output; ``GEMV.pack_int4g32`` turns natural
+codes + scales into the packed buffer once, as IRON's flm.GEMM ``pack_B`` does)
+and ``n_vec`` multiplies one matrix by ``n_vec`` vectors (a decode batch).
 """
 
 from __future__ import annotations
@@ -97,8 +98,7 @@ class GEMV(MLIROperator):
         vec = (self.n_vec,) if self.n_vec > 1 else ()
         if self.weight_dtype == "int4g32":
             return [
-                AIERuntimeArgSpec("in", (self.M, self.K // 2), dtype=np.uint8),  # codes
-                AIERuntimeArgSpec("in", (self.M, self.K // 32)),  # bf16 scales
+                AIERuntimeArgSpec("in", (self.packed_bytes(self.M, self.K),), dtype=np.uint8),
                 AIERuntimeArgSpec("in", vec + (self.K,)),  # vector(s)
                 AIERuntimeArgSpec("out", vec + (self.M,)),  # output
             ]
@@ -109,13 +109,43 @@ class GEMV(MLIROperator):
             AIERuntimeArgSpec("out", batch_dim + vec + (self.M,)),  # output
         ]
 
+    # -- int4g32 weights ----------------------------------------------------------
+    @staticmethod
+    def packed_bytes(M: int, K: int) -> int:
+        return (M // 16) * (K // 128) * 1152
+
+    @staticmethod
+    def pack_int4g32(codes, scales):
+        """Natural codes uint8 [M, K/2] + bf16 scales [M, K/32] (CUDA tensors) ->
+        the packed uint8 buffer the int4g32 GEMV streams."""
+        import torch
+
+        M, K = codes.shape[0], codes.shape[1] * 2
+        out = torch.empty(GEMV.packed_bytes(M, K), dtype=torch.uint8, device=codes.device)
+        _lib.call("iron_pack_int4g32", _lib.dptr(codes), _lib.dptr(scales), _lib.dptr(out), M, K,
+                  _lib.current_stream())
+        return out
+
+    def workspace(self):
+        """Zero-filled scratch for the int4g32 kernel (one per operator; calls
+        that share it must not overlap on the GPU)."""
+        import torch
+
+        ws = getattr(self, "_ws", None)
+        if ws is None or ws.device.index != torch.cuda.current_device():
+            nbytes = _lib.load().iron_gemv_int4g32_workspace_bytes(self.M, self.K, self.n_vec)
+            ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+            self._ws = ws
+        return ws
+
     def _launch(self, *bufs, stream, residual=None, flags=0):
         p = _lib.dptr
         res = p(residual) if residual is not None else None
         if self.weight_dtype == "int4g32":
-            q, s, x, y = bufs
-            _lib.call("iron_gemv_int4g32", p(q), p(s), p(x), p(y), self.M, self.K,
-                      self.n_vec, res, flags, stream)
+            w, x, y = bufs
+            ws = self.workspace()
+            _lib.call("iron_gemv_int4g32", p(w), p(x), p(y), self.M, self.K, self.n_vec, res,
+                      ws.data_ptr(), ws.numel(), flags, stream)
             return
         A, x, y = bufs
         epi = _lib.IRON_EPI_GELU if self.epilogue == "gelu" else _lib.IRON_EPI_NONE

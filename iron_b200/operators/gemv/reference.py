@@ -15,9 +15,21 @@ def dequant_s4g32(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
     return (q * s).to(torch.bfloat16)
 
 
+def unpack_packed_s4g32(packed: torch.Tensor, M: int, K: int):
+    """Inverse of iron_pack_int4g32: packed units -> (codes [M, K/2], scales [M, K/32])."""
+    cpt = K // 128
+    u = packed.reshape(M // 16, cpt, 1152)
+    code = u[:, :, :1024].reshape(M // 16, cpt, 2, 8, 4, 4, 4)  # tile,c,h,gid,tid,j,byte
+    code = code.permute(0, 2, 3, 1, 5, 4, 6).reshape(M, K // 2)
+    sc = u[:, :, 1024:].reshape(M // 16, cpt, 8, 2, 4, 2).contiguous().view(torch.int16)
+    sc = sc.reshape(M // 16, cpt, 8, 2, 4).permute(0, 3, 2, 1, 4).reshape(M, K // 32)
+    return code.contiguous(), sc.contiguous().view(torch.bfloat16)
+
+
 def reference(op, *inputs):
     if op.weight_dtype == "int4g32":
-        codes, scales, x = inputs
+        packed, x = inputs
+        codes, scales = unpack_packed_s4g32(packed.reshape(-1), op.M, op.K)
         A = dequant_s4g32(codes, scales)
     else:
         A, x = inputs

@@ -80,3 +80,24 @@ def make_s4g32(n: int, k: int, seed: int = 42, smin: float = 0.005, smax: float 
     q = rng.integers(-8, 8, size=(n, k), dtype=np.int16)
     s = rng.uniform(smin, smax, size=(n, k // 32)).astype(np.float32)
     return pack_s4g32(q), f32_to_bf16_bits(s), q
+
+
+def pack_s4g32_units(codes: np.ndarray, scale_bits: np.ndarray) -> np.ndarray:
+    """Streaming layout of the int4g32 GEMV (the unit format iron_pack_int4g32 writes).
+
+    Unit (t, c) covers rows 16t..16t+15 and k 128c..128c+127 and is 1152 bytes:
+    bytes [h*512 + lane*16 + 4j, +4) = code bytes [(4c+j)*16 + 4*tid, +4) of row
+    16t + gid + 8h (lane = 4*gid + tid); bytes [1024 + 16*gid, +16) = the bf16
+    scales of groups 4c..4c+3 of row 16t+gid, then of row 16t+gid+8.
+    """
+    codes = np.asarray(codes, dtype=np.uint8)
+    sb = np.asarray(scale_bits, dtype=np.uint16)
+    M, Kh = codes.shape
+    K = Kh * 2
+    T, C = M // 16, K // 128
+    # codes: row = 16t + gid + 8h ; byte = (4c + j)*16 + 4*tid + b
+    cc = codes.reshape(T, 2, 8, C, 4, 4, 4)  # t, h, gid, c, j, tid, b
+    cc = cc.transpose(0, 3, 1, 2, 5, 4, 6).reshape(T, C, 1024)  # t, c, h, gid, tid, j, b
+    ss = sb.reshape(T, 2, 8, C, 4).transpose(0, 3, 2, 1, 4).reshape(T, C, 64)  # t,c,gid,h,j
+    units = np.concatenate([cc, ss.view(np.uint8).reshape(T, C, 128)], axis=2)
+    return units.reshape(-1)

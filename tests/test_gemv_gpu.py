@@ -106,37 +106,89 @@ def _s4_case(N, K, nv, seed=42):
 def test_dequant_s4g32_rows_bit_exact(N, K):
     codes, scales, _, W = _s4_case(N, K, 1)
     out = torch.empty(N, K, dtype=torch.bfloat16, device="cuda")
-    _lib.call("iron_dequant_s4g32_rows", codes.cuda().data_ptr(), scales.cuda().data_ptr(),
-              out.data_ptr(), N, K, _lib.current_stream())
+    c, s = codes.cuda(), scales.cuda()  # keep the device copies alive until the kernel ran
+    _lib.call("iron_dequant_s4g32_rows", c.data_ptr(), s.data_ptr(), out.data_ptr(), N, K,
+              _lib.current_stream())
+    torch.cuda.synchronize()
     np.testing.assert_array_equal(bits(out), bits(W))
+
+
+@pytest.mark.parametrize("N,K", [(8192, 2048), (16, 128), (2048, 8192), (14336, 4096)])
+def test_pack_int4g32_matches_oracle_packer(N, K):
+    codes, scales, _, _ = _s4_case(N, K, 1)
+    c, s = codes.cuda(), scales.cuda()
+    packed = GEMV.pack_int4g32(c, s)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(packed.cpu().numpy(),
+                                  quant.pack_s4g32_units(codes.numpy(), bits(scales)))
 
 
 @pytest.mark.parametrize("N,K,nv", [(8192, 2048, 1), (8192, 2048, 4), (8192, 2048, 8), (16, 128, 1),
                                     (2048, 8192, 1), (512, 2048, 3), (8192, 2048, 16), (2048, 2048, 64),
-                                    (14336 // 2, 4096, 1)])
+                                    (14336, 4096, 1), (128256, 2048, 1), (3072, 2048, 5), (32, 1024, 9)])
 def test_gemv_int4g32(N, K, nv):
     codes, scales, X, W = _s4_case(N, K, nv)
     op = GEMV(M=N, K=K, weight_dtype="int4g32", n_vec=nv)
+    packed = GEMV.pack_int4g32(codes.cuda(), scales.cuda()).cpu()
     vec = X if nv > 1 else X[0]
     exp = ops.gemv_multi(W, X) if nv > 1 else ops.gemv(W, X[0])
-    errors, _, _ = run_test(op, {"codes": codes, "scales": scales, "vector": vec}, {"output": exp},
+    errors, _, _ = run_test(op, {"packed": packed, "vector": vec}, {"output": exp},
                             rel_tol=2e-2, abs_tol=1e-2)
     assert not errors
+    ws = op.workspace()
+    assert int(ws[:4].view(torch.int32).item()) == 0, "device error word set"
+    counters = ws[16:16 + (N // 16) * 4].view(torch.int32)
+    assert int(counters.abs().sum().item()) == 0, "split-tile counters not reset"
 
 
 def test_gemv_int4g32_residual_and_determinism():
     N, K, nv = 8192, 2048, 2
     codes, scales, X, W = _s4_case(N, K, nv, seed=5)
     R = torch.randn(nv, N).to(torch.bfloat16)
-    c, s, x, r = (t.cuda() for t in (codes, scales, X, R))
+    x, r = X.cuda(), R.cuda()
+    packed = GEMV.pack_int4g32(codes.cuda(), scales.cuda())
+    op = GEMV(M=N, K=K, weight_dtype="int4g32", n_vec=nv)
+    ws = op.workspace()
     outs = []
     for _ in range(3):
         y = torch.empty(nv, N, dtype=torch.bfloat16, device="cuda")
-        _lib.call("iron_gemv_int4g32", c.data_ptr(), s.data_ptr(), x.data_ptr(), y.data_ptr(),
-                  N, K, nv, r.data_ptr(), 0, _lib.current_stream())
+        _lib.call("iron_gemv_int4g32", packed.data_ptr(), x.data_ptr(), y.data_ptr(), N, K, nv,
+                  r.data_ptr(), ws.data_ptr(), ws.numel(), 0, _lib.current_stream())
         outs.append(y.cpu())
     assert all(torch.equal(outs[0], o) for o in outs[1:]), "int4 GEMV not bitwise deterministic"
     assert_close(outs[0], ops.add(ops.gemv_multi(W, X), R), 2e-2, 1e-2, what="int4+residual")
+    counters = ws[16:16 + (N // 16) * 4].view(torch.int32)
+    assert int(counters.abs().sum().item()) == 0, "split-tile counters not reset"
+
+
+def test_gemv_int4g32_pdl_chain_in_graph():
+    """A CUDA graph of PDL-launched GEMVs over different weights gives the same
+    results as plain launches (weights streamed before the dependency wait)."""
+    N, K = 2048, 2048
+    outs_ref, mats = [], []
+    for i in range(4):
+        codes, scales, X, W = _s4_case(N, K, 1, seed=20 + i)
+        mats.append(GEMV.pack_int4g32(codes.cuda(), scales.cuda()))
+    x = torch.randn(K).to(torch.bfloat16).cuda()
+    op = GEMV(M=N, K=K, weight_dtype="int4g32")
+    ws = op.workspace()
+    ys = [torch.empty(N, dtype=torch.bfloat16, device="cuda") for _ in mats]
+    for m, y in zip(mats, ys):
+        _lib.call("iron_gemv_int4g32", m.data_ptr(), x.data_ptr(), y.data_ptr(), N, K, 1, None,
+                  ws.data_ptr(), ws.numel(), 0, _lib.current_stream())
+    ref = [y.clone() for y in ys]
+    s = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for m, y in zip(mats, ys):
+            _lib.call("iron_gemv_int4g32", m.data_ptr(), x.data_ptr(), y.data_ptr(), N, K, 1, None,
+                      ws.data_ptr(), ws.numel(), _lib.IRON_FLAG_PDL, s.cuda_stream)
+    for y in ys:
+        y.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(ys, ref):
+        assert torch.equal(a, b)
 
 
 # ---- Dequant (IRON uint4 tiles) -----------------------------------------------
