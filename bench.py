@@ -51,6 +51,7 @@ def _args():
     ap.add_argument("--workload", choices=["int4_gemv", "bf16_gemv"], default="int4_gemv")
     ap.add_argument("--n-vec", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     return ap.parse_args()
 
 
@@ -210,6 +211,7 @@ def run_ours(args, world, rank, local):
     from iron_b200.operators import GEMV
 
     lib = _lib.load()
+    pdl_flag = 0 if args.no_pdl else _lib.IRON_FLAG_PDL
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     sp = stream.cuda_stream
@@ -219,14 +221,13 @@ def run_ours(args, world, rank, local):
         codes, scales, x, y = _make_int4_device(wl, copies)
         N, K, nv = wl.N, wl.K, wl.n_vec
         packed = torch.stack([GEMV.pack_int4g32(codes[j], scales[j]) for j in range(copies)])
-        op = GEMV(M=N, K=K, weight_dtype="int4g32", n_vec=nv)
-        ws = op.workspace()
-        pp, xp, yp, wsp, wsn = packed.data_ptr(), x.data_ptr(), y.data_ptr(), ws.data_ptr(), ws.numel()
+        pp, xp, yp = packed.data_ptr(), x.data_ptr(), y.data_ptr()
         pstride = packed[0].numel()
 
-        def launch(i, flags=_lib.IRON_FLAG_PDL):
+        def launch(i, flags=None):
+            flags = pdl_flag if flags is None else flags
             j = i % copies
-            return lib.iron_gemv_int4g32(pp + j * pstride, xp, yp, N, K, nv, None, wsp, wsn, flags, sp)
+            return lib.iron_gemv_int4g32(pp + j * pstride, xp, yp, N, K, nv, None, flags, sp)
 
         kernel_key = "gemv_s4g32_stream_kernel"
     else:
@@ -244,7 +245,8 @@ def run_ours(args, world, rank, local):
         y = torch.empty(M, dtype=torch.bfloat16, device="cuda")
         wp, xp, yp, wst = W.data_ptr(), x.data_ptr(), y.data_ptr(), M * K * 2
 
-        def launch(i, flags=_lib.IRON_FLAG_PDL):
+        def launch(i, flags=None):
+            flags = pdl_flag if flags is None else flags
             return lib.iron_gemv_bf16(wp + (i % copies) * wst, xp, yp, M, K, K, 1, 0, 0, 0, 1,
                                       None, 0, flags, sp)
 

@@ -92,18 +92,13 @@ int iron_gemv_bf16(const uint16_t *W, const uint16_t *x, uint16_t *y,
  */
 int iron_pack_int4g32(const uint8_t *codes, const uint16_t *scales, uint8_t *packed,
                       int N, int K, void *stream);
-size_t iron_gemv_int4g32_workspace_bytes(int N, int K, int n_vec);
-/*   y[v, n] = sum_k q[n,k] * scale[n,k/32] * x[v,k]  (fp32; one bf16 rounding)
- *             + residual[v, n] if residual != NULL.
- *   x: bf16 [n_vec, K]; y: bf16 [n_vec, N]; K % 128 == 0, N % 16 == 0, n_vec <= 64.
- *   workspace: >= iron_gemv_int4g32_workspace_bytes(N, K, n_vec) bytes, 16-byte
- *   aligned, zero-filled before its first use; every call leaves it zero-filled
- *   except word 0, a sticky device error code (IRON_ERR_TIMEOUT after a bounded
- *   wait gave up). Calls that share a workspace must not overlap on the GPU.
+/*   y[v, n] = sum_k bf16(q[n,k] * scale[n,k/32]) * x[v,k]  (fp32 accumulate; one
+ *             bf16 rounding) + residual[v, n] if residual != NULL -- the dequantized
+ *   weights are exactly IRON Dequant's. x: bf16 [n_vec, K]; y: bf16 [n_vec, N];
+ *   K % 128 == 0, N % 16 == 0, 1 <= n_vec <= 64. Needs no workspace.
  */
 int iron_gemv_int4g32(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,
-                      int n_vec, const uint16_t *residual, void *workspace,
-                      size_t workspace_bytes, unsigned flags, void *stream);
+                      int n_vec, const uint16_t *residual, unsigned flags, void *stream);
 
 /* Dequantize natural-layout int4g32 weights to bf16 [N, K], bit-exact:
  * out[n,k] = bf16(q[n,k] * scale[n,k/32]) (the fp32 product rounded once). */

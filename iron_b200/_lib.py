@@ -30,12 +30,11 @@ SIGNATURES: dict[str, list] = {
     "iron_gemv_bf16": [P, P, P, c_int, c_int, c_int64, c_int, c_int64, c_int64, c_int64,
                        c_int, P, c_int, c_uint, P],
     "iron_pack_int4g32": [P, P, P, c_int, c_int, P],
-    "iron_gemv_int4g32_workspace_bytes": [c_int, c_int, c_int],
-    "iron_gemv_int4g32": [P, P, P, c_int, c_int, c_int, P, P, c_size_t, c_uint, P],
+    "iron_gemv_int4g32": [P, P, P, c_int, c_int, c_int, P, c_uint, P],
     "iron_dequant_s4g32_rows": [P, P, P, c_int, c_int, P],
     "iron_dequant_u4": [P, P, c_int64, c_int, c_int, P],
 }
-_RESTYPES = {"iron_strerror": c_char_p, "iron_gemv_int4g32_workspace_bytes": c_size_t}
+_RESTYPES = {"iron_strerror": c_char_p}
 
 _lock = threading.Lock()
 _lib = None

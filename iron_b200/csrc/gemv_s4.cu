@@ -1,46 +1,41 @@
-// int4 group-32 GEMV, streamed through a bulk-copy shared-memory ring.
+// int4 group-32 GEMV (the fused Dequant + GEMV).
 //
 // Weights are first repacked (iron_pack_int4g32) into units of one 16-row tile x
 // 128 k (4 groups): 1024 code bytes in the order the MMA fragments want them
-// (lane-major, so every warp reads 512 contiguous bytes) followed by the tile's
-// 16 x 4 bf16 scales (128 B). A unit is 1152 bytes; the units of a matrix are
-// stored tile-major, so any contiguous range of units is one contiguous block.
+// (lane-major, so every warp load is 512 contiguous bytes) followed by the tile's
+// 16 x 4 bf16 scales (128 B). A unit is 1152 bytes; units are stored tile-major.
 //
-// One CTA per SM takes an equal share of the units (ranges may split a tile
-// between neighbouring CTAs). A producer warp streams the share into a ring of
-// shared-memory stages with cp.async.bulk + mbarriers; the first stages are
-// issued before griddepcontrol.wait, so under programmatic dependent launch a
-// GEMV streams its weights while the previous kernel is still running. Eight
-// consumer warps unpack the codes with a LOP3 bf16 "magic number" (exact values
-// 136 + q), reduce each 32-k group with two bf16 MMAs (plus two MMAs with a
-// constant -136 operand that cancel the bias) and apply the group scale in fp32
-// to the MMA result. Tiles split between CTAs are combined by the last CTA to
-// arrive (per-tile counter), summing the partials in CTA order, so the result is
+// One CTA of four warps per 16-row tile; its warps split the tile's units (and a
+// thread-block cluster splits K further when the matrix has too few tiles to put
+// two CTAs on every SM). Every warp issues the loads of its units straight into
+// registers, launches its dependents and only then waits for the previous kernel
+// (griddepcontrol.wait): the weights never depend on it, so consecutive GEMVs of
+// an inference graph stream their weights while their predecessor finishes.
+//
+// Codes are unpacked with a LOP3 bf16 "magic number" into the exact dequantized
+// weights bf16(q * scale) -- the values IRON's Dequant produces -- and reduced
+// against the activations with bf16 MMAs, fp32 accumulate, used as a warp-wide
+// dot-product engine. Warp partials are summed in a fixed order through shared
+// memory (and distributed shared memory across a cluster), so results are
 // bitwise deterministic.
-#include "pipeline.cuh"
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace iron {
 
 constexpr int kS4UnitBytes = 1152;
 constexpr int kS4CodeBytes = 1024;
-constexpr int kS4StepUnits = 16;   // units per pipeline stage
-constexpr int kS4Stages = 4;
-constexpr int kS4Consumers = 8;    // consumer warps
-constexpr int kS4Threads = 32 * (kS4Consumers + 1);
-constexpr int kS4MaxCtas = 256;    // bound used for the workspace size
 
-struct S4Work {
-  int64_t U;   // total units
-  int cpt;     // units (chunks of 128 k) per tile
-  int G;       // CTAs
+struct S4Range {
+  int b, e;
 };
-
-__device__ __forceinline__ int64_t s4_unit_begin(int64_t c, const S4Work &w) {
-  return c * w.U / w.G;
-}
-// CTA owning unit u: the largest c with floor(c*U/G) <= u.
-__device__ __forceinline__ int s4_owner(int64_t u, const S4Work &w) {
-  return static_cast<int>(((u + 1) * w.G - 1) / w.U);
+// Part i of `parts` near-equal contiguous parts of [b, e).
+__device__ __forceinline__ S4Range s4_split(int b, int e, int parts, int i) {
+  const int n = e - b;
+  return {b + i * n / parts, b + (i + 1) * n / parts};
 }
 
 __device__ __forceinline__ uint32_t lop3_and_xor_(uint32_t a, uint32_t b, uint32_t c) {
@@ -53,228 +48,172 @@ __device__ __forceinline__ uint32_t prmt_(uint32_t a, uint32_t b, uint32_t sel) 
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
   return d;
 }
-__device__ __forceinline__ void mma_zero(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                         uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
-      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+// Signed int4 pair -> the exactly dequantized bf16x2 (IRON's Dequant then GEMV).
+// `w` holds the wanted nibble at bits 0-3 and 16-19. OR-ing (nib ^ 8) into the
+// mantissa of bf16 128.0 gives 136 + q exactly (q in [-8, 7]); subtracting 136 is
+// exact; the scale multiply rounds the exact product once: bf16(q * s).
+__device__ __forceinline__ uint32_t s4x2_dequant_(uint32_t w, uint32_t scale2) {
+  uint32_t biased = lop3_and_xor_(w, 0x000f000fu, 0x43084308u), q, r;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(biased), "r"(0x43084308u));
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(q), "r"(scale2));
+  return r;
 }
 
-// ws layout: [int err, pad to 16][int counters[tiles], pad to 16][float slots[G][2][NT*512/4]]
-__host__ __device__ inline int64_t s4_counters_off() { return 16; }
-__host__ __device__ inline int64_t s4_slots_off(int64_t tiles) {
-  return 16 + ((tiles * 4 + 15) / 16) * 16;
+// Store a finished 16-row tile (C-fragment layout v) with the residual added.
+template <int NT>
+__device__ __forceinline__ void s4_store(const float (&v)[NT][4], int tile, int N, int n_vec,
+                                         uint16_t *__restrict__ y,
+                                         const uint16_t *__restrict__ residual) {
+  const int lane = threadIdx.x & 31, gid = lane >> 2, tid = lane & 3;
+  const int row0 = tile * 16;
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int row = row0 + gid + ((e >> 1) << 3);
+      const int vv = t * 8 + tid * 2 + (e & 1);
+      if (vv < n_vec) {
+        const int64_t o = static_cast<int64_t>(vv) * N + row;
+        float r = v[t][e];
+        if (residual) r += bf16_bits_to_float(residual[o]);
+        y[o] = float_to_bf16_bits(r);
+      }
+    }
 }
 
 template <int NT>
-__global__ void __launch_bounds__(kS4Threads, (NT == 1) ? 2 : 1)
-gemv_s4g32_stream_kernel(const uint8_t *__restrict__ packed, const uint16_t *__restrict__ x,
-                         uint16_t *__restrict__ y, int N, int K, int n_vec,
-                         const uint16_t *__restrict__ residual, uint8_t *__restrict__ ws,
-                         S4Work w) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ __align__(8) uint64_t full_bar[kS4Stages];
-  __shared__ __align__(8) uint64_t empty_bar[kS4Stages];
-  uint8_t *stages = smem;
-  float *red = reinterpret_cast<float *>(smem + kS4Stages * kS4StepUnits * kS4UnitBytes);
+__device__ __forceinline__ void s4_unit_gx(float (&d)[2][NT][4], const uint4 &clo, const uint4 &chi,
+                                           const uint4 &sc, const uint16_t *__restrict__ x, int K,
+                                           int n_vec, int kbase) {
+  const int lane = threadIdx.x & 31, gid = lane >> 2, tid = lane & 3;
+  const uint32_t wl[4] = {clo.x, clo.y, clo.z, clo.w};
+  const uint32_t wh[4] = {chi.x, chi.y, chi.z, chi.w};
+  const uint32_t sl2[2] = {sc.x, sc.y}, sh2[2] = {sc.z, sc.w};
+  uint4 xr[4][NT];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const int vv = t * 8 + gid;
+      xr[j][t] = make_uint4(0u, 0u, 0u, 0u);
+      if (vv < n_vec) xr[j][t] = __ldg(reinterpret_cast<const uint4 *>(x + static_cast<int64_t>(vv) * K + kbase + j * 32 + tid * 8));
+    }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t sel = (j & 1) ? 0x3232u : 0x1010u;
+    const uint32_t s2_lo = prmt_(sl2[j >> 1], sl2[j >> 1], sel);
+    const uint32_t s2_hi = prmt_(sh2[j >> 1], sh2[j >> 1], sel);
+    uint32_t pl[4], ph[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      pl[q] = s4x2_dequant_(wl[j] >> (4 * q), s2_lo);
+      ph[q] = s4x2_dequant_(wh[j] >> (4 * q), s2_hi);
+    }
+    const uint32_t A0[4] = {pl[0], ph[0], pl[1], ph[1]};
+    const uint32_t A1[4] = {pl[2], ph[2], pl[3], ph[3]};
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const uint4 e = xr[j][t];
+      mma_bf16_16816(d[j & 1][t], A0, prmt_(e.x, e.z, 0x5410u), prmt_(e.x, e.z, 0x7632u));
+      mma_bf16_16816(d[j & 1][t], A1, prmt_(e.y, e.w, 0x5410u), prmt_(e.y, e.w, 0x7632u));
+    }
+  }
+}
 
+// Tile kernel: one CTA of four warps per 16-row tile (or per K-slice of a tile
+// when a cluster splits K), every warp loading all of its units straight into
+// registers before griddepcontrol.wait; partials reduced through shared memory
+// and, across a cluster, distributed shared memory.
+constexpr int kT4Warps = 4;
+constexpr int kT4Units = 4;  // units per warp per round (all loads issued at once)
+
+template <int NT, int CS>
+__global__ void __launch_bounds__(32 * kT4Warps)
+gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__restrict__ x,
+                       uint16_t *__restrict__ y, int N, int K, int n_vec,
+                       const uint16_t *__restrict__ residual) {
+  __shared__ float red[(kT4Warps + CS) * NT * 128];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int cta = blockIdx.x;
-  const int64_t u0 = s4_unit_begin(cta, w), u1 = s4_unit_begin(cta + 1, w);
-  int *err = ws ? reinterpret_cast<int *>(ws) : nullptr;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kS4Stages; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], kS4Consumers);
-    }
-    mbar_init_fence();
-  }
-  __syncthreads();
-  // The next kernel of the stream may launch now: it can only stream its own
-  // weights until it reaches griddepcontrol.wait, which waits for this grid.
-  pdl_launch_dependents();
-
-  // ---------------- producer warp ----------------
-  if (warp == kS4Consumers) {
-    if (lane == 0) {
-      int64_t pos = u0;
-      int step = 0;
-      bool ok = true;
-      while (pos < u1) {
-        const int64_t tile_end = (pos / w.cpt + 1) * w.cpt;
-        const int64_t end = min(min(u1, tile_end), pos + kS4StepUnits);
-        const int s = step % kS4Stages;
-        if (step >= kS4Stages) {
-          if (!mbar_wait(&empty_bar[s], ((step / kS4Stages) - 1) & 1)) {
-            raise_error(err, IRON_ERR_TIMEOUT);
-            ok = false;
-            break;
-          }
-        }
-        const uint32_t bytes = static_cast<uint32_t>((end - pos) * kS4UnitBytes);
-        mbar_arrive_expect_tx(&full_bar[s], bytes);
-        bulk_g2s(stages + s * kS4StepUnits * kS4UnitBytes, packed + pos * kS4UnitBytes, bytes,
-                 &full_bar[s]);
-        pos = end;
-        ++step;
-      }
-      // Do not leave with copies in flight: wait (bounded) for the last stages.
-      if (ok) {
-        for (int k = max(0, step - kS4Stages); k < step; ++k)
-          (void)mbar_wait(&full_bar[k % kS4Stages], (k / kS4Stages) & 1);
-      }
-    }
-    return;
-  }
-
-  // ---------------- consumer warps ----------------
-  pdl_wait();  // activations and outputs belong to the preceding kernel's world
   const int gid = lane >> 2, tid = lane & 3;
-  const uint32_t kBias[4] = {0xC308C308u, 0xC308C308u, 0xC308C308u, 0xC308C308u};  // -136
-  float acc[NT][4];
-  int64_t pos = u0;
-  int step = 0;
-  int tile_count = 0;
-  bool failed = false;  // after a timed-out wait: skip work, keep barrier participation
-  while (pos < u1) {
-    const int64_t tile = pos / w.cpt;
-    const int64_t tile_begin = tile * w.cpt, tile_end = tile_begin + w.cpt;
-    if (pos == u0 || pos == tile_begin) {
+  const int rank = (CS > 1) ? static_cast<int>(blockIdx.x % CS) : 0;
+  const int tile = blockIdx.x / CS;
+  const int cpt = K / 128;
+  const S4Range kr = s4_split(0, cpt, CS * kT4Warps, rank * kT4Warps + warp);  // my chunks
+  const uint8_t *base = packed + (static_cast<int64_t>(tile) * cpt) * kS4UnitBytes;
+
+  float acc[2][NT][4];
 #pragma unroll
-      for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
-    }
-    const int64_t end = min(min(u1, tile_end), pos + kS4StepUnits);
-    const int s = step % kS4Stages;
-    if (!failed && !mbar_wait(&full_bar[s], (step / kS4Stages) & 1)) {
-      raise_error(err, IRON_ERR_TIMEOUT);
-      failed = true;
-    }
-    const uint8_t *stage = stages + s * kS4StepUnits * kS4UnitBytes;
-#pragma unroll 1
-    for (int64_t u = pos + warp; !failed && u < end; u += kS4Consumers) {
-      const uint8_t *unit = stage + (u - pos) * kS4UnitBytes;
-      const uint4 clo = *reinterpret_cast<const uint4 *>(unit + lane * 16);
-      const uint4 chi = *reinterpret_cast<const uint4 *>(unit + 512 + lane * 16);
-      const uint4 sc = *reinterpret_cast<const uint4 *>(unit + kS4CodeBytes + gid * 16);
-      const int c = static_cast<int>(u - tile_begin);  // chunk within the row
-      const uint32_t wl[4] = {clo.x, clo.y, clo.z, clo.w};
-      const uint32_t wh[4] = {chi.x, chi.y, chi.z, chi.w};
-      const uint32_t sl2[2] = {sc.x, sc.y}, sh2[2] = {sc.z, sc.w};
+  for (int a = 0; a < 2; ++a)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t pl[4], ph[4];
+    for (int t = 0; t < NT; ++t) acc[a][t][0] = acc[a][t][1] = acc[a][t][2] = acc[a][t][3] = 0.f;
+
+  uint4 lo[kT4Units], hi[kT4Units], sc[kT4Units];
+  auto load = [&](int c0) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          pl[i] = lop3_and_xor_(wl[j] >> (4 * i), 0x000f000fu, 0x43084308u);
-          ph[i] = lop3_and_xor_(wh[j] >> (4 * i), 0x000f000fu, 0x43084308u);
-        }
-        const float s_lo = (j & 1) ? bf16_hi(sl2[j >> 1]) : bf16_lo(sl2[j >> 1]);
-        const float s_hi = (j & 1) ? bf16_hi(sh2[j >> 1]) : bf16_lo(sh2[j >> 1]);
-        const uint32_t A0[4] = {pl[0], ph[0], pl[1], ph[1]};
-        const uint32_t A1[4] = {pl[2], ph[2], pl[3], ph[3]};
-        const int kx = (c * 4 + j) * 32 + tid * 8;
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          const int v = t * 8 + gid;
-          uint4 xb = make_uint4(0u, 0u, 0u, 0u);
-          if (v < n_vec) xb = __ldg(reinterpret_cast<const uint4 *>(x + static_cast<int64_t>(v) * K + kx));
-          const uint32_t b0 = prmt_(xb.x, xb.z, 0x5410u), b1 = prmt_(xb.x, xb.z, 0x7632u);
-          const uint32_t b2 = prmt_(xb.y, xb.w, 0x5410u), b3 = prmt_(xb.y, xb.w, 0x7632u);
-          float d[4];
-          mma_zero(d, A0, b0, b1);
-          mma_bf16_16816(d, kBias, b0, b1);
-          mma_bf16_16816(d, A1, b2, b3);
-          mma_bf16_16816(d, kBias, b2, b3);
-          acc[t][0] = fmaf(s_lo, d[0], acc[t][0]);
-          acc[t][1] = fmaf(s_lo, d[1], acc[t][1]);
-          acc[t][2] = fmaf(s_hi, d[2], acc[t][2]);
-          acc[t][3] = fmaf(s_hi, d[3], acc[t][3]);
-        }
+    for (int u = 0; u < kT4Units; ++u) {
+      if (c0 + u < kr.e) {
+        const uint8_t *p = base + static_cast<int64_t>(c0 + u) * kS4UnitBytes;
+        lo[u] = ld_stream_v4(p + lane * 16);
+        hi[u] = ld_stream_v4(p + 512 + lane * 16);
+        sc[u] = ld_stream_v4(p + kS4CodeBytes + gid * 16);
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty_bar[s]);
-
-    const bool tile_done = (end == tile_end) || (end == u1);
-    if (tile_done) {
-      float *rb = red + (tile_count & 1) * (kS4Consumers * NT * 128);
+  };
+  load(kr.b);
+  pdl_launch_dependents();
+  pdl_wait();
+  for (int c0 = kr.b; c0 < kr.e; c0 += kT4Units) {
+#pragma unroll
+    for (int u = 0; u < kT4Units; ++u) {
+      const int c = c0 + u;
+      if (c < kr.e) {
+        // B fragments straight from the activations (L1-cached), permuted to the
+        // nibble-pair order: pieces (x[8m+i], x[8m+4+i]) for this lane's m = 4(4c+j)+tid
+        s4_unit_gx<NT>(acc, lo[u], hi[u], sc[u], x, K, n_vec, c * 128);
+      }
+    }
+    if (c0 + kT4Units < kr.e) load(c0 + kT4Units);
+  }
+  // reduce over warps (and cluster ranks) in fixed order
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) red[((warp * NT + t) * 4 + e) * 32 + lane] = acc[0][t][e] + acc[1][t][e];
+  __syncthreads();
+  float v[NT][4];
+  if (warp == 0) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float sum = 0.f;
+#pragma unroll
+        for (int q = 0; q < kT4Warps; ++q) sum += red[((q * NT + t) * 4 + e) * 32 + lane];
+        v[t][e] = sum;
+      }
+  }
+  if constexpr (CS > 1) {
+    cg::cluster_group cluster = cg::this_cluster();
+    float *slot0 = red + kT4Warps * NT * 128;
+    if (warp == 0 && rank > 0) {
+      float *remote = cluster.map_shared_rank(slot0, 0);
 #pragma unroll
       for (int t = 0; t < NT; ++t)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) rb[((warp * NT + t) * 4 + e) * 32 + lane] = acc[t][e];
-      named_sync(1, 32 * kS4Consumers);
-      if (warp == 0) {
-        float v[NT][4];
-#pragma unroll
-        for (int t = 0; t < NT; ++t)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float sum = 0.f;
-#pragma unroll
-            for (int q = 0; q < kS4Consumers; ++q) sum += rb[((q * NT + t) * 4 + e) * 32 + lane];
-            v[t][e] = sum;
-          }
-        const bool whole = tile_begin >= u0 && tile_end <= u1;
-        bool store = whole && !failed;
-        if (!whole && !failed) {
-          // Publish this CTA's partial; the last contributor combines in CTA order.
-          const int side = (tile == u0 / w.cpt) ? 0 : 1;
-          float *slots = reinterpret_cast<float *>(ws + s4_slots_off(static_cast<int64_t>(w.U / w.cpt)));
-          float *mine = slots + (static_cast<int64_t>(cta) * 2 + side) * (NT * 128);
-#pragma unroll
-          for (int t = 0; t < NT; ++t)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) mine[(t * 4 + e) * 32 + lane] = v[t][e];
-          __threadfence();
-          __syncwarp();
-          int *counter = reinterpret_cast<int *>(ws + s4_counters_off()) + tile;
-          const int c_first = s4_owner(tile_begin, w), c_last = s4_owner(tile_end - 1, w);
-          int prev = 0;
-          if (lane == 0) prev = atomicAdd(counter, 1);
-          prev = __shfl_sync(0xffffffffu, prev, 0);
-          if (prev == c_last - c_first) {
-            __threadfence();
-#pragma unroll
-            for (int t = 0; t < NT; ++t)
-#pragma unroll
-              for (int e = 0; e < 4; ++e) v[t][e] = 0.f;
-            for (int cc = c_first; cc <= c_last; ++cc) {
-              const int sd = (tile == s4_unit_begin(cc, w) / w.cpt) ? 0 : 1;
-              const float *theirs = slots + (static_cast<int64_t>(cc) * 2 + sd) * (NT * 128);
-#pragma unroll
-              for (int t = 0; t < NT; ++t)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) v[t][e] += __ldcg(theirs + (t * 4 + e) * 32 + lane);
-            }
-            if (lane == 0) *counter = 0;  // leave the workspace zeroed for the next call
-            store = true;
-          }
-        }
-        if (store) {
-          const int row0 = static_cast<int>(tile) * 16;
-#pragma unroll
-          for (int t = 0; t < NT; ++t)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int row = row0 + gid + ((e >> 1) << 3);
-              const int vv = t * 8 + tid * 2 + (e & 1);
-              if (vv < n_vec) {
-                const int64_t o = static_cast<int64_t>(vv) * N + row;
-                float r = v[t][e];
-                if (residual) r += bf16_bits_to_float(residual[o]);
-                y[o] = float_to_bf16_bits(r);
-              }
-            }
-        }
-      }
-      ++tile_count;
+        for (int e = 0; e < 4; ++e) remote[((rank * NT + t) * 4 + e) * 32 + lane] = v[t][e];
     }
-    pos = end;
-    ++step;
+    cluster.sync();
+    if (rank != 0) return;
+    if (warp == 0) {
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+#pragma unroll
+          for (int r = 1; r < CS; ++r) v[t][e] += slot0[((r * NT + t) * 4 + e) * 32 + lane];
+    }
   }
+  if (warp == 0) s4_store<NT>(v, tile, N, n_vec, y, residual);
 }
 
 // Repack natural-layout codes [N, K/2] + scales [N, K/32] into GEMV units.
@@ -314,47 +253,57 @@ __global__ void pack_s4g32_kernel(const uint8_t *__restrict__ codes,
   reinterpret_cast<uint4 *>(out)[p] = make_uint4(words[0], words[1], words[2], words[3]);
 }
 
-static int s4_grid(int64_t units) {
-  const int64_t g = sm_count();
-  return static_cast<int>(units < g ? units : g);
+template <int NT, int CS>
+static int launch_s4_tile(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,
+                          int n_vec, const uint16_t *res, bool pdl, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((N / 16) * CS));
+  cfg.blockDim = dim3(32 * kT4Warps);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (CS > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = CS;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  cudaError_t e =
+      cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS>, packed, x, y, N, K, n_vec, res);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    (void)cudaGetLastError();
+    return IRON_ERR_CUDA;
+  }
+  return IRON_OK;
 }
 
 template <int NT>
-static int launch_s4_stream(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,
-                            int n_vec, const uint16_t *res, uint8_t *ws, bool pdl,
-                            cudaStream_t s) {
-  S4Work w;
-  w.cpt = K / 128;
-  w.U = static_cast<int64_t>(N / 16) * w.cpt;
-  w.G = s4_grid(w.U);
-  const size_t smem = static_cast<size_t>(kS4Stages) * kS4StepUnits * kS4UnitBytes +
-                      2 * kS4Consumers * NT * 128 * sizeof(float);
-  static bool attr_set[9] = {false};
-  if (!attr_set[NT]) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_s4g32_stream_kernel<NT>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) {
-      set_last_cuda_error(e);
-      return IRON_ERR_CUDA;
-    }
-    attr_set[NT] = true;
+static int launch_s4_tile_cs(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,
+                             int n_vec, const uint16_t *res, bool pdl, cudaStream_t s) {
+  // split K over a cluster until every SM holds >= 2 CTAs (and each warp >= 1 chunk)
+  const int tiles = N / 16, cpt = K / 128;
+  int cs = 1;
+  while (cs < 8 && tiles * cs < 2 * sm_count() && cpt >= kT4Warps * cs * 2) cs *= 2;
+  switch (cs) {
+    case 1: return launch_s4_tile<NT, 1>(packed, x, y, N, K, n_vec, res, pdl, s);
+    case 2: return launch_s4_tile<NT, 2>(packed, x, y, N, K, n_vec, res, pdl, s);
+    case 4: return launch_s4_tile<NT, 4>(packed, x, y, N, K, n_vec, res, pdl, s);
+    default: return launch_s4_tile<NT, 8>(packed, x, y, N, K, n_vec, res, pdl, s);
   }
-  return launch(gemv_s4g32_stream_kernel<NT>, dim3(w.G), dim3(kS4Threads), smem, s, pdl, packed, x,
-                y, N, K, n_vec, res, ws, w);
 }
 
 }  // namespace iron
 
 using namespace iron;
-
-extern "C" size_t iron_gemv_int4g32_workspace_bytes(int N, int K, int n_vec) {
-  if (N <= 0 || K <= 0 || n_vec <= 0) return 0;
-  const int nt = n_vec <= 8 ? 1 : n_vec <= 16 ? 2 : n_vec <= 32 ? 4 : 8;
-  const int64_t tiles = N / 16;
-  return static_cast<size_t>(s4_slots_off(tiles) +
-                             static_cast<int64_t>(kS4MaxCtas) * 2 * nt * 128 * sizeof(float));
-}
 
 extern "C" int iron_pack_int4g32(const uint8_t *codes, const uint16_t *scales, uint8_t *packed,
                                  int N, int K, void *stream) {
@@ -369,19 +318,17 @@ extern "C" int iron_pack_int4g32(const uint8_t *codes, const uint16_t *scales, u
 }
 
 extern "C" int iron_gemv_int4g32(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N,
-                                 int K, int n_vec, const uint16_t *residual, void *workspace,
-                                 size_t workspace_bytes, unsigned flags, void *stream) {
-  if (!packed || !x || !y || !workspace) return IRON_ERR_NULL;
+                                 int K, int n_vec, const uint16_t *residual, unsigned flags,
+                                 void *stream) {
+  if (!packed || !x || !y) return IRON_ERR_NULL;
   if (N <= 0 || K <= 0 || n_vec <= 0 || n_vec > 64) return IRON_ERR_SHAPE;
   if (K % 128 || N % 16) return IRON_ERR_SHAPE;
-  if (!aligned16(packed) || !aligned16(x) || !aligned16(workspace)) return IRON_ERR_ALIGN;
-  if (workspace_bytes < iron_gemv_int4g32_workspace_bytes(N, K, n_vec)) return IRON_ERR_WORKSPACE;
-  if (sm_count() > kS4MaxCtas) return IRON_ERR_UNSUPPORTED;
+  if (static_cast<int64_t>(N / 16) * (K / 128) > 0x7fffffffLL) return IRON_ERR_SHAPE;
+  if (!aligned16(packed) || !aligned16(x)) return IRON_ERR_ALIGN;
   const bool pdl = (flags & IRON_FLAG_PDL) != 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  uint8_t *ws = static_cast<uint8_t *>(workspace);
-  if (n_vec <= 8) return launch_s4_stream<1>(packed, x, y, N, K, n_vec, residual, ws, pdl, s);
-  if (n_vec <= 16) return launch_s4_stream<2>(packed, x, y, N, K, n_vec, residual, ws, pdl, s);
-  if (n_vec <= 32) return launch_s4_stream<4>(packed, x, y, N, K, n_vec, residual, ws, pdl, s);
-  return launch_s4_stream<8>(packed, x, y, N, K, n_vec, residual, ws, pdl, s);
+  if (n_vec <= 8) return launch_s4_tile_cs<1>(packed, x, y, N, K, n_vec, residual, pdl, s);
+  if (n_vec <= 16) return launch_s4_tile_cs<2>(packed, x, y, N, K, n_vec, residual, pdl, s);
+  if (n_vec <= 32) return launch_s4_tile_cs<4>(packed, x, y, N, K, n_vec, residual, pdl, s);
+  return launch_s4_tile_cs<8>(packed, x, y, N, K, n_vec, residual, pdl, s);
 }

@@ -126,26 +126,13 @@ class GEMV(MLIROperator):
                   _lib.current_stream())
         return out
 
-    def workspace(self):
-        """Zero-filled scratch for the int4g32 kernel (one per operator; calls
-        that share it must not overlap on the GPU)."""
-        import torch
-
-        ws = getattr(self, "_ws", None)
-        if ws is None or ws.device.index != torch.cuda.current_device():
-            nbytes = _lib.load().iron_gemv_int4g32_workspace_bytes(self.M, self.K, self.n_vec)
-            ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
-            self._ws = ws
-        return ws
-
     def _launch(self, *bufs, stream, residual=None, flags=0):
         p = _lib.dptr
         res = p(residual) if residual is not None else None
         if self.weight_dtype == "int4g32":
             w, x, y = bufs
-            ws = self.workspace()
             _lib.call("iron_gemv_int4g32", p(w), p(x), p(y), self.M, self.K, self.n_vec, res,
-                      ws.data_ptr(), ws.numel(), flags, stream)
+                      flags, stream)
             return
         A, x, y = bufs
         epi = _lib.IRON_EPI_GELU if self.epilogue == "gelu" else _lib.IRON_EPI_NONE

@@ -51,11 +51,10 @@ def test_null_pointer_rejected_without_launch():
     # Host-side validation runs before any CUDA call, so this is safe on a CPU box.
     st = _lib.load().iron_gemv_bf16(None, None, None, 16, 16, 16, 1, 0, 0, 0, 1, None, 0, 0, None)
     assert st == -1
-    st = _lib.load().iron_gemv_int4g32(16, 32, 16, 16, 100, 1, None, 64, 1 << 20, 0, None)  # K % 128
+    st = _lib.load().iron_gemv_int4g32(16, 32, 16, 16, 100, 1, None, 0, None)  # K % 128
     assert st == -2
-    st = _lib.load().iron_gemv_int4g32(16, 32, 16, 16, 128, 1, None, 64, 16, 0, None)  # small ws
-    assert st == -6
-    assert _lib.load().iron_gemv_int4g32_workspace_bytes(8192, 2048, 1) > 8192 // 16 * 4
+    st = _lib.load().iron_gemv_int4g32(16, 32, 16, 24, 128, 1, None, 0, None)  # N % 16
+    assert st == -2
     st = _lib.load().iron_dequant_u4(16, 32, 2048, 1024, 33, None)  # odd group
     assert st == -2
 

@@ -135,10 +135,6 @@ def test_gemv_int4g32(N, K, nv):
     errors, _, _ = run_test(op, {"packed": packed, "vector": vec}, {"output": exp},
                             rel_tol=2e-2, abs_tol=1e-2)
     assert not errors
-    ws = op.workspace()
-    assert int(ws[:4].view(torch.int32).item()) == 0, "device error word set"
-    counters = ws[16:16 + (N // 16) * 4].view(torch.int32)
-    assert int(counters.abs().sum().item()) == 0, "split-tile counters not reset"
 
 
 def test_gemv_int4g32_residual_and_determinism():
@@ -147,18 +143,14 @@ def test_gemv_int4g32_residual_and_determinism():
     R = torch.randn(nv, N).to(torch.bfloat16)
     x, r = X.cuda(), R.cuda()
     packed = GEMV.pack_int4g32(codes.cuda(), scales.cuda())
-    op = GEMV(M=N, K=K, weight_dtype="int4g32", n_vec=nv)
-    ws = op.workspace()
     outs = []
     for _ in range(3):
         y = torch.empty(nv, N, dtype=torch.bfloat16, device="cuda")
         _lib.call("iron_gemv_int4g32", packed.data_ptr(), x.data_ptr(), y.data_ptr(), N, K, nv,
-                  r.data_ptr(), ws.data_ptr(), ws.numel(), 0, _lib.current_stream())
+                  r.data_ptr(), 0, _lib.current_stream())
         outs.append(y.cpu())
     assert all(torch.equal(outs[0], o) for o in outs[1:]), "int4 GEMV not bitwise deterministic"
     assert_close(outs[0], ops.add(ops.gemv_multi(W, X), R), 2e-2, 1e-2, what="int4+residual")
-    counters = ws[16:16 + (N // 16) * 4].view(torch.int32)
-    assert int(counters.abs().sum().item()) == 0, "split-tile counters not reset"
 
 
 def test_gemv_int4g32_pdl_chain_in_graph():
@@ -170,19 +162,17 @@ def test_gemv_int4g32_pdl_chain_in_graph():
         codes, scales, X, W = _s4_case(N, K, 1, seed=20 + i)
         mats.append(GEMV.pack_int4g32(codes.cuda(), scales.cuda()))
     x = torch.randn(K).to(torch.bfloat16).cuda()
-    op = GEMV(M=N, K=K, weight_dtype="int4g32")
-    ws = op.workspace()
     ys = [torch.empty(N, dtype=torch.bfloat16, device="cuda") for _ in mats]
     for m, y in zip(mats, ys):
         _lib.call("iron_gemv_int4g32", m.data_ptr(), x.data_ptr(), y.data_ptr(), N, K, 1, None,
-                  ws.data_ptr(), ws.numel(), 0, _lib.current_stream())
+                  0, _lib.current_stream())
     ref = [y.clone() for y in ys]
     s = torch.cuda.Stream()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=s):
         for m, y in zip(mats, ys):
             _lib.call("iron_gemv_int4g32", m.data_ptr(), x.data_ptr(), y.data_ptr(), N, K, 1, None,
-                      ws.data_ptr(), ws.numel(), _lib.IRON_FLAG_PDL, s.cuda_stream)
+                      _lib.IRON_FLAG_PDL, s.cuda_stream)
     for y in ys:
         y.zero_()
     g.replay()
