@@ -117,6 +117,73 @@ int iron_dequant_s4g32_rows(const uint8_t *codes, const uint16_t *scales,
 int iron_dequant_u4(const uint8_t *payload, uint16_t *out, int64_t size,
                     int tile_size, int group_size, void *stream);
 
+
+/* ---- RMSNorm ----------------------------------------------------------------
+ * Replaces RMSNorm(size, ..., tile_size, weighted, epsilon) -- iron/operators/rms_norm/op.py:19-122,
+ * golden iron/operators/rms_norm/reference.py:7-16.
+ *   y[r, :] = x[r, :] / sqrt(mean(x[r, :]^2) + eps) * (weight ? weight : 1), fp32 statistics.
+ *   residual != NULL: x := bf16(x + residual) first (stored to x_out if != NULL) --
+ *   the decode block's residual add fused with the following norm.
+ */
+int iron_rmsnorm(const uint16_t *x, const uint16_t *residual, uint16_t *x_out,
+                 const uint16_t *weight, uint16_t *y, int rows, int cols, float eps,
+                 unsigned flags, void *stream);
+
+/* ---- RoPE -------------------------------------------------------------------
+ * Replaces RoPE(rows, cols, angle_rows, method_type) -- iron/operators/rope/op.py:18-92,
+ * golden iron/operators/rope/reference.py:69-102. angles: [*, cols] interleaved
+ * cos/sin (bf16 `angles` or fp32 `angles_f32`, one of them). Row r of x uses angle
+ * row r / (rows / angle_rows), or pos[r / (rows / angle_rows)] when pos != NULL.
+ * method 0: two halves (HF); 1: interleaved pairs. fp32 math, one rounding.
+ */
+int iron_rope(const uint16_t *x, const uint16_t *angles, const float *angles_f32, uint16_t *y,
+              int rows, int cols, int angle_rows, const int32_t *pos, int method,
+              unsigned flags, void *stream);
+
+/* ---- Softmax ----------------------------------------------------------------
+ * Replaces Softmax(rows, cols, ..., vector_size_parameter) -- iron/operators/softmax/op.py:21-97,
+ * golden iron/operators/softmax/reference.py:9-11, mask iron/operators/softmax/design.py:85-91.
+ * Row softmax over the first `valid` columns (valid_dev, if set, is read on the
+ * device at run time); columns >= valid are 0. fp32 math.
+ */
+int iron_softmax(const uint16_t *x, uint16_t *y, int rows, int cols, int valid,
+                 const int32_t *valid_dev, unsigned flags, void *stream);
+
+/* ---- element-wise -------------------------------------------------------------
+ * Replaces SiLU (iron/operators/silu/op.py:12-26), ElementwiseMul
+ * (iron/operators/elementwise_mul/op.py:12-24), ElementwiseAdd
+ * (iron/operators/elementwise_add/op.py:12-24) and SwiGLUDecode's SiLU+Mul pair
+ * (iron/operators/swiglu_decode/op.py:56-62). op: 0 silu(a), 1 a*b, 2 a+b, 3 silu(a)*b.
+ */
+int iron_eltwise(const uint16_t *a, const uint16_t *b, uint16_t *y, int64_t n, int op,
+                 unsigned flags, void *stream);
+
+/* ---- StridedCopy ------------------------------------------------------------
+ * Replaces StridedCopy -- iron/operators/strided_copy/op.py:18-100, golden
+ * iron/operators/strided_copy/reference.py:37-75 (the decode KV-cache append).
+ * Each access pattern (<= 4 dims, element strides) is padded to 4-D; the innermost
+ * dimension is split into `channels` parts; element j of channel c moves from the
+ * input pattern (+ *in_addend_dev) to the output pattern (+ *out_addend_dev).
+ * Addends are element counts read on the device (runtime parameters). Elements
+ * whose source or destination falls outside [0, in_size) / [0, out_size) are skipped.
+ */
+int iron_strided_copy(const void *in, void *out, int elem_size, int ndim_in,
+                      const int64_t *in_sizes, const int64_t *in_strides, int64_t in_offset,
+                      int ndim_out, const int64_t *out_sizes, const int64_t *out_strides,
+                      int64_t out_offset, int channels, const int32_t *in_addend_dev,
+                      const int32_t *out_addend_dev, int64_t in_size, int64_t out_size,
+                      unsigned flags, void *stream);
+
+/* ---- Repeat / Transpose -------------------------------------------------------
+ * Replace Repeat (iron/operators/repeat/op.py:17-69; repeat_interleave along dim 0 of
+ * rows x row_bytes) and Transpose (iron/operators/transpose/op.py:18-120; `batches`
+ * independent M x N -> N x M, elem_size 2 or 4).
+ */
+int iron_repeat_interleave(const void *in, void *out, int64_t rows, int64_t row_bytes,
+                           int repeat, unsigned flags, void *stream);
+int iron_transpose(const void *in, void *out, int M, int N, int batches, int elem_size,
+                   unsigned flags, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -33,6 +33,14 @@ SIGNATURES: dict[str, list] = {
     "iron_gemv_int4g32": [P, P, P, c_int, c_int, c_int, P, c_uint, P],
     "iron_dequant_s4g32_rows": [P, P, P, c_int, c_int, P],
     "iron_dequant_u4": [P, P, c_int64, c_int, c_int, P],
+    "iron_rmsnorm": [P, P, P, P, P, c_int, c_int, c_float, c_uint, P],
+    "iron_rope": [P, P, P, P, c_int, c_int, c_int, P, c_int, c_uint, P],
+    "iron_softmax": [P, P, c_int, c_int, c_int, P, c_uint, P],
+    "iron_eltwise": [P, P, P, c_int64, c_int, c_uint, P],
+    "iron_strided_copy": [P, P, c_int, c_int, P, P, c_int64, c_int, P, P, c_int64, c_int, P, P,
+                          c_int64, c_int64, c_uint, P],
+    "iron_repeat_interleave": [P, P, c_int64, c_int64, c_int, c_uint, P],
+    "iron_transpose": [P, P, c_int, c_int, c_int, c_int, c_uint, P],
 }
 _RESTYPES = {"iron_strerror": c_char_p}
 
