@@ -184,6 +184,24 @@ int iron_repeat_interleave(const void *in, void *out, int64_t rows, int64_t row_
 int iron_transpose(const void *in, void *out, int M, int N, int batches, int elem_size,
                    unsigned flags, void *stream);
 
+/* ---- GQA decode attention (split-KV) -------------------------------------------
+ * Replaces the decode attention steps of IRON's Llama pipeline (Repeat x2, scores
+ * GEMV, scale, masked Softmax, per-head Transpose, context GEMV:
+ * iron/applications/llama_3.2_1b/llama_npu.py:495-529; CPU truth
+ * iron/applications/llama_3.2_1b/llama_cpu.py:118-140).
+ *   q: bf16 [B, Hq, D]; caches: element (b, h, t, d) at b*kv_batch_stride +
+ *   h*kv_head_stride + t*D + d; lens: int32 [B] valid tokens (device).
+ *   out[b, hq] = softmax(scale * q K_{hq/(Hq/Hkv)}^T over t < lens[b]) V, fp32 softmax.
+ *   D == 64; Hq % Hkv == 0, Hq/Hkv <= 16. Long caches are split over CTAs; then
+ *   `workspace` (>= iron_attn_decode_workspace_bytes) holds the partials (no
+ *   zeroing needed; calls sharing a workspace must not overlap on the GPU).
+ */
+size_t iron_attn_decode_workspace_bytes(int B, int Hq, int Hkv, int Lmax);
+int iron_attn_decode(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                     const int32_t *lens, uint16_t *out, int B, int Hq, int Hkv, int D, int Lmax,
+                     int64_t kv_batch_stride, int64_t kv_head_stride, float scale,
+                     void *workspace, size_t workspace_bytes, unsigned flags, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

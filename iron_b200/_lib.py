@@ -41,8 +41,11 @@ SIGNATURES: dict[str, list] = {
                           c_int64, c_int64, c_uint, P],
     "iron_repeat_interleave": [P, P, c_int64, c_int64, c_int, c_uint, P],
     "iron_transpose": [P, P, c_int, c_int, c_int, c_int, c_uint, P],
+    "iron_attn_decode_workspace_bytes": [c_int, c_int, c_int, c_int],
+    "iron_attn_decode": [P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int64, c_int64,
+                         c_float, P, c_size_t, c_uint, P],
 }
-_RESTYPES = {"iron_strerror": c_char_p}
+_RESTYPES = {"iron_strerror": c_char_p, "iron_attn_decode_workspace_bytes": c_size_t}
 
 _lock = threading.Lock()
 _lib = None

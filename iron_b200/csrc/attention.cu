@@ -1,0 +1,313 @@
+// GQA decode attention with split-KV (flash-decoding) and the combine pass.
+//
+// Replaces the decode attention of IRON's Llama pipeline -- the Repeat x2,
+// score GEMV, scale, masked Softmax, 32x Transpose and context GEMV of
+// iron/applications/llama_3.2_1b/llama_npu.py:495-529 (CPU truth
+// iron/applications/llama_3.2_1b/llama_cpu.py:118-140) -- which copy the whole
+// padded cache several times per token, by one pass over each sequence's valid
+// K/V rows.
+//
+// One CTA = (split, kv head, sequence); its four warps take 16-token blocks in
+// turn. The query heads sharing the kv head (the GQA group, <= 16) are the rows
+// of m16n8k16 bf16 MMAs: S = Q K^T reads K fragments straight from the cache rows
+// (the logical k order inside an MMA is free as long as A and B agree, so each
+// lane feeds its own 16 contiguous bytes), the online softmax runs in fp32 in
+// exp2 space, and O += P V takes P from the S accumulators and V through a
+// padded shared-memory tile read with ldmatrix.trans. Partial (max, sum, O) of
+// each split go to the workspace; a second kernel merges the splits.
+// Memory-bound: each cache row is read once per kv head, not once per q head.
+#include "common.cuh"
+
+namespace iron {
+
+constexpr int kAD = 64;       // head dim (IRON's MHA supports d = 64 only, mha/op.py:39-41)
+constexpr int kAWarps = 4;
+constexpr int kABlk = 16;     // tokens per warp step
+constexpr int kAVStride = 72; // padded V tile row (elements): 144 B, conflict-free ldmatrix
+constexpr int kAMinChunk = 256;
+
+struct AttnArgs {
+  const uint16_t *q;    // [B, Hq, 64]
+  const uint16_t *k;    // cache, element (b, h, t, d) at b*bstride + h*hstride + t*64 + d
+  const uint16_t *v;
+  const int *lens;      // [B] valid tokens per sequence
+  uint16_t *out;        // [B, Hq, 64]
+  float *ws;            // [B, Hq, splits, 2 + 64] partial (max, sum, o)
+  int64_t bstride, hstride;
+  int Hq, Hkv, splits, chunk;
+  float scale_log2;     // softmax scale * log2(e)
+};
+
+__device__ __forceinline__ uint4 ldg16(const uint16_t *p) {
+  return __ldg(reinterpret_cast<const uint4 *>(p));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void *smem) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a));
+}
+
+__global__ void __launch_bounds__(32 * kAWarps)
+attn_decode_kernel(AttnArgs a) {
+  __shared__ __align__(16) uint16_t vtile[kAWarps][kABlk * kAVStride];
+  __shared__ float red_m[kAWarps][16], red_l[kAWarps][16];
+  __shared__ float red_o[kAWarps][16][kAD];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tid = lane & 3;
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int g = a.Hq / a.Hkv;      // query heads per kv head (MMA rows used)
+  const int hq0 = h * g;
+
+  pdl_wait();
+  const int len = a.lens[b];
+  const int t_begin = split * a.chunk;
+  const int t_end = min(len, t_begin + a.chunk);
+
+  const uint16_t *kb = a.k + b * a.bstride + h * a.hstride;
+  const uint16_t *vb = a.v + b * a.bstride + h * a.hstride;
+
+  // Q fragments (rows = heads of the group; rows >= g are zero). k-step ks covers
+  // physical d = 32*(ks/2) + 8*tid + 4*(ks%2) + {0,1 | 2,3} for logical {2tid | 2tid+8}.
+  uint32_t qa[4][4];
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+    const int d = 32 * (ks >> 1) + 8 * tid + 4 * (ks & 1);
+    const uint32_t *q0 = reinterpret_cast<const uint32_t *>(a.q + (static_cast<int64_t>(b) * a.Hq + hq0 + gid) * kAD + d);
+    const uint32_t *q8 = reinterpret_cast<const uint32_t *>(a.q + (static_cast<int64_t>(b) * a.Hq + hq0 + gid + 8) * kAD + d);
+    qa[ks][0] = gid < g ? q0[0] : 0u;
+    qa[ks][1] = gid + 8 < g ? q8[0] : 0u;
+    qa[ks][2] = gid < g ? q0[1] : 0u;
+    qa[ks][3] = gid + 8 < g ? q8[1] : 0u;
+  }
+
+  float o[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m_lo = -INFINITY, m_hi = -INFINITY;  // running max of rows gid / gid+8 (log2 units)
+  float l_lo = 0.f, l_hi = 0.f;              // this lane's share of the running sums
+  uint16_t *vs = vtile[warp];
+
+  // register prefetch of one block: K rows (token gid of each 8-token half, 16 B x 2)
+  // and this lane's four 16-byte pieces of the V tile
+  auto load_block = [&](int blk, uint4 (&kr)[2][2], uint4 (&vr)[4]) {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int t = blk + nt * 8 + gid;
+#pragma unroll
+      for (int db = 0; db < 2; ++db)
+        kr[nt][db] = t < t_end ? ldg16(kb + static_cast<int64_t>(t) * kAD + db * 32 + tid * 8)
+                               : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int idx = i * 32 + lane, row = idx >> 3, c16 = idx & 7;
+      const int t = blk + row;
+      vr[i] = t < t_end ? ldg16(vb + static_cast<int64_t>(t) * kAD + c16 * 8) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+
+  uint4 kr[2][2], vr[4];
+  int blk = t_begin + warp * kABlk;
+  if (blk < t_end) load_block(blk, kr, vr);
+  for (; blk < t_end; blk += kAWarps * kABlk) {
+    // stage V, then prefetch the next block while this one computes
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int idx = i * 32 + lane, row = idx >> 3, c16 = idx & 7;
+      *reinterpret_cast<uint4 *>(vs + row * kAVStride + c16 * 8) = vr[i];
+    }
+    uint4 kc[2][2] = {{kr[0][0], kr[0][1]}, {kr[1][0], kr[1][1]}};
+    const int nxt = blk + kAWarps * kABlk;
+    if (nxt < t_end) load_block(nxt, kr, vr);
+
+    // S = Q K^T for the two 8-token halves
+    float s[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        const uint4 &w = kc[nt][ks >> 1];
+        const uint32_t b0 = (ks & 1) ? w.z : w.x, b1 = (ks & 1) ? w.w : w.y;
+        mma_bf16_16816(s[nt], qa[ks], b0, b1);
+      }
+    }
+    // scale, mask, block max per row
+    float mx_lo = -INFINITY, mx_hi = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int t = blk + nt * 8 + 2 * tid + (e & 1);
+        s[nt][e] = t < t_end ? s[nt][e] * a.scale_log2 : -INFINITY;
+        if (e < 2) mx_lo = fmaxf(mx_lo, s[nt][e]); else mx_hi = fmaxf(mx_hi, s[nt][e]);
+      }
+#pragma unroll
+    for (int o_ = 1; o_ <= 2; o_ <<= 1) {
+      mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, o_));
+      mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, o_));
+    }
+    const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
+    const float al_lo = (mn_lo == -INFINITY) ? 1.f : exp2f(m_lo - mn_lo);
+    const float al_hi = (mn_hi == -INFINITY) ? 1.f : exp2f(m_hi - mn_hi);
+    m_lo = mn_lo;
+    m_hi = mn_hi;
+    float p[2][4];
+    float ps_lo = 0.f, ps_hi = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float mr = (e < 2) ? mn_lo : mn_hi;
+        p[nt][e] = (mr == -INFINITY) ? 0.f : exp2f(s[nt][e] - mr);
+        if (e < 2) ps_lo += p[nt][e]; else ps_hi += p[nt][e];
+      }
+    l_lo = l_lo * al_lo + ps_lo;
+    l_hi = l_hi * al_hi + ps_hi;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      o[j][0] *= al_lo; o[j][1] *= al_lo;
+      o[j][2] *= al_hi; o[j][3] *= al_hi;
+    }
+    // P as the A operand (rows = heads, k = the 16 tokens)
+    const uint32_t pa[4] = {pack_bf16x2(p[0][0], p[0][1]), pack_bf16x2(p[0][2], p[0][3]),
+                            pack_bf16x2(p[1][0], p[1][1]), pack_bf16x2(p[1][2], p[1][3])};
+    __syncwarp();  // V tile stores visible to ldmatrix
+#pragma unroll
+    for (int jp = 0; jp < 4; ++jp) {
+      const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+      const int col = jp * 16 + (lane >> 4) * 8;
+      uint32_t vb4[4];
+      ldsm_x4_trans(vb4, vs + row * kAVStride + col);
+      mma_bf16_16816(o[2 * jp], pa, vb4[0], vb4[1]);
+      mma_bf16_16816(o[2 * jp + 1], pa, vb4[2], vb4[3]);
+    }
+    __syncwarp();  // done reading the V tile before the next block overwrites it
+  }
+  // full row sums across the four lanes of each row
+#pragma unroll
+  for (int o_ = 1; o_ <= 2; o_ <<= 1) {
+    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, o_);
+    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, o_);
+  }
+  // merge the four warps
+  if (tid == 0) {
+    red_m[warp][gid] = m_lo; red_m[warp][gid + 8] = m_hi;
+    red_l[warp][gid] = l_lo; red_l[warp][gid + 8] = l_hi;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    red_o[warp][gid][8 * j + 2 * tid] = o[j][0];
+    red_o[warp][gid][8 * j + 2 * tid + 1] = o[j][1];
+    red_o[warp][gid + 8][8 * j + 2 * tid] = o[j][2];
+    red_o[warp][gid + 8][8 * j + 2 * tid + 1] = o[j][3];
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+  for (int idx = threadIdx.x; idx < g * kAD; idx += blockDim.x) {
+    const int r = idx / kAD, d = idx % kAD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAWarps; ++w) M = fmaxf(M, red_m[w][r]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kAWarps; ++w) {
+        const float f = exp2f(red_m[w][r] - M);
+        L += red_l[w][r] * f;
+        O += red_o[w][r][d] * f;
+      }
+    }
+    const int64_t hq = static_cast<int64_t>(b) * a.Hq + hq0 + r;
+    if (a.splits == 1) {
+      a.out[hq * kAD + d] = float_to_bf16_bits(L > 0.f ? O / L : 0.f);
+    } else {
+      float *pw = a.ws + (hq * a.splits + split) * (2 + kAD);
+      if (d == 0) {
+        pw[0] = M;
+        pw[1] = L;
+      }
+      pw[2 + d] = O;
+    }
+  }
+}
+
+// Merge the splits of each (sequence, q head): out = sum_s O_s 2^(m_s - M) / sum_s L_s 2^(m_s - M).
+__global__ void attn_combine_kernel(const float *__restrict__ ws, uint16_t *__restrict__ out, int splits) {
+  pdl_wait();
+  const int64_t hq = blockIdx.x;
+  const int d = threadIdx.x;
+  const float *p = ws + hq * splits * (2 + kAD);
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, p[s * (2 + kAD)]);
+  float L = 0.f, O = 0.f;
+  if (M != -INFINITY) {
+    for (int s = 0; s < splits; ++s) {
+      const float *q = p + s * (2 + kAD);
+      const float f = exp2f(q[0] - M);
+      L += q[1] * f;
+      O += q[2 + d] * f;
+    }
+  }
+  out[hq * kAD + d] = float_to_bf16_bits(L > 0.f ? O / L : 0.f);
+  pdl_launch_dependents();
+}
+
+// Split count: enough CTAs for two waves of 148 SMs, chunks of >= 256 tokens.
+__host__ __device__ inline int attn_splits(int B, int Hkv, int Lmax, int sms) {
+  const int max_splits = (Lmax + kAMinChunk - 1) / kAMinChunk;
+  int s = 1;
+  while (s < max_splits && static_cast<int64_t>(B) * Hkv * s < 2LL * sms) s *= 2;
+  return s < max_splits ? s : max_splits;
+}
+
+}  // namespace iron
+
+using namespace iron;
+
+extern "C" size_t iron_attn_decode_workspace_bytes(int B, int Hq, int Hkv, int Lmax) {
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Lmax <= 0) return 0;
+  const int s = attn_splits(B, Hkv, Lmax, sm_count());
+  if (s == 1) return 0;
+  return static_cast<size_t>(B) * Hq * s * (2 + kAD) * sizeof(float);
+}
+
+extern "C" int iron_attn_decode(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                                const int32_t *lens, uint16_t *out, int B, int Hq, int Hkv, int D,
+                                int Lmax, int64_t kv_batch_stride, int64_t kv_head_stride,
+                                float scale, void *workspace, size_t workspace_bytes,
+                                unsigned flags, void *stream) {
+  if (!q || !k_cache || !v_cache || !lens || !out) return IRON_ERR_NULL;
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Lmax <= 0 || B > 65535 || Hkv > 65535) return IRON_ERR_SHAPE;
+  if (D != kAD) return IRON_ERR_UNSUPPORTED;
+  if (Hq % Hkv || Hq / Hkv > 16) return IRON_ERR_SHAPE;
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || (kv_batch_stride % 8) ||
+      (kv_head_stride % 8))
+    return IRON_ERR_ALIGN;
+  AttnArgs a;
+  a.q = q;
+  a.k = k_cache;
+  a.v = v_cache;
+  a.lens = lens;
+  a.out = out;
+  a.bstride = kv_batch_stride;
+  a.hstride = kv_head_stride;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.splits = attn_splits(B, Hkv, Lmax, sm_count());
+  a.chunk = ((Lmax + a.splits - 1) / a.splits + kAWarps * kABlk - 1) / (kAWarps * kABlk) * (kAWarps * kABlk);
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.ws = static_cast<float *>(workspace);
+  if (a.splits > 1) {
+    if (!workspace) return IRON_ERR_NULL;
+    if (workspace_bytes < iron_attn_decode_workspace_bytes(B, Hq, Hkv, Lmax)) return IRON_ERR_WORKSPACE;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool pdl = (flags & IRON_FLAG_PDL) != 0;
+  int st = launch(attn_decode_kernel, dim3(a.splits, Hkv, B), dim3(32 * kAWarps), 0, s, pdl, a);
+  if (st != IRON_OK || a.splits == 1) return st;
+  return launch(attn_combine_kernel, dim3(B * Hq), dim3(kAD), 0, s, pdl,
+                static_cast<const float *>(a.ws), out, a.splits);
+}
