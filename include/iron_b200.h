@@ -202,6 +202,27 @@ int iron_attn_decode(const uint16_t *q, const uint16_t *k_cache, const uint16_t 
                      int64_t kv_batch_stride, int64_t kv_head_stride, float scale,
                      void *workspace, size_t workspace_bytes, unsigned flags, void *stream);
 
+/* Decode attention without a caller-provided workspace. No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory -- code
+ * whose device memory is owned by another allocator (a serving engine that
+ * reserves the GPU's memory up front and hands out nothing more) and code on a
+ * latency-critical path where cudaMalloc's implicit device synchronisation is
+ * not acceptable. Same arguments and results as iron_attn_decode minus the
+ * workspace: the split partials go to a fixed 1 MiB array inside the library
+ * (per device, held until the process exits; enough for 32 query / 8 kv heads up
+ * to 32768 tokens at any batch). Requests needing more than 1 MiB
+ * (iron_attn_decode_workspace_bytes > 1 MiB) return IRON_ERR_WORKSPACE. The
+ * first call on a device looks up the array's device address (with that device
+ * current) and caches it, so make that first call before any stream capture.
+ * Nothing is allocated: no cudaMalloc or cudaFree. Every call uses the same
+ * array, so calls that overlap on the GPU (other streams, other threads) race;
+ * each call writes every partial it reads, so no clearing is needed.
+ */
+int iron_attn_decode_noalloc(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                             const int32_t *lens, uint16_t *out, int B, int Hq, int Hkv, int D,
+                             int Lmax, int64_t kv_batch_stride, int64_t kv_head_stride,
+                             float scale, unsigned flags, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

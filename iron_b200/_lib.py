@@ -44,6 +44,8 @@ SIGNATURES: dict[str, list] = {
     "iron_attn_decode_workspace_bytes": [c_int, c_int, c_int, c_int],
     "iron_attn_decode": [P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int64, c_int64,
                          c_float, P, c_size_t, c_uint, P],
+    "iron_attn_decode_noalloc": [P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int64, c_int64,
+                                 c_float, c_uint, P],
 }
 _RESTYPES = {"iron_strerror": c_char_p, "iron_attn_decode_workspace_bytes": c_size_t}
 

@@ -16,6 +16,8 @@
 // padded shared-memory tile read with ldmatrix.trans. Partial (max, sum, O) of
 // each split go to the workspace; a second kernel merges the splits.
 // Memory-bound: each cache row is read once per kv head, not once per q head.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace iron {
@@ -263,6 +265,43 @@ __host__ __device__ inline int attn_splits(int B, int Hkv, int Lmax, int sms) {
   return s < max_splits ? s : max_splits;
 }
 
+// ---------------------------------------------------------------------------
+// Fixed scratch for iron_attn_decode_noalloc: the split partials of callers that
+// cannot allocate device memory. 1 MiB per device (room for the partials of the
+// Llama shapes up to 32 K tokens), held by every GPU that loads the library
+// until the process exits.
+constexpr size_t kAttnScratchBytes = static_cast<size_t>(1) << 20;
+static __device__ __align__(256) float g_attn_scratch[kAttnScratchBytes / sizeof(float)];
+
+// Device address of g_attn_scratch on the current device. In host code the
+// symbol names a host-side stand-in, not device memory, so the address is
+// looked up once per device (with that device current) and cached.
+static float *attn_scratch_address(int *status) {
+  static std::mutex mu;
+  static float *cache[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    set_last_cuda_error(e);
+    *status = IRON_ERR_CUDA;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[dev]) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_scratch);
+    if (e != cudaSuccess || !p) {
+      set_last_cuda_error(e);
+      (void)cudaGetLastError();
+      *status = IRON_ERR_CUDA;
+      return nullptr;
+    }
+    cache[dev] = static_cast<float *>(p);
+  }
+  *status = IRON_OK;
+  return cache[dev];
+}
+
 }  // namespace iron
 
 using namespace iron;
@@ -310,4 +349,24 @@ extern "C" int iron_attn_decode(const uint16_t *q, const uint16_t *k_cache, cons
   if (st != IRON_OK || a.splits == 1) return st;
   return launch(attn_combine_kernel, dim3(B * Hq), dim3(kAD), 0, s, pdl,
                 static_cast<const float *>(a.ws), out, a.splits);
+}
+
+// Same computation as iron_attn_decode, for callers that cannot allocate the
+// workspace: the split partials go to the library's fixed per-device array.
+extern "C" int iron_attn_decode_noalloc(const uint16_t *q, const uint16_t *k_cache,
+                                        const uint16_t *v_cache, const int32_t *lens, uint16_t *out,
+                                        int B, int Hq, int Hkv, int D, int Lmax,
+                                        int64_t kv_batch_stride, int64_t kv_head_stride, float scale,
+                                        unsigned flags, void *stream) {
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Lmax <= 0) return IRON_ERR_SHAPE;
+  const size_t need = iron_attn_decode_workspace_bytes(B, Hq, Hkv, Lmax);
+  if (need > kAttnScratchBytes) return IRON_ERR_WORKSPACE;  // beyond the fixed array
+  void *ws = nullptr;
+  if (need > 0) {
+    int st = IRON_OK;
+    ws = attn_scratch_address(&st);
+    if (st != IRON_OK) return st;
+  }
+  return iron_attn_decode(q, k_cache, v_cache, lens, out, B, Hq, Hkv, D, Lmax, kv_batch_stride,
+                          kv_head_stride, scale, ws, need, flags, stream);
 }
