@@ -45,6 +45,10 @@ typedef enum {
 } iron_status_t;
 
 #define IRON_FLAG_PDL 0x1u
+/* iron_gemv_int4g32: SwiGLU epilogue. Each 16-row tile holds 8 gate rows then the
+ * 8 matching up rows; y gets N/2 columns: bf16(silu(gate)) * up, IRON's
+ * SwiGLUDecode rounding (iron/operators/swiglu_decode/reference.py:49-53). */
+#define IRON_FLAG_SWIGLU 0x2u
 
 /* GEMV epilogues (applied in fp32 to each output before the bf16 store). */
 #define IRON_EPI_NONE 0
@@ -94,8 +98,9 @@ int iron_pack_int4g32(const uint8_t *codes, const uint16_t *scales, uint8_t *pac
                       int N, int K, void *stream);
 /*   y[v, n] = sum_k bf16(q[n,k] * scale[n,k/32]) * x[v,k]  (fp32 accumulate; one
  *             bf16 rounding) + residual[v, n] if residual != NULL -- the dequantized
- *   weights are exactly IRON Dequant's. x: bf16 [n_vec, K]; y: bf16 [n_vec, N];
- *   K % 128 == 0, N % 16 == 0, 1 <= n_vec <= 64. Needs no workspace.
+ *   weights are exactly IRON Dequant's. x: bf16 [n_vec, K]; y: bf16 [n_vec, N]
+ *   (N/2 with IRON_FLAG_SWIGLU); K % 128 == 0, N % 16 == 0, 1 <= n_vec <= 64.
+ *   Needs no workspace.
  */
 int iron_gemv_int4g32(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,
                       int n_vec, const uint16_t *residual, unsigned flags, void *stream);
@@ -222,6 +227,26 @@ int iron_attn_decode_noalloc(const uint16_t *q, const uint16_t *k_cache, const u
                              const int32_t *lens, uint16_t *out, int B, int Hq, int Hkv, int D,
                              int Lmax, int64_t kv_batch_stride, int64_t kv_head_stride,
                              float scale, unsigned flags, void *stream);
+
+/* ---- decode-step glue ----------------------------------------------------------
+ * iron_rope_kv_append replaces the decode RoPE of q and k plus the two StridedCopy
+ * KV-cache writes at the runtime cache_offset (iron/applications/llama_3.2_1b/
+ * llama_npu.py:481-495, :1161-1169): qkv bf16 [B, (Hq + 2 Hkv) * D] (q heads, then k,
+ * then v), pos int32 [B] (tokens already cached), lut fp32 [ctx, D] interleaved
+ * cos/sin. Writes q_out bf16 [B, Hq, D] (two-halves RoPE), k/v into cache slot
+ * pos[b] (same strides as iron_attn_decode) and lens[b] = pos[b] + 1 (if lens).
+ * iron_embed: x[b] = table[tokens[b]] (bf16 rows of E). iron_argmax: first index
+ * of each row's maximum into out[b]; if pos != NULL, pos[b] += 1 afterwards (so a
+ * replayed decode graph feeds its own output to the next step).
+ */
+int iron_rope_kv_append(const uint16_t *qkv, const int32_t *pos, const float *lut,
+                        uint16_t *q_out, uint16_t *k_cache, uint16_t *v_cache, int32_t *lens,
+                        int B, int Hq, int Hkv, int D, int64_t kv_batch_stride,
+                        int64_t kv_head_stride, unsigned flags, void *stream);
+int iron_embed(const int32_t *tokens, const uint16_t *table, uint16_t *x, int B, int E,
+               unsigned flags, void *stream);
+int iron_argmax(const uint16_t *logits, int32_t *out, int B, int V, int32_t *pos, unsigned flags,
+                void *stream);
 
 #ifdef __cplusplus
 }

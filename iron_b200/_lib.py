@@ -16,6 +16,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libiron_b200.so"
 
 IRON_OK = 0
 IRON_FLAG_PDL = 0x1
+IRON_FLAG_SWIGLU = 0x2
 IRON_EPI_NONE = 0
 IRON_EPI_GELU = 1
 
@@ -46,6 +47,10 @@ SIGNATURES: dict[str, list] = {
                          c_float, P, c_size_t, c_uint, P],
     "iron_attn_decode_noalloc": [P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int64, c_int64,
                                  c_float, c_uint, P],
+    "iron_rope_kv_append": [P, P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int64, c_int64,
+                            c_uint, P],
+    "iron_embed": [P, P, P, c_int, c_int, c_uint, P],
+    "iron_argmax": [P, P, c_int, c_int, P, c_uint, P],
 }
 _RESTYPES = {"iron_strerror": c_char_p, "iron_attn_decode_workspace_bytes": c_size_t}
 

@@ -1,0 +1,216 @@
+"""Llama-3.2-1B decode on one B200: the fused int4 decode step of IRON's pipeline.
+
+IRON's decode step (iron/applications/llama_3.2_1b/llama_npu.py:459-584, driven
+by llama_forward_pass_decode :1156-1195) is one fused OperatorSequence of ~40
+operators per layer. Here the same computation -- RMSNorm, q/k/v projections,
+RoPE, KV-cache append, GQA attention, o projection, residual, RMSNorm, SwiGLU
+MLP, residual; final norm and tied lm-head (llama_cpu.py:170-285) -- runs as
+nine kernels per layer with int4 group-32 weights, for a batch of sequences at
+their own positions, captured once as a CUDA graph whose kernels are launched
+with programmatic dependent launch (each GEMV streams its weights while its
+predecessor finishes). Greedy argmax picks the next token on the device and
+advances every sequence's position, so graph replays chain decode steps.
+
+Weights are random (seeded): int4 codes ~ U{-8..7} and bf16 group scales, the
+embedding table being the exact dequantization of the tied lm-head weights.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from ... import _lib
+from ...operators.gemv.op import GEMV
+
+
+@dataclass
+class LlamaShape:
+    """Model dimensions (iron/applications/llama_3.2_1b/llama_inference_harness.py:28-48)."""
+
+    vocab_size: int = 128256
+    emb_dim: int = 2048
+    n_layers: int = 16
+    n_heads: int = 32
+    n_kv_groups: int = 8
+    head_dim: int = 64
+    hidden_dim: int = 8192
+    rope_base: float = 500000.0
+    eps: float = 1e-5
+
+    @property
+    def qkv_dim(self) -> int:
+        return (self.n_heads + 2 * self.n_kv_groups) * self.head_dim
+
+    def weight_params(self) -> int:
+        E, H, Q = self.emb_dim, self.hidden_dim, self.qkv_dim
+        per_layer = Q * E + E * self.n_heads * self.head_dim + 2 * H * E + E * H
+        return self.n_layers * per_layer + self.vocab_size * E
+
+
+def rope_table(head_dim: int, positions: int, base: float, device) -> torch.Tensor:
+    """fp32 [positions, head_dim] interleaved cos/sin
+    (iron/applications/llama_3.2_1b/llama_inference_harness.py:109-123)."""
+    inv = 1.0 / (base ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))
+    f = torch.outer(torch.arange(positions, dtype=torch.float32), inv)
+    t = torch.empty(positions, head_dim, dtype=torch.float32)
+    t[:, 0::2] = torch.cos(f)
+    t[:, 1::2] = torch.sin(f)
+    return t.to(device)
+
+
+class Int4Matrix:
+    """int4 group-32 weights: natural codes/scales (for checks) and the packed GEMV layout."""
+
+    def __init__(self, rows: int, cols: int, gen: torch.Generator, smin: float, smax: float,
+                 keep_natural: bool = False):
+        dev = gen.device
+        codes = torch.randint(0, 256, (rows, cols // 2), dtype=torch.uint8, device=dev, generator=gen)
+        scales = (torch.rand(rows, cols // 32, device=dev, generator=gen) * (smax - smin) + smin).to(torch.bfloat16)
+        self.rows, self.cols = rows, cols
+        self.packed = GEMV.pack_int4g32(codes, scales)
+        self.codes = codes if keep_natural else None
+        self.scales = scales if keep_natural else None
+        if not keep_natural:
+            del codes, scales
+
+    def dequant(self) -> torch.Tensor:
+        """Exact bf16 weights [rows, cols] (needs keep_natural)."""
+        out = torch.empty(self.rows, self.cols, dtype=torch.bfloat16, device=self.codes.device)
+        _lib.call("iron_dequant_s4g32_rows", self.codes.data_ptr(), self.scales.data_ptr(),
+                  out.data_ptr(), self.rows, self.cols, _lib.current_stream())
+        return out
+
+
+def interleave_gate_up(gate_rows: int) -> torch.Tensor:
+    """Row permutation placing 8 gate rows then the 8 matching up rows in each
+    16-row tile (the layout the SwiGLU epilogue of the int4 GEMV expects)."""
+    t = torch.arange(gate_rows // 8)
+    idx = torch.stack([t * 8 + i for i in range(8)] + [gate_rows + t * 8 + i for i in range(8)], 1)
+    return idx.reshape(-1)
+
+
+class LlamaDecodeEngine:
+    """Batched greedy decode of a random-init int4 Llama-3.2-1B-shape model."""
+
+    def __init__(self, shape: LlamaShape, batch: int, max_seq: int, seed: int = 0,
+                 keep_natural: bool = False, pdl: bool = True):
+        self.s, self.B, self.L = shape, batch, max_seq
+        self.dev = torch.device("cuda", torch.cuda.current_device())
+        self.flags = _lib.IRON_FLAG_PDL if pdl else 0
+        s, dev = shape, self.dev
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        E, Hd = s.emb_dim, s.head_dim
+        self.layers = []
+        for _ in range(s.n_layers):
+            lay = {
+                "n1": (1 + 0.02 * torch.randn(E, device=dev, generator=g)).to(torch.bfloat16),
+                "n2": (1 + 0.02 * torch.randn(E, device=dev, generator=g)).to(torch.bfloat16),
+                "qkv": Int4Matrix(s.qkv_dim, E, g, 0.001, 0.004, keep_natural),
+                "o": Int4Matrix(E, s.n_heads * Hd, g, 0.001, 0.004, keep_natural),
+                # gate rows then up rows, interleaved per 8 rows (see interleave_gate_up)
+                "gu": Int4Matrix(2 * s.hidden_dim, E, g, 0.001, 0.004, keep_natural),
+                "d": Int4Matrix(E, s.hidden_dim, g, 0.0005, 0.002, keep_natural),
+            }
+            self.layers.append(lay)
+        self.nf = (1 + 0.02 * torch.randn(E, device=dev, generator=g)).to(torch.bfloat16)
+        self.lm = Int4Matrix(s.vocab_size, E, g, 0.001, 0.004, keep_natural=True)
+        self.embed_table = self.lm.dequant()  # tied: the embedding is the dequantized lm-head
+        if not keep_natural:
+            self.lm.codes = self.lm.scales = None
+        self.lut = rope_table(Hd, max_seq, s.rope_base, dev)
+        B = batch
+        self.kc = torch.zeros(s.n_layers, B, s.n_kv_groups, max_seq, Hd, dtype=torch.bfloat16, device=dev)
+        self.vc = torch.zeros_like(self.kc)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        self.x = torch.zeros(B, E, **bf)
+        self.xn = torch.zeros(B, E, **bf)
+        self.h = torch.zeros(B, E, **bf)
+        self.qkv = torch.zeros(B, s.qkv_dim, **bf)
+        self.q = torch.zeros(B, s.n_heads, Hd, **bf)
+        self.attn = torch.zeros(B, s.n_heads * Hd, **bf)
+        self.act = torch.zeros(B, s.hidden_dim, **bf)
+        self.logits = torch.zeros(B, s.vocab_size, **bf)
+        self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.lens = torch.zeros(B, dtype=torch.int32, device=dev)
+        wsb = _lib.load().iron_attn_decode_workspace_bytes(B, s.n_heads, s.n_kv_groups, max_seq)
+        self.attn_ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
+        self.graph = None
+
+    # -- bytes moved per step (the roofline numerator) ---------------------------------
+    def weight_bytes(self) -> int:
+        return self.s.weight_params() * 9 // 16  # 0.5 B codes + 2 B / 32 scales per weight
+
+    def kv_bytes(self, positions) -> int:
+        """K and V bytes the attention reads for sequences at the given positions."""
+        s = self.s
+        return int(sum(int(p) + 1 for p in positions)) * s.n_layers * 2 * s.n_kv_groups * s.head_dim * 2
+
+    # -- one decode step ----------------------------------------------------------------
+    def _launch_step(self, stream: int):
+        s, B, f = self.s, self.B, self.flags
+        call, p = _lib.call, lambda t: t.data_ptr()
+        E, Hd = s.emb_dim, s.head_dim
+        L = self.L
+        kv_b, kv_h = s.n_kv_groups * L * Hd, L * Hd
+        call("iron_embed", p(self.tokens), p(self.embed_table), p(self.x), B, E, f, stream)
+        for li, lay in enumerate(self.layers):
+            call("iron_rmsnorm", p(self.x), None, None, p(lay["n1"]), p(self.xn), B, E, s.eps, f, stream)
+            call("iron_gemv_int4g32", p(lay["qkv"].packed), p(self.xn), p(self.qkv), s.qkv_dim, E, B,
+                 None, f, stream)
+            kc, vc = self.kc[li], self.vc[li]
+            call("iron_rope_kv_append", p(self.qkv), p(self.pos), p(self.lut), p(self.q), p(kc), p(vc),
+                 p(self.lens), B, s.n_heads, s.n_kv_groups, Hd, kv_b, kv_h, f, stream)
+            call("iron_attn_decode", p(self.q), p(kc), p(vc), p(self.lens), p(self.attn), B, s.n_heads,
+                 s.n_kv_groups, Hd, L, kv_b, kv_h, 1.0 / math.sqrt(Hd), p(self.attn_ws),
+                 self.attn_ws.numel(), f, stream)
+            call("iron_gemv_int4g32", p(lay["o"].packed), p(self.attn), p(self.h), E, s.n_heads * Hd, B,
+                 p(self.x), f, stream)
+            call("iron_rmsnorm", p(self.h), None, None, p(lay["n2"]), p(self.xn), B, E, s.eps, f, stream)
+            call("iron_gemv_int4g32", p(lay["gu"].packed), p(self.xn), p(self.act), 2 * s.hidden_dim, E,
+                 B, None, f | _lib.IRON_FLAG_SWIGLU, stream)
+            call("iron_gemv_int4g32", p(lay["d"].packed), p(self.act), p(self.x), E, s.hidden_dim, B,
+                 p(self.h), f, stream)
+        call("iron_rmsnorm", p(self.x), None, None, p(self.nf), p(self.xn), B, E, s.eps, f, stream)
+        call("iron_gemv_int4g32", p(self.lm.packed), p(self.xn), p(self.logits), s.vocab_size, E, B,
+             None, f, stream)
+        call("iron_argmax", p(self.logits), p(self.tokens), B, s.vocab_size, p(self.pos), f, stream)
+
+    def kernels_per_step(self) -> int:
+        B, s = self.B, self.s
+        splits = 1 if self.attn_ws.numel() <= 16 else 2  # combine pass when partials are used
+        return 1 + s.n_layers * (8 + (1 if splits > 1 else 0)) + 3
+
+    def set_state(self, tokens, positions):
+        self.tokens.copy_(torch.as_tensor(tokens, dtype=torch.int32))
+        self.pos.copy_(torch.as_tensor(positions, dtype=torch.int32))
+
+    def step(self):
+        """One decode step (graph replay once captured)."""
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._launch_step(torch.cuda.current_stream().cuda_stream)
+
+    def capture(self):
+        """Capture one decode step as a CUDA graph (positions/tokens are device state)."""
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        saved_tok, saved_pos = self.tokens.clone(), self.pos.clone()
+        with torch.cuda.stream(s):
+            self._launch_step(s.cuda_stream)  # warm-up outside capture
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        self.tokens.copy_(saved_tok)
+        self.pos.copy_(saved_pos)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=s):
+            self._launch_step(s.cuda_stream)
+        torch.cuda.synchronize()
+        self.tokens.copy_(saved_tok)
+        self.pos.copy_(saved_pos)
+        torch.cuda.synchronize()

@@ -134,7 +134,7 @@ __device__ __forceinline__ void gemv_reduce_store(float (&acc)[NT][4], float *re
         float r = acc[t][e];
         if (epilogue == IRON_EPI_GELU) r = gelu_tanh(r);
         const int64_t o = static_cast<int64_t>(v) * M + row;
-        if (residual) r += bf16_bits_to_float(residual[o]);
+        if (residual) r = __bfloat162float(__float2bfloat16_rn(r)) + bf16_bits_to_float(residual[o]);
         y[o] = float_to_bf16_bits(r);
       }
     }

@@ -59,13 +59,33 @@ __device__ __forceinline__ uint32_t s4x2_dequant_(uint32_t w, uint32_t scale2) {
   return r;
 }
 
-// Store a finished 16-row tile (C-fragment layout v) with the residual added.
+// Store a finished 16-row tile (C-fragment layout v). swiglu == 0: rows as they
+// are, plus the residual. swiglu == 1: the tile's rows 0-7 are gate rows and
+// 8-15 the matching up rows of output rows 8*tile..8*tile+7 (y has N/2 columns):
+// y = bf16(bf16(silu(bf16(gate))) * bf16(up)), the rounding sequence of IRON's
+// SwiGLUDecode (iron/operators/swiglu_decode/reference.py:49-53).
 template <int NT>
 __device__ __forceinline__ void s4_store(const float (&v)[NT][4], int tile, int N, int n_vec,
                                          uint16_t *__restrict__ y,
-                                         const uint16_t *__restrict__ residual) {
+                                         const uint16_t *__restrict__ residual, int swiglu) {
   const int lane = threadIdx.x & 31, gid = lane >> 2, tid = lane & 3;
   const int row0 = tile * 16;
+  if (swiglu) {
+    const int H = N / 2;
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int vv = t * 8 + tid * 2 + e;
+        if (vv < n_vec) {
+          const float gte = __bfloat162float(__float2bfloat16_rn(v[t][e]));
+          const float up = __bfloat162float(__float2bfloat16_rn(v[t][e + 2]));
+          const float sw = __bfloat162float(__float2bfloat16_rn(gte / (1.f + __expf(-gte))));
+          y[static_cast<int64_t>(vv) * H + tile * 8 + gid] = float_to_bf16_bits(sw * up);
+        }
+      }
+    return;
+  }
 #pragma unroll
   for (int t = 0; t < NT; ++t)
 #pragma unroll
@@ -75,7 +95,9 @@ __device__ __forceinline__ void s4_store(const float (&v)[NT][4], int tile, int 
       if (vv < n_vec) {
         const int64_t o = static_cast<int64_t>(vv) * N + row;
         float r = v[t][e];
-        if (residual) r += bf16_bits_to_float(residual[o]);
+        // the residual is added to the bf16-rounded projection, as IRON adds two
+        // bf16 buffers (iron/operators/elementwise_add/reference.py:7-9)
+        if (residual) r = __bfloat162float(__float2bfloat16_rn(r)) + bf16_bits_to_float(residual[o]);
         y[o] = float_to_bf16_bits(r);
       }
     }
@@ -131,7 +153,7 @@ template <int NT, int CS>
 __global__ void __launch_bounds__(32 * kT4Warps)
 gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__restrict__ x,
                        uint16_t *__restrict__ y, int N, int K, int n_vec,
-                       const uint16_t *__restrict__ residual) {
+                       const uint16_t *__restrict__ residual, int swiglu) {
   __shared__ float red[(kT4Warps + CS) * NT * 128];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tid = lane & 3;
@@ -213,7 +235,7 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
           for (int r = 1; r < CS; ++r) v[t][e] += slot0[((r * NT + t) * 4 + e) * 32 + lane];
     }
   }
-  if (warp == 0) s4_store<NT>(v, tile, N, n_vec, y, residual);
+  if (warp == 0) s4_store<NT>(v, tile, N, n_vec, y, residual, swiglu);
 }
 
 // Repack natural-layout codes [N, K/2] + scales [N, K/32] into GEMV units.
@@ -255,7 +277,7 @@ __global__ void pack_s4g32_kernel(const uint8_t *__restrict__ codes,
 
 template <int NT, int CS>
 static int launch_s4_tile(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,
-                          int n_vec, const uint16_t *res, bool pdl, cudaStream_t s) {
+                          int n_vec, const uint16_t *res, int swiglu, bool pdl, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>((N / 16) * CS));
   cfg.blockDim = dim3(32 * kT4Warps);
@@ -277,7 +299,7 @@ static int launch_s4_tile(const uint8_t *packed, const uint16_t *x, uint16_t *y,
   cfg.attrs = attr;
   cfg.numAttrs = na;
   cudaError_t e =
-      cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS>, packed, x, y, N, K, n_vec, res);
+      cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS>, packed, x, y, N, K, n_vec, res, swiglu);
   if (e != cudaSuccess) {
     set_last_cuda_error(e);
     (void)cudaGetLastError();
@@ -288,16 +310,16 @@ static int launch_s4_tile(const uint8_t *packed, const uint16_t *x, uint16_t *y,
 
 template <int NT>
 static int launch_s4_tile_cs(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,
-                             int n_vec, const uint16_t *res, bool pdl, cudaStream_t s) {
+                             int n_vec, const uint16_t *res, int swiglu, bool pdl, cudaStream_t s) {
   // split K over a cluster until every SM holds >= 2 CTAs (and each warp >= 1 chunk)
   const int tiles = N / 16, cpt = K / 128;
   int cs = 1;
   while (cs < 8 && tiles * cs < 2 * sm_count() && cpt >= kT4Warps * cs * 2) cs *= 2;
   switch (cs) {
-    case 1: return launch_s4_tile<NT, 1>(packed, x, y, N, K, n_vec, res, pdl, s);
-    case 2: return launch_s4_tile<NT, 2>(packed, x, y, N, K, n_vec, res, pdl, s);
-    case 4: return launch_s4_tile<NT, 4>(packed, x, y, N, K, n_vec, res, pdl, s);
-    default: return launch_s4_tile<NT, 8>(packed, x, y, N, K, n_vec, res, pdl, s);
+    case 1: return launch_s4_tile<NT, 1>(packed, x, y, N, K, n_vec, res, swiglu, pdl, s);
+    case 2: return launch_s4_tile<NT, 2>(packed, x, y, N, K, n_vec, res, swiglu, pdl, s);
+    case 4: return launch_s4_tile<NT, 4>(packed, x, y, N, K, n_vec, res, swiglu, pdl, s);
+    default: return launch_s4_tile<NT, 8>(packed, x, y, N, K, n_vec, res, swiglu, pdl, s);
   }
 }
 
@@ -326,9 +348,11 @@ extern "C" int iron_gemv_int4g32(const uint8_t *packed, const uint16_t *x, uint1
   if (static_cast<int64_t>(N / 16) * (K / 128) > 0x7fffffffLL) return IRON_ERR_SHAPE;
   if (!aligned16(packed) || !aligned16(x)) return IRON_ERR_ALIGN;
   const bool pdl = (flags & IRON_FLAG_PDL) != 0;
+  const int swiglu = (flags & IRON_FLAG_SWIGLU) ? 1 : 0;
+  if (swiglu && residual) return IRON_ERR_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (n_vec <= 8) return launch_s4_tile_cs<1>(packed, x, y, N, K, n_vec, residual, pdl, s);
-  if (n_vec <= 16) return launch_s4_tile_cs<2>(packed, x, y, N, K, n_vec, residual, pdl, s);
-  if (n_vec <= 32) return launch_s4_tile_cs<4>(packed, x, y, N, K, n_vec, residual, pdl, s);
-  return launch_s4_tile_cs<8>(packed, x, y, N, K, n_vec, residual, pdl, s);
+  if (n_vec <= 8) return launch_s4_tile_cs<1>(packed, x, y, N, K, n_vec, residual, swiglu, pdl, s);
+  if (n_vec <= 16) return launch_s4_tile_cs<2>(packed, x, y, N, K, n_vec, residual, swiglu, pdl, s);
+  if (n_vec <= 32) return launch_s4_tile_cs<4>(packed, x, y, N, K, n_vec, residual, swiglu, pdl, s);
+  return launch_s4_tile_cs<8>(packed, x, y, N, K, n_vec, residual, swiglu, pdl, s);
 }

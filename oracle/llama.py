@@ -33,7 +33,7 @@ def block_decode(x, k_cache, v_cache, pos, W, angles, n_heads, n_kv, head_dim, e
     lens = []
     for b in range(B):
         p = int(pos[b])
-        ang = angles[p : p + 1].to(BF16)
+        ang = angles[p : p + 1]
         q[b] = ops.rope(q[b], ang)
         k[b] = ops.rope(k[b], ang)
         k_cache[b, :, p] = k[b]
@@ -56,9 +56,19 @@ def block_mlp_half(x, k_cache, v_cache, pos, W, angles, n_heads, n_kv, head_dim,
     v = ops.gemv_multi(W["v"], xn).view(B, n_kv, head_dim)
     for b in range(B):
         p = int(pos[b])
-        ang = angles[p : p + 1].to(BF16)
+        ang = angles[p : p + 1]
         q[b] = ops.rope(q[b], ang)
         k_cache[b, :, p] = ops.rope(k[b], ang)
         v_cache[b, :, p] = v[b]
     act = ops.swiglu_act(ops.gemv_multi(W["g"], xn), ops.gemv_multi(W["u"], xn))
     return q, ops.gemv_multi(W["d"], act)
+
+
+def model_decode(tokens, pos, layers, nf, embed, lm, k_caches, v_caches, angles, n_heads, n_kv,
+                 head_dim, eps=1e-5):
+    """One greedy decode step of the whole model (llama_cpu.py:221-285, decode form):
+    embedding, the blocks, final RMSNorm, lm-head. Returns logits [B, V] (bf16)."""
+    x = embed[torch.as_tensor(tokens, dtype=torch.long)].clone()
+    for li, W in enumerate(layers):
+        x = block_decode(x, k_caches[li], v_caches[li], pos, W, angles, n_heads, n_kv, head_dim, eps)
+    return ops.gemv_multi(lm, ops.rms_norm(x, nf, eps))
