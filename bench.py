@@ -1,25 +1,33 @@
 #!/usr/bin/env python3
-"""Benchmark of the IRON hot path on B200 (one JSON line on rank 0).
+"""Benchmark of IRON's LLM-operator hot path on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload int4_gemv|bf16_gemv] [--n-vec B]
+                    [--workload decode|int4_gemv|bf16_gemv] [--batch B] [--n-vec V]
 
+Metric: "Llama-3.2-1B-shape decode tok/s; int4 GEMV achieved HBM GB/s".
 Workloads:
-  int4_gemv (default, config 2): y = dequant(W) x, W [8192 x 2048] signed int4 with
-      a bf16 scale per 32 k, x [B x 2048] bf16. One step = one GEMV call.
+  decode (default, config 5's decode phase): a random-init Llama-3.2-1B-shape
+      model (16 layers, vocab 128256, int4 group-32 weights, bf16 activations)
+      decodes B sequences greedily from position 2048 (the 2048-token prompt's
+      KV cache is synthetic). One step = one decode step of the batch = one
+      CUDA-graph replay (embedding, 16 x [RMSNorm, QKV GEMV, RoPE+KV append,
+      attention (+combine), O GEMV+residual, RMSNorm, gate/up GEMV+SwiGLU, down
+      GEMV+residual], final RMSNorm, lm-head GEMV, argmax). value = tokens/s.
+      The line also carries the config-2 int4 GEMV figure under "int4_gemv".
+  int4_gemv (config 2): y = dequant(W) x, W [8192 x 2048] signed int4 with a
+      bf16 scale per 32 k, x [V x 2048] bf16. One step = one GEMV call.
   bf16_gemv (config 1): W [2048 x 8192] bf16, x [8192].
 
 Timing: W warm-up steps, then exactly K steps bracketed by a barrier and
-cuda.synchronize, timed with CUDA events on the launching stream; the step loop
-is a captured CUDA graph (one kernel per step, launched with programmatic
-dependent launch so each GEMV streams its weights while the previous one
-drains). Step i uses weight copy i mod R; the R copies span > 2x the 126 MB L2,
-so every step reads its weights from HBM. With N > 1 (torchrun), every rank runs
-the same workload on its own GPU (data-parallel replicas, no collective in the
-step); value = all ranks' bytes / max-over-ranks time.
+cuda.synchronize, timed with CUDA events on the launching stream. Every step
+reads more than the 126 MB L2 from HBM: a decode step streams 695 MB of weights;
+the GEMV workloads rotate weight copies spanning > 2x L2. With N > 1
+(torchrun), every rank runs the same workload on its own GPU (data-parallel
+replicas, no collective in the step); value = all ranks' work / max-over-ranks
+time.
 
-`--impl reference` times IRON's CPU path for the same workload on the host cores
-(the oracle port of IRON's goldens: restated dequant, then torch `A @ B`).
+`--impl reference` times IRON's CPU path for the same workload on the host
+cores (the oracle restatement of IRON's torch goldens / llama_cpu.py).
 """
 
 from __future__ import annotations
@@ -45,14 +53,23 @@ FALLBACK_HBM_GBS = 6650.0
 def _args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20000)
-    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default: 256 decode steps, 20000 GEMVs)")
+    ap.add_argument("--warmup", type=int, default=None, help="warm-up steps (default: 5 decode, 200 GEMV)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["int4_gemv", "bf16_gemv"], default="int4_gemv")
-    ap.add_argument("--n-vec", type=int, default=1)
+    ap.add_argument("--workload", choices=["decode", "int4_gemv", "bf16_gemv"], default="decode")
+    ap.add_argument("--batch", type=int, default=1, help="decode batch per GPU")
+    ap.add_argument("--n-vec", type=int, default=1, help="vectors per GEMV call (int4_gemv)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
-    return ap.parse_args()
+    a = ap.parse_args()
+    if a.steps is None:
+        a.steps = 256 if a.workload == "decode" else 20000
+    if a.warmup is None:
+        a.warmup = 5 if a.workload == "decode" else 200
+    if a.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    return a
 
 
 # ---- distributed plumbing ------------------------------------------------------
@@ -229,7 +246,6 @@ def run_ours(args, world, rank, local):
             j = i % copies
             return lib.iron_gemv_int4g32(pp + j * pstride, xp, yp, N, K, nv, None, flags, sp)
 
-        kernel_key = "gemv_s4g32_stream_kernel"
     else:
         M, K = 2048, 8192
         wl = Int4Gemv(1)
@@ -250,7 +266,6 @@ def run_ours(args, world, rank, local):
             return lib.iron_gemv_bf16(wp + (i % copies) * wst, xp, yp, M, K, K, 1, 0, 0, 0, 1,
                                       None, 0, flags, sp)
 
-        kernel_key = "gemv_bf16_kernel"
 
     # correctness guard on the exact bench inputs (first copy) before timing
     _check_first_copy(args, wl, locals())
@@ -306,7 +321,7 @@ def run_ours(args, world, rank, local):
     value = wl.bytes_per_step * steps * world / (ms_max * 1e-3) / 1e9
     achieved = wl.bytes_per_step / (ms / steps * 1e-3) / 1e9
     peak, peak_kind = _peak_hbm()
-    traffic = _profile_traffic(f"{kernel_key}:{args.workload}:nv{getattr(wl, 'n_vec', 1)}")
+    traffic = _profile_traffic(f"{args.workload}:nv{getattr(wl, 'n_vec', 1)}")
     line = {
         "metric": "int4 GEMV achieved HBM GB/s" if args.workload == "int4_gemv" else "bf16 GEMV achieved HBM GB/s",
         "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": steps,
@@ -483,15 +498,274 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+# ---- decode (config 5) ------------------------------------------------------------------
+PREFIX = 2048  # prompt tokens already in the KV cache when decode starts
+
+
+def _int4_gemv_figure(pdl: bool, n_vec: int = 1, launches: int = 4096):
+    """Config-2 int4 GEMV GB/s (device-timed graph of launches over rotating copies)."""
+    from iron_b200 import _lib
+    from iron_b200.operators import GEMV
+
+    wl = Int4Gemv(n_vec)
+    copies = max(2, -(-3 * L2_BYTES // wl.weight_bytes))
+    codes, scales, x, y = _make_int4_device(wl, copies)
+    packed = torch.stack([GEMV.pack_int4g32(codes[j], scales[j]) for j in range(copies)])
+    del codes, scales
+    lib, cap = _lib.load(), torch.cuda.Stream()
+    flags = _lib.IRON_FLAG_PDL if pdl else 0
+    pstride = packed[0].numel()
+    per = copies * max(1, 256 // copies)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=cap):
+        for i in range(per):
+            st = lib.iron_gemv_int4g32(packed.data_ptr() + (i % copies) * pstride, x.data_ptr(), y.data_ptr(),
+                                       wl.N, wl.K, n_vec, None, flags, torch.cuda.current_stream().cuda_stream)
+            if st != 0:
+                raise RuntimeError(_lib.strerror(st))
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    reps = max(1, launches // per)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * per)
+    peak, _ = _peak_hbm()
+    gbs = wl.bytes_per_step / (us * 1e-6) / 1e9
+    return {"metric": "int4 GEMV achieved HBM GB/s (config 2)", "value": round(gbs, 1), "unit": "GB/s",
+            "n_vec": n_vec, "us_per_launch": round(us, 3), "launches": reps * per, "peak": peak,
+            "frac": round(gbs / peak, 4), "algorithmic_bytes_per_launch": wl.bytes_per_step,
+            "traffic": _profile_traffic(f"int4_gemv:nv{n_vec}")}
+
+
+def _decode_bytes(eng, positions):
+    """Algorithmic HBM bytes of one decode step: every weight byte once, the K/V
+    rows the attention reads (positions + the new one), the K/V rows written, the
+    embedding rows, and the logits written and re-read by the argmax."""
+    s, B = eng.s, eng.B
+    kv_row = s.n_layers * 2 * s.n_kv_groups * s.head_dim * 2
+    return (eng.weight_bytes() + eng.kv_bytes(positions) + B * kv_row
+            + B * s.emb_dim * 2 + 2 * B * s.vocab_size * 2)
+
+
+def run_decode(args, world, rank, local):
+    from iron_b200.applications.llama_3_2_1b.decode import LlamaDecodeEngine, LlamaShape
+
+    B, K, W = args.batch, args.steps, args.warmup
+    e2e_steps = min(K, 64)
+    shape = LlamaShape()
+    max_seq = PREFIX + max(W, e2e_steps, K) + 16
+    eng = LlamaDecodeEngine(shape, B, max_seq, seed=1234 + rank, pdl=not args.no_pdl)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(99 + rank)
+    for li in range(shape.n_layers):  # the prompt's KV cache (synthetic)
+        eng.kc[li, :, :, :PREFIX].normal_(generator=g)
+        eng.vc[li, :, :, :PREFIX].normal_(generator=g)
+    toks = torch.randint(0, shape.vocab_size, (B,), device="cuda", generator=g, dtype=torch.int32)
+    eng.set_state(toks, [PREFIX] * B)
+    eng.capture()
+    stream = torch.cuda.current_stream()
+
+    for _ in range(W):
+        eng.step()
+    torch.cuda.synchronize()
+    eng.set_state(eng.tokens.clone(), [PREFIX] * B)  # the timed steps decode positions 2048 .. 2048+K-1
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    _barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if sampler:
+        sampler.mark("t0")
+    torch.cuda.nvtx.range_push("bench_timed")  # lets a profiler select the timed steps
+    e0.record(stream)
+    for _ in range(K):
+        eng.step()
+    e1.record(stream)
+    torch.cuda.nvtx.range_pop()
+    e1.synchronize()
+    if sampler:
+        sampler.mark("t1")
+    torch.cuda.synchronize()
+    _barrier(world)
+    ms = e0.elapsed_time(e1)
+    ms_max = _max_over_ranks(ms, world)
+    clocks = sampler.stop() if sampler else None
+    pos_after = eng.pos.cpu()
+    if not bool((pos_after == PREFIX + K).all()):
+        raise RuntimeError(f"decode positions advanced to {pos_after.tolist()}, expected {PREFIX + K}")
+
+    bytes_per_step = sum(_decode_bytes(eng, [PREFIX + i] * B) for i in range(K)) / K
+    achieved = bytes_per_step / (ms / K * 1e-3) / 1e9
+    peak, peak_kind = _peak_hbm()
+    e2e = _decode_e2e(eng, B, e2e_steps)
+    gemv = _int4_gemv_figure(not args.no_pdl)
+    line = {
+        "metric": "Llama-3.2-1B-shape decode tok/s", "value": round(B * K * world / (ms_max * 1e-3), 1),
+        "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_max / K,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 (int4 g32 weights dequantized exactly to bf16, fp32 accumulate)",
+        "data": "synthetic (random-init weights, random prompt KV cache; seeded)",
+        "config": {"workload": "decode (BASELINE config 5)", "model": "Llama-3.2-1B shape, random init",
+                   "weights": "int4 group-32 (bf16 scales)", "batch_per_gpu": B, "global_batch": B * world,
+                   "context_start": PREFIX, "seq_len": PREFIX + K,
+                   "l2": "no flush: each step streams %.0f MB of weights (> L2)" % (eng.weight_bytes() / 1e6),
+                   "parallelism": f"dp{world} (independent replicas)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4),
+                     "traffic": _profile_traffic(f"decode:B{B}"),
+                     "scope": "whole decode step (one CUDA graph replay)",
+                     "algorithmic_bytes_per_step": int(bytes_per_step),
+                     "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                     else "fallback 6650 GB/s"},
+        "int4_gemv": gemv,
+        "gpu_launches": eng.kernels_per_step() * K,
+        "e2e": e2e,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_decode(B, budget_s=15.0)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        eng.graph = None
+        dist.destroy_process_group()
+
+
+def _decode_e2e(eng, B, steps):
+    """tok/s through the engine API with host token ids: each step copies the
+    batch's input tokens from pinned host memory, replays the decode graph and
+    reads the sampled tokens back to pinned host memory."""
+    host_in = eng.tokens.cpu().pin_memory()
+    host_out = torch.empty(B, dtype=torch.int32).pin_memory()
+    eng.set_state(host_in, [PREFIX] * B)
+    for _ in range(3):
+        eng.tokens.copy_(host_in, non_blocking=True)
+        eng.step()
+        host_out.copy_(eng.tokens, non_blocking=True)
+    torch.cuda.synchronize()
+    eng.set_state(host_in, [PREFIX] * B)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        eng.tokens.copy_(host_in, non_blocking=True)
+        eng.step()
+        host_out.copy_(eng.tokens, non_blocking=True)
+    e1.record()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    return {"value": round(B * steps / (ms * 1e-3), 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
+            "d2h_bytes_per_step": 4 * B, "steps": steps, "ms_per_step": ms / steps,
+            "path": "LlamaDecodeEngine.step (CUDA graph of C-ABI kernels), pinned host token ids in and out"}
+
+
+def _cpu_decode_model(B, layers, seed=5):
+    """bf16 weights (N(0, 0.02)-scaled) and a 2048-token KV cache for the CPU decode step."""
+    from iron_b200.applications.llama_3_2_1b.decode import LlamaShape
+
+    s = LlamaShape()
+    gen = torch.Generator()
+    gen.manual_seed(seed)
+    E, H, Hd = s.emb_dim, s.hidden_dim, s.head_dim
+
+    def w(o, i):
+        return (torch.randn(o, i, generator=gen) * 0.02).to(torch.bfloat16)
+
+    Ws = [{"n1": torch.ones(E, dtype=torch.bfloat16), "n2": torch.ones(E, dtype=torch.bfloat16),
+           "q": w(s.n_heads * Hd, E), "k": w(s.n_kv_groups * Hd, E), "v": w(s.n_kv_groups * Hd, E),
+           "o": w(E, s.n_heads * Hd), "g": w(H, E), "u": w(H, E), "d": w(E, H)} for _ in range(layers)]
+    lm = w(s.vocab_size, E)
+    kcs = [torch.randn(B, s.n_kv_groups, PREFIX + 8, Hd, generator=gen).to(torch.bfloat16) for _ in range(layers)]
+    vcs = [torch.randn(B, s.n_kv_groups, PREFIX + 8, Hd, generator=gen).to(torch.bfloat16) for _ in range(layers)]
+    return s, Ws, lm, kcs, vcs
+
+
+def _cpu_decode_timer(B):
+    """IRON's CPU decode step (llama_cpu.py's blocks, final norm and tied lm-head,
+    restated in oracle/llama.py) on all host threads; returns a step() closure."""
+    from oracle import llama as ollama
+    from oracle import ops
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    s_layers = 16
+    s, Ws, lm, kcs, vcs = _cpu_decode_model(B, s_layers)
+    angles = ops.rope_angles(s.head_dim, PREFIX + 8, s.rope_base)
+    nf = torch.ones(s.emb_dim, dtype=torch.bfloat16)
+    toks = [(7 * b) % s.vocab_size for b in range(B)]
+
+    def step():
+        return ollama.model_decode(toks, [PREFIX] * B, Ws, nf, lm, lm, kcs, vcs, angles,
+                                   s.n_heads, s.n_kv_groups, s.head_dim)
+
+    return step, s_layers
+
+
+def cpu_baseline_decode(B, budget_s=15.0):
+    step, layers = _cpu_decode_timer(B)
+    step()
+    n, t0 = 0, time.perf_counter()
+    while n < 1 or time.perf_counter() - t0 < budget_s:
+        step()
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    return {"value": round(B / dt, 3), "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n} full decode steps (all {layers} layers + lm-head) of batch {B} at context {PREFIX}: "
+                      f"llama_cpu.py restated in torch, bf16 weights", "s_per_step": round(dt, 4)}
+
+
+def run_reference_decode(args, world, rank):
+    if rank != 0:
+        return
+    B = args.batch
+    step, layers = _cpu_decode_timer(B)
+    steps = max(1, min(args.steps, 8))
+    for _ in range(min(args.warmup, 1)):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = (time.perf_counter() - t0) / steps
+    value = round(B / dt, 3)
+    threads = torch.get_num_threads()
+    sample = (f"{steps} decode steps (of {args.steps} requested) of batch {B} at context {PREFIX}, "
+              f"all {layers} layers + lm-head, llama_cpu.py restated in torch, bf16 weights")
+    line = {"impl": "reference", "metric": "Llama-3.2-1B-shape decode tok/s", "value": value, "unit": "tok/s",
+            "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init weights; seeded)",
+            "config": {"workload": "decode (BASELINE config 5)", "model": "Llama-3.2-1B shape, random init",
+                       "batch_per_gpu": B, "context_start": PREFIX},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = _args()
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))
-        run_reference(args, world, rank)
+        if args.workload == "decode":
+            run_reference_decode(args, world, rank)
+        else:
+            run_reference(args, world, rank)
         return
     world, rank, local = _dist_init(args.gpus)
-    run_ours(args, world, rank, local)
+    if args.workload == "decode":
+        run_decode(args, world, rank, local)
+    else:
+        run_ours(args, world, rank, local)
 
 
 if __name__ == "__main__":
