@@ -106,6 +106,17 @@ class MLIROperator(AIEOperatorBase):
         )
         return f"{type(self).__name__}_{'_'.join(parts)}_{DEVICE_NAME}"
 
+    def runtime_parameters(self) -> list[str]:
+        """Names of the int32 runtime parameters this operator reads at launch
+        (an OperatorSequence binds each to a device word with ``bind_param``)."""
+        return []
+
+    def bind_param(self, name: str, device_word) -> None:
+        raise KeyError(f"{type(self).__name__} has no runtime parameter {name!r}")
+
+    def prepare(self) -> None:
+        """Allocate whatever the launch needs (workspaces) ahead of a CUDA-graph capture."""
+
     def reference_tolerance(self) -> Tolerance | None:
         """The tolerance the kernel's output is held to against ``reference()``."""
         return getattr(self, "_tolerance", None)

@@ -58,18 +58,68 @@ def _cuda_ok() -> bool:
     return torch.cuda.is_available()
 
 
-class _Storage:
-    """Byte arrays shared by a tensor and its subviews."""
+class _Intervals:
+    """Sorted, disjoint half-open byte ranges."""
 
-    def __init__(self, nbytes: int):
+    def __init__(self):
+        self.iv: list[tuple[int, int]] = []
+
+    def add(self, s: int, e: int) -> None:
+        if e <= s:
+            return
+        out, placed = [], False
+        for a, b in self.iv:
+            if b < s or a > e:
+                if a > e and not placed:
+                    out.append((s, e))
+                    placed = True
+                out.append((a, b))
+            else:
+                s, e = min(a, s), max(b, e)
+        if not placed:
+            out.append((s, e))
+        self.iv = sorted(out)
+
+    def take(self, s: int, e: int) -> list[tuple[int, int]]:
+        """Remove and return the parts of the set inside [s, e)."""
+        got, keep = [], []
+        for a, b in self.iv:
+            lo, hi = max(a, s), min(b, e)
+            if lo < hi:
+                got.append((lo, hi))
+                if a < lo:
+                    keep.append((a, lo))
+                if hi < b:
+                    keep.append((hi, b))
+            else:
+                keep.append((a, b))
+        self.iv = sorted(keep)
+        return got
+
+
+class _Storage:
+    """Byte arrays shared by a tensor and its subviews, with a coherence map:
+    ``host_dirty`` ranges were written on the host since the last upload,
+    ``dev_dirty`` ranges were written by kernels since the last download."""
+
+    def __init__(self, nbytes: int, host_only: bool = False):
         self.nbytes = max(int(nbytes), 1)
-        pin = _cuda_ok()
+        self.host_only = host_only
+        pin = _cuda_ok() and not host_only
         self.host = torch.zeros(self.nbytes, dtype=torch.uint8, pin_memory=pin)
         self._dev = None
+        self.host_dirty = _Intervals()
+        self.dev_dirty = _Intervals()
+
+    @property
+    def allocated(self) -> bool:
+        return self._dev is not None
 
     @property
     def dev(self) -> torch.Tensor:
         if self._dev is None:
+            if self.host_only:
+                raise RuntimeError("this buffer is host-only (reference dispatch)")
             if not _cuda_ok():
                 raise RuntimeError("no CUDA device: iron_b200 buffers live in B200 HBM")
             self._dev = torch.zeros(self.nbytes, dtype=torch.uint8, device="cuda")
@@ -77,7 +127,16 @@ class _Storage:
 
 
 class Tensor:
-    """Explicit-sync host/HBM buffer (the XRTTensor surface on a B200)."""
+    """Explicit-sync host/HBM buffer (the XRTTensor surface on a B200).
+
+    A host view handed out by ``torch_view()`` / ``numpy()`` is assumed written:
+    its range is uploaded by the next ``to("npu")``. Ranges that kernels wrote
+    (``mark_device_written``, done by the sequence callables after a run) are
+    downloaded before the host view is handed out, so host reads never see
+    stale data and a host write never clobbers newer device data.
+    """
+
+    _host_only = False
 
     def __init__(self, shape, dtype=None, *, _storage=None, _offset=0):
         if dtype is None:
@@ -86,7 +145,7 @@ class Tensor:
         self.shape = tuple(int(s) for s in (shape if isinstance(shape, (tuple, list)) else (shape,)))
         self._offset = int(_offset)
         self._nbytes = int(np.prod(self.shape, dtype=np.int64)) * self.dtype.itemsize
-        self._storage = _storage if _storage is not None else _Storage(self._nbytes)
+        self._storage = _storage if _storage is not None else _Storage(self._nbytes, self._host_only)
         if self._offset + self._nbytes > self._storage.nbytes:
             raise ValueError("subview exceeds its parent buffer")
         self.device = "cpu"
@@ -97,22 +156,36 @@ class Tensor:
         t = t.detach()
         out = cls(tuple(t.shape), np_dtype(t.dtype))
         out.torch_view().copy_(t.reshape(out.shape).cpu())
-        if _cuda_ok():
+        if _cuda_ok() and not cls._host_only:
             out.to("npu")
         return out
 
     def subview(self, byte_offset: int, shape, dtype) -> "Tensor":
-        sub = Tensor(shape, dtype, _storage=self._storage, _offset=self._offset + int(byte_offset))
+        sub = type(self)(shape, dtype, _storage=self._storage, _offset=self._offset + int(byte_offset))
         sub.device = self.device
         return sub
 
     # -- views ---------------------------------------------------------------
+    @property
+    def _range(self) -> tuple[int, int]:
+        return self._offset, self._offset + self._nbytes
+
     def _bytes(self, t: torch.Tensor) -> torch.Tensor:
         return t[self._offset : self._offset + self._nbytes]
 
+    def _pull_stale(self) -> None:
+        st = self._storage
+        for s, e in st.dev_dirty.take(*self._range):
+            st.host[s:e].copy_(st.dev[s:e])
+
+    def _host_view(self) -> torch.Tensor:
+        return self._bytes(self._storage.host).view(torch_dtype(self.dtype)).view(self.shape)
+
     def torch_view(self) -> torch.Tensor:
         """Host view (what the next ``to("npu")`` uploads)."""
-        return self._bytes(self._storage.host).view(torch_dtype(self.dtype)).view(self.shape)
+        self._pull_stale()
+        self._storage.host_dirty.add(*self._range)
+        return self._host_view()
 
     @property
     def device_tensor(self) -> torch.Tensor:
@@ -127,26 +200,44 @@ class Tensor:
         return self.numpy()
 
     def numpy(self) -> np.ndarray:
+        self._pull_stale()
+        self._storage.host_dirty.add(*self._range)
         raw = self._bytes(self._storage.host).numpy()
         return raw.view(self.dtype).reshape(self.shape)
 
     # -- synchronisation -----------------------------------------------------
     def to(self, where: str) -> "Tensor":
+        st = self._storage
         if where in ("npu", "cuda", "gpu"):
-            self._bytes(self._storage.dev).copy_(self._bytes(self._storage.host), non_blocking=False)
+            if st.host_only:
+                return self
+            dev = st.dev
+            for s, e in st.host_dirty.take(*self._range):
+                dev[s:e].copy_(st.host[s:e], non_blocking=False)
             self.device = "npu"
         elif where == "cpu":
-            src = self._bytes(self._storage.dev)
-            self._bytes(self._storage.host).copy_(src, non_blocking=False)
+            if st.allocated:
+                self._bytes(st.host).copy_(self._bytes(st.dev), non_blocking=False)
+            st.host_dirty.take(*self._range)
+            st.dev_dirty.take(*self._range)
             self.device = "cpu"
         else:
             raise ValueError(f"unknown location {where!r}")
         return self
 
+    def mark_device_written(self) -> None:
+        """Kernels rewrote this range: the device copy is authoritative."""
+        st = self._storage
+        if st.host_only:
+            return
+        st.host_dirty.take(*self._range)
+        st.dev_dirty.add(*self._range)
+        self.device = "npu"
+
     def to_torch(self) -> torch.Tensor:
-        if self._storage._dev is not None:
+        if self._storage.allocated:
             self.to("cpu")
-        return self.torch_view().clone()
+        return self._host_view().clone()
 
     def fill_(self, value) -> "Tensor":
         self.torch_view().fill_(value)
@@ -155,7 +246,13 @@ class Tensor:
         return self
 
     def __repr__(self) -> str:
-        return f"Tensor(shape={self.shape}, dtype={self.dtype}, device={self.device})"
+        return f"{type(self).__name__}(shape={self.shape}, dtype={self.dtype}, device={self.device})"
+
+
+class CPUOnlyTensor(Tensor):
+    """Host-only buffer for CPU evaluation (the reference dispatch); device syncs are no-ops."""
+
+    _host_only = True
 
 
 XRTTensor = Tensor

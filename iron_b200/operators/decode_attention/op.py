@@ -61,6 +61,9 @@ class DecodeAttention(MLIROperator):
             self._ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device="cuda")
         return self._ws
 
+    def prepare(self):
+        self.workspace()
+
     def _launch(self, q, k, v, lens, out, *, stream, flags=0):
         p = _lib.dptr
         ws = self.workspace()

@@ -45,6 +45,9 @@ class Softmax(MLIROperator):
         self._param_dev = None
         MLIROperator.__init__(self, context=self.context)
 
+    def runtime_parameters(self) -> list[str]:
+        return [self.vector_size_parameter] if self.vector_size_parameter else []
+
     def bind_param(self, name: str, device_word) -> None:
         """Read the mask length from `device_word` (an int32 CUDA tensor) at run time."""
         if name == self.vector_size_parameter:

@@ -71,6 +71,9 @@ class StridedCopy(MLIROperator):
         self._params = {}
         MLIROperator.__init__(self, context=self.context)
 
+    def runtime_parameters(self) -> list[str]:
+        return [n for n in (self.input_offset_parameter, self.output_offset_parameter) if n]
+
     def bind_param(self, name: str, device_word) -> None:
         """Read an offset addend (elements) from `device_word` (int32 CUDA tensor) at run time."""
         if name in (self.input_offset_parameter, self.output_offset_parameter):
