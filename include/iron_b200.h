@@ -248,6 +248,28 @@ int iron_embed(const int32_t *tokens, const uint16_t *table, uint16_t *x, int B,
 int iron_argmax(const uint16_t *logits, int32_t *out, int B, int V, int32_t *pos, unsigned flags,
                 void *stream);
 
+/* ---- tensor-core GEMM (prefill projections) -------------------------------------
+ * C = epilogue(A . B^T) on tcgen05 tensor cores with TMEM accumulators: A bf16
+ * [M, K] (row pitch lda), B bf16 [N, K] K-major (row pitch ldb), C bf16 [M, N]
+ * (row pitch ldc), fp32 accumulation. Replaces the NPU GEMMs of
+ * iron/operators/gemm/op.py:21-231 (b_col_maj=True layout; the Python operator
+ * transposes a row-major B first) and iron/operators/flm/gemm/op.py:64-499, whose
+ * epilogue it fuses: the accumulator is rounded to bf16, then `epilogue` (bits 0-7:
+ * 0 none, 1 gelu as x*sigmoid(1.702x), 2 silu, 3 sigmoid) and, if `clamp`, a clamp
+ * to [clamp_lo, clamp_hi] (flm/gemm/reference.py:8-57); bit 8 of `epilogue`
+ * (IRON_GEMM_ROUND_FLOOR) rounds every fp32 -> bf16 conversion toward -inf
+ * (flm Rounding.FLOOR) instead of to nearest even. K, N, lda, ldb, ldc multiples
+ * of 8; pointers 16-byte aligned. block_n = 0 picks the tile width (64/128/256).
+ * iron_gemm_status returns IRON_ERR_TIMEOUT if any GEMM since the last reset hit
+ * its bounded-wait deadline (reset != 0 clears it); it synchronises the device.
+ */
+#define IRON_GEMM_ROUND_FLOOR 0x100
+
+int iron_gemm_bf16(const uint16_t *A, const uint16_t *B, uint16_t *C, int M, int N, int K,
+                   int64_t lda, int64_t ldb, int64_t ldc, int epilogue, int clamp, float clamp_lo,
+                   float clamp_hi, int block_n, unsigned flags, void *stream);
+int iron_gemm_status(int reset);
+
 #ifdef __cplusplus
 }
 #endif

@@ -17,8 +17,11 @@ LIB_PATH = Path(__file__).resolve().parent / "libiron_b200.so"
 IRON_OK = 0
 IRON_FLAG_PDL = 0x1
 IRON_FLAG_SWIGLU = 0x2
+(IRON_OK, IRON_ERR_NULL, IRON_ERR_SHAPE, IRON_ERR_ALIGN, IRON_ERR_UNSUPPORTED, IRON_ERR_CUDA,
+ IRON_ERR_WORKSPACE, IRON_ERR_TIMEOUT, IRON_ERR_ARG) = (0, -1, -2, -3, -4, -5, -6, -7, -8)
 IRON_EPI_NONE = 0
 IRON_EPI_GELU = 1
+IRON_GEMM_ROUND_FLOOR = 0x100
 
 P = c_void_p  # every tensor is passed as a raw device address
 
@@ -51,6 +54,9 @@ SIGNATURES: dict[str, list] = {
                             c_uint, P],
     "iron_embed": [P, P, P, c_int, c_int, c_uint, P],
     "iron_argmax": [P, P, c_int, c_int, P, c_uint, P],
+    "iron_gemm_bf16": [P, P, P, c_int, c_int, c_int, c_int64, c_int64, c_int64, c_int, c_int, c_float,
+                       c_float, c_int, c_uint, P],
+    "iron_gemm_status": [c_int],
 }
 _RESTYPES = {"iron_strerror": c_char_p, "iron_attn_decode_workspace_bytes": c_size_t}
 

@@ -186,3 +186,27 @@ def rope_angles(head_dim: int, context_length: int, base: float = 500000.0) -> t
     angles[:, ::2] = torch.cos(freqs)
     angles[:, 1::2] = torch.sin(freqs)
     return angles
+
+
+def gemm(A: torch.Tensor, B: torch.Tensor, b_col_maj: bool = False, c_col_maj: bool = False) -> torch.Tensor:
+    """C = A @ B from stored layouts (iron/operators/gemm/reference.py:7-18), fp32
+    accumulation, bf16 out."""
+    Bm = B.T if b_col_maj else B
+    C = (A.float() @ Bm.float()).to(BF16)
+    return C.T if c_col_maj else C
+
+
+def flm_gemm(A: torch.Tensor, B: torch.Tensor, epilogue: str = "none", clamp=None) -> torch.Tensor:
+    """flm GEMM (iron/operators/flm/gemm/reference.py:8-57): fp32 accumulation,
+    conversion to bf16, then the activation (gelu = x*sigmoid(1.702x)) and the
+    clamp, evaluated in bf16 torch ops as the golden does."""
+    C = (A.float() @ B.float()).to(A.dtype)
+    if epilogue == "gelu":
+        C = C * torch.sigmoid(1.702 * C)
+    elif epilogue == "silu":
+        C = C * torch.sigmoid(C)
+    elif epilogue == "sigmoid":
+        C = torch.sigmoid(C)
+    if clamp is not None:
+        C = torch.clamp(C, clamp[0], clamp[1])
+    return C

@@ -195,10 +195,46 @@ def main(ref: Path):
           dims=np.array([emb, nh, nkv, hd, hid, past]))
 
 
+def gemm_fixtures(ref: Path):
+    """GEMM goldens: iron/operators/gemm/reference.py as is, and the flm GEMM
+    golden (flm/gemm/reference.py), whose import of its design module (which
+    needs mlir_aie) is satisfied by a module holding only the Epilogue enum with
+    IRON's member names and order."""
+    gm = _load(ref, "iron/operators/gemm/reference.py", "ref_gemm")
+    for M, K, N, bc, cc in [(128, 256, 64, False, False), (128, 256, 64, True, False),
+                            (128, 256, 64, True, True), (64, 512, 256, False, True)]:
+        d = gm.generate_golden_reference(M=M, K=K, N=N, b_col_maj=bc, c_col_maj=cc)
+        _save(f"gemm_M{M}_K{K}_N{N}_bc{int(bc)}_cc{int(cc)}", A=d["input"], B=d["input_b"][0],
+              C=d["output"][0])
+
+    import enum
+
+    class Epilogue(enum.StrEnum):
+        NONE = "none"
+        GELU = "gelu"
+        SILU = "silu"
+        SIGMOID = "sigmoid"
+
+    for mname in ("iron", "iron.operators", "iron.operators.flm", "iron.operators.flm.gemm"):
+        sys.modules.setdefault(mname, types.ModuleType(mname))
+    design = types.ModuleType("iron.operators.flm.gemm.design")
+    design.Epilogue = Epilogue
+    sys.modules["iron.operators.flm.gemm.design"] = design
+    fm = _load(ref, "iron/operators/flm/gemm/reference.py", "ref_flm_gemm")
+    for epi, clamp, scale in [("none", None, 4.0), ("silu", None, 0.5), ("gelu", None, 0.5),
+                              ("sigmoid", None, 0.5), ("none", (-2.0, 2.0), 4.0), ("silu", (-4.0, 4.0), 0.5)]:
+        d = fm.generate_golden_reference(M=128, K=512, N=128, epilogue=Epilogue(epi), clamp=clamp, scale=scale)
+        tag = f"_cl{int(clamp[1])}" if clamp else ""
+        _save(f"flm_gemm_{epi}{tag}_M128_K512_N128", A=d["input"], B=d["input_b"], C=d["output"])
+
+
 if __name__ == "__main__":
     import os
 
-    src = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("IRON_REFERENCE_DIR")
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    src = args[0] if args else os.environ.get("IRON_REFERENCE_DIR")
     if not src:
-        sys.exit("usage: make_golden.py <path to the IRON checkout>")
-    main(Path(src))
+        sys.exit("usage: make_golden.py <path to the IRON checkout> [--only-gemm]")
+    if "--only-gemm" not in sys.argv:
+        main(Path(src))
+    gemm_fixtures(Path(src))

@@ -176,3 +176,25 @@ def test_llama_block_decode_matches_llama_cpu():
     assert_close(y, bf16(d["y"]).reshape(1, emb), 2e-2, 2e-2, what="block output")
     assert_close(kc[:, :, : past + 1], bf16(d["k_new"]), 2e-2, 2e-2, what="k cache")
     assert_close(vc[:, :, : past + 1], bf16(d["v_new"]), 2e-2, 2e-2, what="v cache")
+
+
+# ---- GEMM (iron/operators/gemm/reference.py, flm/gemm/reference.py) ------------------
+@pytest.mark.parametrize("name,bc,cc", [("gemm_M128_K256_N64_bc0_cc0", False, False),
+                                        ("gemm_M128_K256_N64_bc1_cc0", True, False),
+                                        ("gemm_M128_K256_N64_bc1_cc1", True, True),
+                                        ("gemm_M64_K512_N256_bc0_cc1", False, True)])
+def test_gemm_matches_golden(name, bc, cc):
+    d = {k: bf16(v) for k, v in load(name).items()}
+    got = ops.gemm(d["A"], d["B"], bc, cc)
+    # IRON's golden runs torch's bf16 matmul; both accumulate in fp32 and round once
+    assert_close(got, d["C"], 0.005, 0.005, what=name)
+    assert (got.view(torch.int16) == d["C"].view(torch.int16)).float().mean() > 0.99
+
+
+@pytest.mark.parametrize("epi,clamp", [("none", None), ("silu", None), ("gelu", None), ("sigmoid", None),
+                                       ("none", (-2.0, 2.0)), ("silu", (-4.0, 4.0))])
+def test_flm_gemm_matches_golden(epi, clamp):
+    tag = f"_cl{int(clamp[1])}" if clamp else ""
+    d = {k: bf16(v) for k, v in load(f"flm_gemm_{epi}{tag}_M128_K512_N128").items()}
+    got = ops.flm_gemm(d["A"], d["B"], epi, clamp)
+    assert_close(got, d["C"], 0.005, 0.005, what=epi)
