@@ -7,18 +7,12 @@
 // The flm epilogue (activation after the bf16 conversion, then an optional
 // clamp) is fused into the TMEM drain.
 //
-// One CTA computes one 128 x BN output tile with four warps:
-//   warp 0, one thread : TMA producer -- A and B k-blocks (64 wide, 128-byte
-//                        swizzle) into a ring of shared-memory stages;
-//   warp 1, one thread : MMA issuer -- four tcgen05.mma (K = 16) per stage into
-//                        a 128 x BN fp32 accumulator in TMEM, a commit per
-//                        stage releasing it to the producer, a final commit;
-//   warp 2            : allocates / frees the TMEM columns;
-//   all four warps    : epilogue -- each warp drains its 32 TMEM lanes (rows),
-//                        32 columns at a time, converts, applies the
-//                        activation and writes 64 contiguous bytes per row.
-// Every mbarrier wait is bounded by a 2-second deadline; a timeout sets the
-// status word and the CTA leaves after freeing its TMEM.
+// Persistent and warp-specialised: one CTA per SM walks 128 x BN output tiles
+// with a ring of shared-memory stages (TMA loads of 64-wide k-blocks, 128-byte
+// swizzle) and two TMEM accumulators, so the drain of one tile overlaps the
+// mainloop of the next. Every mbarrier wait gives up after 2 s without
+// progress; a timeout sets the status word and the CTA leaves after freeing
+// its TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -31,7 +25,8 @@ namespace iron {
 namespace gemm {
 
 constexpr int BM = 128, BK = 64;
-constexpr int kThreads = 128;
+constexpr int kEpiWarps = 4;
+constexpr int kThreads = 32 * (2 + kEpiWarps);
 constexpr uint64_t kDeadlineNs = 2000000000ull;
 
 __device__ unsigned g_gemm_status;  // 0 = ok, else the first failing role's code
@@ -67,24 +62,35 @@ struct Cfg {
   static constexpr int kSmem = 1024 + kStages * kStage + 256;
 };
 
+// Persistent, warp-specialised kernel. Each CTA walks the output tiles
+// blockIdx.x, blockIdx.x + gridDim.x, ... with two TMEM accumulators, so the
+// epilogue of one tile overlaps the mainloop of the next:
+//   warp 0, one thread : TMA producer (A and B k-blocks into the stage ring);
+//   warp 1, one thread : MMA issuer (accumulator i % 2 of the CTA's i-th tile);
+//   warp 2            : allocates / frees 2 * BN TMEM columns;
+//   warps 2..5        : epilogue, warp w draining TMEM lanes 32 (w % 4) ..
+//                       32 (w % 4) + 31 (the lane quarter that warp may access).
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    uint16_t *__restrict__ C, int M, int N, int K, int64_t ldc, Epi epi) {
   using G = Cfg<BN>;
   constexpr int S = G::kStages;
+  constexpr uint32_t kCols = 2 * BN;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;  // 128-byte swizzle atoms need 1024-B alignment
   const uint32_t stage0 = base;
-  const uint32_t bars = base + S * G::kStage;  // full[S], empty[S], accum
-  const uint32_t full0 = bars, empty0 = bars + 8 * S, accum = bars + 16 * S;
-  const uint32_t tslot = accum + 8;
+  const uint32_t bars = base + S * G::kStage;
+  const uint32_t full0 = bars, empty0 = bars + 8 * S;
+  const uint32_t tfull0 = bars + 16 * S, tempty0 = tfull0 + 16;  // [2] each
+  const uint32_t tslot = tempty0 + 16;
   uint32_t *tslot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tslot - raw));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
   const int kb_count = (K + BK - 1) / BK;
+  const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
+  const int tiles = m_tiles * n_tiles;
 
   if (threadIdx.x == 0) {
     tc::prefetch_tmap(&tmA);
@@ -93,96 +99,123 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::mbar_init_u32(full0 + 8 * s, 1);
       tc::mbar_init_u32(empty0 + 8 * s, 1);
     }
-    tc::mbar_init_u32(accum, 1);
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init_u32(tfull0 + 8 * a, 1);
+      tc::mbar_init_u32(tempty0 + 8 * a, kEpiWarps);
+    }
     mbar_init_fence();
   }
-  if (warp == 2) tc::tmem_alloc(tslot, BN);
+  if (warp == 2) tc::tmem_alloc(tslot, kCols);
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tslot_ptr;
   pdl_wait();  // A is the previous kernel's output; the prologue above overlapped it
-  const uint64_t deadline = tc::globaltimer_ns() + kDeadlineNs;
+  constexpr uint64_t deadline = kDeadlineNs;  // per wait
 
-  bool ok = true;
-  if (warp == 0 && lane == 0) {
-    // ---- producer ----
-    int issued = 0;
-    for (int kb = 0; kb < kb_count; ++kb) {
-      const int s = kb % S;
-      const uint32_t par = ((kb / S) & 1) ^ 1;
-      if (!tc::wait_until(empty0 + 8 * s, par, deadline)) {
-        ok = false;
-        break;
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- producer ----
+      bool ok = true;
+      int it = 0, issued = 0;  // it: k-blocks issued by this CTA over all its tiles
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
+        for (int kb = 0; kb < kb_count; ++kb, ++it) {
+          const int s = it % S;
+          if (!tc::wait_until(empty0 + 8 * s, ((it / S) & 1) ^ 1, deadline)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = stage0 + s * G::kStage, sb = sa + G::kStageA;
+          tc::expect_tx(full0 + 8 * s, G::kStage);
+          tc::tma_load_2d(sa, &tmA, kb * BK, m0, full0 + 8 * s);
+          tc::tma_load_2d(sb, &tmB, kb * BK, n0, full0 + 8 * s);
+          issued = it + 1;
+        }
       }
-      const uint32_t sa = stage0 + s * G::kStage, sb = sa + G::kStageA;
-      tc::expect_tx(full0 + 8 * s, G::kStage);
-      tc::tma_load_2d(sa, &tmA, kb * BK, m0, full0 + 8 * s);
-      tc::tma_load_2d(sb, &tmB, kb * BK, n0, full0 + 8 * s);
-      issued = kb + 1;
+      if (!ok) {
+        atomicCAS(&g_gemm_status, 0u, 1u);
+        // let copies already in flight land before the CTA's shared memory goes away
+        for (int j = (issued > S ? issued - S : 0); j < issued; ++j)
+          tc::wait_until(full0 + 8 * (j % S), (j / S) & 1, 100000000ull);
+      }
     }
-    if (!ok) {
-      atomicCAS(&g_gemm_status, 0u, 1u);
-      // let copies already in flight land before the CTA's shared memory goes away
-      for (int kb = (issued > S ? issued - S : 0); kb < issued; ++kb)
-        tc::wait_until(full0 + 8 * (kb % S), (kb / S) & 1, tc::globaltimer_ns() + 100000000ull);
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer ----
+      constexpr uint32_t idesc = tc::idesc_bf16_f32(BM, BN);
+      bool ok = true;
+      int it = 0, i = 0;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
+        const int acc = i & 1;
+        const uint32_t d = tmem + acc * BN;
+        if (!tc::wait_until(tempty0 + 8 * acc, ((i >> 1) & 1) ^ 1, deadline)) {  // epilogue drained it
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        for (int kb = 0; kb < kb_count; ++kb, ++it) {
+          const int s = it % S;
+          if (!tc::wait_until(full0 + 8 * s, (it / S) & 1, deadline)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const uint32_t sa = stage0 + s * G::kStage, sb = sa + G::kStageA;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            tc::mma_bf16(d, tc::sdesc_kmajor_sw128(sa + 32 * k), tc::sdesc_kmajor_sw128(sb + 32 * k), idesc,
+                         (kb | k) != 0);
+          tc::mma_commit(empty0 + 8 * s);  // stage free once these MMAs have read it
+        }
+        tc::mma_commit(tfull0 + 8 * acc);  // accumulator ready (partial on error)
+      }
+      if (!ok) atomicCAS(&g_gemm_status, 0u, 2u);
     }
-  } else if (warp == 1 && lane == 0) {
-    // ---- MMA issuer ----
-    constexpr uint32_t idesc = tc::idesc_bf16_f32(BM, BN);
-    for (int kb = 0; kb < kb_count; ++kb) {
-      const int s = kb % S;
-      if (!tc::wait_until(full0 + 8 * s, (kb / S) & 1, deadline)) {
-        ok = false;
+  } else {
+    // ---- epilogue: TMEM -> registers -> bf16 -> HBM ----
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int i = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+      const int acc = i & 1;
+      const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
+      const bool have = __all_sync(0xffffffffu, tc::wait_until(tfull0 + 8 * acc, (i >> 1) & 1, deadline));
+      if (!have) {
+        if (lane == 0) atomicCAS(&g_gemm_status, 0u, 3u);
         break;
       }
       tc::fence_after_sync();
-      const uint32_t sa = stage0 + s * G::kStage, sb = sa + G::kStageA;
-#pragma unroll
-      for (int k = 0; k < BK / 16; ++k) {
-        tc::mma_bf16(tmem, tc::sdesc_kmajor_sw128(sa + 32 * k), tc::sdesc_kmajor_sw128(sb + 32 * k), idesc,
-                     (kb | k) != 0);
-      }
-      tc::mma_commit(empty0 + 8 * s);  // stage free once these MMAs have read it
-    }
-    if (!ok) atomicCAS(&g_gemm_status, 0u, 2u);
-    tc::mma_commit(accum);  // accumulator complete (or the MMAs issued so far, on error)
-  }
-  __syncwarp();
-  pdl_launch_dependents();
-
-  // ---- epilogue: TMEM -> registers -> bf16 -> HBM ----
-  // warp-uniform verdict: the TMEM loads below are .sync.aligned
-  const bool have = __all_sync(0xffffffffu, tc::wait_until(accum, 0, deadline));
-  tc::fence_after_sync();
-  if (!have) {
-    if (lane == 0) atomicCAS(&g_gemm_status, 0u, 3u);
-  } else {
-    const int row = m0 + warp * 32 + lane;
-    const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+      const int row = m0 + q * 32 + lane;
+      const uint32_t trow = tmem + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      uint32_t r[32];
-      tc::tmem_ld32(trow + c, r);
-      if (row < M) {
-        uint16_t *dst = C + static_cast<int64_t>(row) * ldc + n0 + c;
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tc::tmem_ld32(trow + c, r);
+        if (row < M) {
+          uint16_t *dst = C + static_cast<int64_t>(row) * ldc + n0 + c;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          if (n0 + c + 8 * q + 8 <= N) {
-            uint4 v;
-            v.x = pack_bf16x2(apply_epi(__uint_as_float(r[8 * q + 0]), epi), apply_epi(__uint_as_float(r[8 * q + 1]), epi));
-            v.y = pack_bf16x2(apply_epi(__uint_as_float(r[8 * q + 2]), epi), apply_epi(__uint_as_float(r[8 * q + 3]), epi));
-            v.z = pack_bf16x2(apply_epi(__uint_as_float(r[8 * q + 4]), epi), apply_epi(__uint_as_float(r[8 * q + 5]), epi));
-            v.w = pack_bf16x2(apply_epi(__uint_as_float(r[8 * q + 6]), epi), apply_epi(__uint_as_float(r[8 * q + 7]), epi));
-            *reinterpret_cast<uint4 *>(dst + 8 * q) = v;
+          for (int g = 0; g < 4; ++g) {
+            if (n0 + c + 8 * g + 8 <= N) {
+              uint4 v;
+              v.x = pack_bf16x2(apply_epi(__uint_as_float(r[8 * g + 0]), epi), apply_epi(__uint_as_float(r[8 * g + 1]), epi));
+              v.y = pack_bf16x2(apply_epi(__uint_as_float(r[8 * g + 2]), epi), apply_epi(__uint_as_float(r[8 * g + 3]), epi));
+              v.z = pack_bf16x2(apply_epi(__uint_as_float(r[8 * g + 4]), epi), apply_epi(__uint_as_float(r[8 * g + 5]), epi));
+              v.w = pack_bf16x2(apply_epi(__uint_as_float(r[8 * g + 6]), epi), apply_epi(__uint_as_float(r[8 * g + 7]), epi));
+              *reinterpret_cast<uint4 *>(dst + 8 * g) = v;
+            }
           }
         }
       }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tempty0 + 8 * acc) : "memory");
     }
   }
+  __syncwarp();
+  pdl_launch_dependents();
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 2) tc::tmem_free(tmem, BN);
+  if (warp == 2) tc::tmem_free(tmem, kCols);
 }
 
 // ---- host side ---------------------------------------------------------------------
@@ -250,7 +283,8 @@ int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, uint16_t *C, int M
       return launch_status();
     attr_set[dev] = true;
   }
-  dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+  const int64_t tiles = static_cast<int64_t>((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  dim3 grid(static_cast<unsigned>(tiles < sm_count() ? tiles : sm_count()));
   return launch(gemm_tc_kernel<BN>, grid, dim3(kThreads), G::kSmem, s, pdl, ta, tb, C, M, N, K, ldc, epi);
 }
 

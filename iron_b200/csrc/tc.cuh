@@ -19,8 +19,10 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 
 // Wait for the phase of parity `parity` of the mbarrier at shared address `bar`
-// to complete, giving up at `deadline` (globaltimer ns). Returns false on timeout.
-__device__ __forceinline__ bool wait_until(uint32_t bar, uint32_t parity, uint64_t deadline) {
+// to complete, giving up once `timeout_ns` (globaltimer) have passed since the
+// first unsuccessful poll. Returns false on timeout.
+__device__ __forceinline__ bool wait_until(uint32_t bar, uint32_t parity, uint64_t timeout_ns) {
+  uint64_t start = 0;
   for (uint32_t i = 0;; ++i) {
     uint32_t done;
     asm volatile(
@@ -31,7 +33,11 @@ __device__ __forceinline__ bool wait_until(uint32_t bar, uint32_t parity, uint64
         : "r"(bar), "r"(parity)
         : "memory");
     if (done) return true;
-    if ((i & 63u) == 63u && globaltimer_ns() > deadline) return false;
+    if ((i & 63u) == 0u) {
+      const uint64_t now = globaltimer_ns();
+      if (start == 0) start = now;
+      else if (now - start > timeout_ns) return false;
+    }
   }
 }
 
