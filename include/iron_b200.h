@@ -248,6 +248,21 @@ int iron_embed(const int32_t *tokens, const uint16_t *table, uint16_t *x, int B,
 int iron_argmax(const uint16_t *logits, int32_t *out, int B, int V, int32_t *pos, unsigned flags,
                 void *stream);
 
+/* ---- prefill attention ------------------------------------------------------------
+ * Causal (or full) grouped-query attention over a sequence, replacing IRON's MHA
+ * operator (iron/operators/mha/op.py:21-135, golden mha/reference.py:27-94) and the
+ * CPU attention of its Llama prefill. D = 64; H a multiple of Hkv (query head h
+ * reads kv head h / (H / Hkv)). Element (b, h, t, d) of q / out lives at
+ * b*s[0] + h*s[1] + t*s[2] + d for the strides s = q_strides / out_strides (3
+ * int64 each, multiples of 8), and likewise for k and v with kv_strides. Queries
+ * t < S attend to keys j < S_kv (and j <= t if causal); output rows S <= t < S_pad
+ * are written as zeros. S_pad must be a multiple of 64. scale multiplies the logits.
+ */
+int iron_attn_prefill(const uint16_t *q, const uint16_t *k, const uint16_t *v, uint16_t *out, int B, int H,
+                      int Hkv, int D, int S, int S_pad, int S_kv, const int64_t *q_strides,
+                      const int64_t *kv_strides, const int64_t *out_strides, float scale, int causal,
+                      unsigned flags, void *stream);
+
 /* ---- tensor-core GEMM (prefill projections) -------------------------------------
  * C = epilogue(A . B^T) on tcgen05 tensor cores with TMEM accumulators: A bf16
  * [M, K] (row pitch lda), B bf16 [N, K] K-major (row pitch ldb), C bf16 [M, N]

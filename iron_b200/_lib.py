@@ -57,6 +57,8 @@ SIGNATURES: dict[str, list] = {
     "iron_gemm_bf16": [P, P, P, c_int, c_int, c_int, c_int64, c_int64, c_int64, c_int, c_int, c_float,
                        c_float, c_int, c_uint, P],
     "iron_gemm_status": [c_int],
+    "iron_attn_prefill": [P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, c_float, c_int,
+                          c_uint, P],
 }
 _RESTYPES = {"iron_strerror": c_char_p, "iron_attn_decode_workspace_bytes": c_size_t}
 

@@ -145,18 +145,25 @@ def strided_copy(inp, in_sizes, in_strides, in_offset, out_size, out_sizes, out_
 
 
 # ---- attention ------------------------------------------------------------
-def mha_prefill(Q, K, V, causal=True):
+def mha_prefill(Q, K, V, causal=True, chunk=1024):
     """Causal SDPA with GQA via repeat_interleave, scale 1/sqrt(d), fp32
-    (iron/operators/mha/reference.py:27-94). Q [H, S, d], K/V [Hkv, S, d]."""
+    (iron/operators/mha/reference.py:27-94). Q [H, S, d], K/V [Hkv, S_kv, d].
+    Query rows are processed `chunk` at a time (same math, bounded memory)."""
     g = Q.shape[0] // K.shape[0]
-    Kr = K.float().repeat_interleave(g, dim=0)
-    Vr = V.float().repeat_interleave(g, dim=0)
-    s = Q.float() @ Kr.transpose(-1, -2) / math.sqrt(Q.shape[-1])
-    if causal:
-        S = Q.shape[1]
-        m = torch.triu(torch.ones(S, S, dtype=torch.bool), diagonal=1)
-        s = s.masked_fill(m, -math.inf)
-    return (torch.softmax(s, dim=-1) @ Vr).to(BF16)
+    H, S, d = Q.shape
+    out = torch.empty(H, S, V.shape[-1], dtype=BF16)
+    for h in range(H):
+        Kh = K[h // g].float()
+        Vh = V[h // g].float()
+        for r0 in range(0, S, chunk):
+            q = Q[h, r0 : r0 + chunk].float()
+            s = q @ Kh.T / math.sqrt(d)
+            if causal:
+                rows = torch.arange(r0, r0 + q.shape[0]).unsqueeze(1)
+                cols = torch.arange(Kh.shape[0]).unsqueeze(0)
+                s = s.masked_fill(cols > rows, -math.inf)
+            out[h, r0 : r0 + chunk] = (torch.softmax(s, dim=-1) @ Vh).to(BF16)
+    return out
 
 
 def attn_decode(q, k_cache, v_cache, lens):
