@@ -608,6 +608,7 @@ def run_decode(args, world, rank, local):
     peak, peak_kind = _peak_hbm()
     e2e = _decode_e2e(eng, B, e2e_steps)
     gemv = _int4_gemv_figure(not args.no_pdl)
+    prefill = _prefill_figure(eng, PREFIX)
     line = {
         "metric": "Llama-3.2-1B-shape decode tok/s", "value": round(B * K * world / (ms_max * 1e-3), 1),
         "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_max / K,
@@ -627,6 +628,7 @@ def run_decode(args, world, rank, local):
                      "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback 6650 GB/s"},
         "int4_gemv": gemv,
+        "prefill": prefill,
         "gpu_launches": eng.kernels_per_step() * K,
         "e2e": e2e,
         "clocks": clocks,
@@ -640,6 +642,40 @@ def run_decode(args, world, rank, local):
 
         eng.graph = None
         dist.destroy_process_group()
+
+
+def _peak_tensor():
+    try:
+        d = json.loads((REPO / "MEASURED_PEAKS.json").read_text())
+        return float(d["bf16_tflops"]), "measured burst (MEASURED_PEAKS.json bf16_tflops)"
+    except Exception:
+        return 1590.0, "fallback 1590 TFLOP/s"
+
+
+def _prefill_figure(eng, S, reps=3):
+    """Config 5's prompt phase: an S-token prefill of sequence 0 (int4 weights
+    unpacked per matrix, tcgen05 GEMMs, causal prefill attention), device-timed."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    toks = torch.randint(0, eng.s.vocab_size, (S,), device="cuda", generator=g, dtype=torch.int32)
+    for _ in range(2):
+        eng.prefill(toks, seq=0)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        eng.prefill(toks, seq=0)
+    e1.record()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    flops = eng.prefill_flops(S)
+    peak, src = _peak_tensor()
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"tokens": S, "ms": round(ms, 3), "tok_s": round(S / (ms * 1e-3), 1), "tflops": round(tf, 1),
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(tf / peak, 4), "peak_source": src,
+                         "algorithmic_flops": flops,
+                         "note": "includes the per-matrix int4 -> bf16 unpack and all non-GEMM kernels"}}
 
 
 def _decode_e2e(eng, B, steps):

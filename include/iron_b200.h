@@ -102,6 +102,10 @@ int iron_pack_int4g32(const uint8_t *codes, const uint16_t *scales, uint8_t *pac
  *   (N/2 with IRON_FLAG_SWIGLU); K % 128 == 0, N % 16 == 0, 1 <= n_vec <= 64.
  *   Needs no workspace.
  */
+/* iron_unpack_int4g32: the packed layout back to bf16 rows out [N, K], each weight
+ * bf16(q * scale) exactly (bit-identical to iron_dequant_s4g32_rows on the natural
+ * codes); the prefill GEMMs read int4 weights through it. */
+int iron_unpack_int4g32(const uint8_t *packed, uint16_t *out, int N, int K, void *stream);
 int iron_gemv_int4g32(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,
                       int n_vec, const uint16_t *residual, unsigned flags, void *stream);
 
@@ -273,16 +277,23 @@ int iron_attn_prefill(const uint16_t *q, const uint16_t *k, const uint16_t *v, u
  * 0 none, 1 gelu as x*sigmoid(1.702x), 2 silu, 3 sigmoid) and, if `clamp`, a clamp
  * to [clamp_lo, clamp_hi] (flm/gemm/reference.py:8-57); bit 8 of `epilogue`
  * (IRON_GEMM_ROUND_FLOOR) rounds every fp32 -> bf16 conversion toward -inf
- * (flm Rounding.FLOOR) instead of to nearest even. K, N, lda, ldb, ldc multiples
+ * (flm Rounding.FLOOR) instead of to nearest even. If `residual` (bf16 [M, N], row pitch
+ * ldr) is given, C = bf16(bf16(epilogue(acc)) + residual), the residual add of a
+ * decoder block. Epilogue 4 (IRON_GEMM_EPI_SWIGLU) is the SwiGLU of an interleaved
+ * gate/up projection: B's rows come in groups of 16 (8 gate rows, then the 8 matching
+ * up rows) and C [M, N/2] gets bf16(bf16(silu(bf16(gate))) * bf16(up)) per pair
+ * (no residual, clamp or floor rounding with it; N a multiple of 16). K, N, lda, ldb, ldc multiples
  * of 8; pointers 16-byte aligned. block_n = 0 picks the tile width (64/128/256).
  * iron_gemm_status returns IRON_ERR_TIMEOUT if any GEMM since the last reset hit
  * its bounded-wait deadline (reset != 0 clears it); it synchronises the device.
  */
 #define IRON_GEMM_ROUND_FLOOR 0x100
+#define IRON_GEMM_EPI_SWIGLU 4
 
 int iron_gemm_bf16(const uint16_t *A, const uint16_t *B, uint16_t *C, int M, int N, int K,
-                   int64_t lda, int64_t ldb, int64_t ldc, int epilogue, int clamp, float clamp_lo,
-                   float clamp_hi, int block_n, unsigned flags, void *stream);
+                   int64_t lda, int64_t ldb, int64_t ldc, const uint16_t *residual, int64_t ldr,
+                   int epilogue, int clamp, float clamp_lo, float clamp_hi, int block_n, unsigned flags,
+                   void *stream);
 int iron_gemm_status(int reset);
 
 #ifdef __cplusplus

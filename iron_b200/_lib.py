@@ -22,6 +22,7 @@ IRON_FLAG_SWIGLU = 0x2
 IRON_EPI_NONE = 0
 IRON_EPI_GELU = 1
 IRON_GEMM_ROUND_FLOOR = 0x100
+IRON_GEMM_EPI_SWIGLU = 4
 
 P = c_void_p  # every tensor is passed as a raw device address
 
@@ -54,9 +55,10 @@ SIGNATURES: dict[str, list] = {
                             c_uint, P],
     "iron_embed": [P, P, P, c_int, c_int, c_uint, P],
     "iron_argmax": [P, P, c_int, c_int, P, c_uint, P],
-    "iron_gemm_bf16": [P, P, P, c_int, c_int, c_int, c_int64, c_int64, c_int64, c_int, c_int, c_float,
-                       c_float, c_int, c_uint, P],
+    "iron_gemm_bf16": [P, P, P, c_int, c_int, c_int, c_int64, c_int64, c_int64, P, c_int64, c_int, c_int,
+                       c_float, c_float, c_int, c_uint, P],
     "iron_gemm_status": [c_int],
+    "iron_unpack_int4g32": [P, P, c_int, c_int, P],
     "iron_attn_prefill": [P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, c_float, c_int,
                           c_uint, P],
 }

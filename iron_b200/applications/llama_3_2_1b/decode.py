@@ -17,6 +17,7 @@ embedding table being the exact dequantization of the tied lm-head weights.
 
 from __future__ import annotations
 
+import ctypes
 import math
 from dataclasses import dataclass
 
@@ -179,6 +180,87 @@ class LlamaDecodeEngine:
         call("iron_gemv_int4g32", p(self.lm.packed), p(self.xn), p(self.logits), s.vocab_size, E, B,
              None, f, stream)
         call("iron_argmax", p(self.logits), p(self.tokens), B, s.vocab_size, p(self.pos), f, stream)
+
+    # -- prefill: a whole prompt through the tensor-core GEMMs -----------------------------
+    def _prefill_buffers(self, S: int):
+        S = -(-S // 64) * 64  # the attention writes its padded rows (zeros) too
+        if getattr(self, "_pf_S", 0) >= S:
+            return
+        s, dev = self.s, self.dev
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        E, H = s.emb_dim, s.hidden_dim
+        self._pf = {
+            "x": torch.empty(S, E, **bf), "xn": torch.empty(S, E, **bf), "h": torch.empty(S, E, **bf),
+            "qkv": torch.empty(S, s.qkv_dim, **bf), "q": torch.empty(S, s.n_heads, s.head_dim, **bf),
+            "attn": torch.empty(S, s.n_heads * s.head_dim, **bf), "act": torch.empty(S, H, **bf),
+            "w": torch.empty(2 * H * E, **bf),  # one layer matrix, dequantized
+            "pos": torch.arange(S, dtype=torch.int32, device=dev), "lens": torch.empty(S, dtype=torch.int32, device=dev),
+            "tok": torch.empty(S, dtype=torch.int32, device=dev),
+        }
+        self._pf_S = S
+
+    def _gemm(self, A, mat, C, M, residual=None, swiglu=False, stream=0):
+        """C = A . dequant(mat)^T (+ residual | SwiGLU) on the tcgen05 tensor cores."""
+        p, w = (lambda t: t.data_ptr()), self._pf["w"]
+        _lib.call("iron_unpack_int4g32", p(mat.packed), p(w), mat.rows, mat.cols, stream)
+        N, K = mat.rows, mat.cols
+        _lib.call("iron_gemm_bf16", p(A), p(w), p(C), M, N, K, K, K, N // 2 if swiglu else N,
+                  p(residual) if residual is not None else None, N if residual is not None else 0,
+                  _lib.IRON_GEMM_EPI_SWIGLU if swiglu else 0, 0, 0.0, 0.0, 0, self.flags, stream)
+
+    def _launch_prefill(self, S: int, seq: int, stream: int):
+        s, f, pf = self.s, self.flags, self._pf
+        call, p = _lib.call, (lambda t: t.data_ptr())
+        E, Hd, L = s.emb_dim, s.head_dim, self.L
+        Hq, Hk = s.n_heads, s.n_kv_groups
+        kv_h = L * Hd
+        qst = (ctypes.c_int64 * 3)(0, Hd, Hq * Hd)
+        kvst = (ctypes.c_int64 * 3)(0, kv_h, Hd)
+        call("iron_embed", p(pf["tok"]), p(self.embed_table), p(pf["x"]), S, E, f, stream)
+        for li, lay in enumerate(self.layers):
+            kc = self.kc[li, seq]
+            vc = self.vc[li, seq]
+            call("iron_rmsnorm", p(pf["x"]), None, None, p(lay["n1"]), p(pf["xn"]), S, E, s.eps, f, stream)
+            self._gemm(pf["xn"], lay["qkv"], pf["qkv"], S, stream=stream)
+            # every prompt token is a "sequence" of the RoPE + cache-append kernel at position t
+            call("iron_rope_kv_append", p(pf["qkv"]), p(pf["pos"]), p(self.lut), p(pf["q"]), p(kc), p(vc),
+                 p(pf["lens"]), S, Hq, Hk, Hd, 0, kv_h, f, stream)
+            call("iron_attn_prefill", p(pf["q"]), p(kc), p(vc), p(pf["attn"]), 1, Hq, Hk, Hd, S,
+                 -(-S // 64) * 64, S, qst, kvst, qst, 1.0 / math.sqrt(Hd), 1, f, stream)
+            self._gemm(pf["attn"], lay["o"], pf["h"], S, residual=pf["x"], stream=stream)
+            call("iron_rmsnorm", p(pf["h"]), None, None, p(lay["n2"]), p(pf["xn"]), S, E, s.eps, f, stream)
+            self._gemm(pf["xn"], lay["gu"], pf["act"], S, swiglu=True, stream=stream)
+            self._gemm(pf["act"], lay["d"], pf["x"], S, residual=pf["h"], stream=stream)
+        # next token from the last position only
+        last = pf["x"][S - 1 : S]
+        xn1 = self.xn[seq : seq + 1]
+        call("iron_rmsnorm", p(last), None, None, p(self.nf), p(xn1), 1, E, s.eps, f, stream)
+        call("iron_gemv_int4g32", p(self.lm.packed), p(xn1), p(self.logits[seq : seq + 1]), s.vocab_size, E, 1,
+             None, f, stream)
+        call("iron_argmax", p(self.logits[seq : seq + 1]), p(self.tokens[seq : seq + 1]), 1, s.vocab_size, None,
+             f, stream)
+
+    def prefill(self, tokens, seq: int = 0):
+        """Run a prompt through the model for sequence `seq`: fills its KV cache at
+        positions 0..S-1, leaves the greedy next token in tokens[seq] and sets
+        pos[seq] = S (so decode steps continue from there)."""
+        toks = torch.as_tensor(tokens, dtype=torch.int32).reshape(-1)
+        S = int(toks.numel())
+        if S < 1 or S > self.L:
+            raise ValueError(f"prompt of {S} tokens does not fit the cache ({self.L})")
+        self._prefill_buffers(S)
+        self._pf["tok"][:S].copy_(toks)
+        self._launch_prefill(S, seq, torch.cuda.current_stream().cuda_stream)
+        self.pos[seq] = S
+        self.lens[seq] = S
+
+    def prefill_flops(self, S: int) -> int:
+        """Tensor-core FLOPs of the prefill GEMMs and attention for an S-token prompt."""
+        s = self.s
+        E, H, Q, Hd = s.emb_dim, s.hidden_dim, s.qkv_dim, s.head_dim
+        gemm = 2 * S * (Q * E + E * s.n_heads * Hd + 2 * H * E + E * H)
+        attn = 4 * s.n_heads * Hd * S * (S + 1) // 2
+        return s.n_layers * (gemm + attn)
 
     def kernels_per_step(self) -> int:
         B, s = self.B, self.s

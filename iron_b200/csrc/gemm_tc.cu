@@ -32,7 +32,7 @@ constexpr uint64_t kDeadlineNs = 2000000000ull;
 __device__ unsigned g_gemm_status;  // 0 = ok, else the first failing role's code
 
 struct Epi {
-  int mode;   // 0 none, 1 gelu (x * sigmoid(1.702 x)), 2 silu, 3 sigmoid
+  int mode;   // 0 none, 1 gelu (x * sigmoid(1.702 x)), 2 silu, 3 sigmoid, 4 swiglu (interleaved 8 + 8)
   int floor;  // round fp32 -> bf16 toward -inf instead of to nearest even
   int clamp;
   float lo, hi;
@@ -51,6 +51,19 @@ __device__ __forceinline__ float apply_epi(float c, const Epi &e) {
   else if (e.mode == 3) c = 1.0f / (1.0f + __expf(-c));
   if (e.clamp) c = fminf(fmaxf(c, e.lo), e.hi);
   return to_bf16(c, e.floor);
+}
+
+// Gate/up pair of the interleaved SwiGLU layout: bf16(bf16(silu(bf16(g))) * bf16(u)).
+__device__ __forceinline__ float swiglu_pair(float g, float u) {
+  g = __bfloat162float(__float2bfloat16_rn(g));
+  u = __bfloat162float(__float2bfloat16_rn(u));
+  const float sw = __bfloat162float(__float2bfloat16_rn(g / (1.0f + __expf(-g))));
+  return sw * u;
+}
+
+__device__ __forceinline__ uint32_t add_res2(uint32_t packed, uint32_t res) {
+  // bf16(projection) + bf16(residual), rounded once more
+  return pack_bf16x2(bf16_lo(packed) + bf16_lo(res), bf16_hi(packed) + bf16_hi(res));
 }
 
 template <int BN>
@@ -73,7 +86,8 @@ struct Cfg {
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   uint16_t *__restrict__ C, int M, int N, int K, int64_t ldc, Epi epi) {
+                   uint16_t *__restrict__ C, int M, int N, int K, int64_t ldc,
+                   const uint16_t *__restrict__ R, int64_t ldr, Epi epi) {
   using G = Cfg<BN>;
   constexpr int S = G::kStages;
   constexpr uint32_t kCols = 2 * BN;
@@ -191,8 +205,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
         tc::tmem_ld32(trow + c, r);
-        if (row < M) {
+        if (row < M && epi.mode == 4) {
+          // two 16-column groups: 8 gate then 8 up columns -> 8 outputs each
+          uint16_t *dst = C + static_cast<int64_t>(row) * ldc + (n0 + c) / 2;
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            if (n0 + c + 16 * g + 16 <= N) {
+              const uint32_t *rg = r + 16 * g;
+              uint4 v;
+              v.x = pack_bf16x2(swiglu_pair(__uint_as_float(rg[0]), __uint_as_float(rg[8])),
+                                swiglu_pair(__uint_as_float(rg[1]), __uint_as_float(rg[9])));
+              v.y = pack_bf16x2(swiglu_pair(__uint_as_float(rg[2]), __uint_as_float(rg[10])),
+                                swiglu_pair(__uint_as_float(rg[3]), __uint_as_float(rg[11])));
+              v.z = pack_bf16x2(swiglu_pair(__uint_as_float(rg[4]), __uint_as_float(rg[12])),
+                                swiglu_pair(__uint_as_float(rg[5]), __uint_as_float(rg[13])));
+              v.w = pack_bf16x2(swiglu_pair(__uint_as_float(rg[6]), __uint_as_float(rg[14])),
+                                swiglu_pair(__uint_as_float(rg[7]), __uint_as_float(rg[15])));
+              *reinterpret_cast<uint4 *>(dst + 8 * g) = v;
+            }
+          }
+        } else if (row < M) {
           uint16_t *dst = C + static_cast<int64_t>(row) * ldc + n0 + c;
+          const uint16_t *res = R ? R + static_cast<int64_t>(row) * ldr + n0 + c : nullptr;
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
             if (n0 + c + 8 * g + 8 <= N) {
@@ -201,6 +235,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               v.y = pack_bf16x2(apply_epi(__uint_as_float(r[8 * g + 2]), epi), apply_epi(__uint_as_float(r[8 * g + 3]), epi));
               v.z = pack_bf16x2(apply_epi(__uint_as_float(r[8 * g + 4]), epi), apply_epi(__uint_as_float(r[8 * g + 5]), epi));
               v.w = pack_bf16x2(apply_epi(__uint_as_float(r[8 * g + 6]), epi), apply_epi(__uint_as_float(r[8 * g + 7]), epi));
+              if (res) {
+                const uint4 rv = *reinterpret_cast<const uint4 *>(res + 8 * g);
+                v.x = add_res2(v.x, rv.x);
+                v.y = add_res2(v.y, rv.y);
+                v.z = add_res2(v.z, rv.z);
+                v.w = add_res2(v.w, rv.w);
+              }
               *reinterpret_cast<uint4 *>(dst + 8 * g) = v;
             }
           }
@@ -272,7 +313,7 @@ int pick_bn(int M, int N, int sms) {
 
 template <int BN>
 int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, uint16_t *C, int M, int N, int K, int64_t ldc,
-                Epi epi, cudaStream_t s, bool pdl) {
+                const uint16_t *R, int64_t ldr, Epi epi, cudaStream_t s, bool pdl) {
   using G = Cfg<BN>;
   static bool attr_set[64] = {};
   int dev = 0;
@@ -285,7 +326,7 @@ int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, uint16_t *C, int M
   }
   const int64_t tiles = static_cast<int64_t>((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   dim3 grid(static_cast<unsigned>(tiles < sm_count() ? tiles : sm_count()));
-  return launch(gemm_tc_kernel<BN>, grid, dim3(kThreads), G::kSmem, s, pdl, ta, tb, C, M, N, K, ldc, epi);
+  return launch(gemm_tc_kernel<BN>, grid, dim3(kThreads), G::kSmem, s, pdl, ta, tb, C, M, N, K, ldc, R, ldr, epi);
 }
 
 }  // namespace gemm
@@ -295,14 +336,19 @@ using namespace iron;
 using namespace iron::gemm;
 
 extern "C" int iron_gemm_bf16(const uint16_t *A, const uint16_t *B, uint16_t *C, int M, int N, int K,
-                              int64_t lda, int64_t ldb, int64_t ldc, int epilogue, int clamp, float clamp_lo,
-                              float clamp_hi, int block_n, unsigned flags, void *stream) {
+                              int64_t lda, int64_t ldb, int64_t ldc, const uint16_t *residual, int64_t ldr,
+                              int epilogue, int clamp, float clamp_lo, float clamp_hi, int block_n, unsigned flags,
+                              void *stream) {
   if (!A || !B || !C) return IRON_ERR_NULL;
   if (M <= 0 || N <= 0 || K <= 0) return IRON_ERR_SHAPE;
-  if (K % 8 || N % 8 || lda < K || ldb < K || ldc < N) return IRON_ERR_SHAPE;
-  if (lda % 8 || ldb % 8 || ldc % 8 || !aligned16(A) || !aligned16(B) || !aligned16(C)) return IRON_ERR_ALIGN;
   const int act = epilogue & 0xff, floor_rnd = (epilogue >> 8) & 1;
-  if (act > 3 || (epilogue & ~0x1ff) || (clamp && !(clamp_lo <= clamp_hi))) return IRON_ERR_ARG;
+  if (act > 4 || (epilogue & ~0x1ff) || (clamp && !(clamp_lo <= clamp_hi))) return IRON_ERR_ARG;
+  if (act == 4 && (residual || clamp || floor_rnd || N % 16)) return IRON_ERR_ARG;
+  const int64_t out_cols = act == 4 ? N / 2 : N;
+  if (K % 8 || N % 8 || lda < K || ldb < K || ldc < out_cols) return IRON_ERR_SHAPE;
+  if (residual && ldr < N) return IRON_ERR_SHAPE;
+  if (lda % 8 || ldb % 8 || ldc % 8 || !aligned16(A) || !aligned16(B) || !aligned16(C)) return IRON_ERR_ALIGN;
+  if (residual && (ldr % 8 || !aligned16(residual))) return IRON_ERR_ALIGN;
   int bn = block_n ? block_n : pick_bn(M, N, sm_count());
   if (bn != 64 && bn != 128 && bn != 256) return IRON_ERR_ARG;
   CUtensorMap ta, tb;
@@ -313,9 +359,9 @@ extern "C" int iron_gemm_bf16(const uint16_t *A, const uint16_t *B, uint16_t *C,
   auto s = static_cast<cudaStream_t>(stream);
   const bool pdl = (flags & IRON_FLAG_PDL) != 0;
   switch (bn) {
-    case 256: return launch_gemm<256>(ta, tb, C, M, N, K, ldc, epi, s, pdl);
-    case 128: return launch_gemm<128>(ta, tb, C, M, N, K, ldc, epi, s, pdl);
-    default: return launch_gemm<64>(ta, tb, C, M, N, K, ldc, epi, s, pdl);
+    case 256: return launch_gemm<256>(ta, tb, C, M, N, K, ldc, residual, ldr, epi, s, pdl);
+    case 128: return launch_gemm<128>(ta, tb, C, M, N, K, ldc, residual, ldr, epi, s, pdl);
+    default: return launch_gemm<64>(ta, tb, C, M, N, K, ldc, residual, ldr, epi, s, pdl);
   }
 }
 

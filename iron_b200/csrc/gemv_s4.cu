@@ -323,6 +323,42 @@ static int launch_s4_tile_cs(const uint8_t *packed, const uint16_t *x, uint16_t 
   }
 }
 
+// Inverse of pack_s4g32_kernel: one thread per 16-byte code piece writes its
+// row's 4 x 8 dequantized weights, bf16(q * s) exactly (the products of a 4-bit
+// integer and a bf16 scale are exact in fp32, so one rounding gives the
+// Dequant golden's value).
+__global__ void unpack_s4g32_kernel(const uint8_t *__restrict__ packed, uint16_t *__restrict__ out, int K,
+                                    int64_t pieces) {
+  const int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (p >= pieces) return;
+  const int cpt = K / 128;
+  const int64_t unit = p / 64;
+  const int piece = static_cast<int>(p % 64);
+  const int64_t tile = unit / cpt;
+  const int c = static_cast<int>(unit % cpt);
+  const int h = piece >> 5, lane = piece & 31, gid = lane >> 2, tid = lane & 3;
+  const uint4 *u = reinterpret_cast<const uint4 *>(packed) + unit * 72;
+  const uint4 cw = u[piece];
+  const uint4 sw = u[64 + gid];
+  const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
+  const uint32_t sc[2] = {h ? sw.z : sw.x, h ? sw.w : sw.y};  // groups (0,1), (2,3) of the row
+  const int64_t row = tile * 16 + gid + 8 * h;
+  uint16_t *dst = out + row * K + c * 128 + tid * 8;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float scale = (j & 1) ? bf16_hi(sc[j >> 1]) : bf16_lo(sc[j >> 1]);
+    uint32_t o[4];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const uint32_t byte = (words[j] >> (8 * b)) & 0xffu;
+      const float lo = static_cast<float>(static_cast<int>((byte & 0xfu) ^ 8u) - 8) * scale;
+      const float hi = static_cast<float>(static_cast<int>((byte >> 4) ^ 8u) - 8) * scale;
+      o[b] = pack_bf16x2(lo, hi);
+    }
+    *reinterpret_cast<uint4 *>(dst + j * 32) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 }  // namespace iron
 
 using namespace iron;
@@ -336,6 +372,17 @@ extern "C" int iron_pack_int4g32(const uint8_t *codes, const uint16_t *scales, u
   const int threads = 256;
   pack_s4g32_kernel<<<static_cast<unsigned>((pieces + threads - 1) / threads), threads, 0,
                       static_cast<cudaStream_t>(stream)>>>(codes, scales, packed, N, K, pieces);
+  return launch_status();
+}
+
+extern "C" int iron_unpack_int4g32(const uint8_t *packed, uint16_t *out, int N, int K, void *stream) {
+  if (!packed || !out) return IRON_ERR_NULL;
+  if (N <= 0 || K <= 0 || N % 16 || K % 128) return IRON_ERR_SHAPE;
+  if (!aligned16(packed) || !aligned16(out)) return IRON_ERR_ALIGN;
+  const int64_t pieces = static_cast<int64_t>(N / 16) * (K / 128) * 64;
+  const int threads = 256;
+  unpack_s4g32_kernel<<<static_cast<unsigned>((pieces + threads - 1) / threads), threads, 0,
+                        static_cast<cudaStream_t>(stream)>>>(packed, out, K, pieces);
   return launch_status();
 }
 

@@ -117,7 +117,7 @@ class GEMM(MLIROperator):
         p = _lib.dptr
         epi = self.epilogue.mode | (_lib.IRON_GEMM_ROUND_FLOOR if self.rounding is Rounding.FLOOR else 0)
         lo, hi = self.clamp if self.clamp is not None else (0.0, 0.0)
-        _lib.call("iron_gemm_bf16", p(A), p(B), p(C), self.M, self.N, self.K, self.K, self.K, self.N, epi,
+        _lib.call("iron_gemm_bf16", p(A), p(B), p(C), self.M, self.N, self.K, self.K, self.K, self.N, None, 0, epi,
                   int(self.clamp is not None), float(lo), float(hi), 0, flags, stream)
 
     def reference(self, A, B):

@@ -94,9 +94,9 @@ class GEMM(MLIROperator):
             bk = self._bt.data_ptr()
         M, N, K = self.M, self.N, self.K
         if self.c_col_maj:  # C^T [N, M] = B [N, K] . A [M, K]^T
-            _lib.call("iron_gemm_bf16", bk, p(A), p(C), N, M, K, K, K, M, 0, 0, 0.0, 0.0, 0, flags, stream)
+            _lib.call("iron_gemm_bf16", bk, p(A), p(C), N, M, K, K, K, M, None, 0, 0, 0, 0.0, 0.0, 0, flags, stream)
         else:
-            _lib.call("iron_gemm_bf16", p(A), bk, p(C), M, N, K, K, K, N, 0, 0, 0.0, 0.0, 0, flags, stream)
+            _lib.call("iron_gemm_bf16", p(A), bk, p(C), M, N, K, K, K, N, None, 0, 0, 0, 0.0, 0.0, 0, flags, stream)
 
     def reference(self, A, B):
         from .reference import reference

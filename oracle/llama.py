@@ -72,3 +72,29 @@ def model_decode(tokens, pos, layers, nf, embed, lm, k_caches, v_caches, angles,
     for li, W in enumerate(layers):
         x = block_decode(x, k_caches[li], v_caches[li], pos, W, angles, n_heads, n_kv, head_dim, eps)
     return ops.gemv_multi(lm, ops.rms_norm(x, nf, eps))
+
+
+def model_prefill(tokens, layers, nf, embed, lm, k_caches, v_caches, angles, n_heads, n_kv, head_dim,
+                  eps=1e-5):
+    """A whole prompt through the model (llama_cpu.py:221-285 at prefill: every
+    position, causal attention), for one sequence. Caches [n_kv, Lmax, hd] get
+    positions 0..S-1. Returns the last position's logits [1, V] (bf16)."""
+    tok = torch.as_tensor(tokens, dtype=torch.long)
+    S = tok.numel()
+    x = embed[tok].clone()
+    for li, W in enumerate(layers):
+        xn = ops.rms_norm(x, W["n1"], eps)
+        q = ops.gemv_multi(W["q"], xn).reshape(S * n_heads, head_dim)
+        k = ops.gemv_multi(W["k"], xn).reshape(S * n_kv, head_dim)
+        v = ops.gemv_multi(W["v"], xn).reshape(S, n_kv, head_dim)
+        # row r of a token-major [S * heads, hd] view is token r // heads: angle row r // heads
+        q = ops.rope(q, angles[:S]).reshape(S, n_heads, head_dim)
+        k = ops.rope(k, angles[:S]).reshape(S, n_kv, head_dim)
+        k_caches[li][:, :S] = k.transpose(0, 1)
+        v_caches[li][:, :S] = v.transpose(0, 1)
+        att = ops.mha_prefill(q.transpose(0, 1), k.transpose(0, 1), v.transpose(0, 1))
+        h = ops.add(x, ops.gemv_multi(W["o"], att.transpose(0, 1).reshape(S, n_heads * head_dim)))
+        hn = ops.rms_norm(h, W["n2"], eps)
+        act = ops.swiglu_act(ops.gemv_multi(W["g"], hn), ops.gemv_multi(W["u"], hn))
+        x = ops.add(h, ops.gemv_multi(W["d"], act))
+    return ops.gemv_multi(lm, ops.rms_norm(x[S - 1 : S], nf, eps))

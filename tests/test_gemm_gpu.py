@@ -108,7 +108,7 @@ def test_gemm_tile_widths_and_ragged_m(block_n):
     A, Bt = _inputs(M, K, N, b_col_maj=True, seed=block_n)
     Ad, Bd = A.cuda(), Bt.cuda()
     C = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
-    _lib.call("iron_gemm_bf16", Ad.data_ptr(), Bd.data_ptr(), C.data_ptr(), M, N, K, K, K, N, 0, 0, 0.0, 0.0,
+    _lib.call("iron_gemm_bf16", Ad.data_ptr(), Bd.data_ptr(), C.data_ptr(), M, N, K, K, K, N, None, 0, 0, 0, 0.0, 0.0,
               block_n, 0, _lib.current_stream())
     torch.cuda.synchronize()
     assert_close(C.cpu(), ops.gemm(A, Bt, True, False), 0.005, 0.005)
@@ -127,7 +127,7 @@ def test_gemm_pdl_chain_in_graph():
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=s):
         for X, W, Y, k in ((A, B1, C1, K), (C1, B2, C2, N)):
-            _lib.call("iron_gemm_bf16", X.data_ptr(), W.data_ptr(), Y.data_ptr(), M, N, k, k, k, N, 0, 0, 0.0,
+            _lib.call("iron_gemm_bf16", X.data_ptr(), W.data_ptr(), Y.data_ptr(), M, N, k, k, k, N, None, 0, 0, 0, 0.0,
                       0.0, 0, _lib.IRON_FLAG_PDL, s.cuda_stream)
     for _ in range(3):
         graph.replay()
@@ -141,13 +141,13 @@ def test_gemm_rejects_bad_arguments():
     lib = _lib.load()
     A = torch.zeros(128, 64, dtype=torch.bfloat16, device="cuda")
     s = _lib.current_stream()
-    assert lib.iron_gemm_bf16(A.data_ptr(), A.data_ptr(), A.data_ptr(), 128, 64, 60, 64, 64, 64, 0, 0, 0.0,
+    assert lib.iron_gemm_bf16(A.data_ptr(), A.data_ptr(), A.data_ptr(), 128, 64, 60, 64, 64, 64, None, 0, 0, 0, 0.0,
                               0.0, 0, 0, s) == _lib.IRON_ERR_SHAPE
-    assert lib.iron_gemm_bf16(A.data_ptr(), A.data_ptr(), A.data_ptr(), 128, 64, 64, 64, 64, 64, 9, 0, 0.0,
+    assert lib.iron_gemm_bf16(A.data_ptr(), A.data_ptr(), A.data_ptr(), 128, 64, 64, 64, 64, 64, None, 0, 9, 0, 0.0,
                               0.0, 0, 0, s) == _lib.IRON_ERR_ARG
-    assert lib.iron_gemm_bf16(A.data_ptr(), A.data_ptr(), A.data_ptr(), 128, 64, 64, 64, 64, 64, 0, 0, 0.0,
+    assert lib.iron_gemm_bf16(A.data_ptr(), A.data_ptr(), A.data_ptr(), 128, 64, 64, 64, 64, 64, None, 0, 0, 0, 0.0,
                               0.0, 96, 0, s) == _lib.IRON_ERR_ARG
-    assert lib.iron_gemm_bf16(A.data_ptr() + 2, A.data_ptr(), A.data_ptr(), 64, 64, 64, 64, 64, 64, 0, 0, 0.0,
+    assert lib.iron_gemm_bf16(A.data_ptr() + 2, A.data_ptr(), A.data_ptr(), 64, 64, 64, 64, 64, 64, None, 0, 0, 0, 0.0,
                               0.0, 0, 0, s) == _lib.IRON_ERR_ALIGN
 
 
@@ -198,3 +198,37 @@ def test_flm_gemm_golden_fixtures(epi, clamp):
                             rel_tol=0.04, abs_tol=float(0.0002 * 512 * d["A"].abs().float().mean()
                                                         * d["B"].abs().float().mean()))
     assert not errors
+
+
+def test_gemm_residual_epilogue():
+    """C = bf16(bf16(A B^T) + R): the o_proj / down_proj residual of a decoder block."""
+    M, K, N = 384, 1024, 768
+    g = torch.Generator().manual_seed(11)
+    A = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    W = (torch.randn(N, K, generator=g) * 0.03).to(torch.bfloat16)
+    R = torch.randn(M, N, generator=g).to(torch.bfloat16)
+    Ad, Wd, Rd = A.cuda(), W.cuda(), R.cuda()
+    C = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    _lib.call("iron_gemm_bf16", Ad.data_ptr(), Wd.data_ptr(), C.data_ptr(), M, N, K, K, K, N, Rd.data_ptr(), N,
+              0, 0, 0.0, 0.0, 0, 0, _lib.current_stream())
+    torch.cuda.synchronize()
+    assert_close(C.cpu(), ops.add(R, ops.gemm(A, W, True, False)), 0.02, 0.01)
+
+
+def test_gemm_swiglu_epilogue():
+    """Interleaved gate/up rows (8 + 8 per 16) -> silu(gate) * up, N/2 outputs."""
+    M, K, H = 256, 512, 1024
+    g = torch.Generator().manual_seed(12)
+    A = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    Wg = (torch.randn(H, K, generator=g) * 0.05).to(torch.bfloat16)
+    Wu = (torch.randn(H, K, generator=g) * 0.05).to(torch.bfloat16)
+    t = torch.arange(H // 8)
+    idx = torch.stack([t * 8 + i for i in range(8)] + [H + t * 8 + i for i in range(8)], 1).reshape(-1)
+    Wgu = torch.cat([Wg, Wu])[idx].contiguous()
+    Ad, Wd = A.cuda(), Wgu.cuda()
+    C = torch.empty(M, H, dtype=torch.bfloat16, device="cuda")
+    _lib.call("iron_gemm_bf16", Ad.data_ptr(), Wd.data_ptr(), C.data_ptr(), M, 2 * H, K, K, K, H, None, 0,
+              _lib.IRON_GEMM_EPI_SWIGLU, 0, 0.0, 0.0, 0, 0, _lib.current_stream())
+    torch.cuda.synchronize()
+    ref = ops.swiglu_act(ops.gemm(A, Wg, True, False), ops.gemm(A, Wu, True, False))
+    assert_close(C.cpu(), ref, 0.04, 1e-3)

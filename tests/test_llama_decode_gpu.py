@@ -79,3 +79,39 @@ def test_graph_replay_matches_eager_steps():
         runs.append(outs)
     for (ta, la), (tb, lb) in zip(*runs):
         assert torch.equal(ta, tb) and torch.equal(la, lb)
+
+
+@pytest.mark.parametrize("S", [100, 192])
+def test_prefill_matches_oracle_then_decodes(S):
+    """Prompt through the tensor-core prefill (int4 weights unpacked to bf16, tcgen05
+    GEMMs with fused residual / SwiGLU epilogues, causal prefill attention), then one
+    decode step, against the oracle's prefill + decode on the dequantized weights."""
+    shape = LlamaShape(n_layers=2, vocab_size=4096)
+    L = 256
+    eng = LlamaDecodeEngine(shape, 2, L, seed=11, keep_natural=True)
+    toks = [(13 * i + 5) % shape.vocab_size for i in range(S)]
+    eng.set_state([0, 0], [0, 0])
+    eng.prefill(toks, seq=1)
+    torch.cuda.synchronize()
+    W = _oracle_weights(eng)
+    kcs = [torch.zeros(shape.n_kv_groups, L, shape.head_dim, dtype=torch.bfloat16) for _ in range(shape.n_layers)]
+    vcs = [torch.zeros_like(k) for k in kcs]
+    lm = eng.lm.dequant().cpu()
+    logits = ollama.model_prefill(toks, W, eng.nf.cpu(), eng.embed_table.cpu(), lm, kcs, vcs, eng.lut.cpu(),
+                                  shape.n_heads, shape.n_kv_groups, shape.head_dim)
+    assert_close(eng.logits[1:2].cpu(), logits, 2e-2, 2e-2, what="prefill logits")
+    for li in range(shape.n_layers):
+        assert_close(eng.kc[li, 1, :, :S].cpu(), kcs[li][:, :S], 2e-2, 2e-2, max_mismatch_frac=1e-3, what="k")
+        assert_close(eng.vc[li, 1, :, :S].cpu(), vcs[li][:, :S], 2e-2, 2e-2, max_mismatch_frac=1e-3, what="v")
+    assert int(eng.pos[1]) == S
+    nxt = int(eng.tokens[1])
+    got = eng.logits[1].cpu().float()
+    assert got[nxt] == got.max()
+    # one decode step continues the sequence from position S
+    eng.step()
+    torch.cuda.synchronize()
+    kcs2 = [torch.stack([torch.zeros_like(k), k]) for k in kcs]
+    vcs2 = [torch.stack([torch.zeros_like(v), v]) for v in vcs]
+    lg2 = ollama.model_decode([0, nxt], [0, S], W, eng.nf.cpu(), eng.embed_table.cpu(), lm, kcs2, vcs2,
+                              eng.lut.cpu(), shape.n_heads, shape.n_kv_groups, shape.head_dim)
+    assert_close(eng.logits[1:2].cpu(), lg2[1:2], 3e-2, 3e-2, what="decode after prefill")
