@@ -57,16 +57,17 @@ def _args():
                     help="timed steps (default: 256 decode steps, 20000 GEMVs)")
     ap.add_argument("--warmup", type=int, default=None, help="warm-up steps (default: 5 decode, 200 GEMV)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "int4_gemv", "bf16_gemv"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "int4_gemv", "bf16_gemv", "gemm"], default="decode")
+    ap.add_argument("--gemm-shape", default="2048,2048,8192", help="M,K,N of the gemm workload")
     ap.add_argument("--batch", type=int, default=1, help="decode batch per GPU")
     ap.add_argument("--n-vec", type=int, default=1, help="vectors per GEMV call (int4_gemv)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     a = ap.parse_args()
     if a.steps is None:
-        a.steps = 256 if a.workload == "decode" else 20000
+        a.steps = {"decode": 256, "gemm": 200}.get(a.workload, 20000)
     if a.warmup is None:
-        a.warmup = 5 if a.workload == "decode" else 200
+        a.warmup = {"decode": 5, "gemm": 10}.get(a.workload, 200)
     if a.warmup < 3:
         ap.error("--warmup must be >= 3")
     return a
@@ -787,6 +788,77 @@ def run_reference_decode(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+# ---- tensor-core GEMM (config 5's prefill projections) -----------------------------------
+def run_gemm(args, world, rank, local):
+    """C = A . B^T, bf16 in/out, fp32 accumulation, on tcgen05 (iron_gemm_bf16)."""
+    from iron_b200 import _lib
+
+    M, K, N = (int(v) for v in args.gemm_shape.split(","))
+    g = torch.Generator(device="cuda")
+    g.manual_seed(42 + rank)
+    A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    B = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    C = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    lib, stream = _lib.load(), torch.cuda.current_stream()
+    flags = 0 if args.no_pdl else _lib.IRON_FLAG_PDL
+    lib.iron_gemm_status(1)
+
+    def step(i):
+        st = lib.iron_gemm_bf16(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, K, K, N, None, 0, 0, 0,
+                                0.0, 0.0, 0, flags, stream.cuda_stream)
+        if st != 0:
+            raise RuntimeError(_lib.strerror(st))
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    ref = (A[:256].float() @ B.float().T).to(torch.bfloat16)
+    err = (C[:256].float() - ref.float()).abs().max().item()
+    if not err <= 1e-2 + 2e-2 * ref.float().abs().max().item():
+        raise RuntimeError(f"gemm self-check failed: {err}")
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    _barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if sampler:
+        sampler.mark("t0")
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    e1.synchronize()
+    if sampler:
+        sampler.mark("t1")
+    torch.cuda.synchronize()
+    _barrier(world)
+    if lib.iron_gemm_status(1) != 0:
+        raise RuntimeError("a GEMM hit its bounded-wait deadline")
+    ms = e0.elapsed_time(e1)
+    ms_max = _max_over_ranks(ms, world)
+    clocks = sampler.stop() if sampler else None
+    flops = 2 * M * N * K
+    tf = flops * args.steps / (ms * 1e-3) / 1e12
+    peak, src = _peak_tensor()
+    line = {"metric": "tcgen05 GEMM TFLOP/s", "value": round(flops * args.steps * world / (ms_max * 1e-3) / 1e12, 1),
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 (fp32 accumulate)", "data": "synthetic (seeded)",
+            "config": {"workload": f"gemm M={M} K={K} N={N} (prefill projection shape)",
+                       "l2": "operands L2-resident across steps (compute-bound)", "parallelism": f"dp{world}"},
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(tf / peak, 4), "traffic": None, "peak_source": src},
+            "gpu_launches": args.steps, "clocks": clocks, "e2e": None}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
 def main():
     args = _args()
     if args.impl == "reference":
@@ -800,6 +872,8 @@ def main():
     world, rank, local = _dist_init(args.gpus)
     if args.workload == "decode":
         run_decode(args, world, rank, local)
+    elif args.workload == "gemm":
+        run_gemm(args, world, rank, local)
     else:
         run_ours(args, world, rank, local)
 
