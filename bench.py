@@ -57,7 +57,8 @@ def _args():
                     help="timed steps (default: 256 decode steps, 20000 GEMVs)")
     ap.add_argument("--warmup", type=int, default=None, help="warm-up steps (default: 5 decode, 200 GEMV)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "int4_gemv", "bf16_gemv", "gemm"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "int4_gemv", "bf16_gemv", "gemm", "tp_block"],
+                    default="decode")
     ap.add_argument("--gemm-shape", default="2048,2048,8192", help="M,K,N of the gemm workload")
     ap.add_argument("--batch", type=int, default=1, help="decode batch per GPU")
     ap.add_argument("--n-vec", type=int, default=1, help="vectors per GEMV call (int4_gemv)")
@@ -65,9 +66,9 @@ def _args():
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     a = ap.parse_args()
     if a.steps is None:
-        a.steps = {"decode": 256, "gemm": 200}.get(a.workload, 20000)
+        a.steps = {"decode": 256, "gemm": 200, "tp_block": 2000}.get(a.workload, 20000)
     if a.warmup is None:
-        a.warmup = {"decode": 5, "gemm": 10}.get(a.workload, 200)
+        a.warmup = {"decode": 5, "gemm": 10, "tp_block": 20}.get(a.workload, 200)
     if a.warmup < 3:
         ap.error("--warmup must be >= 3")
     return a
@@ -859,6 +860,93 @@ def run_gemm(args, world, rank, local):
         dist.destroy_process_group()
 
 
+# ---- tensor-parallel Llama-3-8B block (config 5's TP leg) ----------------------------
+def run_tp_block(args, world, rank, local):
+    """One Llama-3-8B decoder block, decode step, tensor-parallel over the ranks
+    (NCCL all-reduce after o_proj and after down_proj); strong scaling: the same
+    block and batch at every N."""
+    import torch.distributed as dist
+
+    from iron_b200.applications.llama3_8b.sharding import BlockShape
+    from iron_b200.applications.llama3_8b.tp_block import TPDecoderBlock
+
+    shape, B = BlockShape(), args.batch
+    ctx = PREFIX
+    blk = TPDecoderBlock(shape, world, rank, B, ctx + 16, seed=13, pdl=not args.no_pdl)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7 + rank)
+    blk.kc[:, :, :ctx].normal_(generator=g)
+    blk.vc[:, :, :ctx].normal_(generator=g)
+    blk.x.normal_(generator=g)
+    blk.pos.fill_(ctx)
+    blk.capture()
+    stream = torch.cuda.current_stream()
+    ms, clocks = None, None
+    for i in range(args.warmup):
+        blk.step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    _barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if sampler:
+        sampler.mark("t0")
+    e0.record(stream)
+    for _ in range(args.steps):
+        blk.step()
+    e1.record(stream)
+    e1.synchronize()
+    if sampler:
+        sampler.mark("t1")
+    torch.cuda.synchronize()
+    _barrier(world)
+    ms = e0.elapsed_time(e1)
+    ms_max = _max_over_ranks(ms, world)
+    clocks = sampler.stop() if sampler else None
+    # the all-reduce alone, same message, same number per step
+    ar_us = None
+    if world > 1:
+        buf = torch.randn(B, shape.hidden, device="cuda").to(torch.bfloat16)
+        for _ in range(20):
+            dist.all_reduce(buf)
+        torch.cuda.synchronize()
+        _barrier(world)
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = 400
+        a0.record()
+        for _ in range(n):
+            dist.all_reduce(buf)
+        a1.record()
+        a1.synchronize()
+        ar_us = _max_over_ranks(a0.elapsed_time(a1) * 1e3 / n, world)
+    us = ms_max * 1e3 / args.steps
+    bytes_rank = blk.weight_bytes() + blk.kv_bytes([ctx] * B) + B * blk.hk * shape.head_dim * 2 * 2
+    peak, _ = _peak_hbm()
+    achieved = bytes_rank / (ms / args.steps * 1e-3) / 1e9
+    line = {"metric": "Llama-3-8B block decode step, tensor-parallel", "value": round(B * 1e6 / us, 1),
+            "unit": "tok/s through one block", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16 activations, int4 g32 weights, fp32 accumulate",
+            "data": "synthetic (random-init int4 weights, random KV cache; seeded)",
+            "config": {"workload": "tp_block (BASELINE config 5, Llama-3-8B block)", "batch": B,
+                       "context": ctx, "tp": world, "allreduce": "NCCL bf16 sum of [B, 4096], 2 per block",
+                       "parallelism": f"tp{world}"},
+            "us_per_block": round(us, 2), "allreduce_us": round(ar_us, 2) if ar_us is not None else None,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "scope": "one rank's block step (its weight shard + kv heads)",
+                         "algorithmic_bytes_per_step": int(bytes_rank)},
+            "gpu_launches": (8 + int(blk.ws.numel() > 16)) * args.steps, "clocks": clocks, "e2e": None}
+    blk.release()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = _args()
     if args.impl == "reference":
@@ -874,6 +962,8 @@ def main():
         run_decode(args, world, rank, local)
     elif args.workload == "gemm":
         run_gemm(args, world, rank, local)
+    elif args.workload == "tp_block":
+        run_tp_block(args, world, rank, local)
     else:
         run_ours(args, world, rank, local)
 

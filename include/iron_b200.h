@@ -201,11 +201,13 @@ int iron_transpose(const void *in, void *out, int M, int N, int batches, int ele
  *   q: bf16 [B, Hq, D]; caches: element (b, h, t, d) at b*kv_batch_stride +
  *   h*kv_head_stride + t*D + d; lens: int32 [B] valid tokens (device).
  *   out[b, hq] = softmax(scale * q K_{hq/(Hq/Hkv)}^T over t < lens[b]) V, fp32 softmax.
- *   D == 64; Hq % Hkv == 0, Hq/Hkv <= 16. Long caches are split over CTAs; then
- *   `workspace` (>= iron_attn_decode_workspace_bytes) holds the partials (no
- *   zeroing needed; calls sharing a workspace must not overlap on the GPU).
+ *   D == 64 (Llama-3.2-1B) or 128 (Llama-3-8B); Hq % Hkv == 0, Hq/Hkv <= 16. Long
+ *   caches are split over CTAs; then `workspace` (>= iron_attn_decode_workspace_bytes_d,
+ *   or iron_attn_decode_workspace_bytes for D == 64) holds the partials (no zeroing
+ *   needed; calls sharing a workspace must not overlap on the GPU).
  */
 size_t iron_attn_decode_workspace_bytes(int B, int Hq, int Hkv, int Lmax);
+size_t iron_attn_decode_workspace_bytes_d(int B, int Hq, int Hkv, int Lmax, int D);
 int iron_attn_decode(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
                      const int32_t *lens, uint16_t *out, int B, int Hq, int Hkv, int D, int Lmax,
                      int64_t kv_batch_stride, int64_t kv_head_stride, float scale,

@@ -47,6 +47,7 @@ SIGNATURES: dict[str, list] = {
     "iron_repeat_interleave": [P, P, c_int64, c_int64, c_int, c_uint, P],
     "iron_transpose": [P, P, c_int, c_int, c_int, c_int, c_uint, P],
     "iron_attn_decode_workspace_bytes": [c_int, c_int, c_int, c_int],
+    "iron_attn_decode_workspace_bytes_d": [c_int, c_int, c_int, c_int, c_int],
     "iron_attn_decode": [P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int64, c_int64,
                          c_float, P, c_size_t, c_uint, P],
     "iron_attn_decode_noalloc": [P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int64, c_int64,
@@ -62,7 +63,8 @@ SIGNATURES: dict[str, list] = {
     "iron_attn_prefill": [P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, c_float, c_int,
                           c_uint, P],
 }
-_RESTYPES = {"iron_strerror": c_char_p, "iron_attn_decode_workspace_bytes": c_size_t}
+_RESTYPES = {"iron_strerror": c_char_p, "iron_attn_decode_workspace_bytes": c_size_t,
+             "iron_attn_decode_workspace_bytes_d": c_size_t}
 
 _lock = threading.Lock()
 _lib = None

@@ -22,19 +22,20 @@
 
 namespace iron {
 
-constexpr int kAD = 64;       // head dim (IRON's MHA supports d = 64 only, mha/op.py:39-41)
+// Head dims: 64 (Llama-3.2-1B; IRON's MHA supports d = 64 only, mha/op.py:39-41) and
+// 128 (the Llama-3-8B block).
+constexpr int kAMaxD = 128;
 constexpr int kAWarps = 4;
 constexpr int kABlk = 16;     // tokens per warp step
-constexpr int kAVStride = 72; // padded V tile row (elements): 144 B, conflict-free ldmatrix
 constexpr int kAMinChunk = 256;
 
 struct AttnArgs {
-  const uint16_t *q;    // [B, Hq, 64]
-  const uint16_t *k;    // cache, element (b, h, t, d) at b*bstride + h*hstride + t*64 + d
+  const uint16_t *q;    // [B, Hq, D]
+  const uint16_t *k;    // cache, element (b, h, t, d) at b*bstride + h*hstride + t*D + d
   const uint16_t *v;
   const int *lens;      // [B] valid tokens per sequence
-  uint16_t *out;        // [B, Hq, 64]
-  float *ws;            // [B, Hq, splits, 2 + 64] partial (max, sum, o)
+  uint16_t *out;        // [B, Hq, D]
+  float *ws;            // [B, Hq, splits, 2 + D] partial (max, sum, o)
   int64_t bstride, hstride;
   int Hq, Hkv, splits, chunk;
   float scale_log2;     // softmax scale * log2(e)
@@ -51,11 +52,17 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void *smem
                : "r"(a));
 }
 
+template <int kAD>
 __global__ void __launch_bounds__(32 * kAWarps)
 attn_decode_kernel(AttnArgs a) {
-  __shared__ __align__(16) uint16_t vtile[kAWarps][kABlk * kAVStride];
+  constexpr int kAVStride = kAD + 8;  // padded V tile row: an odd number of 16-byte chunks
+  constexpr int kVBytes = kAWarps * kABlk * kAVStride * 2;
+  constexpr int kOBytes = kAWarps * 16 * kAD * 4;
+  // the V tiles (loop) and the warp-merge buffer (after it) share the storage
+  __shared__ __align__(16) uint8_t smem[kVBytes > kOBytes ? kVBytes : kOBytes];
   __shared__ float red_m[kAWarps][16], red_l[kAWarps][16];
-  __shared__ float red_o[kAWarps][16][kAD];
+  uint16_t (*vtile)[kABlk * kAVStride] = reinterpret_cast<uint16_t (*)[kABlk * kAVStride]>(smem);
+  float (*red_o)[16][kAD] = reinterpret_cast<float (*)[16][kAD]>(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tid = lane & 3;
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -72,9 +79,9 @@ attn_decode_kernel(AttnArgs a) {
 
   // Q fragments (rows = heads of the group; rows >= g are zero). k-step ks covers
   // physical d = 32*(ks/2) + 8*tid + 4*(ks%2) + {0,1 | 2,3} for logical {2tid | 2tid+8}.
-  uint32_t qa[4][4];
+  uint32_t qa[kAD / 16][4];
 #pragma unroll
-  for (int ks = 0; ks < 4; ++ks) {
+  for (int ks = 0; ks < kAD / 16; ++ks) {
     const int d = 32 * (ks >> 1) + 8 * tid + 4 * (ks & 1);
     const uint32_t *q0 = reinterpret_cast<const uint32_t *>(a.q + (static_cast<int64_t>(b) * a.Hq + hq0 + gid) * kAD + d);
     const uint32_t *q8 = reinterpret_cast<const uint32_t *>(a.q + (static_cast<int64_t>(b) * a.Hq + hq0 + gid + 8) * kAD + d);
@@ -84,43 +91,49 @@ attn_decode_kernel(AttnArgs a) {
     qa[ks][3] = gid + 8 < g ? q8[1] : 0u;
   }
 
-  float o[8][4];
+  float o[kAD / 8][4];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  for (int j = 0; j < kAD / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m_lo = -INFINITY, m_hi = -INFINITY;  // running max of rows gid / gid+8 (log2 units)
   float l_lo = 0.f, l_hi = 0.f;              // this lane's share of the running sums
   uint16_t *vs = vtile[warp];
 
   // register prefetch of one block: K rows (token gid of each 8-token half, 16 B x 2)
   // and this lane's four 16-byte pieces of the V tile
-  auto load_block = [&](int blk, uint4 (&kr)[2][2], uint4 (&vr)[4]) {
+  constexpr int kDB = kAD / 32;  // 16-byte K pieces per token per lane
+  constexpr int kVR = kAD / 16;  // 16-byte V pieces per lane per block
+  auto load_block = [&](int blk, uint4 (&kr)[2][kDB], uint4 (&vr)[kVR]) {
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
       const int t = blk + nt * 8 + gid;
 #pragma unroll
-      for (int db = 0; db < 2; ++db)
+      for (int db = 0; db < kDB; ++db)
         kr[nt][db] = t < t_end ? ldg16(kb + static_cast<int64_t>(t) * kAD + db * 32 + tid * 8)
                                : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int idx = i * 32 + lane, row = idx >> 3, c16 = idx & 7;
+    for (int i = 0; i < kVR; ++i) {
+      const int idx = i * 32 + lane, row = idx / (kAD / 8), c16 = idx % (kAD / 8);
       const int t = blk + row;
       vr[i] = t < t_end ? ldg16(vb + static_cast<int64_t>(t) * kAD + c16 * 8) : make_uint4(0u, 0u, 0u, 0u);
     }
   };
 
-  uint4 kr[2][2], vr[4];
+  uint4 kr[2][kDB], vr[kVR];
   int blk = t_begin + warp * kABlk;
   if (blk < t_end) load_block(blk, kr, vr);
   for (; blk < t_end; blk += kAWarps * kABlk) {
     // stage V, then prefetch the next block while this one computes
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int idx = i * 32 + lane, row = idx >> 3, c16 = idx & 7;
+    for (int i = 0; i < kVR; ++i) {
+      const int idx = i * 32 + lane, row = idx / (kAD / 8), c16 = idx % (kAD / 8);
       *reinterpret_cast<uint4 *>(vs + row * kAVStride + c16 * 8) = vr[i];
     }
-    uint4 kc[2][2] = {{kr[0][0], kr[0][1]}, {kr[1][0], kr[1][1]}};
+    uint4 kc[2][kDB];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int db = 0; db < kDB; ++db) kc[nt][db] = kr[nt][db];
     const int nxt = blk + kAWarps * kABlk;
     if (nxt < t_end) load_block(nxt, kr, vr);
 
@@ -130,7 +143,7 @@ attn_decode_kernel(AttnArgs a) {
     for (int nt = 0; nt < 2; ++nt) {
       s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
+      for (int ks = 0; ks < kAD / 16; ++ks) {
         const uint4 &w = kc[nt][ks >> 1];
         const uint32_t b0 = (ks & 1) ? w.z : w.x, b1 = (ks & 1) ? w.w : w.y;
         mma_bf16_16816(s[nt], qa[ks], b0, b1);
@@ -169,7 +182,7 @@ attn_decode_kernel(AttnArgs a) {
     l_lo = l_lo * al_lo + ps_lo;
     l_hi = l_hi * al_hi + ps_hi;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < kAD / 8; ++j) {
       o[j][0] *= al_lo; o[j][1] *= al_lo;
       o[j][2] *= al_hi; o[j][3] *= al_hi;
     }
@@ -178,7 +191,7 @@ attn_decode_kernel(AttnArgs a) {
                             pack_bf16x2(p[1][0], p[1][1]), pack_bf16x2(p[1][2], p[1][3])};
     __syncwarp();  // V tile stores visible to ldmatrix
 #pragma unroll
-    for (int jp = 0; jp < 4; ++jp) {
+    for (int jp = 0; jp < kAD / 16; ++jp) {
       const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
       const int col = jp * 16 + (lane >> 4) * 8;
       uint32_t vb4[4];
@@ -194,13 +207,14 @@ attn_decode_kernel(AttnArgs a) {
     l_lo += __shfl_xor_sync(0xffffffffu, l_lo, o_);
     l_hi += __shfl_xor_sync(0xffffffffu, l_hi, o_);
   }
-  // merge the four warps
+  // merge the four warps (red_o reuses the V tiles: every warp must be done with them)
+  __syncthreads();
   if (tid == 0) {
     red_m[warp][gid] = m_lo; red_m[warp][gid + 8] = m_hi;
     red_l[warp][gid] = l_lo; red_l[warp][gid + 8] = l_hi;
   }
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
+  for (int j = 0; j < kAD / 8; ++j) {
     red_o[warp][gid][8 * j + 2 * tid] = o[j][0];
     red_o[warp][gid][8 * j + 2 * tid + 1] = o[j][1];
     red_o[warp][gid + 8][8 * j + 2 * tid] = o[j][2];
@@ -237,6 +251,7 @@ attn_decode_kernel(AttnArgs a) {
 }
 
 // Merge the splits of each (sequence, q head): out = sum_s O_s 2^(m_s - M) / sum_s L_s 2^(m_s - M).
+template <int kAD>
 __global__ void attn_combine_kernel(const float *__restrict__ ws, uint16_t *__restrict__ out, int splits) {
   pdl_wait();
   const int64_t hq = blockIdx.x;
@@ -306,11 +321,19 @@ static float *attn_scratch_address(int *status) {
 
 using namespace iron;
 
-extern "C" size_t iron_attn_decode_workspace_bytes(int B, int Hq, int Hkv, int Lmax) {
+static size_t attn_ws_bytes(int B, int Hq, int Hkv, int Lmax, int D) {
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Lmax <= 0) return 0;
   const int s = attn_splits(B, Hkv, Lmax, sm_count());
   if (s == 1) return 0;
-  return static_cast<size_t>(B) * Hq * s * (2 + kAD) * sizeof(float);
+  return static_cast<size_t>(B) * Hq * s * (2 + D) * sizeof(float);
+}
+
+extern "C" size_t iron_attn_decode_workspace_bytes(int B, int Hq, int Hkv, int Lmax) {
+  return attn_ws_bytes(B, Hq, Hkv, Lmax, 64);
+}
+
+extern "C" size_t iron_attn_decode_workspace_bytes_d(int B, int Hq, int Hkv, int Lmax, int D) {
+  return (D == 64 || D == 128) ? attn_ws_bytes(B, Hq, Hkv, Lmax, D) : 0;
 }
 
 extern "C" int iron_attn_decode(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
@@ -320,7 +343,7 @@ extern "C" int iron_attn_decode(const uint16_t *q, const uint16_t *k_cache, cons
                                 unsigned flags, void *stream) {
   if (!q || !k_cache || !v_cache || !lens || !out) return IRON_ERR_NULL;
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Lmax <= 0 || B > 65535 || Hkv > 65535) return IRON_ERR_SHAPE;
-  if (D != kAD) return IRON_ERR_UNSUPPORTED;
+  if (D != 64 && D != 128) return IRON_ERR_UNSUPPORTED;
   if (Hq % Hkv || Hq / Hkv > 16) return IRON_ERR_SHAPE;
   if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || (kv_batch_stride % 8) ||
       (kv_head_stride % 8))
@@ -341,14 +364,17 @@ extern "C" int iron_attn_decode(const uint16_t *q, const uint16_t *k_cache, cons
   a.ws = static_cast<float *>(workspace);
   if (a.splits > 1) {
     if (!workspace) return IRON_ERR_NULL;
-    if (workspace_bytes < iron_attn_decode_workspace_bytes(B, Hq, Hkv, Lmax)) return IRON_ERR_WORKSPACE;
+    if (workspace_bytes < attn_ws_bytes(B, Hq, Hkv, Lmax, D)) return IRON_ERR_WORKSPACE;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool pdl = (flags & IRON_FLAG_PDL) != 0;
-  int st = launch(attn_decode_kernel, dim3(a.splits, Hkv, B), dim3(32 * kAWarps), 0, s, pdl, a);
+  int st = D == 64 ? launch(attn_decode_kernel<64>, dim3(a.splits, Hkv, B), dim3(32 * kAWarps), 0, s, pdl, a)
+                   : launch(attn_decode_kernel<128>, dim3(a.splits, Hkv, B), dim3(32 * kAWarps), 0, s, pdl, a);
   if (st != IRON_OK || a.splits == 1) return st;
-  return launch(attn_combine_kernel, dim3(B * Hq), dim3(kAD), 0, s, pdl,
-                static_cast<const float *>(a.ws), out, a.splits);
+  return D == 64 ? launch(attn_combine_kernel<64>, dim3(B * Hq), dim3(64), 0, s, pdl,
+                          static_cast<const float *>(a.ws), out, a.splits)
+                 : launch(attn_combine_kernel<128>, dim3(B * Hq), dim3(128), 0, s, pdl,
+                          static_cast<const float *>(a.ws), out, a.splits);
 }
 
 // Same computation as iron_attn_decode, for callers that cannot allocate the
@@ -359,7 +385,8 @@ extern "C" int iron_attn_decode_noalloc(const uint16_t *q, const uint16_t *k_cac
                                         int64_t kv_batch_stride, int64_t kv_head_stride, float scale,
                                         unsigned flags, void *stream) {
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Lmax <= 0) return IRON_ERR_SHAPE;
-  const size_t need = iron_attn_decode_workspace_bytes(B, Hq, Hkv, Lmax);
+  if (D != 64 && D != 128) return IRON_ERR_UNSUPPORTED;
+  const size_t need = attn_ws_bytes(B, Hq, Hkv, Lmax, D);
   if (need > kAttnScratchBytes) return IRON_ERR_WORKSPACE;  // beyond the fixed array
   void *ws = nullptr;
   if (need > 0) {

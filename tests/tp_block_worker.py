@@ -1,0 +1,65 @@
+"""torchrun worker of tests/test_tp_block_gpu.py: the tensor-parallel block on
+WORLD_SIZE GPUs against the single-GPU block on the same weights and inputs."""
+
+import datetime
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), ".."))
+
+from iron_b200.applications.llama3_8b.sharding import BlockShape  # noqa: E402
+from iron_b200.applications.llama3_8b.tp_block import TPDecoderBlock  # noqa: E402
+
+
+def _close(a, b, rtol=2e-2, atol=2e-2):
+    a, b = a.float(), b.float()
+    bad = ~((a - b).abs() <= torch.maximum(torch.full_like(a, atol), rtol * (a.abs() + b.abs())))
+    return int(bad.sum())
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", int(os.environ["LOCAL_RANK"])))
+    shape, B, L = BlockShape(), 2, 64
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x0 = torch.randn(B, shape.hidden, device="cuda", generator=g).to(torch.bfloat16)
+    kc = torch.randn(B, shape.n_kv, L, shape.head_dim, device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn(B, shape.n_kv, L, shape.head_dim, device="cuda", generator=g).to(torch.bfloat16)
+    pos = torch.tensor([5, 40], dtype=torch.int32, device="cuda")
+
+    def run(tp, r, group, graph):
+        blk = TPDecoderBlock(shape, tp, r, B, L, seed=13, group=group)
+        blk.kc.copy_(kc[:, blk.sh.k0:blk.sh.k1])
+        blk.vc.copy_(vc[:, blk.sh.k0:blk.sh.k1])
+        blk.x.copy_(x0)
+        blk.pos.copy_(pos)
+        if graph:
+            blk.capture()
+        blk.step()
+        torch.cuda.synchronize()
+        out = blk.x.clone()
+        kcs = blk.kc.clone()
+        blk.release()
+        return out, kcs, blk.sh
+
+    failures = 0
+    for graph in (False, True):
+        out_tp, kc_tp, sh = run(world, rank, None, graph)
+        out_1, kc_1, _ = run(1, 0, None, False)
+        failures += _close(out_tp, out_1)
+        failures += _close(kc_tp, kc_1[:, sh.k0:sh.k1])
+    other = torch.tensor([failures], device="cuda")
+    dist.all_reduce(other)
+    dist.destroy_process_group()
+    if rank == 0:
+        print(f"tp={world}: {int(other)} mismatching elements")
+    sys.exit(0 if int(other) == 0 else 1)
+
+
+if __name__ == "__main__":
+    main()
