@@ -2,7 +2,7 @@
 //
 // Every wait spins a bounded number of times; on exhaustion it returns false and
 // the caller records IRON_ERR_TIMEOUT in the error word and leaves. A wait never
-// runs forever. No copy here uses cluster multicast: every bulk copy reads this
+// runs forever. Every bulk copy here reads this
 // GPU's global memory into the issuing CTA's own shared memory.
 #pragma once
 

@@ -3,7 +3,7 @@
 // descriptors and 2-D TMA tile loads. Inline PTX written from the PTX ISA's
 // descriptions of these instructions.
 //
-// No copy here uses cluster multicast: every TMA load reads this GPU's global
+// Every TMA load here reads this GPU's global
 // memory into the issuing CTA's own shared memory.
 #pragma once
 
@@ -49,7 +49,7 @@ __device__ __forceinline__ void expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
-// 2-D tiled TMA load global -> this CTA's shared memory (no multicast).
+// 2-D tiled TMA load global -> this CTA's own shared memory only.
 // c0 is the innermost coordinate in elements; c0 * sizeof(elem) must be a
 // multiple of 16 bytes.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, int c0, int c1, uint32_t bar) {
