@@ -60,11 +60,15 @@ SIGNATURES: dict[str, list] = {
                        c_float, c_float, c_int, c_uint, P],
     "iron_gemm_status": [c_int],
     "iron_unpack_int4g32": [P, P, c_int, c_int, P],
+    "iron_llama_decode_persistent_scratch_bytes": [c_int, c_int],
+    "iron_llama_decode_persistent": [P, c_int, P, P, P, c_int, P, P, P, P, P, P, P, P, P, c_int, c_int, c_int64,
+                                     c_int64, c_float, P, c_size_t, P, c_uint, P],
     "iron_attn_prefill": [P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, c_float, c_int,
                           c_uint, P],
 }
 _RESTYPES = {"iron_strerror": c_char_p, "iron_attn_decode_workspace_bytes": c_size_t,
-             "iron_attn_decode_workspace_bytes_d": c_size_t}
+             "iron_attn_decode_workspace_bytes_d": c_size_t,
+             "iron_llama_decode_persistent_scratch_bytes": c_size_t}
 
 _lock = threading.Lock()
 _lib = None

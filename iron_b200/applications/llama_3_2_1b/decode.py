@@ -97,7 +97,7 @@ class LlamaDecodeEngine:
     """Batched greedy decode of a random-init int4 Llama-3.2-1B-shape model."""
 
     def __init__(self, shape: LlamaShape, batch: int, max_seq: int, seed: int = 0,
-                 keep_natural: bool = False, pdl: bool = True):
+                 keep_natural: bool = False, pdl: bool = True, persistent: bool | None = None):
         self.s, self.B, self.L = shape, batch, max_seq
         self.dev = torch.device("cuda", torch.cuda.current_device())
         self.flags = _lib.IRON_FLAG_PDL if pdl else 0
@@ -141,6 +141,22 @@ class LlamaDecodeEngine:
         wsb = _lib.load().iron_attn_decode_workspace_bytes(B, s.n_heads, s.n_kv_groups, max_seq)
         self.attn_ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
         self.graph = None
+        # The persistent single-kernel step (iron_llama_decode_persistent) serves the
+        # Llama-3.2-1B layer shape at B <= 8; it is opt-in: measured on B200 it is slower
+        # than the PDL-chained graph (1.26 vs 0.63 ms per batch-1 step).
+        fits = (B <= 8 and (s.emb_dim, s.n_heads, s.n_kv_groups, s.head_dim, s.hidden_dim)
+                == (2048, 32, 8, 64, 8192))
+        self.persistent = bool(persistent)
+        if self.persistent:
+            if not fits:
+                raise ValueError("the persistent decode step needs the Llama-3.2-1B layer shape and batch <= 8")
+            ptrs = [[lay[k].packed.data_ptr() for k in ("qkv", "o", "gu", "d")]
+                    + [lay["n1"].data_ptr(), lay["n2"].data_ptr(), self.kc[i].data_ptr(), self.vc[i].data_ptr()]
+                    for i, lay in enumerate(self.layers)]
+            self._mk_layers = torch.tensor(ptrs, dtype=torch.int64, device=dev)
+            nb = _lib.load().iron_llama_decode_persistent_scratch_bytes(B, max_seq)
+            self._mk_scratch = torch.zeros(nb, dtype=torch.uint8, device=dev)
+            self._mk_status = torch.zeros(4, dtype=torch.int32, device=dev)
 
     # -- bytes moved per step (the roofline numerator) ---------------------------------
     def weight_bytes(self) -> int:
@@ -153,6 +169,30 @@ class LlamaDecodeEngine:
 
     # -- one decode step ----------------------------------------------------------------
     def _launch_step(self, stream: int):
+        if self.persistent:
+            self._launch_step_persistent(stream)
+        else:
+            self._launch_step_graph_kernels(stream)
+
+    def _launch_step_persistent(self, stream: int):
+        s, B, p = self.s, self.B, (lambda t: t.data_ptr())
+        L, Hd = self.L, s.head_dim
+        _lib.call("iron_llama_decode_persistent", p(self._mk_layers), s.n_layers, p(self.embed_table), p(self.nf),
+                  p(self.lm.packed), s.vocab_size, p(self.lut), p(self.tokens), p(self.pos), p(self.x), p(self.h),
+                  p(self.qkv), p(self.attn), p(self.act), p(self.logits), B, L, s.n_kv_groups * L * Hd, L * Hd,
+                  s.eps, p(self._mk_scratch), self._mk_scratch.numel(), p(self._mk_status), self.flags, stream)
+
+    def check_status(self):
+        """Raise if a persistent step's grid barrier gave up (then re-arm its scratch)."""
+        if self.persistent:
+            st = int(self._mk_status[0])
+            if st:
+                self._mk_scratch.zero_()
+                self._mk_status.zero_()
+                what = "a grid barrier wait timed out" if st & 1 else "a position or token is out of range"
+                raise RuntimeError(f"persistent decode step: {what}")
+
+    def _launch_step_graph_kernels(self, stream: int):
         s, B, f = self.s, self.B, self.flags
         call, p = _lib.call, lambda t: t.data_ptr()
         E, Hd = s.emb_dim, s.head_dim
@@ -263,6 +303,8 @@ class LlamaDecodeEngine:
         return s.n_layers * (gemm + attn)
 
     def kernels_per_step(self) -> int:
+        if self.persistent:
+            return 1
         B, s = self.B, self.s
         splits = 1 if self.attn_ws.numel() <= 16 else 2  # combine pass when partials are used
         return 1 + s.n_layers * (8 + (1 if splits > 1 else 0)) + 3

@@ -21,6 +21,7 @@
 #include <cooperative_groups.h>
 
 #include "common.cuh"
+#include "s4.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -36,27 +37,6 @@ struct S4Range {
 __device__ __forceinline__ S4Range s4_split(int b, int e, int parts, int i) {
   const int n = e - b;
   return {b + i * n / parts, b + (i + 1) * n / parts};
-}
-
-__device__ __forceinline__ uint32_t lop3_and_xor_(uint32_t a, uint32_t b, uint32_t c) {
-  uint32_t d;
-  asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
-__device__ __forceinline__ uint32_t prmt_(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t d;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
-  return d;
-}
-// Signed int4 pair -> the exactly dequantized bf16x2 (IRON's Dequant then GEMV).
-// `w` holds the wanted nibble at bits 0-3 and 16-19. OR-ing (nib ^ 8) into the
-// mantissa of bf16 128.0 gives 136 + q exactly (q in [-8, 7]); subtracting 136 is
-// exact; the scale multiply rounds the exact product once: bf16(q * s).
-__device__ __forceinline__ uint32_t s4x2_dequant_(uint32_t w, uint32_t scale2) {
-  uint32_t biased = lop3_and_xor_(w, 0x000f000fu, 0x43084308u), q, r;
-  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(biased), "r"(0x43084308u));
-  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(q), "r"(scale2));
-  return r;
 }
 
 // Store a finished 16-row tile (C-fragment layout v). swiglu == 0: rows as they
