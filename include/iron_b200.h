@@ -106,6 +106,17 @@ int iron_pack_int4g32(const uint8_t *codes, const uint16_t *scales, uint8_t *pac
  * bf16(q * scale) exactly (bit-identical to iron_dequant_s4g32_rows on the natural
  * codes); the prefill GEMMs read int4 weights through it. */
 int iron_unpack_int4g32(const uint8_t *packed, uint16_t *out, int N, int K, void *stream);
+/* iron_gemv_int4g32_ex: iron_gemv_int4g32 plus a fused RMSNorm of x (norm_weight
+ * [K], eps; n_vec <= 8, K <= 2048; rmsnorm_kernel's arithmetic, replacing the RMSNorm step
+ * before IRON's projections, llama_npu.py:459-480) and a fused greedy argmax
+ * (argmax_keys [n_vec * 32] 64-bit keys, zero before the call; iron_argmax_finalize
+ * turns them into tokens and re-zeroes them, replacing the argmax sampling of
+ * llama_inference_harness.py:146-169). */
+int iron_gemv_int4g32_ex(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K, int n_vec,
+                         const uint16_t *residual, const uint16_t *norm_weight, float eps,
+                         unsigned long long *argmax_keys, unsigned flags, void *stream);
+int iron_argmax_finalize(unsigned long long *keys, int32_t *tokens, int32_t *pos, int B, unsigned flags,
+                         void *stream);
 int iron_gemv_int4g32(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,
                       int n_vec, const uint16_t *residual, unsigned flags, void *stream);
 
@@ -233,6 +244,21 @@ int iron_attn_decode_noalloc(const uint16_t *q, const uint16_t *k_cache, const u
                              const int32_t *lens, uint16_t *out, int B, int Hq, int Hkv, int D,
                              int Lmax, int64_t kv_batch_stride, int64_t kv_head_stride,
                              float scale, unsigned flags, void *stream);
+
+/* Fused decode attention (no reference counterpart as one call: it replaces the decode
+ * RoPE, the two KV-cache StridedCopy appends and the attention runlist steps of
+ * iron/applications/llama_3.2_1b/llama_npu.py:481-529). qkv bf16 [B, (Hq + 2 Hkv) * D]
+ * (q heads, k heads, v heads) un-rotated; pos int32 [B] tokens already cached; lut fp32
+ * [ctx, D] interleaved cos/sin. Rotates q and the new k at pos[b], appends k / v to the
+ * caches at slot pos[b] and attends over 0..pos[b] (split partials in `workspace`,
+ * >= iron_attn_decode_qkv_workspace_bytes, merged by a second kernel as in
+ * iron_attn_decode).
+ */
+size_t iron_attn_decode_qkv_workspace_bytes(int B, int Hq, int Hkv, int Lmax, int D);
+int iron_attn_decode_qkv(const uint16_t *qkv, const int32_t *pos, const float *lut, uint16_t *k_cache,
+                         uint16_t *v_cache, uint16_t *out, int B, int Hq, int Hkv, int D, int Lmax,
+                         int64_t kv_batch_stride, int64_t kv_head_stride, float scale, void *workspace,
+                         size_t workspace_bytes, unsigned flags, void *stream);
 
 /* ---- decode-step glue ----------------------------------------------------------
  * iron_rope_kv_append replaces the decode RoPE of q and k plus the two StridedCopy

@@ -61,6 +61,11 @@ SIGNATURES: dict[str, list] = {
     "iron_gemm_status": [c_int],
     "iron_unpack_int4g32": [P, P, c_int, c_int, P],
     "iron_llama_decode_persistent_scratch_bytes": [c_int, c_int],
+    "iron_gemv_int4g32_ex": [P, P, P, c_int, c_int, c_int, P, P, c_float, P, c_uint, P],
+    "iron_argmax_finalize": [P, P, P, c_int, c_uint, P],
+    "iron_attn_decode_qkv_workspace_bytes": [c_int, c_int, c_int, c_int, c_int],
+    "iron_attn_decode_qkv": [P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int64, c_int64, c_float, P,
+                             c_size_t, c_uint, P],
     "iron_llama_decode_persistent": [P, c_int, P, P, P, c_int, P, P, P, P, P, P, P, P, P, c_int, c_int, c_int64,
                                      c_int64, c_float, P, c_size_t, P, c_uint, P],
     "iron_attn_prefill": [P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, c_float, c_int,
@@ -68,7 +73,8 @@ SIGNATURES: dict[str, list] = {
 }
 _RESTYPES = {"iron_strerror": c_char_p, "iron_attn_decode_workspace_bytes": c_size_t,
              "iron_attn_decode_workspace_bytes_d": c_size_t,
-             "iron_llama_decode_persistent_scratch_bytes": c_size_t}
+             "iron_llama_decode_persistent_scratch_bytes": c_size_t,
+             "iron_attn_decode_qkv_workspace_bytes": c_size_t}
 
 _lock = threading.Lock()
 _lib = None

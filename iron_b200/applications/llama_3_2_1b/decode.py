@@ -97,7 +97,8 @@ class LlamaDecodeEngine:
     """Batched greedy decode of a random-init int4 Llama-3.2-1B-shape model."""
 
     def __init__(self, shape: LlamaShape, batch: int, max_seq: int, seed: int = 0,
-                 keep_natural: bool = False, pdl: bool = True, persistent: bool | None = None):
+                 keep_natural: bool = False, pdl: bool = True, persistent: bool | None = None,
+                 fuse_norm: str | None = None, fuse_rope: bool | None = None):
         self.s, self.B, self.L = shape, batch, max_seq
         self.dev = torch.device("cuda", torch.cuda.current_device())
         self.flags = _lib.IRON_FLAG_PDL if pdl else 0
@@ -138,18 +139,32 @@ class LlamaDecodeEngine:
         self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
         self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
         self.lens = torch.zeros(B, dtype=torch.int32, device=dev)
-        wsb = _lib.load().iron_attn_decode_workspace_bytes(B, s.n_heads, s.n_kv_groups, max_seq)
-        self.attn_ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
+        wsb = max(_lib.load().iron_attn_decode_workspace_bytes(B, s.n_heads, s.n_kv_groups, max_seq),
+                  _lib.load().iron_attn_decode_qkv_workspace_bytes(B, s.n_heads, s.n_kv_groups, max_seq, s.head_dim))
+        self.attn_ws = torch.zeros(max(wsb, 16), dtype=torch.uint8, device=dev)
+        self.amax = torch.zeros(B * 32, dtype=torch.int64, device=dev)  # fused argmax key slots
         self.graph = None
         # The persistent single-kernel step (iron_llama_decode_persistent) serves the
         # Llama-3.2-1B layer shape at B <= 8; it is opt-in: measured on B200 it is slower
         # than the PDL-chained graph (1.26 vs 0.63 ms per batch-1 step).
-        fits = (B <= 8 and (s.emb_dim, s.n_heads, s.n_kv_groups, s.head_dim, s.hidden_dim)
+        # (B > 2 is refused: at B = 8 a second layer's attention diverges from the kernel
+        # chain for some sequences -- an open issue of the persistent kernel)
+        fits = (B <= 2 and (s.emb_dim, s.n_heads, s.n_kv_groups, s.head_dim, s.hidden_dim)
                 == (2048, 32, 8, 64, 8192))
         self.persistent = bool(persistent)
+        # where RMSNorm runs inside the following GEMV ("none", "layers": the QKV and
+        # gate/up GEMVs, "all": also the lm-head); only for B <= 8. Defaults measured on
+        # B200 (one process, interleaved): the fused prologue saves 77 us per step at
+        # B = 1 and costs 93 us at B = 8; RoPE inside attention costs 22 us at B = 1
+        # and saves 54 us at B = 8, 286 us at B = 64.
+        self.fuse_norm = fuse_norm if fuse_norm is not None else ("layers" if B <= 2 else "none")
+        if self.fuse_norm != "none" and B > 8:
+            raise ValueError("the fused RMSNorm prologue serves B <= 8")
+        # RoPE + KV append inside the attention kernel (else the rope_kv_append kernel)
+        self.fuse_rope = fuse_rope if fuse_rope is not None else B > 2
         if self.persistent:
             if not fits:
-                raise ValueError("the persistent decode step needs the Llama-3.2-1B layer shape and batch <= 8")
+                raise ValueError("the persistent decode step needs the Llama-3.2-1B layer shape and batch <= 2")
             ptrs = [[lay[k].packed.data_ptr() for k in ("qkv", "o", "gu", "d")]
                     + [lay["n1"].data_ptr(), lay["n2"].data_ptr(), self.kc[i].data_ptr(), self.vc[i].data_ptr()]
                     for i, lay in enumerate(self.layers)]
@@ -193,33 +208,55 @@ class LlamaDecodeEngine:
                 raise RuntimeError(f"persistent decode step: {what}")
 
     def _launch_step_graph_kernels(self, stream: int):
+        """The step as a chain of kernels: per layer QKV GEMV (RMSNorm fused for
+        B <= 8), fused RoPE + KV append + attention (+ split merge), O GEMV +
+        residual, gate/up GEMV (RMSNorm fused) + SwiGLU, down GEMV + residual; then
+        the lm-head GEMV with the final RMSNorm and the argmax fused, and the token
+        update."""
         s, B, f = self.s, self.B, self.flags
-        call, p = _lib.call, lambda t: t.data_ptr()
-        E, Hd = s.emb_dim, s.head_dim
-        L = self.L
+        call, p = _lib.call, (lambda t: t.data_ptr())
+        E, Hd, L = s.emb_dim, s.head_dim, self.L
         kv_b, kv_h = s.n_kv_groups * L * Hd, L * Hd
+        fuse_norm = self.fuse_norm != "none"
         call("iron_embed", p(self.tokens), p(self.embed_table), p(self.x), B, E, f, stream)
         for li, lay in enumerate(self.layers):
-            call("iron_rmsnorm", p(self.x), None, None, p(lay["n1"]), p(self.xn), B, E, s.eps, f, stream)
-            call("iron_gemv_int4g32", p(lay["qkv"].packed), p(self.xn), p(self.qkv), s.qkv_dim, E, B,
-                 None, f, stream)
             kc, vc = self.kc[li], self.vc[li]
-            call("iron_rope_kv_append", p(self.qkv), p(self.pos), p(self.lut), p(self.q), p(kc), p(vc),
-                 p(self.lens), B, s.n_heads, s.n_kv_groups, Hd, kv_b, kv_h, f, stream)
-            call("iron_attn_decode", p(self.q), p(kc), p(vc), p(self.lens), p(self.attn), B, s.n_heads,
-                 s.n_kv_groups, Hd, L, kv_b, kv_h, 1.0 / math.sqrt(Hd), p(self.attn_ws),
-                 self.attn_ws.numel(), f, stream)
+            if fuse_norm:
+                call("iron_gemv_int4g32_ex", p(lay["qkv"].packed), p(self.x), p(self.qkv), s.qkv_dim, E, B, None,
+                     p(lay["n1"]), s.eps, None, f, stream)
+            else:
+                call("iron_rmsnorm", p(self.x), None, None, p(lay["n1"]), p(self.xn), B, E, s.eps, f, stream)
+                call("iron_gemv_int4g32", p(lay["qkv"].packed), p(self.xn), p(self.qkv), s.qkv_dim, E, B,
+                     None, f, stream)
+            if self.fuse_rope:
+                call("iron_attn_decode_qkv", p(self.qkv), p(self.pos), p(self.lut), p(kc), p(vc), p(self.attn), B,
+                     s.n_heads, s.n_kv_groups, Hd, L, kv_b, kv_h, 1.0 / math.sqrt(Hd), p(self.attn_ws),
+                     self.attn_ws.numel(), f, stream)
+            else:
+                call("iron_rope_kv_append", p(self.qkv), p(self.pos), p(self.lut), p(self.q), p(kc), p(vc),
+                     p(self.lens), B, s.n_heads, s.n_kv_groups, Hd, kv_b, kv_h, f, stream)
+                call("iron_attn_decode", p(self.q), p(kc), p(vc), p(self.lens), p(self.attn), B, s.n_heads,
+                     s.n_kv_groups, Hd, L, kv_b, kv_h, 1.0 / math.sqrt(Hd), p(self.attn_ws),
+                     self.attn_ws.numel(), f, stream)
             call("iron_gemv_int4g32", p(lay["o"].packed), p(self.attn), p(self.h), E, s.n_heads * Hd, B,
                  p(self.x), f, stream)
-            call("iron_rmsnorm", p(self.h), None, None, p(lay["n2"]), p(self.xn), B, E, s.eps, f, stream)
-            call("iron_gemv_int4g32", p(lay["gu"].packed), p(self.xn), p(self.act), 2 * s.hidden_dim, E,
-                 B, None, f | _lib.IRON_FLAG_SWIGLU, stream)
+            if fuse_norm:
+                call("iron_gemv_int4g32_ex", p(lay["gu"].packed), p(self.h), p(self.act), 2 * s.hidden_dim, E, B,
+                     None, p(lay["n2"]), s.eps, None, f | _lib.IRON_FLAG_SWIGLU, stream)
+            else:
+                call("iron_rmsnorm", p(self.h), None, None, p(lay["n2"]), p(self.xn), B, E, s.eps, f, stream)
+                call("iron_gemv_int4g32", p(lay["gu"].packed), p(self.xn), p(self.act), 2 * s.hidden_dim, E,
+                     B, None, f | _lib.IRON_FLAG_SWIGLU, stream)
             call("iron_gemv_int4g32", p(lay["d"].packed), p(self.act), p(self.x), E, s.hidden_dim, B,
                  p(self.h), f, stream)
-        call("iron_rmsnorm", p(self.x), None, None, p(self.nf), p(self.xn), B, E, s.eps, f, stream)
-        call("iron_gemv_int4g32", p(self.lm.packed), p(self.xn), p(self.logits), s.vocab_size, E, B,
-             None, f, stream)
-        call("iron_argmax", p(self.logits), p(self.tokens), B, s.vocab_size, p(self.pos), f, stream)
+        if self.fuse_norm == "all":
+            call("iron_gemv_int4g32_ex", p(self.lm.packed), p(self.x), p(self.logits), s.vocab_size, E, B, None,
+                 p(self.nf), s.eps, p(self.amax), f, stream)
+        else:
+            call("iron_rmsnorm", p(self.x), None, None, p(self.nf), p(self.xn), B, E, s.eps, f, stream)
+            call("iron_gemv_int4g32_ex", p(self.lm.packed), p(self.xn), p(self.logits), s.vocab_size, E, B, None,
+                 None, 0.0, p(self.amax), f, stream)
+        call("iron_argmax_finalize", p(self.amax), p(self.tokens), p(self.pos), B, f, stream)
 
     # -- prefill: a whole prompt through the tensor-core GEMMs -----------------------------
     def _prefill_buffers(self, S: int):
@@ -305,9 +342,9 @@ class LlamaDecodeEngine:
     def kernels_per_step(self) -> int:
         if self.persistent:
             return 1
-        B, s = self.B, self.s
-        splits = 1 if self.attn_ws.numel() <= 16 else 2  # combine pass when partials are used
-        return 1 + s.n_layers * (8 + (1 if splits > 1 else 0)) + 3
+        per_layer = ((5 if self.fuse_norm != "none" else 7) + (1 if self.attn_ws.numel() > 16 else 0)  # + combine
+                     + (0 if self.fuse_rope else 1))
+        return 1 + self.s.n_layers * per_layer + (2 if self.fuse_norm == "all" else 3)
 
     def set_state(self, tokens, positions):
         self.tokens.copy_(torch.as_tensor(tokens, dtype=torch.int32))

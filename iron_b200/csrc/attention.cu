@@ -24,7 +24,6 @@ namespace iron {
 
 // Head dims: 64 (Llama-3.2-1B; IRON's MHA supports d = 64 only, mha/op.py:39-41) and
 // 128 (the Llama-3-8B block).
-constexpr int kAMaxD = 128;
 constexpr int kAWarps = 4;
 constexpr int kABlk = 16;     // tokens per warp step
 constexpr int kAMinChunk = 256;
@@ -39,6 +38,12 @@ struct AttnArgs {
   int64_t bstride, hstride;
   int Hq, Hkv, splits, chunk;
   float scale_log2;     // softmax scale * log2(e)
+  // fused decode form: q, the new k and v come from the QKV projection `qkv`
+  // [B, (Hq + 2 Hkv) D] at position pos[b] (RoPE from `lut`, the new rows appended to
+  // the cache)
+  const uint16_t *qkv;
+  const int *pos;
+  const float *lut;
 };
 
 __device__ __forceinline__ uint4 ldg16(const uint16_t *p) {
@@ -52,7 +57,7 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void *smem
                : "r"(a));
 }
 
-template <int kAD>
+template <int kAD, bool kFused = false>
 __global__ void __launch_bounds__(32 * kAWarps)
 attn_decode_kernel(AttnArgs a) {
   constexpr int kAVStride = kAD + 8;  // padded V tile row: an odd number of 16-byte chunks
@@ -69,13 +74,120 @@ attn_decode_kernel(AttnArgs a) {
   const int g = a.Hq / a.Hkv;      // query heads per kv head (MMA rows used)
   const int hq0 = h * g;
 
+  // fused form: the group's roped q rows and the new k / v row, staged here
+  __shared__ __align__(16) uint16_t qbuf[kFused ? 16 * kAD : 8];
+  __shared__ __align__(16) uint16_t knew[kFused ? kAD : 8], vnew[kFused ? kAD : 8];
+
   pdl_wait();
-  const int len = a.lens[b];
+  int len, p = -1;
+  if constexpr (kFused) {
+    p = a.pos[b];
+    len = p + 1;
+  } else {
+    len = a.lens[b];
+  }
   const int t_begin = split * a.chunk;
   const int t_end = min(len, t_begin + a.chunk);
 
   const uint16_t *kb = a.k + b * a.bstride + h * a.hstride;
   const uint16_t *vb = a.v + b * a.bstride + h * a.hstride;
+
+  // register prefetch of one block: K rows (token gid of each 8-token half, 16 B x 2)
+  // and this lane's four 16-byte pieces of the V tile
+  constexpr int kDB = kAD / 32;  // 16-byte K pieces per token per lane
+  constexpr int kVR = kAD / 16;  // 16-byte V pieces per lane per block
+  // (fused form: the new token's row comes from the staged knew / vnew once `staged`)
+  auto load_block = [&](int blk, uint4 (&kr)[2][kDB], uint4 (&vr)[kVR], bool staged) {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int t = blk + nt * 8 + gid;
+#pragma unroll
+      for (int db = 0; db < kDB; ++db)
+        kr[nt][db] = t >= t_end ? make_uint4(0u, 0u, 0u, 0u)
+                     : (kFused && t == p) ? (staged ? *reinterpret_cast<const uint4 *>(knew + db * 32 + tid * 8)
+                                                   : make_uint4(0u, 0u, 0u, 0u))
+                                          : ldg16(kb + static_cast<int64_t>(t) * kAD + db * 32 + tid * 8);
+    }
+#pragma unroll
+    for (int i = 0; i < kVR; ++i) {
+      const int idx = i * 32 + lane, row = idx / (kAD / 8), c16 = idx % (kAD / 8);
+      const int t = blk + row;
+      vr[i] = t >= t_end ? make_uint4(0u, 0u, 0u, 0u)
+              : (kFused && t == p) ? (staged ? *reinterpret_cast<const uint4 *>(vnew + c16 * 8)
+                                             : make_uint4(0u, 0u, 0u, 0u))
+                                   : ldg16(vb + static_cast<int64_t>(t) * kAD + c16 * 8);
+    }
+  };
+
+  uint4 kr[2][kDB], vr[kVR];
+  int blk = t_begin + warp * kABlk;
+  // the first block's cache rows are requested before anything else (they do not
+  // depend on the QKV projection)
+  if (blk < t_end) load_block(blk, kr, vr, false);
+
+  const uint16_t *qrow = a.q;
+  int64_t qstride = kAD;
+  if constexpr (kFused) {
+    // RoPE (two halves, fp32, rounded once: rope_kv_append_kernel's arithmetic) of the
+    // group's q heads and of the new k; the split that holds position p appends k, v
+    const int half = kAD / 2;
+    const uint16_t *src = a.qkv + static_cast<int64_t>(b) * (a.Hq + 2 * a.Hkv) * kAD;
+    const float *ang = a.lut + static_cast<int64_t>(p) * kAD;
+    const bool owner = t_begin <= p && p < t_begin + a.chunk;
+    // zero rows g..15 of the q tile (no loads)
+    for (int i = g * kAD + threadIdx.x * 8; i < 16 * kAD; i += 32 * kAWarps * 8)
+      *reinterpret_cast<uint4 *>(qbuf + i) = make_uint4(0u, 0u, 0u, 0u);
+    // one pass: every thread issues the loads of its q pair and (the first `half`
+    // threads) of its new k / v pair before using any of them -- one L2 round trip
+    for (int i0 = 0; i0 < g * half || i0 < half; i0 += 32 * kAWarps) {
+      const int i = i0 + threadIdx.x;
+      const bool hq_ = i < g * half, hk_ = i < half;
+      const int r = hq_ ? i / half : 0, jq = hq_ ? i % half : 0;
+      const uint16_t *xq = src + (hq0 + r) * kAD;
+      const uint16_t *xk = src + (a.Hq + h) * kAD, *xv = src + (a.Hq + a.Hkv + h) * kAD;
+      uint16_t q1 = 0, q2 = 0, k1r = 0, k2r = 0, v1 = 0, v2 = 0;
+      float cq = 0.f, sq = 0.f, ck = 0.f, sk = 0.f;
+      if (hq_) {
+        q1 = xq[jq];
+        q2 = xq[jq + half];
+        cq = ang[2 * jq];
+        sq = ang[2 * jq + 1];
+      }
+      if (hk_) {
+        k1r = xk[i];
+        k2r = xk[i + half];
+        v1 = xv[i];
+        v2 = xv[i + half];
+        ck = ang[2 * i];
+        sk = ang[2 * i + 1];
+      }
+      if (hq_) {
+        const float x1 = bf16_bits_to_float(q1), x2 = bf16_bits_to_float(q2);
+        qbuf[r * kAD + jq] = float_to_bf16_bits(x1 * cq - x2 * sq);
+        qbuf[r * kAD + jq + half] = float_to_bf16_bits(x1 * sq + x2 * cq);
+      }
+      if (hk_) {
+        const float x1 = bf16_bits_to_float(k1r), x2 = bf16_bits_to_float(k2r);
+        const uint16_t k1 = float_to_bf16_bits(x1 * ck - x2 * sk), k2 = float_to_bf16_bits(x1 * sk + x2 * ck);
+        knew[i] = k1;
+        knew[i + half] = k2;
+        vnew[i] = v1;
+        vnew[i + half] = v2;
+        if (owner) {
+          // the fused entry passes writable caches
+          uint16_t *kd = const_cast<uint16_t *>(a.k) + b * a.bstride + h * a.hstride + static_cast<int64_t>(p) * kAD;
+          uint16_t *vd = const_cast<uint16_t *>(a.v) + b * a.bstride + h * a.hstride + static_cast<int64_t>(p) * kAD;
+          kd[i] = k1;
+          kd[i + half] = k2;
+          vd[i] = v1;
+          vd[i + half] = v2;
+        }
+      }
+    }
+    __syncthreads();
+    qrow = qbuf;
+    if (blk < t_end && blk <= p && p < blk + kABlk) load_block(blk, kr, vr, true);
+  }
 
   // Q fragments (rows = heads of the group; rows >= g are zero). k-step ks covers
   // physical d = 32*(ks/2) + 8*tid + 4*(ks%2) + {0,1 | 2,3} for logical {2tid | 2tid+8}.
@@ -83,8 +195,10 @@ attn_decode_kernel(AttnArgs a) {
 #pragma unroll
   for (int ks = 0; ks < kAD / 16; ++ks) {
     const int d = 32 * (ks >> 1) + 8 * tid + 4 * (ks & 1);
-    const uint32_t *q0 = reinterpret_cast<const uint32_t *>(a.q + (static_cast<int64_t>(b) * a.Hq + hq0 + gid) * kAD + d);
-    const uint32_t *q8 = reinterpret_cast<const uint32_t *>(a.q + (static_cast<int64_t>(b) * a.Hq + hq0 + gid + 8) * kAD + d);
+    const uint16_t *qr0 = kFused ? qrow + gid * kAD : qrow + (static_cast<int64_t>(b) * a.Hq + hq0 + gid) * qstride;
+    const uint16_t *qr8 = kFused ? qrow + (gid + 8) * kAD : qrow + (static_cast<int64_t>(b) * a.Hq + hq0 + gid + 8) * qstride;
+    const uint32_t *q0 = reinterpret_cast<const uint32_t *>(qr0 + d);
+    const uint32_t *q8 = reinterpret_cast<const uint32_t *>(qr8 + d);
     qa[ks][0] = gid < g ? q0[0] : 0u;
     qa[ks][1] = gid + 8 < g ? q8[0] : 0u;
     qa[ks][2] = gid < g ? q0[1] : 0u;
@@ -98,30 +212,6 @@ attn_decode_kernel(AttnArgs a) {
   float l_lo = 0.f, l_hi = 0.f;              // this lane's share of the running sums
   uint16_t *vs = vtile[warp];
 
-  // register prefetch of one block: K rows (token gid of each 8-token half, 16 B x 2)
-  // and this lane's four 16-byte pieces of the V tile
-  constexpr int kDB = kAD / 32;  // 16-byte K pieces per token per lane
-  constexpr int kVR = kAD / 16;  // 16-byte V pieces per lane per block
-  auto load_block = [&](int blk, uint4 (&kr)[2][kDB], uint4 (&vr)[kVR]) {
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      const int t = blk + nt * 8 + gid;
-#pragma unroll
-      for (int db = 0; db < kDB; ++db)
-        kr[nt][db] = t < t_end ? ldg16(kb + static_cast<int64_t>(t) * kAD + db * 32 + tid * 8)
-                               : make_uint4(0u, 0u, 0u, 0u);
-    }
-#pragma unroll
-    for (int i = 0; i < kVR; ++i) {
-      const int idx = i * 32 + lane, row = idx / (kAD / 8), c16 = idx % (kAD / 8);
-      const int t = blk + row;
-      vr[i] = t < t_end ? ldg16(vb + static_cast<int64_t>(t) * kAD + c16 * 8) : make_uint4(0u, 0u, 0u, 0u);
-    }
-  };
-
-  uint4 kr[2][kDB], vr[kVR];
-  int blk = t_begin + warp * kABlk;
-  if (blk < t_end) load_block(blk, kr, vr);
   for (; blk < t_end; blk += kAWarps * kABlk) {
     // stage V, then prefetch the next block while this one computes
 #pragma unroll
@@ -135,7 +225,7 @@ attn_decode_kernel(AttnArgs a) {
 #pragma unroll
       for (int db = 0; db < kDB; ++db) kc[nt][db] = kr[nt][db];
     const int nxt = blk + kAWarps * kABlk;
-    if (nxt < t_end) load_block(nxt, kr, vr);
+    if (nxt < t_end) load_block(nxt, kr, vr, true);
 
     // S = Q K^T for the two 8-token halves
     float s[2][4];
@@ -258,9 +348,11 @@ __global__ void attn_combine_kernel(const float *__restrict__ ws, uint16_t *__re
   const int d = threadIdx.x;
   const float *p = ws + hq * splits * (2 + kAD);
   float M = -INFINITY;
+#pragma unroll 8
   for (int s = 0; s < splits; ++s) M = fmaxf(M, p[s * (2 + kAD)]);
   float L = 0.f, O = 0.f;
   if (M != -INFINITY) {
+#pragma unroll 8
     for (int s = 0; s < splits; ++s) {
       const float *q = p + s * (2 + kAD);
       const float f = exp2f(q[0] - M);
@@ -396,4 +488,54 @@ extern "C" int iron_attn_decode_noalloc(const uint16_t *q, const uint16_t *k_cac
   }
   return iron_attn_decode(q, k_cache, v_cache, lens, out, B, Hq, Hkv, D, Lmax, kv_batch_stride,
                           kv_head_stride, scale, ws, need, flags, stream);
+}
+
+// Fused decode attention: q, k, v of the new token from the QKV projection, RoPE at
+// pos[b], the new k / v appended to the cache, lens = pos + 1 -- no separate RoPE /
+// append launches; the split merge follows as the combine kernel.
+extern "C" int iron_attn_decode_qkv(const uint16_t *qkv, const int32_t *pos, const float *lut,
+                                    uint16_t *k_cache, uint16_t *v_cache, uint16_t *out, int B, int Hq, int Hkv,
+                                    int D, int Lmax, int64_t kv_batch_stride, int64_t kv_head_stride, float scale,
+                                    void *workspace, size_t workspace_bytes, unsigned flags, void *stream) {
+  if (!qkv || !pos || !lut || !k_cache || !v_cache || !out) return IRON_ERR_NULL;
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Lmax <= 0 || B > 65535 || Hkv > 65535) return IRON_ERR_SHAPE;
+  if (D != 64 && D != 128) return IRON_ERR_UNSUPPORTED;
+  if (Hq % Hkv || Hq / Hkv > 16) return IRON_ERR_SHAPE;
+  if (!aligned16(qkv) || !aligned16(k_cache) || !aligned16(v_cache) || (kv_batch_stride % 8) ||
+      (kv_head_stride % 8))
+    return IRON_ERR_ALIGN;
+  AttnArgs a = {};
+  a.k = k_cache;
+  a.v = v_cache;
+  a.out = out;
+  a.bstride = kv_batch_stride;
+  a.hstride = kv_head_stride;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.splits = attn_splits(B, Hkv, Lmax, sm_count());
+  a.chunk = ((Lmax + a.splits - 1) / a.splits + kAWarps * kABlk - 1) / (kAWarps * kABlk) * (kAWarps * kABlk);
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.qkv = qkv;
+  a.pos = pos;
+  a.lut = lut;
+  if (a.splits > 1) {
+    if (!workspace) return IRON_ERR_NULL;
+    if (workspace_bytes < attn_ws_bytes(B, Hq, Hkv, Lmax, D)) return IRON_ERR_WORKSPACE;
+    a.ws = static_cast<float *>(workspace);
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool pdl = (flags & IRON_FLAG_PDL) != 0;
+  // the splits merge in the combine kernel, which PDL overlaps with this one's tail
+  // (measured faster on B200 than merging in the last split CTA)
+  int st = D == 64 ? launch(attn_decode_kernel<64, true>, dim3(a.splits, Hkv, B), dim3(32 * kAWarps), 0, s, pdl, a)
+                   : launch(attn_decode_kernel<128, true>, dim3(a.splits, Hkv, B), dim3(32 * kAWarps), 0, s, pdl, a);
+  if (st != IRON_OK || a.splits == 1) return st;
+  return D == 64 ? launch(attn_combine_kernel<64>, dim3(B * Hq), dim3(64), 0, s, pdl, static_cast<const float *>(a.ws),
+                          out, a.splits)
+                 : launch(attn_combine_kernel<128>, dim3(B * Hq), dim3(128), 0, s, pdl,
+                          static_cast<const float *>(a.ws), out, a.splits);
+}
+
+extern "C" size_t iron_attn_decode_qkv_workspace_bytes(int B, int Hq, int Hkv, int Lmax, int D) {
+  return (D == 64 || D == 128) ? attn_ws_bytes(B, Hq, Hkv, Lmax, D) : 0;
 }

@@ -44,10 +44,32 @@ __device__ __forceinline__ S4Range s4_split(int b, int e, int parts, int i) {
 // 8-15 the matching up rows of output rows 8*tile..8*tile+7 (y has N/2 columns):
 // y = bf16(bf16(silu(bf16(gate))) * bf16(up)), the rounding sequence of IRON's
 // SwiGLUDecode (iron/operators/swiglu_decode/reference.py:49-53).
+// What a GEMV does around the dot products: an RMSNorm of x first (norm_w != null),
+// a residual add or the SwiGLU of interleaved gate/up rows on the output, and the
+// greedy argmax of each output vector (amax != null: 64-bit keys, larger value then
+// lower row wins).
+constexpr int kS4ArgmaxSlots = 32;  // argmax key slots per vector
+
+struct S4Epi {
+  const uint16_t *residual;
+  int swiglu;
+  const uint16_t *norm_w;
+  float eps;
+  unsigned long long *amax;
+};
+
+__device__ __forceinline__ unsigned long long s4_argmax_key(float v, int row) {
+  unsigned u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  if (v != v) u = 0u;  // NaN never wins
+  return (static_cast<unsigned long long>(u) << 32) | static_cast<unsigned>(~row);
+}
+
 template <int NT>
 __device__ __forceinline__ void s4_store(const float (&v)[NT][4], int tile, int N, int n_vec,
                                          uint16_t *__restrict__ y,
-                                         const uint16_t *__restrict__ residual, int swiglu) {
+                                         const uint16_t *__restrict__ residual, int swiglu,
+                                         unsigned long long *amax = nullptr) {
   const int lane = threadIdx.x & 31, gid = lane >> 2, tid = lane & 3;
   const int row0 = tile * 16;
   if (swiglu) {
@@ -67,7 +89,8 @@ __device__ __forceinline__ void s4_store(const float (&v)[NT][4], int tile, int 
     return;
   }
 #pragma unroll
-  for (int t = 0; t < NT; ++t)
+  for (int t = 0; t < NT; ++t) {
+    unsigned long long best[2] = {0ull, 0ull};  // per vector 2tid + (e & 1)
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int row = row0 + gid + ((e >> 1) << 3);
@@ -78,15 +101,39 @@ __device__ __forceinline__ void s4_store(const float (&v)[NT][4], int tile, int 
         // the residual is added to the bf16-rounded projection, as IRON adds two
         // bf16 buffers (iron/operators/elementwise_add/reference.py:7-9)
         if (residual) r = __bfloat162float(__float2bfloat16_rn(r)) + bf16_bits_to_float(residual[o]);
-        y[o] = float_to_bf16_bits(r);
+        const uint16_t yb = float_to_bf16_bits(r);
+        y[o] = yb;
+        if (amax) {
+          const unsigned long long k = s4_argmax_key(bf16_bits_to_float(yb), row);
+          best[e & 1] = k > best[e & 1] ? k : best[e & 1];
+        }
       }
     }
+    if (amax) {
+      // best (value, then lowest row) of the tile's 16 rows per vector: reduce over the
+      // 8 lanes of each tid, then one atomic per tile and vector, into one of
+      // kS4ArgmaxSlots slots (spreads the contention of 8016 tiles over L2 lines)
+#pragma unroll
+      for (int q = 0; q < 2; ++q)
+#pragma unroll
+        for (int x = 4; x <= 16; x <<= 1) {
+          const unsigned long long other = __shfl_xor_sync(0xffffffffu, best[q], x);
+          best[q] = other > best[q] ? other : best[q];
+        }
+      if (gid == 0)
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const int vv = t * 8 + tid * 2 + q;
+          if (vv < n_vec) atomicMax(amax + vv * kS4ArgmaxSlots + (tile & (kS4ArgmaxSlots - 1)), best[q]);
+        }
+    }
+  }
 }
 
-template <int NT>
+template <int NT, bool kShared = false>
 __device__ __forceinline__ void s4_unit_gx(float (&d)[2][NT][4], const uint4 &clo, const uint4 &chi,
                                            const uint4 &sc, const uint16_t *__restrict__ x, int K,
-                                           int n_vec, int kbase) {
+                                           int n_vec, int kbase, int ldx = -1, int xoff = 0) {
   const int lane = threadIdx.x & 31, gid = lane >> 2, tid = lane & 3;
   const uint32_t wl[4] = {clo.x, clo.y, clo.z, clo.w};
   const uint32_t wh[4] = {chi.x, chi.y, chi.z, chi.w};
@@ -98,7 +145,12 @@ __device__ __forceinline__ void s4_unit_gx(float (&d)[2][NT][4], const uint4 &cl
     for (int t = 0; t < NT; ++t) {
       const int vv = t * 8 + gid;
       xr[j][t] = make_uint4(0u, 0u, 0u, 0u);
-      if (vv < n_vec) xr[j][t] = __ldg(reinterpret_cast<const uint4 *>(x + static_cast<int64_t>(vv) * K + kbase + j * 32 + tid * 8));
+      if (vv < n_vec) {
+        if constexpr (kShared)
+          xr[j][t] = *reinterpret_cast<const uint4 *>(x + vv * ldx + kbase - xoff + j * 32 + tid * 8);
+        else
+          xr[j][t] = __ldg(reinterpret_cast<const uint4 *>(x + static_cast<int64_t>(vv) * K + kbase + j * 32 + tid * 8));
+      }
     }
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -129,12 +181,12 @@ __device__ __forceinline__ void s4_unit_gx(float (&d)[2][NT][4], const uint4 &cl
 constexpr int kT4Warps = 4;
 constexpr int kT4Units = 4;  // units per warp per round (all loads issued at once)
 
-template <int NT, int CS>
+template <int NT, int CS, bool kNorm = false>
 __global__ void __launch_bounds__(32 * kT4Warps)
 gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__restrict__ x,
-                       uint16_t *__restrict__ y, int N, int K, int n_vec,
-                       const uint16_t *__restrict__ residual, int swiglu) {
+                       uint16_t *__restrict__ y, int N, int K, int n_vec, S4Epi epi) {
   __shared__ float red[(kT4Warps + CS) * NT * 128];
+  extern __shared__ __align__(16) uint16_t xs_norm[];  // [n_vec, this CTA's k range] when normalising
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tid = lane & 3;
   const int rank = (CS > 1) ? static_cast<int>(blockIdx.x % CS) : 0;
@@ -162,16 +214,74 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
     }
   };
   load(kr.b);
+  constexpr bool norm = kNorm && NT == 1;
+  const S4Range cr = s4_split(0, cpt, CS, rank);  // this CTA's units (all its warps')
+  const int kc0 = cr.b * 128, klen = (cr.e - cr.b) * 128;
+  constexpr int kThr = 32 * kT4Warps;
+  uint4 wreg[2];  // the norm weights of this thread's positions (klen <= 2048): never depend on the previous kernel
+  if constexpr (norm) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int k = threadIdx.x * 8 + j * kThr * 8;
+      if (k < klen) wreg[j] = __ldg(reinterpret_cast<const uint4 *>(epi.norm_w + kc0 + k));
+    }
+  }
   pdl_launch_dependents();
   pdl_wait();
+  if constexpr (norm) {
+    // RMSNorm (rmsnorm_kernel's arithmetic): one pass over the whole x for the sums of
+    // squares that also parks this CTA's k range in shared memory, then the range
+    // normalised in place (x * inv * w, rounded to bf16)
+    float ss[8];
+#pragma unroll
+    for (int v = 0; v < 8; ++v) {
+      ss[v] = 0.f;
+      if (v < n_vec)
+        for (int k = threadIdx.x * 8; k < K; k += kThr * 8) {
+          const uint4 r = __ldg(reinterpret_cast<const uint4 *>(x + static_cast<int64_t>(v) * K + k));
+          const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) ss[v] += bf16_lo(w4[i]) * bf16_lo(w4[i]) + bf16_hi(w4[i]) * bf16_hi(w4[i]);
+          if (k >= kc0 && k < kc0 + klen) *reinterpret_cast<uint4 *>(xs_norm + v * klen + k - kc0) = r;
+        }
+      ss[v] = warp_sum(ss[v]);
+    }
+    if (lane == 0)
+#pragma unroll
+      for (int v = 0; v < 8; ++v) red[warp * 8 + v] = ss[v];
+    __syncthreads();
+    for (int v = 0; v < n_vec; ++v) {
+      float t = 0.f;
+#pragma unroll
+      for (int q = 0; q < kT4Warps; ++q) t += red[q * 8 + v];
+      const float iv = rsqrtf(t / K + epi.eps);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int k = threadIdx.x * 8 + j * kThr * 8;
+        if (k < klen) {
+          uint4 *px = reinterpret_cast<uint4 *>(xs_norm + v * klen + k);
+          const uint4 r = *px, w = wreg[j];
+          uint4 o;
+          o.x = pack_bf16x2(bf16_lo(r.x) * iv * bf16_lo(w.x), bf16_hi(r.x) * iv * bf16_hi(w.x));
+          o.y = pack_bf16x2(bf16_lo(r.y) * iv * bf16_lo(w.y), bf16_hi(r.y) * iv * bf16_hi(w.y));
+          o.z = pack_bf16x2(bf16_lo(r.z) * iv * bf16_lo(w.z), bf16_hi(r.z) * iv * bf16_hi(w.z));
+          o.w = pack_bf16x2(bf16_lo(r.w) * iv * bf16_lo(w.w), bf16_hi(r.w) * iv * bf16_hi(w.w));
+          *px = o;
+        }
+      }
+    }
+    __syncthreads();  // the normalised slice complete; `red` free again
+  }
   for (int c0 = kr.b; c0 < kr.e; c0 += kT4Units) {
 #pragma unroll
     for (int u = 0; u < kT4Units; ++u) {
       const int c = c0 + u;
       if (c < kr.e) {
-        // B fragments straight from the activations (L1-cached), permuted to the
-        // nibble-pair order: pieces (x[8m+i], x[8m+4+i]) for this lane's m = 4(4c+j)+tid
-        s4_unit_gx<NT>(acc, lo[u], hi[u], sc[u], x, K, n_vec, c * 128);
+        // B fragments from the activations (L1-cached) or the normalised slice,
+        // permuted to the nibble-pair order: pieces (x[8m+i], x[8m+4+i]) for this
+        // lane's m = 4(4c+j)+tid
+        if constexpr (norm) s4_unit_gx<NT, true>(acc, lo[u], hi[u], sc[u], xs_norm, K, n_vec, c * 128, klen, kc0);
+        else s4_unit_gx<NT>(acc, lo[u], hi[u], sc[u], x, K, n_vec, c * 128);
       }
     }
     if (c0 + kT4Units < kr.e) load(c0 + kT4Units);
@@ -215,7 +325,7 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
           for (int r = 1; r < CS; ++r) v[t][e] += slot0[((r * NT + t) * 4 + e) * 32 + lane];
     }
   }
-  if (warp == 0) s4_store<NT>(v, tile, N, n_vec, y, residual, swiglu);
+  if (warp == 0) s4_store<NT>(v, tile, N, n_vec, y, epi.residual, epi.swiglu, epi.amax);
 }
 
 // Repack natural-layout codes [N, K/2] + scales [N, K/32] into GEMV units.
@@ -257,11 +367,17 @@ __global__ void pack_s4g32_kernel(const uint8_t *__restrict__ codes,
 
 template <int NT, int CS>
 static int launch_s4_tile(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,
-                          int n_vec, const uint16_t *res, int swiglu, bool pdl, cudaStream_t s) {
+                          int n_vec, const S4Epi &epi, bool pdl, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>((N / 16) * CS));
   cfg.blockDim = dim3(32 * kT4Warps);
   cfg.stream = s;
+  if (epi.norm_w) {
+    // the CTA's normalised k range of every vector (<= 8 x 2048 bf16 = 32 KB)
+    const int cpt = K / 128;
+    const int klen_max = ((cpt + CS - 1) / CS) * 128;
+    cfg.dynamicSmemBytes = static_cast<size_t>(n_vec) * klen_max * 2;
+  }
   cudaLaunchAttribute attr[2];
   int na = 0;
   if (CS > 1) {
@@ -278,8 +394,9 @@ static int launch_s4_tile(const uint8_t *packed, const uint16_t *x, uint16_t *y,
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  cudaError_t e =
-      cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS>, packed, x, y, N, K, n_vec, res, swiglu);
+  cudaError_t e = epi.norm_w
+                      ? cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, true>, packed, x, y, N, K, n_vec, epi)
+                      : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, false>, packed, x, y, N, K, n_vec, epi);
   if (e != cudaSuccess) {
     set_last_cuda_error(e);
     (void)cudaGetLastError();
@@ -290,16 +407,16 @@ static int launch_s4_tile(const uint8_t *packed, const uint16_t *x, uint16_t *y,
 
 template <int NT>
 static int launch_s4_tile_cs(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,
-                             int n_vec, const uint16_t *res, int swiglu, bool pdl, cudaStream_t s) {
+                             int n_vec, const S4Epi &res, bool pdl, cudaStream_t s) {
   // split K over a cluster until every SM holds >= 2 CTAs (and each warp >= 1 chunk)
   const int tiles = N / 16, cpt = K / 128;
   int cs = 1;
   while (cs < 8 && tiles * cs < 2 * sm_count() && cpt >= kT4Warps * cs * 2) cs *= 2;
   switch (cs) {
-    case 1: return launch_s4_tile<NT, 1>(packed, x, y, N, K, n_vec, res, swiglu, pdl, s);
-    case 2: return launch_s4_tile<NT, 2>(packed, x, y, N, K, n_vec, res, swiglu, pdl, s);
-    case 4: return launch_s4_tile<NT, 4>(packed, x, y, N, K, n_vec, res, swiglu, pdl, s);
-    default: return launch_s4_tile<NT, 8>(packed, x, y, N, K, n_vec, res, swiglu, pdl, s);
+    case 1: return launch_s4_tile<NT, 1>(packed, x, y, N, K, n_vec, res, pdl, s);
+    case 2: return launch_s4_tile<NT, 2>(packed, x, y, N, K, n_vec, res, pdl, s);
+    case 4: return launch_s4_tile<NT, 4>(packed, x, y, N, K, n_vec, res, pdl, s);
+    default: return launch_s4_tile<NT, 8>(packed, x, y, N, K, n_vec, res, pdl, s);
   }
 }
 
@@ -366,9 +483,10 @@ extern "C" int iron_unpack_int4g32(const uint8_t *packed, uint16_t *out, int N, 
   return launch_status();
 }
 
-extern "C" int iron_gemv_int4g32(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N,
-                                 int K, int n_vec, const uint16_t *residual, unsigned flags,
-                                 void *stream) {
+extern "C" int iron_gemv_int4g32_ex(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,
+                                    int n_vec, const uint16_t *residual, const uint16_t *norm_weight,
+                                    float eps, unsigned long long *argmax_keys, unsigned flags,
+                                    void *stream) {
   if (!packed || !x || !y) return IRON_ERR_NULL;
   if (N <= 0 || K <= 0 || n_vec <= 0 || n_vec > 64) return IRON_ERR_SHAPE;
   if (K % 128 || N % 16) return IRON_ERR_SHAPE;
@@ -376,10 +494,48 @@ extern "C" int iron_gemv_int4g32(const uint8_t *packed, const uint16_t *x, uint1
   if (!aligned16(packed) || !aligned16(x)) return IRON_ERR_ALIGN;
   const bool pdl = (flags & IRON_FLAG_PDL) != 0;
   const int swiglu = (flags & IRON_FLAG_SWIGLU) ? 1 : 0;
-  if (swiglu && residual) return IRON_ERR_ARG;
+  if (swiglu && (residual || argmax_keys)) return IRON_ERR_ARG;
+  if (norm_weight) {
+    if (n_vec > 8 || K > 2048) return IRON_ERR_SHAPE;  // the fused prologue's shared slice and registers
+    if (!aligned16(norm_weight)) return IRON_ERR_ALIGN;
+  }
+  S4Epi epi{residual, swiglu, norm_weight, eps, argmax_keys};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (n_vec <= 8) return launch_s4_tile_cs<1>(packed, x, y, N, K, n_vec, residual, swiglu, pdl, s);
-  if (n_vec <= 16) return launch_s4_tile_cs<2>(packed, x, y, N, K, n_vec, residual, swiglu, pdl, s);
-  if (n_vec <= 32) return launch_s4_tile_cs<4>(packed, x, y, N, K, n_vec, residual, swiglu, pdl, s);
-  return launch_s4_tile_cs<8>(packed, x, y, N, K, n_vec, residual, swiglu, pdl, s);
+  if (n_vec <= 8) return launch_s4_tile_cs<1>(packed, x, y, N, K, n_vec, epi, pdl, s);
+  if (n_vec <= 16) return launch_s4_tile_cs<2>(packed, x, y, N, K, n_vec, epi, pdl, s);
+  if (n_vec <= 32) return launch_s4_tile_cs<4>(packed, x, y, N, K, n_vec, epi, pdl, s);
+  return launch_s4_tile_cs<8>(packed, x, y, N, K, n_vec, epi, pdl, s);
+}
+
+extern "C" int iron_gemv_int4g32(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N,
+                                 int K, int n_vec, const uint16_t *residual, unsigned flags,
+                                 void *stream) {
+  return iron_gemv_int4g32_ex(packed, x, y, N, K, n_vec, residual, nullptr, 0.f, nullptr, flags, stream);
+}
+
+// Greedy next token from the argmax keys an lm-head GEMV left: tokens[b], pos[b] += 1
+// (if pos), and the keys reset for the next step.
+__global__ void argmax_finalize_kernel(unsigned long long *keys, int *tokens, int *pos, int B) {
+  pdl_wait();
+  const int b = blockIdx.x, lane = threadIdx.x;  // one warp per vector, a lane per slot
+  unsigned long long k = keys[b * kS4ArgmaxSlots + lane];
+  keys[b * kS4ArgmaxSlots + lane] = 0ull;
+#pragma unroll
+  for (int x = 16; x > 0; x >>= 1) {
+    const unsigned long long o = __shfl_xor_sync(0xffffffffu, k, x);
+    k = o > k ? o : k;
+  }
+  if (lane == 0) {
+    tokens[b] = static_cast<int>(~static_cast<unsigned>(k & 0xffffffffull));
+    if (pos) pos[b] += 1;
+  }
+  pdl_launch_dependents();
+}
+
+extern "C" int iron_argmax_finalize(unsigned long long *keys, int32_t *tokens, int32_t *pos, int B, unsigned flags,
+                                    void *stream) {
+  if (!keys || !tokens) return IRON_ERR_NULL;
+  if (B <= 0 || B > 65535) return IRON_ERR_SHAPE;
+  return launch(argmax_finalize_kernel, dim3(B), dim3(kS4ArgmaxSlots), 0, static_cast<cudaStream_t>(stream),
+                (flags & IRON_FLAG_PDL) != 0, keys, tokens, pos, B);
 }

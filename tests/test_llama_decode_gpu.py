@@ -32,12 +32,20 @@ def _oracle_weights(eng):
     return out
 
 
-@pytest.mark.parametrize("persistent", [False, True])
-@pytest.mark.parametrize("batch,prefix", [(1, [9]), (3, [0, 5, 40]), (8, [1, 2, 3, 63, 64, 65, 100, 127])])
-def test_decode_step_matches_oracle(batch, prefix, persistent):
+@pytest.mark.parametrize("persistent,fuse", [(False, None), (True, None), (False, ("layers", True)),
+                                             (False, ("none", False))])
+@pytest.mark.parametrize("batch,prefix", [(1, [9]), (2, [63, 65]), (3, [0, 5, 40]),
+                                          (8, [1, 2, 3, 63, 64, 65, 100, 127]),
+                                          (12, [0, 1, 2, 3, 5, 8, 13, 21, 34, 55, 89, 144])])
+def test_decode_step_matches_oracle(batch, prefix, persistent, fuse):
+    if persistent and batch > 2:
+        pytest.skip("the persistent step serves batch <= 2")
+    if fuse and fuse[0] != "none" and batch > 8:
+        pytest.skip("the fused RMSNorm prologue serves batch <= 8")
     shape = LlamaShape(n_layers=2, vocab_size=4096)
     L = 160
-    eng = LlamaDecodeEngine(shape, batch, L, seed=7, keep_natural=True, persistent=persistent)
+    kw = dict(fuse_norm=fuse[0], fuse_rope=fuse[1]) if fuse else {}
+    eng = LlamaDecodeEngine(shape, batch, L, seed=7, keep_natural=True, persistent=persistent, **kw)
     g = torch.Generator(device="cuda").manual_seed(1)
     eng.kc.copy_(torch.randn(eng.kc.shape, generator=g, device="cuda").to(torch.bfloat16))
     eng.vc.copy_(torch.randn(eng.vc.shape, generator=g, device="cuda").to(torch.bfloat16))
@@ -64,8 +72,10 @@ def test_decode_step_matches_oracle(batch, prefix, persistent):
     # caches got the new rows, positions advanced, greedy token consistent
     for li in range(shape.n_layers):
         for b, p in enumerate(prefix):
-            assert_close(eng.kc[li, b, :, p].cpu(), kcs[li][b, :, p], 2e-2, 2e-2, what="k row")
-            assert_close(eng.vc[li, b, :, p].cpu(), vcs[li][b, :, p], 2e-2, 2e-2, what="v row")
+            assert_close(eng.kc[li, b, :, p].cpu(), kcs[li][b, :, p], 2e-2, 2e-2, max_mismatch_frac=1e-2,
+                         what="k row")
+            assert_close(eng.vc[li, b, :, p].cpu(), vcs[li][b, :, p], 2e-2, 2e-2, max_mismatch_frac=1e-2,
+                         what="v row")
     assert eng.pos.cpu().tolist() == [p + 1 for p in prefix]
     top = eng.tokens.cpu().long()
     got = eng.logits.cpu().float()
@@ -150,3 +160,31 @@ def test_persistent_step_matches_kernel_chain_full_model():
     assert p0.tolist() == p1.tolist() == [68, 35]
     assert_close(l1[0].cpu(), l0[0].cpu(), 2e-2, 2e-2, what="first-step logits")
     assert_close(k1, k0, 2e-2, 2e-2, max_mismatch_frac=1e-3, what="caches")
+
+
+@pytest.mark.parametrize("n_vec", [1, 3, 8])
+def test_gemv_ex_fused_rmsnorm_and_argmax(n_vec):
+    """iron_gemv_int4g32_ex: RMSNorm of x fused into the GEMV's prologue and the greedy
+    argmax into its epilogue, against the oracle's rms_norm -> gemv -> argmax."""
+    from iron_b200 import _lib
+    from iron_b200.applications.llama_3_2_1b.decode import Int4Matrix
+    from oracle import ops
+
+    N, K = 4096, 2048
+    g = torch.Generator(device="cuda").manual_seed(n_vec)
+    W = Int4Matrix(N, K, g, 0.001, 0.004, keep_natural=True)
+    x = torch.randn(n_vec, K, device="cuda", generator=g).to(torch.bfloat16)
+    w = (1 + 0.02 * torch.randn(K, device="cuda", generator=g)).to(torch.bfloat16)
+    y = torch.empty(n_vec, N, dtype=torch.bfloat16, device="cuda")
+    keys = torch.zeros(n_vec * 32, dtype=torch.int64, device="cuda")
+    tok = torch.zeros(n_vec, dtype=torch.int32, device="cuda")
+    s = _lib.current_stream()
+    _lib.call("iron_gemv_int4g32_ex", W.packed.data_ptr(), x.data_ptr(), y.data_ptr(), N, K, n_vec, None,
+              w.data_ptr(), 1e-5, keys.data_ptr(), 0, s)
+    _lib.call("iron_argmax_finalize", keys.data_ptr(), tok.data_ptr(), None, n_vec, 0, s)
+    torch.cuda.synchronize()
+    ref = ops.gemv_multi(W.dequant().cpu(), ops.rms_norm(x.cpu(), w.cpu(), 1e-5))
+    assert_close(y.cpu(), ref, 2e-2, 1e-2, what="normed gemv")
+    got = y.cpu().float()
+    assert torch.equal(tok.cpu().long(), got.argmax(1))  # first index of the max of what it wrote
+    assert int(keys.abs().sum()) == 0  # keys reset for the next step
