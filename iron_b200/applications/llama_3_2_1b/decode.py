@@ -154,14 +154,14 @@ class LlamaDecodeEngine:
         self.persistent = bool(persistent)
         # where RMSNorm runs inside the following GEMV ("none", "layers": the QKV and
         # gate/up GEMVs, "all": also the lm-head); only for B <= 8. Defaults measured on
-        # B200 (one process, interleaved): the fused prologue saves 77 us per step at
-        # B = 1 and costs 93 us at B = 8; RoPE inside attention costs 22 us at B = 1
-        # and saves 54 us at B = 8, 286 us at B = 64.
-        self.fuse_norm = fuse_norm if fuse_norm is not None else ("layers" if B <= 2 else "none")
+        # B200 (one process, interleaved, 8-warp GEMV tiles): the fused prologue costs
+        # 24 us per step at B = 1 and 172 us at B = 8; RoPE inside attention costs 33 us
+        # at B = 1 and saves 62 us at B = 8, 305 us at B = 64.
+        self.fuse_norm = fuse_norm if fuse_norm is not None else "none"
         if self.fuse_norm != "none" and B > 8:
             raise ValueError("the fused RMSNorm prologue serves B <= 8")
         # RoPE + KV append inside the attention kernel (else the rope_kv_append kernel)
-        self.fuse_rope = fuse_rope if fuse_rope is not None else B > 2
+        self.fuse_rope = fuse_rope if fuse_rope is not None else B > 1
         if self.persistent:
             if not fits:
                 raise ValueError("the persistent decode step needs the Llama-3.2-1B layer shape and batch <= 2")

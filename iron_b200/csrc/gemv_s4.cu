@@ -178,13 +178,21 @@ __device__ __forceinline__ void s4_unit_gx(float (&d)[2][NT][4], const uint4 &cl
 // when a cluster splits K), every warp loading all of its units straight into
 // registers before griddepcontrol.wait; partials reduced through shared memory
 // and, across a cluster, distributed shared memory.
-constexpr int kT4Warps = 4;
-constexpr int kT4Units = 4;  // units per warp per round (all loads issued at once)
+// Warps per CTA and units each warp loads per round (all at once). Up to 16 vectors:
+// 8 warps x 2 units (a 16-unit K = 2048 tile entirely in flight, 59 registers --
+// measured on B200: 3.76 us per config-2 launch against 5.3 us at 4 x 4); more
+// vectors keep 4 x 4 (the reduction buffer and the wider accumulators).
+template <int NT>
+constexpr int s4_warps() { return NT <= 2 ? 8 : 4; }
+template <int NT>
+constexpr int s4_units() { return NT <= 2 ? 2 : 4; }
 
 template <int NT, int CS, bool kNorm = false>
-__global__ void __launch_bounds__(32 * kT4Warps)
+__global__ void __launch_bounds__(32 * s4_warps<NT>())
 gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__restrict__ x,
                        uint16_t *__restrict__ y, int N, int K, int n_vec, S4Epi epi) {
+  constexpr int kT4Warps = s4_warps<NT>();
+  constexpr int kT4Units = s4_units<NT>();
   __shared__ float red[(kT4Warps + CS) * NT * 128];
   extern __shared__ __align__(16) uint16_t xs_norm[];  // [n_vec, this CTA's k range] when normalising
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -370,7 +378,7 @@ static int launch_s4_tile(const uint8_t *packed, const uint16_t *x, uint16_t *y,
                           int n_vec, const S4Epi &epi, bool pdl, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>((N / 16) * CS));
-  cfg.blockDim = dim3(32 * kT4Warps);
+  cfg.blockDim = dim3(32 * s4_warps<NT>());
   cfg.stream = s;
   if (epi.norm_w) {
     // the CTA's normalised k range of every vector (<= 8 x 2048 bf16 = 32 KB)
@@ -411,7 +419,7 @@ static int launch_s4_tile_cs(const uint8_t *packed, const uint16_t *x, uint16_t 
   // split K over a cluster until every SM holds >= 2 CTAs (and each warp >= 1 chunk)
   const int tiles = N / 16, cpt = K / 128;
   int cs = 1;
-  while (cs < 8 && tiles * cs < 2 * sm_count() && cpt >= kT4Warps * cs * 2) cs *= 2;
+  while (cs < 8 && tiles * cs < 2 * sm_count() && cpt >= s4_warps<NT>() * cs * 2) cs *= 2;
   switch (cs) {
     case 1: return launch_s4_tile<NT, 1>(packed, x, y, N, K, n_vec, res, pdl, s);
     case 2: return launch_s4_tile<NT, 2>(packed, x, y, N, K, n_vec, res, pdl, s);
@@ -502,9 +510,13 @@ extern "C" int iron_gemv_int4g32_ex(const uint8_t *packed, const uint16_t *x, ui
   S4Epi epi{residual, swiglu, norm_weight, eps, argmax_keys};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (n_vec <= 8) return launch_s4_tile_cs<1>(packed, x, y, N, K, n_vec, epi, pdl, s);
+#ifdef IRON_S4_ONLY_NT1
+  return IRON_ERR_SHAPE;
+#else
   if (n_vec <= 16) return launch_s4_tile_cs<2>(packed, x, y, N, K, n_vec, epi, pdl, s);
   if (n_vec <= 32) return launch_s4_tile_cs<4>(packed, x, y, N, K, n_vec, epi, pdl, s);
   return launch_s4_tile_cs<8>(packed, x, y, N, K, n_vec, epi, pdl, s);
+#endif
 }
 
 extern "C" int iron_gemv_int4g32(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N,
