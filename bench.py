@@ -872,7 +872,8 @@ def run_tp_block(args, world, rank, local):
 
     shape, B = BlockShape(), args.batch
     ctx = PREFIX
-    blk = TPDecoderBlock(shape, world, rank, B, ctx + 16, seed=13, pdl=not args.no_pdl)
+    fused = world > 1 and B <= 8
+    blk = TPDecoderBlock(shape, world, rank, B, ctx + 16, seed=13, pdl=not args.no_pdl, fused_allreduce=fused)
     g = torch.Generator(device="cuda")
     g.manual_seed(7 + rank)
     blk.kc[:, :, :ctx].normal_(generator=g)
@@ -932,14 +933,18 @@ def run_tp_block(args, world, rank, local):
             "vs_baseline": None, "dtype": "bf16 activations, int4 g32 weights, fp32 accumulate",
             "data": "synthetic (random-init int4 weights, random KV cache; seeded)",
             "config": {"workload": "tp_block (BASELINE config 5, Llama-3-8B block)", "batch": B,
-                       "context": ctx, "tp": world, "allreduce": "NCCL bf16 sum of [B, 4096], 2 per block",
+                       "context": ctx, "tp": world,
+                       "allreduce": ("fused into the o_proj / down_proj GEMVs (peer stores over NVLink), 2 per block"
+                                     if fused else "NCCL bf16 sum of [B, 4096], 2 per block"),
                        "parallelism": f"tp{world}"},
-            "us_per_block": round(us, 2), "allreduce_us": round(ar_us, 2) if ar_us is not None else None,
+            "us_per_block": round(us, 2),
+            "nccl_allreduce_us": round(ar_us, 2) if ar_us is not None else None,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": None,
                          "scope": "one rank's block step (its weight shard + kv heads)",
                          "algorithmic_bytes_per_step": int(bytes_rank)},
             "gpu_launches": (8 + int(blk.ws.numel() > 16)) * args.steps, "clocks": clocks, "e2e": None}
+    blk.check_status()
     blk.release()
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -117,6 +117,31 @@ int iron_gemv_int4g32_ex(const uint8_t *packed, const uint16_t *x, uint16_t *y, 
                          unsigned long long *argmax_keys, unsigned flags, void *stream);
 int iron_argmax_finalize(unsigned long long *keys, int32_t *tokens, int32_t *pos, int B, unsigned flags,
                          void *stream);
+/* iron_gemv_int4g32_allreduce (no reference counterpart as one call: it replaces a
+ * row-parallel projection followed by the NCCL all-reduce of the tensor-parallel
+ * block): the int4 GEMV of this rank's input columns (n_vec <= 8), whose output tiles
+ * are all-reduced over the ranks inside the kernel -- each finished 16-row tile's
+ * fp32 partial goes into every rank's receive buffer over NVLink as 8-byte
+ * (value, flag) stores and every rank sums them in rank order -- then rounded to bf16
+ * and, with `residual`, y = bf16(bf16(sum) + residual) on every rank. `peers` points to
+ * an iron_allreduce_peers in host memory; recv[r] is rank r's buffer ([world, N, n_vec]
+ * 8-byte slots, zero before first use and left zero), mapped into this process with
+ * iron_ipc_open for r != rank. All ranks launch it for the same shape; a wait for a peer's tile gives up after 1 s and sets
+ * *status. iron_ipc_alloc / iron_ipc_free give these buffers their own zero-filled
+ * allocations (an IPC handle maps the start of an allocation); iron_ipc_handle /
+ * iron_ipc_open / iron_ipc_close wrap CUDA IPC (64-byte handles). */
+typedef struct {
+  int world, rank;
+  float *recv[8];
+  unsigned *status;
+} iron_allreduce_peers;
+int iron_gemv_int4g32_allreduce(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K, int n_vec,
+                                const uint16_t *residual, const void *peers, unsigned flags, void *stream);
+int iron_ipc_alloc(size_t bytes, void **dev_ptr_out);
+int iron_ipc_free(void *dev_ptr);
+int iron_ipc_handle(const void *dev_ptr, void *handle_out);
+int iron_ipc_open(const void *handle, void **dev_ptr_out);
+int iron_ipc_close(void *dev_ptr);
 int iron_gemv_int4g32(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,
                       int n_vec, const uint16_t *residual, unsigned flags, void *stream);
 

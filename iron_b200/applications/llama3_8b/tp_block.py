@@ -9,13 +9,18 @@ step of a batch of sequences:
     -> down_proj GEMV (local FFN columns; rank 0 adds the residual) -> all-reduce
 
 so the all-reduced o_proj output is the residual stream h and the all-reduced
-down_proj output the block output. The two all-reduces (bf16 sums over NCCL,
-NVLink / NVSwitch) are the only exchange; with tp = 1 they vanish. The kernels are
-the ones of the Llama-3.2-1B decode engine (llama_cpu.py:170-218 semantics).
+down_proj output the block output. The two all-reduces are the only exchange; with
+tp = 1 they vanish. Either NCCL runs them (bf16 sums over NVLink / NVSwitch, rank 0
+adding the residual), or -- fused_allreduce -- the o_proj / down_proj GEMVs do: each
+finished tile's fp32 partial is stored into every rank's receive buffer over NVLink
+(CUDA IPC mappings) and every rank sums the partials in rank order and adds the
+residual, so no collective call runs at all. The kernels are the ones of the
+Llama-3.2-1B decode engine (llama_cpu.py:170-218 semantics).
 """
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -26,9 +31,82 @@ from ..llama_3_2_1b.decode import rope_table
 from .sharding import BlockShape, random_block_weights, shard_of, shard_weights
 
 
+class AllReducePeers(ctypes.Structure):
+    """iron_allreduce_peers (include/iron_b200.h)."""
+
+    _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int), ("recv", ctypes.c_void_p * 8),
+                ("status", ctypes.c_void_p)]
+
+
+class _DeviceBuffer:
+    """A zero-filled allocation of its own (an IPC handle maps an allocation's start),
+    viewed by torch through __cuda_array_interface__."""
+
+    def __init__(self, shape, typestr: str, itemsize: int):
+        n = 1
+        for d in shape:
+            n *= d
+        out = ctypes.c_void_p()
+        _lib.call("iron_ipc_alloc", n * itemsize, ctypes.byref(out))
+        self.ptr = out.value
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (self.ptr, False),
+                                         "version": 3}
+        self.tensor = torch.as_tensor(self, device="cuda")
+
+    def free(self):
+        if self.ptr:
+            _lib.call("iron_ipc_free", self.ptr)
+            self.ptr = None
+
+
+class _PeerSite:
+    """Receive buffer ((value, flag) slots) of one fused all-reduce site, mapped on every rank."""
+
+    def __init__(self, rows: int, n_vec: int, tp: int, rank: int, group):
+        import torch.distributed as dist
+
+        # (fp32 value, flag) 8-byte slots per (source, row, vector)
+        self._bufs = [_DeviceBuffer((tp, rows, n_vec), "<u8", 8)]
+        self.recv = self._bufs[0].tensor
+        self.status = torch.zeros(4, dtype=torch.int32, device=torch.device("cuda", torch.cuda.current_device()))
+        lib = _lib.load()
+        hs = []
+        for b in self._bufs:
+            h = (ctypes.c_char * 64)()
+            _lib.call("iron_ipc_handle", b.ptr, h)
+            hs.append(bytes(h))
+        everyone = [None] * tp
+        dist.all_gather_object(everyone, hs, group=group)
+        self.opened = []
+        self.peers = AllReducePeers()
+        self.peers.world, self.peers.rank = tp, rank
+        for r in range(tp):
+            if r == rank:
+                self.peers.recv[r] = self._bufs[0].ptr
+                continue
+            ptrs = []
+            for hb in everyone[r]:
+                out = ctypes.c_void_p()
+                _lib.call("iron_ipc_open", (ctypes.c_char * 64).from_buffer_copy(hb), ctypes.byref(out))
+                ptrs.append(out.value)
+                self.opened.append(out.value)
+            self.peers.recv[r] = ptrs[0]
+        self.peers.status = self.status.data_ptr()
+        del lib
+
+    def close(self):
+        for p in self.opened:
+            _lib.call("iron_ipc_close", p)
+        self.opened = []
+        self.recv = None
+        for b in self._bufs:
+            b.tensor = None
+            b.free()
+
+
 class TPDecoderBlock:
     def __init__(self, shape: BlockShape, tp: int, rank: int, batch: int, max_seq: int, seed: int = 0,
-                 group=None, pdl: bool = True, keep_full: bool = False):
+                 group=None, pdl: bool = True, keep_full: bool = False, fused_allreduce: bool = False):
         self.s, self.tp, self.rank, self.B, self.L = shape, tp, rank, batch, max_seq
         self.group = group
         self.dev = torch.device("cuda", torch.cuda.current_device())
@@ -64,6 +142,14 @@ class TPDecoderBlock:
         wsb = _lib.load().iron_attn_decode_workspace_bytes_d(B, self.hq, self.hk, max_seq, hd)
         self.ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
         self.graph = None
+        # the two all-reduces inside the o_proj / down_proj GEMVs (peer stores over
+        # NVLink) instead of NCCL calls
+        self.fused = bool(fused_allreduce) and tp > 1
+        if self.fused:
+            if B > 8:
+                raise ValueError("the fused all-reduce GEMV serves batch <= 8")
+            self.site_o = _PeerSite(shape.hidden, B, tp, rank, group)
+            self.site_d = _PeerSite(shape.hidden, B, tp, rank, group)
 
     # -- bytes / launches ---------------------------------------------------------------
     def weight_bytes(self) -> int:
@@ -91,15 +177,23 @@ class TPDecoderBlock:
              p(self.lens), B, self.hq, self.hk, hd, kv_b, kv_h, f, stream)
         call("iron_attn_decode", p(self.q), p(self.kc), p(self.vc), p(self.lens), p(self.attn), B, self.hq,
              self.hk, hd, self.L, kv_b, kv_h, 1.0 / math.sqrt(hd), p(self.ws), self.ws.numel(), f, stream)
-        call("iron_gemv_int4g32", p(self.w["o"]), p(self.attn), p(self.h), E, self.dims["o"][1], B,
-             p(self.x) if lead else None, f, stream)
-        self._allreduce(self.h)
+        if self.fused:
+            call("iron_gemv_int4g32_allreduce", p(self.w["o"]), p(self.attn), p(self.h), E, self.dims["o"][1], B,
+                 p(self.x), ctypes.addressof(self.site_o.peers), f, stream)
+        else:
+            call("iron_gemv_int4g32", p(self.w["o"]), p(self.attn), p(self.h), E, self.dims["o"][1], B,
+                 p(self.x) if lead else None, f, stream)
+            self._allreduce(self.h)
         call("iron_rmsnorm", p(self.h), None, None, p(self.n2), p(self.xn), B, E, s.eps, f, stream)
         call("iron_gemv_int4g32", p(self.w["gu"]), p(self.xn), p(self.act), self.dims["gu"][0], E, B, None,
              f | _lib.IRON_FLAG_SWIGLU, stream)
-        call("iron_gemv_int4g32", p(self.w["d"]), p(self.act), p(self.x), E, self.dims["d"][1], B,
-             p(self.h) if lead else None, f, stream)
-        self._allreduce(self.x)
+        if self.fused:
+            call("iron_gemv_int4g32_allreduce", p(self.w["d"]), p(self.act), p(self.x), E, self.dims["d"][1], B,
+                 p(self.h), ctypes.addressof(self.site_d.peers), f, stream)
+        else:
+            call("iron_gemv_int4g32", p(self.w["d"]), p(self.act), p(self.x), E, self.dims["d"][1], B,
+                 p(self.h) if lead else None, f, stream)
+            self._allreduce(self.x)
 
     def step(self):
         """x <- block(x) for every sequence at its position pos[b] (caches updated)."""
@@ -125,7 +219,15 @@ class TPDecoderBlock:
         self.x.copy_(saved)
         torch.cuda.synchronize()
 
+    def check_status(self):
+        if self.fused and int(self.site_o.status[0] | self.site_d.status[0]) != 0:
+            raise RuntimeError("fused all-reduce: a wait for a peer's tile timed out")
+
     def release(self):
-        """Drop the captured graph (it holds NCCL work; release before destroying the group)."""
+        """Drop the captured graph (it may hold NCCL work; release before destroying the
+        group) and unmap the peers' buffers."""
         self.graph = None
         torch.cuda.synchronize()
+        if self.fused:
+            self.site_o.close()
+            self.site_d.close()

@@ -19,6 +19,7 @@
 // memory (and distributed shared memory across a cluster), so results are
 // bitwise deterministic.
 #include <cooperative_groups.h>
+#include <cstring>
 
 #include "common.cuh"
 #include "s4.cuh"
@@ -39,6 +40,106 @@ __device__ __forceinline__ S4Range s4_split(int b, int e, int parts, int i) {
   return {b + i * n / parts, b + (i + 1) * n / parts};
 }
 
+constexpr int kS4ArgmaxSlots = 32;  // argmax key slots per vector
+
+// Tensor-parallel all-reduce fused into the GEMV epilogue (row-parallel layers):
+// every rank pushes its fp32 partial of each finished 16-row tile into every rank's
+// receive buffer over NVLink (peer stores of value + flag), waits for all sources'
+// values of the tile in its own buffer and sums them in source order -- so every rank
+// holds the bitwise-identical sum without a separate collective. recv[r]: rank r's
+// buffer (peer-mapped for r != rank).
+constexpr int kS4MaxWorld = 8;
+struct S4AllReduce {
+  int world, rank;
+  float *recv[kS4MaxWorld];       // [world (source), N, n_vec] x (fp32 value, flag) 8-byte slots, zero between uses
+  unsigned *status;               // non-zero: a wait for a peer's tile gave up
+};
+
+struct S4Epi {
+  const uint16_t *residual;
+  int swiglu;
+  const uint16_t *norm_w;
+  float eps;
+  unsigned long long *amax;
+  S4AllReduce ar;  // ar.world > 1: all-reduce the output over the ranks first
+};
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+  unsigned r;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(r) : "l"(p) : "memory");
+  return r;
+}
+__device__ __forceinline__ uint64_t s4_now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Warp 0 of the CTA finishing `tile`: exchange the tile's partial (v, rows gid / gid + 8,
+// vectors 2 tid + e) with the other ranks and return the sum over ranks in v. Every value
+// travels as one 8-byte store of (fp32 bits, flag 1) into the receiver's slot [source,
+// row, vector] -- a single NVLink transaction, so the receiver sees the value whenever it
+// sees the flag and no memory fence is needed; the receiver clears the slot after use
+// (the next write to it comes one all-reduce site later, after this rank has passed it).
+__device__ __forceinline__ void st_pair_sys(unsigned long long *p, float v) {
+  const unsigned long long w = (1ull << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_pair_sys(const unsigned long long *p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+
+__device__ __forceinline__ void s4_allreduce_tile(float (&v)[4], int tile, int N, int n_vec, const S4AllReduce &ar) {
+  const int lane = threadIdx.x & 31, gid = lane >> 2, tid = lane & 3;
+  for (int dst = 0; dst < ar.world; ++dst) {
+    unsigned long long *rb = reinterpret_cast<unsigned long long *>(ar.recv[dst]) +
+                             static_cast<int64_t>(ar.rank) * N * n_vec;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int row = tile * 16 + gid + ((e >> 1) << 3), vv = tid * 2 + (e & 1);
+      if (vv < n_vec) st_pair_sys(rb + static_cast<int64_t>(row) * n_vec + vv, v[e]);
+    }
+  }
+  unsigned long long *mine = reinterpret_cast<unsigned long long *>(ar.recv[ar.rank]);
+  bool gave_up = false;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int row = tile * 16 + gid + ((e >> 1) << 3), vv = tid * 2 + (e & 1);
+    float sum = 0.f;
+    if (vv < n_vec) {
+      for (int src = 0; src < ar.world; ++src) {
+        unsigned long long *slot = mine + (static_cast<int64_t>(src) * N + row) * n_vec + vv;
+        unsigned long long w = ld_pair_sys(slot);
+        uint64_t start = 0;
+        for (uint32_t i = 0; (w >> 32) == 0ull && !gave_up; ++i) {
+          if ((i & 63u) == 0u) {
+            if (ld_acquire_sys(ar.status) != 0u) gave_up = true;  // an earlier wait gave up: fail fast
+            const uint64_t t = s4_now_ns();
+            if (start == 0) start = t;
+            else if (t - start > 1000000000ull) {  // 1 s without the peer's value
+              atomicOr(ar.status, 1u);
+              gave_up = true;
+            }
+          }
+          w = ld_pair_sys(slot);
+        }
+        sum += __uint_as_float(static_cast<unsigned>(w & 0xffffffffull));
+        *slot = 0ull;
+      }
+    }
+    v[e] = sum;
+  }
+}
+
+__device__ __forceinline__ unsigned long long s4_argmax_key(float v, int row) {
+  unsigned u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  if (v != v) u = 0u;  // NaN never wins
+  return (static_cast<unsigned long long>(u) << 32) | static_cast<unsigned>(~row);
+}
+
 // Store a finished 16-row tile (C-fragment layout v). swiglu == 0: rows as they
 // are, plus the residual. swiglu == 1: the tile's rows 0-7 are gate rows and
 // 8-15 the matching up rows of output rows 8*tile..8*tile+7 (y has N/2 columns):
@@ -48,23 +149,6 @@ __device__ __forceinline__ S4Range s4_split(int b, int e, int parts, int i) {
 // a residual add or the SwiGLU of interleaved gate/up rows on the output, and the
 // greedy argmax of each output vector (amax != null: 64-bit keys, larger value then
 // lower row wins).
-constexpr int kS4ArgmaxSlots = 32;  // argmax key slots per vector
-
-struct S4Epi {
-  const uint16_t *residual;
-  int swiglu;
-  const uint16_t *norm_w;
-  float eps;
-  unsigned long long *amax;
-};
-
-__device__ __forceinline__ unsigned long long s4_argmax_key(float v, int row) {
-  unsigned u = __float_as_uint(v);
-  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  if (v != v) u = 0u;  // NaN never wins
-  return (static_cast<unsigned long long>(u) << 32) | static_cast<unsigned>(~row);
-}
-
 template <int NT>
 __device__ __forceinline__ void s4_store(const float (&v)[NT][4], int tile, int N, int n_vec,
                                          uint16_t *__restrict__ y,
@@ -333,6 +417,9 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
           for (int r = 1; r < CS; ++r) v[t][e] += slot0[((r * NT + t) * 4 + e) * 32 + lane];
     }
   }
+  if constexpr (NT == 1) {
+    if (warp == 0 && epi.ar.world > 1) s4_allreduce_tile(v[0], tile, N, n_vec, epi.ar);
+  }
   if (warp == 0) s4_store<NT>(v, tile, N, n_vec, y, epi.residual, epi.swiglu, epi.amax);
 }
 
@@ -507,7 +594,8 @@ extern "C" int iron_gemv_int4g32_ex(const uint8_t *packed, const uint16_t *x, ui
     if (n_vec > 8 || K > 2048) return IRON_ERR_SHAPE;  // the fused prologue's shared slice and registers
     if (!aligned16(norm_weight)) return IRON_ERR_ALIGN;
   }
-  S4Epi epi{residual, swiglu, norm_weight, eps, argmax_keys};
+  S4Epi epi{residual, swiglu, norm_weight, eps, argmax_keys, {}};
+  epi.ar.world = 1;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (n_vec <= 8) return launch_s4_tile_cs<1>(packed, x, y, N, K, n_vec, epi, pdl, s);
 #ifdef IRON_S4_ONLY_NT1
@@ -517,6 +605,64 @@ extern "C" int iron_gemv_int4g32_ex(const uint8_t *packed, const uint16_t *x, ui
   if (n_vec <= 32) return launch_s4_tile_cs<4>(packed, x, y, N, K, n_vec, epi, pdl, s);
   return launch_s4_tile_cs<8>(packed, x, y, N, K, n_vec, epi, pdl, s);
 #endif
+}
+
+extern "C" int iron_gemv_int4g32_allreduce(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,
+                                           int n_vec, const uint16_t *residual, const void *peers,
+                                           unsigned flags, void *stream) {
+  if (!packed || !x || !y || !peers) return IRON_ERR_NULL;
+  if (N <= 0 || K <= 0 || n_vec <= 0 || n_vec > 8 || K % 128 || N % 16) return IRON_ERR_SHAPE;
+  if (!aligned16(packed) || !aligned16(x)) return IRON_ERR_ALIGN;
+  if (flags & IRON_FLAG_SWIGLU) return IRON_ERR_ARG;
+  S4Epi epi{residual, 0, nullptr, 0.f, nullptr, {}};
+  std::memcpy(&epi.ar, peers, sizeof(S4AllReduce));
+  if (epi.ar.world < 1 || epi.ar.world > kS4MaxWorld || epi.ar.rank < 0 || epi.ar.rank >= epi.ar.world ||
+      !epi.ar.status)
+    return IRON_ERR_ARG;
+  for (int r = 0; r < epi.ar.world; ++r)
+    if (!epi.ar.recv[r]) return IRON_ERR_NULL;
+  return launch_s4_tile_cs<1>(packed, x, y, N, K, n_vec, epi, (flags & IRON_FLAG_PDL) != 0,
+                              static_cast<cudaStream_t>(stream));
+}
+
+// CUDA IPC plumbing for the peer buffers of the fused all-reduce. A handle maps the
+// START of a cudaMalloc allocation, so the buffers come from iron_ipc_alloc (their own
+// zero-filled allocation), not from a caching allocator's pool.
+extern "C" int iron_ipc_alloc(size_t bytes, void **dev_ptr_out) {
+  if (!dev_ptr_out) return IRON_ERR_NULL;
+  if (bytes == 0) return IRON_ERR_SHAPE;
+  if (cudaMalloc(dev_ptr_out, bytes) != cudaSuccess) return launch_status();
+  if (cudaMemset(*dev_ptr_out, 0, bytes) != cudaSuccess) return launch_status();
+  return IRON_OK;
+}
+
+extern "C" int iron_ipc_free(void *dev_ptr) {
+  if (!dev_ptr) return IRON_ERR_NULL;
+  if (cudaFree(dev_ptr) != cudaSuccess) return launch_status();
+  return IRON_OK;
+}
+
+extern "C" int iron_ipc_handle(const void *dev_ptr, void *handle_out) {
+  if (!dev_ptr || !handle_out) return IRON_ERR_NULL;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, const_cast<void *>(dev_ptr)) != cudaSuccess) return launch_status();
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  std::memcpy(handle_out, &h, sizeof(h));
+  return IRON_OK;
+}
+
+extern "C" int iron_ipc_open(const void *handle, void **dev_ptr_out) {
+  if (!handle || !dev_ptr_out) return IRON_ERR_NULL;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  if (cudaIpcOpenMemHandle(dev_ptr_out, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return launch_status();
+  return IRON_OK;
+}
+
+extern "C" int iron_ipc_close(void *dev_ptr) {
+  if (!dev_ptr) return IRON_ERR_NULL;
+  if (cudaIpcCloseMemHandle(dev_ptr) != cudaSuccess) return launch_status();
+  return IRON_OK;
 }
 
 extern "C" int iron_gemv_int4g32(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N,

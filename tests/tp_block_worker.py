@@ -32,27 +32,36 @@ def main():
     vc = torch.randn(B, shape.n_kv, L, shape.head_dim, device="cuda", generator=g).to(torch.bfloat16)
     pos = torch.tensor([5, 40], dtype=torch.int32, device="cuda")
 
-    def run(tp, r, group, graph):
-        blk = TPDecoderBlock(shape, tp, r, B, L, seed=13, group=group)
+    def run(tp, r, group, graph, fused=False):
+        blk = TPDecoderBlock(shape, tp, r, B, L, seed=13, group=group, fused_allreduce=fused)
         blk.kc.copy_(kc[:, blk.sh.k0:blk.sh.k1])
         blk.vc.copy_(vc[:, blk.sh.k0:blk.sh.k1])
         blk.x.copy_(x0)
         blk.pos.copy_(pos)
         if graph:
             blk.capture()
-        blk.step()
+        for _ in range(3):  # the peer buffers and flags are reused step after step
+            blk.x.copy_(x0)
+            blk.pos.copy_(pos)
+            blk.step()
         torch.cuda.synchronize()
+        blk.check_status()
         out = blk.x.clone()
         kcs = blk.kc.clone()
         blk.release()
         return out, kcs, blk.sh
 
     failures = 0
+    out_1, kc_1, _ = run(1, 0, None, False)
     for graph in (False, True):
-        out_tp, kc_tp, sh = run(world, rank, None, graph)
-        out_1, kc_1, _ = run(1, 0, None, False)
-        failures += _close(out_tp, out_1)
-        failures += _close(kc_tp, kc_1[:, sh.k0:sh.k1])
+        for fused in (False, True):
+            out_tp, kc_tp, sh = run(world, rank, None, graph, fused)
+            failures += _close(out_tp, out_1)
+            failures += _close(kc_tp, kc_1[:, sh.k0:sh.k1])
+            if fused:  # every rank holds the same sum
+                ref = out_tp.clone()
+                dist.broadcast(ref, 0)
+                failures += int((ref != out_tp).sum())
     other = torch.tensor([failures], device="cuda")
     dist.all_reduce(other)
     dist.destroy_process_group()
