@@ -64,6 +64,8 @@ def _args():
     ap.add_argument("--n-vec", type=int, default=1, help="vectors per GEMV call (int4_gemv)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
+    ap.add_argument("--allreduce", choices=["auto", "fused", "nccl"], default="auto",
+                    help="tp_block: the all-reduce inside the GEMVs (fused, batch <= 8) or NCCL calls")
     a = ap.parse_args()
     if a.steps is None:
         a.steps = {"decode": 256, "gemm": 200, "tp_block": 2000}.get(a.workload, 20000)
@@ -872,7 +874,9 @@ def run_tp_block(args, world, rank, local):
 
     shape, B = BlockShape(), args.batch
     ctx = PREFIX
-    fused = world > 1 and B <= 8
+    fused = world > 1 and B <= 8 and args.allreduce != "nccl"
+    if args.allreduce == "fused" and not fused:
+        raise SystemExit("--allreduce fused needs more than one GPU and batch <= 8")
     blk = TPDecoderBlock(shape, world, rank, B, ctx + 16, seed=13, pdl=not args.no_pdl, fused_allreduce=fused)
     g = torch.Generator(device="cuda")
     g.manual_seed(7 + rank)

@@ -165,10 +165,19 @@ class TPDecoderBlock:
             dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
 
     def _launch(self, stream: int):
+        self._attention_half(stream)
+        if not self.fused:
+            self._allreduce(self.h)
+        self._mlp_half(stream)
+        if not self.fused:
+            self._allreduce(self.x)
+
+    def _attention_half(self, stream: int):
+        """RMSNorm -> QKV -> RoPE + KV append -> attention -> o_proj: h (this rank's
+        partial, rank 0's holding the residual; the sum over ranks when fused)."""
         s, B, f = self.s, self.B, self.flags
         call, p = _lib.call, (lambda t: t.data_ptr())
         hd, E = s.head_dim, s.hidden
-        lead = self.rank == 0
         call("iron_rmsnorm", p(self.x), None, None, p(self.n1), p(self.xn), B, E, s.eps, f, stream)
         call("iron_gemv_int4g32", p(self.w["qkv"]), p(self.xn), p(self.qkv), self.dims["qkv"][0], E, B, None, f,
              stream)
@@ -182,8 +191,13 @@ class TPDecoderBlock:
                  p(self.x), ctypes.addressof(self.site_o.peers), f, stream)
         else:
             call("iron_gemv_int4g32", p(self.w["o"]), p(self.attn), p(self.h), E, self.dims["o"][1], B,
-                 p(self.x) if lead else None, f, stream)
-            self._allreduce(self.h)
+                 p(self.x) if self.rank == 0 else None, f, stream)
+
+    def _mlp_half(self, stream: int):
+        """RMSNorm -> gate/up + SwiGLU -> down_proj: x (partial / sum as above)."""
+        s, B, f = self.s, self.B, self.flags
+        call, p = _lib.call, (lambda t: t.data_ptr())
+        E = s.hidden
         call("iron_rmsnorm", p(self.h), None, None, p(self.n2), p(self.xn), B, E, s.eps, f, stream)
         call("iron_gemv_int4g32", p(self.w["gu"]), p(self.xn), p(self.act), self.dims["gu"][0], E, B, None,
              f | _lib.IRON_FLAG_SWIGLU, stream)
@@ -192,8 +206,7 @@ class TPDecoderBlock:
                  p(self.h), ctypes.addressof(self.site_d.peers), f, stream)
         else:
             call("iron_gemv_int4g32", p(self.w["d"]), p(self.act), p(self.x), E, self.dims["d"][1], B,
-                 p(self.h) if lead else None, f, stream)
-            self._allreduce(self.x)
+                 p(self.h) if self.rank == 0 else None, f, stream)
 
     def step(self):
         """x <- block(x) for every sequence at its position pos[b] (caches updated)."""

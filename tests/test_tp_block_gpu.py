@@ -69,6 +69,45 @@ def test_attention_head_dim_128_ragged():
     assert_close(out.cpu(), ops.attn_decode(q, k, v, lens.tolist()), 2e-2, 1e-2)
 
 
+def _block_inputs(blk, x0, kc, vc, pos):
+    blk.kc.copy_(kc[:, blk.sh.k0:blk.sh.k1])
+    blk.vc.copy_(vc[:, blk.sh.k0:blk.sh.k1])
+    blk.x.copy_(x0)
+    blk.pos.copy_(pos)
+
+
+@pytest.mark.parametrize("tp", [2, 4, 8])
+def test_block_tp_emulated_on_one_gpu(tp):
+    """Every rank's shard run on one GPU, the two all-reduces done by torch between
+    the halves (fp32 sum of the bf16 partials, rounded once): the sharded kernels
+    (QKV / gate-up rows, o / down columns, local heads and kv heads) against tp = 1."""
+    shape, B, L = BlockShape(), 2, 64
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x0 = torch.randn(B, shape.hidden, device="cuda", generator=g).to(torch.bfloat16)
+    kc = torch.randn(B, shape.n_kv, L, shape.head_dim, device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn(B, shape.n_kv, L, shape.head_dim, device="cuda", generator=g).to(torch.bfloat16)
+    pos = torch.tensor([5, 40], dtype=torch.int32, device="cuda")
+    one = TPDecoderBlock(shape, 1, 0, B, L, seed=13)
+    _block_inputs(one, x0, kc, vc, pos)
+    one.step()
+    blks = [TPDecoderBlock(shape, tp, r, B, L, seed=13) for r in range(tp)]
+    stream = torch.cuda.current_stream().cuda_stream
+    for b in blks:
+        _block_inputs(b, x0, kc, vc, pos)
+        b._attention_half(stream)
+    h = torch.stack([b.h.float() for b in blks]).sum(0).to(torch.bfloat16)
+    for b in blks:
+        b.h.copy_(h)
+        b._mlp_half(stream)
+    out = torch.stack([b.x.float() for b in blks]).sum(0).to(torch.bfloat16)
+    torch.cuda.synchronize()
+    assert_close(out.cpu(), one.x.cpu(), 2e-2, 2e-2, what=f"tp={tp} block output")
+    for b in blks:
+        for bb, p in enumerate(pos.tolist()):
+            assert_close(b.kc[bb, :, p].cpu(), one.kc[bb, b.sh.k0:b.sh.k1, p].cpu(), 2e-2, 2e-2, what="k row")
+            assert_close(b.vc[bb, :, p].cpu(), one.vc[bb, b.sh.k0:b.sh.k1, p].cpu(), 2e-2, 2e-2, what="v row")
+
+
 @pytest.mark.parametrize("tp", [2, 4, 8])
 def test_block_tensor_parallel_matches_single_gpu(tp):
     if torch.cuda.device_count() < tp:

@@ -14,10 +14,15 @@ from iron_b200.applications.llama3_8b.sharding import BlockShape  # noqa: E402
 from iron_b200.applications.llama3_8b.tp_block import TPDecoderBlock  # noqa: E402
 
 
-def _close(a, b, rtol=2e-2, atol=2e-2):
+def _close(a, b, what, rtol=2e-2, atol=2e-2):
     a, b = a.float(), b.float()
     bad = ~((a - b).abs() <= torch.maximum(torch.full_like(a, atol), rtol * (a.abs() + b.abs())))
-    return int(bad.sum())
+    n = int(bad.sum())
+    if n:
+        i = int(bad.flatten().nonzero()[0])
+        print(f"rank {os.environ['RANK']} {what}: {n} mismatches, first at flat index {i}: "
+              f"{float(a.flatten()[i])} vs {float(b.flatten()[i])}", flush=True)
+    return n
 
 
 def main():
@@ -56,12 +61,16 @@ def main():
     for graph in (False, True):
         for fused in (False, True):
             out_tp, kc_tp, sh = run(world, rank, None, graph, fused)
-            failures += _close(out_tp, out_1)
-            failures += _close(kc_tp, kc_1[:, sh.k0:sh.k1])
+            what = f"graph={graph} fused={fused}"
+            failures += _close(out_tp, out_1, what + " out")
+            failures += _close(kc_tp, kc_1[:, sh.k0:sh.k1], what + " k cache")
             if fused:  # every rank holds the same sum
                 ref = out_tp.clone()
                 dist.broadcast(ref, 0)
-                failures += int((ref != out_tp).sum())
+                n = int((ref != out_tp).sum())
+                if n:
+                    print(f"rank {rank} {what}: {n} elements differ from rank 0's", flush=True)
+                failures += n
     other = torch.tensor([failures], device="cuda")
     dist.all_reduce(other)
     dist.destroy_process_group()
