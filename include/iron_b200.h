@@ -292,7 +292,8 @@ int iron_attn_decode_qkv(const uint16_t *qkv, const int32_t *pos, const float *l
  * then v), pos int32 [B] (tokens already cached), lut fp32 [ctx, D] interleaved
  * cos/sin. Writes q_out bf16 [B, Hq, D] (two-halves RoPE), k/v into cache slot
  * pos[b] (same strides as iron_attn_decode) and lens[b] = pos[b] + 1 (if lens).
- * iron_embed: x[b] = table[tokens[b]] (bf16 rows of E). iron_argmax: first index
+ * iron_embed: x[b] = table[tokens[b]] (bf16 rows of E; table has V rows, and a token
+ * outside [0, V) gives a zero row instead of a read past the table). iron_argmax: first index
  * of each row's maximum into out[b]; if pos != NULL, pos[b] += 1 afterwards (so a
  * replayed decode graph feeds its own output to the next step).
  */
@@ -300,7 +301,7 @@ int iron_rope_kv_append(const uint16_t *qkv, const int32_t *pos, const float *lu
                         uint16_t *q_out, uint16_t *k_cache, uint16_t *v_cache, int32_t *lens,
                         int B, int Hq, int Hkv, int D, int64_t kv_batch_stride,
                         int64_t kv_head_stride, unsigned flags, void *stream);
-int iron_embed(const int32_t *tokens, const uint16_t *table, uint16_t *x, int B, int E,
+int iron_embed(const int32_t *tokens, const uint16_t *table, uint16_t *x, int B, int E, int V,
                unsigned flags, void *stream);
 int iron_argmax(const uint16_t *logits, int32_t *out, int B, int V, int32_t *pos, unsigned flags,
                 void *stream);

@@ -54,7 +54,7 @@ SIGNATURES: dict[str, list] = {
                                  c_float, c_uint, P],
     "iron_rope_kv_append": [P, P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int64, c_int64,
                             c_uint, P],
-    "iron_embed": [P, P, P, c_int, c_int, c_uint, P],
+    "iron_embed": [P, P, P, c_int, c_int, c_int, c_uint, P],
     "iron_argmax": [P, P, c_int, c_int, P, c_uint, P],
     "iron_gemm_bf16": [P, P, P, c_int, c_int, c_int, c_int64, c_int64, c_int64, P, c_int64, c_int, c_int,
                        c_float, c_float, c_int, c_uint, P],

@@ -155,13 +155,14 @@ class LlamaDecodeEngine:
         # where RMSNorm runs inside the following GEMV ("none", "layers": the QKV and
         # gate/up GEMVs, "all": also the lm-head); only for B <= 8. Defaults measured on
         # B200 (one process, interleaved, 8-warp GEMV tiles): the fused prologue costs
-        # 24 us per step at B = 1 and 172 us at B = 8; RoPE inside attention costs 33 us
-        # at B = 1 and saves 62 us at B = 8, 305 us at B = 64.
+        # 28 us per step at B = 1 and 172 us at B = 8; RoPE inside attention (whose cached
+        # K / V rows are then requested before the wait for the QKV projection) saves
+        # 44 us at B = 1, 62 us at B = 8 and 305 us at B = 64.
         self.fuse_norm = fuse_norm if fuse_norm is not None else "none"
         if self.fuse_norm != "none" and B > 8:
             raise ValueError("the fused RMSNorm prologue serves B <= 8")
         # RoPE + KV append inside the attention kernel (else the rope_kv_append kernel)
-        self.fuse_rope = fuse_rope if fuse_rope is not None else B > 1
+        self.fuse_rope = fuse_rope if fuse_rope is not None else True
         if self.persistent:
             if not fits:
                 raise ValueError("the persistent decode step needs the Llama-3.2-1B layer shape and batch <= 2")
@@ -218,7 +219,7 @@ class LlamaDecodeEngine:
         E, Hd, L = s.emb_dim, s.head_dim, self.L
         kv_b, kv_h = s.n_kv_groups * L * Hd, L * Hd
         fuse_norm = self.fuse_norm != "none"
-        call("iron_embed", p(self.tokens), p(self.embed_table), p(self.x), B, E, f, stream)
+        call("iron_embed", p(self.tokens), p(self.embed_table), p(self.x), B, E, s.vocab_size, f, stream)
         for li, lay in enumerate(self.layers):
             kc, vc = self.kc[li], self.vc[li]
             if fuse_norm:
@@ -293,7 +294,7 @@ class LlamaDecodeEngine:
         kv_h = L * Hd
         qst = (ctypes.c_int64 * 3)(0, Hd, Hq * Hd)
         kvst = (ctypes.c_int64 * 3)(0, kv_h, Hd)
-        call("iron_embed", p(pf["tok"]), p(self.embed_table), p(pf["x"]), S, E, f, stream)
+        call("iron_embed", p(pf["tok"]), p(self.embed_table), p(pf["x"]), S, E, s.vocab_size, f, stream)
         for li, lay in enumerate(self.layers):
             kc = self.kc[li, seq]
             vc = self.vc[li, seq]

@@ -26,7 +26,7 @@ namespace iron {
 // 128 (the Llama-3-8B block).
 constexpr int kAWarps = 4;
 constexpr int kABlk = 16;     // tokens per warp step
-constexpr int kAMinChunk = 256;
+constexpr int kAMinChunk = 256;  // tokens per split at least (B200, batch 1: 64 / 128 / 512 tokens measured slower)
 
 struct AttnArgs {
   const uint16_t *q;    // [B, Hq, D]
@@ -37,6 +37,7 @@ struct AttnArgs {
   float *ws;            // [B, Hq, splits, 2 + D] partial (max, sum, o)
   int64_t bstride, hstride;
   int Hq, Hkv, splits, chunk;
+  int maxlen;           // cache rows per (sequence, kv head): lengths / positions beyond it do nothing
   float scale_log2;     // softmax scale * log2(e)
   // fused decode form: q, the new k and v come from the QKV projection `qkv`
   // [B, (Hq + 2 Hkv) D] at position pos[b] (RoPE from `lut`, the new rows appended to
@@ -78,13 +79,20 @@ attn_decode_kernel(AttnArgs a) {
   __shared__ __align__(16) uint16_t qbuf[kFused ? 16 * kAD : 8];
   __shared__ __align__(16) uint16_t knew[kFused ? kAD : 8], vnew[kFused ? kAD : 8];
 
-  pdl_wait();
+  pdl_launch_dependents();  // at entry: the next kernel may start its weight / cache loads
   int len, p = -1;
+  bool valid = true;
   if constexpr (kFused) {
+    // pos is final before this launch (written by the previous step, which the step's
+    // first kernel waits for), so it and the cached rows below it are read before the
+    // wait for the QKV projection
     p = a.pos[b];
-    len = p + 1;
+    valid = p >= 0 && p < a.maxlen;
+    if (!valid) p = 0;
+    len = valid ? p + 1 : 0;
   } else {
-    len = a.lens[b];
+    pdl_wait();
+    len = min(max(a.lens[b], 0), a.maxlen);
   }
   const int t_begin = split * a.chunk;
   const int t_end = min(len, t_begin + a.chunk);
@@ -122,8 +130,20 @@ attn_decode_kernel(AttnArgs a) {
   uint4 kr[2][kDB], vr[kVR];
   int blk = t_begin + warp * kABlk;
   // the first block's cache rows are requested before anything else (they do not
-  // depend on the QKV projection)
+  // depend on the QKV projection; the fused form's new row p comes later)
   if (blk < t_end) load_block(blk, kr, vr, false);
+  if constexpr (kFused) {
+    // the split's further cached rows into L2, then wait for the QKV projection
+    const int r0 = t_begin + kAWarps * kABlk, r1 = min(t_end, p);
+    if (threadIdx.x == 0 && r1 > r0) {
+      const uint32_t bytes = static_cast<uint32_t>(r1 - r0) * kAD * 2;
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(kb + static_cast<int64_t>(r0) * kAD), "r"(bytes)
+                   : "memory");
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(vb + static_cast<int64_t>(r0) * kAD), "r"(bytes)
+                   : "memory");
+    }
+    pdl_wait();
+  }
 
   const uint16_t *qrow = a.q;
   int64_t qstride = kAD;
@@ -133,7 +153,7 @@ attn_decode_kernel(AttnArgs a) {
     const int half = kAD / 2;
     const uint16_t *src = a.qkv + static_cast<int64_t>(b) * (a.Hq + 2 * a.Hkv) * kAD;
     const float *ang = a.lut + static_cast<int64_t>(p) * kAD;
-    const bool owner = t_begin <= p && p < t_begin + a.chunk;
+    const bool owner = valid && t_begin <= p && p < t_begin + a.chunk;
     // zero rows g..15 of the q tile (no loads)
     for (int i = g * kAD + threadIdx.x * 8; i < 16 * kAD; i += 32 * kAWarps * 8)
       *reinterpret_cast<uint4 *>(qbuf + i) = make_uint4(0u, 0u, 0u, 0u);
@@ -311,7 +331,6 @@ attn_decode_kernel(AttnArgs a) {
     red_o[warp][gid + 8][8 * j + 2 * tid + 1] = o[j][3];
   }
   __syncthreads();
-  pdl_launch_dependents();
   for (int idx = threadIdx.x; idx < g * kAD; idx += blockDim.x) {
     const int r = idx / kAD, d = idx % kAD;
     float M = -INFINITY;
@@ -343,6 +362,7 @@ attn_decode_kernel(AttnArgs a) {
 // Merge the splits of each (sequence, q head): out = sum_s O_s 2^(m_s - M) / sum_s L_s 2^(m_s - M).
 template <int kAD>
 __global__ void attn_combine_kernel(const float *__restrict__ ws, uint16_t *__restrict__ out, int splits) {
+  pdl_launch_dependents();  // at entry: the next kernel may start its weight / cache loads
   pdl_wait();
   const int64_t hq = blockIdx.x;
   const int d = threadIdx.x;
@@ -361,7 +381,6 @@ __global__ void attn_combine_kernel(const float *__restrict__ ws, uint16_t *__re
     }
   }
   out[hq * kAD + d] = float_to_bf16_bits(L > 0.f ? O / L : 0.f);
-  pdl_launch_dependents();
 }
 
 // Split count: enough CTAs for two waves of 148 SMs, chunks of >= 256 tokens.
@@ -452,6 +471,7 @@ extern "C" int iron_attn_decode(const uint16_t *q, const uint16_t *k_cache, cons
   a.Hkv = Hkv;
   a.splits = attn_splits(B, Hkv, Lmax, sm_count());
   a.chunk = ((Lmax + a.splits - 1) / a.splits + kAWarps * kABlk - 1) / (kAWarps * kABlk) * (kAWarps * kABlk);
+  a.maxlen = Lmax;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.ws = static_cast<float *>(workspace);
   if (a.splits > 1) {
@@ -514,6 +534,7 @@ extern "C" int iron_attn_decode_qkv(const uint16_t *qkv, const int32_t *pos, con
   a.Hkv = Hkv;
   a.splits = attn_splits(B, Hkv, Lmax, sm_count());
   a.chunk = ((Lmax + a.splits - 1) / a.splits + kAWarps * kABlk - 1) / (kAWarps * kABlk) * (kAWarps * kABlk);
+  a.maxlen = Lmax;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.qkv = qkv;
   a.pos = pos;

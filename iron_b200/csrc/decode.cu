@@ -17,6 +17,7 @@ __global__ void rope_kv_append_kernel(const uint16_t *__restrict__ qkv, const in
                                       uint16_t *__restrict__ k_cache, uint16_t *__restrict__ v_cache,
                                       int *__restrict__ lens, int Hq, int Hkv, int D,
                                       int64_t kv_bstride, int64_t kv_hstride) {
+  pdl_launch_dependents();  // at entry: the next kernel may start its weight / cache loads
   pdl_wait();
   const int b = blockIdx.x;
   const int p = pos[b];
@@ -48,16 +49,22 @@ __global__ void rope_kv_append_kernel(const uint16_t *__restrict__ qkv, const in
     }
   }
   if (threadIdx.x == 0 && lens) lens[b] = p + 1;
-  pdl_launch_dependents();
 }
 
+// A token outside [0, V) (-1 is what iron_argmax_finalize gives when no logit was
+// written) reads nothing: its row becomes zeros.
 __global__ void embed_kernel(const int *__restrict__ tokens, const uint4 *__restrict__ table,
-                             uint4 *__restrict__ x, int row_vecs) {
+                             uint4 *__restrict__ x, int row_vecs, int V) {
+  // The first kernel of a decode step: it lets the step's kernels launch only after the
+  // previous step finished (its token / position update), because some of them read the
+  // positions before their own wait.
   pdl_wait();
+  pdl_launch_dependents();
   const int b = blockIdx.x;
   const int64_t t = tokens[b];
-  for (int i = threadIdx.x; i < row_vecs; i += blockDim.x) x[static_cast<int64_t>(b) * row_vecs + i] = table[t * row_vecs + i];
-  pdl_launch_dependents();
+  const bool ok = t >= 0 && t < V;
+  for (int i = threadIdx.x; i < row_vecs; i += blockDim.x)
+    x[static_cast<int64_t>(b) * row_vecs + i] = ok ? table[t * row_vecs + i] : make_uint4(0u, 0u, 0u, 0u);
 }
 
 // First index of the maximum of each row (NaN never wins).
@@ -65,6 +72,7 @@ __global__ void argmax_kernel(const uint16_t *__restrict__ logits, int *__restri
                               int *__restrict__ pos) {
   __shared__ float sv[32];
   __shared__ int si[32];
+  pdl_launch_dependents();  // at entry: the next kernel may start its weight / cache loads
   pdl_wait();
   const int64_t b = blockIdx.x;
   const uint16_t *row = logits + b * V;
@@ -110,7 +118,6 @@ __global__ void argmax_kernel(const uint16_t *__restrict__ logits, int *__restri
       if (pos) pos[b] += 1;  // the next decode step writes the next cache slot
     }
   }
-  pdl_launch_dependents();
 }
 
 }  // namespace iron
@@ -129,14 +136,14 @@ extern "C" int iron_rope_kv_append(const uint16_t *qkv, const int32_t *pos, cons
                 D, kv_batch_stride, kv_head_stride);
 }
 
-extern "C" int iron_embed(const int32_t *tokens, const uint16_t *table, uint16_t *x, int B, int E,
+extern "C" int iron_embed(const int32_t *tokens, const uint16_t *table, uint16_t *x, int B, int E, int V,
                           unsigned flags, void *stream) {
   if (!tokens || !table || !x) return IRON_ERR_NULL;
-  if (B <= 0 || E <= 0) return IRON_ERR_SHAPE;
+  if (B <= 0 || E <= 0 || V <= 0) return IRON_ERR_SHAPE;
   if (E % 8 || !aligned16(table) || !aligned16(x)) return IRON_ERR_ALIGN;
   return launch(embed_kernel, dim3(B), dim3(256), 0, static_cast<cudaStream_t>(stream),
                 (flags & IRON_FLAG_PDL) != 0, tokens, reinterpret_cast<const uint4 *>(table),
-                reinterpret_cast<uint4 *>(x), E / 8);
+                reinterpret_cast<uint4 *>(x), E / 8, V);
 }
 
 extern "C" int iron_argmax(const uint16_t *logits, int32_t *out, int B, int V, int32_t *pos,

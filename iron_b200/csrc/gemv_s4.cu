@@ -93,7 +93,12 @@ __device__ __forceinline__ unsigned long long ld_pair_sys(const unsigned long lo
 
 __device__ __forceinline__ void s4_allreduce_tile(float (&v)[4], int tile, int N, int n_vec, const S4AllReduce &ar) {
   const int lane = threadIdx.x & 31, gid = lane >> 2, tid = lane & 3;
-  for (int dst = 0; dst < ar.world; ++dst) {
+  // static indices into ar.recv (a runtime index would copy the parameter to local memory)
+  float *own = ar.recv[0];
+#pragma unroll
+  for (int dst = 0; dst < kS4MaxWorld; ++dst) {
+    if (dst >= ar.world) break;
+    if (dst == ar.rank) own = ar.recv[dst];
     unsigned long long *rb = reinterpret_cast<unsigned long long *>(ar.recv[dst]) +
                              static_cast<int64_t>(ar.rank) * N * n_vec;
 #pragma unroll
@@ -102,7 +107,7 @@ __device__ __forceinline__ void s4_allreduce_tile(float (&v)[4], int tile, int N
       if (vv < n_vec) st_pair_sys(rb + static_cast<int64_t>(row) * n_vec + vv, v[e]);
     }
   }
-  unsigned long long *mine = reinterpret_cast<unsigned long long *>(ar.recv[ar.rank]);
+  unsigned long long *mine = reinterpret_cast<unsigned long long *>(own);
   bool gave_up = false;
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
@@ -271,14 +276,17 @@ constexpr int s4_warps() { return NT <= 2 ? 8 : 4; }
 template <int NT>
 constexpr int s4_units() { return NT <= 2 ? 2 : 4; }
 
-template <int NT, int CS, bool kNorm = false>
+// kNorm: the RMSNorm prologue (n_vec <= 8) -- x normalised into shared memory first.
+// (Staging a plain x the same way measured slower on B200: 4.16 against 3.77 us per
+// config-2 launch; the per-unit L1 reads overlap better than one synchronised copy.)
+template <int NT, int CS, bool kNorm = false, bool kAR = false>
 __global__ void __launch_bounds__(32 * s4_warps<NT>())
 gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__restrict__ x,
                        uint16_t *__restrict__ y, int N, int K, int n_vec, S4Epi epi) {
   constexpr int kT4Warps = s4_warps<NT>();
   constexpr int kT4Units = s4_units<NT>();
   __shared__ float red[(kT4Warps + CS) * NT * 128];
-  extern __shared__ __align__(16) uint16_t xs_norm[];  // [n_vec, this CTA's k range] when normalising
+  extern __shared__ __align__(16) uint16_t xs_norm[];  // [n_vec, this CTA's k range] when staged
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tid = lane & 3;
   const int rank = (CS > 1) ? static_cast<int>(blockIdx.x % CS) : 0;
@@ -417,8 +425,8 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
           for (int r = 1; r < CS; ++r) v[t][e] += slot0[((r * NT + t) * 4 + e) * 32 + lane];
     }
   }
-  if constexpr (NT == 1) {
-    if (warp == 0 && epi.ar.world > 1) s4_allreduce_tile(v[0], tile, N, n_vec, epi.ar);
+  if constexpr (kAR && NT == 1) {
+    if (warp == 0) s4_allreduce_tile(v[0], tile, N, n_vec, epi.ar);
   }
   if (warp == 0) s4_store<NT>(v, tile, N, n_vec, y, epi.residual, epi.swiglu, epi.amax);
 }
@@ -469,8 +477,7 @@ static int launch_s4_tile(const uint8_t *packed, const uint16_t *x, uint16_t *y,
   cfg.stream = s;
   if (epi.norm_w) {
     // the CTA's normalised k range of every vector (<= 8 x 2048 bf16 = 32 KB)
-    const int cpt = K / 128;
-    const int klen_max = ((cpt + CS - 1) / CS) * 128;
+    const int klen_max = (((K / 128) + CS - 1) / CS) * 128;
     cfg.dynamicSmemBytes = static_cast<size_t>(n_vec) * klen_max * 2;
   }
   cudaLaunchAttribute attr[2];
@@ -489,9 +496,14 @@ static int launch_s4_tile(const uint8_t *packed, const uint16_t *x, uint16_t *y,
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  cudaError_t e = epi.norm_w
-                      ? cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, true>, packed, x, y, N, K, n_vec, epi)
-                      : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, false>, packed, x, y, N, K, n_vec, epi);
+  cudaError_t e;
+  if (epi.ar.world > 1) {
+    if constexpr (NT != 1) return IRON_ERR_SHAPE;
+    e = cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, true>, packed, x, y, N, K, n_vec, epi);
+  } else {
+    e = epi.norm_w ? cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, true>, packed, x, y, N, K, n_vec, epi)
+                   : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, false>, packed, x, y, N, K, n_vec, epi);
+  }
   if (e != cudaSuccess) {
     set_last_cuda_error(e);
     (void)cudaGetLastError();
@@ -674,6 +686,7 @@ extern "C" int iron_gemv_int4g32(const uint8_t *packed, const uint16_t *x, uint1
 // Greedy next token from the argmax keys an lm-head GEMV left: tokens[b], pos[b] += 1
 // (if pos), and the keys reset for the next step.
 __global__ void argmax_finalize_kernel(unsigned long long *keys, int *tokens, int *pos, int B) {
+  pdl_launch_dependents();  // at entry: the next kernel may start its weight / cache loads
   pdl_wait();
   const int b = blockIdx.x, lane = threadIdx.x;  // one warp per vector, a lane per slot
   unsigned long long k = keys[b * kS4ArgmaxSlots + lane];
@@ -687,7 +700,6 @@ __global__ void argmax_finalize_kernel(unsigned long long *keys, int *tokens, in
     tokens[b] = static_cast<int>(~static_cast<unsigned>(k & 0xffffffffull));
     if (pos) pos[b] += 1;
   }
-  pdl_launch_dependents();
 }
 
 extern "C" int iron_argmax_finalize(unsigned long long *keys, int32_t *tokens, int32_t *pos, int B, unsigned flags,

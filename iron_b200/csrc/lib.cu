@@ -39,4 +39,4 @@ extern "C" const char *iron_strerror(int status) {
 
 extern "C" int iron_last_cuda_error(void) { return iron::g_last_cuda_error; }
 
-extern "C" int iron_abi_version(void) { return (1 << 16) | 0; }
+extern "C" int iron_abi_version(void) { return (1 << 16) | 1; }

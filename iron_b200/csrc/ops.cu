@@ -49,6 +49,7 @@ __global__ void rmsnorm_kernel(const uint16_t *__restrict__ x, const uint16_t *_
                                uint16_t *__restrict__ x_out, const uint16_t *__restrict__ w,
                                uint16_t *__restrict__ y, int cols, float eps) {
   __shared__ float scratch[32];
+  pdl_launch_dependents();  // at entry: the next kernel may start its weight / cache loads
   pdl_wait();
   const int64_t row = blockIdx.x;
   const uint16_t *xr = x + row * cols;
@@ -90,7 +91,6 @@ __global__ void rmsnorm_kernel(const uint16_t *__restrict__ x, const uint16_t *_
         }
         *reinterpret_cast<uint4 *>(yr + c) = pack8(o);
       }
-      pdl_launch_dependents();
       return;
     }
     ss = 0.f;  // row longer than the register cache: fall through to the scalar path
@@ -113,7 +113,6 @@ __global__ void rmsnorm_kernel(const uint16_t *__restrict__ x, const uint16_t *_
     if (w) o *= bf16_bits_to_float(w[c]);
     yr[c] = float_to_bf16_bits(o);
   }
-  pdl_launch_dependents();
 }
 
 // ---------------------------------------------------------------------------
@@ -126,6 +125,7 @@ __global__ void rope_kernel(const uint16_t *__restrict__ x, const uint16_t *__re
                             const float *__restrict__ angles_f32, uint16_t *__restrict__ y,
                             int rows, int cols, int rows_per_angle, const int *__restrict__ pos,
                             int method) {
+  pdl_launch_dependents();  // at entry: the next kernel may start its weight / cache loads
   pdl_wait();
   const int half = cols / 2;
   const int64_t total = static_cast<int64_t>(rows) * half;
@@ -154,7 +154,6 @@ __global__ void rope_kernel(const uint16_t *__restrict__ x, const uint16_t *__re
       yr[2 * j + 1] = float_to_bf16_bits(xe * s + xo * c);
     }
   }
-  pdl_launch_dependents();
 }
 
 // ---------------------------------------------------------------------------
@@ -164,6 +163,7 @@ __global__ void rope_kernel(const uint16_t *__restrict__ x, const uint16_t *__re
 __global__ void softmax_kernel(const uint16_t *__restrict__ x, uint16_t *__restrict__ y, int cols,
                                int valid, const int *__restrict__ valid_dev) {
   __shared__ float scratch[32];
+  pdl_launch_dependents();  // at entry: the next kernel may start its weight / cache loads
   pdl_wait();
   if (valid_dev) valid = *valid_dev;
   valid = max(0, min(valid, cols));
@@ -179,7 +179,6 @@ __global__ void softmax_kernel(const uint16_t *__restrict__ x, uint16_t *__restr
   const float inv = 1.f / s;
   for (int c = threadIdx.x; c < cols; c += blockDim.x)
     yr[c] = float_to_bf16_bits(c < valid ? __expf(bf16_bits_to_float(xr[c]) - m) * inv : 0.f);
-  pdl_launch_dependents();
 }
 
 // ---------------------------------------------------------------------------
@@ -189,6 +188,7 @@ __device__ __forceinline__ float silu_f(float v) { return v / (1.f + __expf(-v))
 
 __global__ void eltwise_kernel(const uint16_t *__restrict__ a, const uint16_t *__restrict__ b,
                                uint16_t *__restrict__ y, int64_t n, int op) {
+  pdl_launch_dependents();  // at entry: the next kernel may start its weight / cache loads
   pdl_wait();
   const int64_t n8 = n / 8;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -208,7 +208,6 @@ __global__ void eltwise_kernel(const uint16_t *__restrict__ a, const uint16_t *_
     const float o = op == 0 ? silu_f(fa) : op == 1 ? fa * fb : op == 2 ? fa + fb : silu_f(fa) * fb;
     y[i] = float_to_bf16_bits(o);
   }
-  pdl_launch_dependents();
 }
 
 // ---------------------------------------------------------------------------
@@ -238,6 +237,7 @@ __global__ void strided_copy_kernel(const T *__restrict__ in, T *__restrict__ ou
                                     int64_t per_channel, const int *__restrict__ in_add,
                                     const int *__restrict__ out_add, int64_t in_size,
                                     int64_t out_size) {
+  pdl_launch_dependents();  // at entry: the next kernel may start its weight / cache loads
   pdl_wait();
   const int64_t ia = in_add ? *in_add : 0, oa = out_add ? *out_add : 0;
   const int64_t total = per_channel * channels;
@@ -249,13 +249,13 @@ __global__ void strided_copy_kernel(const T *__restrict__ in, T *__restrict__ ou
     const int64_t d = tap_offset(dst, dst_split3, c, j) + oa;
     if (so >= 0 && so < in_size && d >= 0 && d < out_size) out[d] = in[so];
   }
-  pdl_launch_dependents();
 }
 
 // ---------------------------------------------------------------------------
 // repeat_interleave along dim 0 (iron/operators/repeat/reference.py:7-9), 16-byte vectors.
 __global__ void repeat_kernel(const uint4 *__restrict__ in, uint4 *__restrict__ out, int64_t rows,
                               int64_t row_vecs, int repeat) {
+  pdl_launch_dependents();  // at entry: the next kernel may start its weight / cache loads
   pdl_wait();
   const int64_t total = rows * repeat * row_vecs;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
@@ -263,13 +263,13 @@ __global__ void repeat_kernel(const uint4 *__restrict__ in, uint4 *__restrict__ 
     const int64_t orow = i / row_vecs, v = i - orow * row_vecs;
     out[i] = in[(orow / repeat) * row_vecs + v];
   }
-  pdl_launch_dependents();
 }
 
 // Batched transpose (iron/operators/transpose/reference.py:7-10) through a 32x33 tile.
 template <typename T>
 __global__ void transpose_kernel(const T *__restrict__ in, T *__restrict__ out, int M, int N) {
   __shared__ T tile[32][33];
+  pdl_launch_dependents();  // at entry: the next kernel may start its weight / cache loads
   pdl_wait();
   const int64_t b = blockIdx.z;
   const T *src = in + b * static_cast<int64_t>(M) * N;
@@ -284,7 +284,6 @@ __global__ void transpose_kernel(const T *__restrict__ in, T *__restrict__ out, 
     const int c = c0 + i, r = r0 + threadIdx.x;  // out row c, col r
     if (r < M && c < N) dst[static_cast<int64_t>(c) * M + r] = tile[threadIdx.x][i];
   }
-  pdl_launch_dependents();
 }
 
 static unsigned grid_for(int64_t work, int threads) {

@@ -204,3 +204,74 @@ def test_dequant_bench_size_bit_exact():
     errors, _, _ = run_test(op, {"payload": torch.from_numpy(payload)}, {"output": bf16(exp)},
                             rel_tol=0.0, abs_tol=0.0)
     assert not errors
+
+
+# ---- int4 GEMV: the Llama-3-8B tensor-parallel shards and ragged / tiny cases ----------
+def _s4_ex(packed, x, N, K, nv, flags, residual=None, norm_w=None, swiglu=False):
+    y = torch.empty(nv, N // 2 if swiglu else N, dtype=torch.bfloat16, device="cuda")
+    f = flags | (_lib.IRON_FLAG_SWIGLU if swiglu else 0)
+    _lib.call("iron_gemv_int4g32_ex", packed.data_ptr(), x.data_ptr(), y.data_ptr(), N, K, nv,
+              residual.data_ptr() if residual is not None else None,
+              norm_w.data_ptr() if norm_w is not None else None, 1e-5, None, f, _lib.current_stream())
+    return y
+
+
+# the Llama-3.2-1B projections, the Llama-3-8B tensor-parallel shards (o / down / qkv at
+# tp 2 and 8), tiny and ragged cases
+@pytest.mark.parametrize("N,K,nv", [(2048, 8192, 2), (16384, 2048, 1), (16, 128, 8), (48, 256, 3),
+                                    (1024, 128, 5), (4096, 512, 2), (4096, 1792, 2), (768, 4096, 2),
+                                    (4096, 7168, 1)])
+def test_gemv_int4g32_shards(N, K, nv):
+    codes, scales, X, W = _s4_case(N, K, nv, seed=N + K + nv)
+    packed = GEMV.pack_int4g32(codes.cuda(), scales.cuda())
+    x = X.cuda()
+    y = _s4_ex(packed, x, N, K, nv, 0)
+    y2 = _s4_ex(packed, x, N, K, nv, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2), "not bitwise deterministic"
+    assert_close(y.cpu(), ops.gemv_multi(W, X), 2e-2, 1e-2, what=f"{N}x{K} n_vec={nv}")
+
+
+def test_gemv_int4g32_epilogues():
+    """Residual add, the SwiGLU of interleaved gate/up rows and the RMSNorm prologue,
+    against the oracle."""
+    N, K, nv = 4096, 2048, 3
+    codes, scales, X, W = _s4_case(N, K, nv, seed=11)
+    packed = GEMV.pack_int4g32(codes.cuda(), scales.cuda())
+    R = torch.randn(nv, N).to(torch.bfloat16)
+    y = _s4_ex(packed, X.cuda(), N, K, nv, 0, residual=R.cuda())
+    gu = _s4_ex(packed, X.cuda(), N, K, nv, 0, swiglu=True)
+    w = (1 + 0.02 * torch.randn(K)).to(torch.bfloat16)
+    yn = _s4_ex(packed, X.cuda(), N, K, nv, 0, norm_w=w.cuda())
+    torch.cuda.synchronize()
+    assert_close(y.cpu(), ops.add(ops.gemv_multi(W, X), R), 2e-2, 1e-2, what="residual")
+    full = ops.gemv_multi(W, X).reshape(nv, N // 16, 16)
+    gate, up = full[:, :, :8].reshape(nv, N // 2), full[:, :, 8:].reshape(nv, N // 2)
+    assert_close(gu.cpu(), ops.swiglu_act(gate, up), 2e-2, 1e-2, what="swiglu")
+    assert_close(yn.cpu(), ops.gemv_multi(W, ops.rms_norm(X, w, 1e-5)), 2e-2, 1e-2, what="rmsnorm prologue")
+
+
+def test_gemv_int4g32_dependent_chain_in_graph():
+    """PDL-launched GEMVs captured in a graph, each reading the previous
+    one's output (the dependency the early weight copies must not break)."""
+    N = K = 2048
+    mats, Ws = [], []
+    for i in range(6):
+        codes, scales, _, W = _s4_case(N, K, 1, seed=40 + i)
+        mats.append(GEMV.pack_int4g32(codes.cuda(), scales.cuda()))
+        Ws.append(W)
+    x0 = (torch.randn(1, K) * 0.5).to(torch.bfloat16)
+    bufs = [x0.cuda()] + [torch.empty(1, N, dtype=torch.bfloat16, device="cuda") for _ in mats]
+    s = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i, m in enumerate(mats):
+            _lib.call("iron_gemv_int4g32", m.data_ptr(), bufs[i].data_ptr(), bufs[i + 1].data_ptr(), N, K, 1,
+                      None, _lib.IRON_FLAG_PDL, s.cuda_stream)
+    g.replay()
+    torch.cuda.synchronize()
+    ref = x0
+    for i, W in enumerate(Ws):
+        # the oracle fed with the kernel's own previous output, so errors do not compound
+        ref = ops.gemv_multi(W, bufs[i].cpu())
+        assert_close(bufs[i + 1].cpu(), ref, 2e-2, 1e-2, what=f"link {i}")
