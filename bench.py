@@ -947,7 +947,7 @@ def run_tp_block(args, world, rank, local):
                          "frac": round(achieved / peak, 4), "traffic": None,
                          "scope": "one rank's block step (its weight shard + kv heads)",
                          "algorithmic_bytes_per_step": int(bytes_rank)},
-            "gpu_launches": (8 + int(blk.ws.numel() > 16)) * args.steps, "clocks": clocks, "e2e": None}
+            "gpu_launches": blk.kernels_per_step() * args.steps, "clocks": clocks, "e2e": None}
     blk.check_status()
     blk.release()
     if rank == 0:

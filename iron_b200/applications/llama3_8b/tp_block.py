@@ -3,7 +3,7 @@
 Each rank holds the int4 shard of ``sharding.shard_weights`` and runs the decode
 step of a batch of sequences:
 
-    RMSNorm -> QKV GEMV (local heads) -> RoPE + KV append -> GQA attention (local
+    RMSNorm -> QKV GEMV (local heads) -> GQA attention with RoPE + KV append (local
     heads, head_dim 128) -> o_proj GEMV (local input columns; rank 0 adds the
     residual) -> all-reduce -> RMSNorm -> gate/up GEMV + SwiGLU (local FFN rows)
     -> down_proj GEMV (local FFN columns; rank 0 adds the residual) -> all-reduce
@@ -133,11 +133,9 @@ class TPDecoderBlock:
         self.xn = torch.zeros_like(self.x)
         self.h = torch.zeros_like(self.x)
         self.qkv = torch.zeros(B, self.dims["qkv"][0], **bf)
-        self.q = torch.zeros(B, self.hq, hd, **bf)
         self.attn = torch.zeros(B, self.hq * hd, **bf)
         self.act = torch.zeros(B, self.ffn_local, **bf)
         self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
-        self.lens = torch.zeros(B, dtype=torch.int32, device=dev)
         self.lut = rope_table(hd, max_seq, shape.rope_base, dev)
         wsb = _lib.load().iron_attn_decode_workspace_bytes_d(B, self.hq, self.hk, max_seq, hd)
         self.ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
@@ -154,6 +152,10 @@ class TPDecoderBlock:
     # -- bytes / launches ---------------------------------------------------------------
     def weight_bytes(self) -> int:
         return sum(r * c * 9 // 16 for r, c in self.dims.values())
+
+    def kernels_per_step(self) -> int:
+        """Launches of one step: 2 RMSNorm, 4 GEMVs, attention (+ its split combine)."""
+        return 7 + int(self.ws.numel() > 16)
 
     def kv_bytes(self, positions) -> int:
         return int(sum(int(p) + 1 for p in positions)) * self.hk * self.s.head_dim * 2 * 2
@@ -182,10 +184,9 @@ class TPDecoderBlock:
         call("iron_gemv_int4g32", p(self.w["qkv"]), p(self.xn), p(self.qkv), self.dims["qkv"][0], E, B, None, f,
              stream)
         kv_b, kv_h = self.hk * self.L * hd, self.L * hd
-        call("iron_rope_kv_append", p(self.qkv), p(self.pos), p(self.lut), p(self.q), p(self.kc), p(self.vc),
-             p(self.lens), B, self.hq, self.hk, hd, kv_b, kv_h, f, stream)
-        call("iron_attn_decode", p(self.q), p(self.kc), p(self.vc), p(self.lens), p(self.attn), B, self.hq,
-             self.hk, hd, self.L, kv_b, kv_h, 1.0 / math.sqrt(hd), p(self.ws), self.ws.numel(), f, stream)
+        # RoPE + KV append inside the attention kernel (q, k, v of the local heads)
+        call("iron_attn_decode_qkv", p(self.qkv), p(self.pos), p(self.lut), p(self.kc), p(self.vc), p(self.attn), B,
+             self.hq, self.hk, hd, self.L, kv_b, kv_h, 1.0 / math.sqrt(hd), p(self.ws), self.ws.numel(), f, stream)
         if self.fused:
             call("iron_gemv_int4g32_allreduce", p(self.w["o"]), p(self.attn), p(self.h), E, self.dims["o"][1], B,
                  p(self.x), ctypes.addressof(self.site_o.peers), f, stream)

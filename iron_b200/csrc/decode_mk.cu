@@ -245,8 +245,8 @@ __device__ __forceinline__ void unit_mma(float (&d)[2][4], const UnitRegs &u, co
     const uint32_t A0[4] = {pl[0], ph[0], pl[1], ph[1]};
     const uint32_t A1[4] = {pl[2], ph[2], pl[3], ph[3]};
     const uint4 e = xr[j];
-    mma_bf16_16816(d[j & 1], A0, prmt_(e.x, e.z, 0x5410u), prmt_(e.x, e.z, 0x7632u));
-    mma_bf16_16816(d[j & 1], A1, prmt_(e.y, e.w, 0x5410u), prmt_(e.y, e.w, 0x7632u));
+    mma_bf16_16816(d[j & 1], A0, e.x, e.y);  // packed nibble order: consecutive k pairs
+    mma_bf16_16816(d[j & 1], A1, e.z, e.w);
   }
 }
 

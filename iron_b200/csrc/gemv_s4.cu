@@ -2,7 +2,8 @@
 //
 // Weights are first repacked (iron_pack_int4g32) into units of one 16-row tile x
 // 128 k (4 groups): 1024 code bytes in the order the MMA fragments want them
-// (lane-major, so every warp load is 512 contiguous bytes) followed by the tile's
+// (lane-major, so every warp load is 512 contiguous bytes; within a 32-bit word the
+// nibbles of k 2q and 2q+1 sit at bits 4q and 16+4q) followed by the tile's
 // 16 x 4 bf16 scales (128 B). A unit is 1152 bytes; units are stored tile-major.
 //
 // One CTA of four warps per 16-row tile; its warps split the tile's units (and a
@@ -257,8 +258,8 @@ __device__ __forceinline__ void s4_unit_gx(float (&d)[2][NT][4], const uint4 &cl
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
       const uint4 e = xr[j][t];
-      mma_bf16_16816(d[j & 1][t], A0, prmt_(e.x, e.z, 0x5410u), prmt_(e.x, e.z, 0x7632u));
-      mma_bf16_16816(d[j & 1][t], A1, prmt_(e.y, e.w, 0x5410u), prmt_(e.y, e.w, 0x7632u));
+      mma_bf16_16816(d[j & 1][t], A0, e.x, e.y);  // k (0,1) / (2,3) of this lane's 8
+      mma_bf16_16816(d[j & 1][t], A1, e.z, e.w);  // k (4,5) / (6,7)
     }
   }
 }
@@ -377,9 +378,8 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
     for (int u = 0; u < kT4Units; ++u) {
       const int c = c0 + u;
       if (c < kr.e) {
-        // B fragments from the activations (L1-cached) or the normalised slice,
-        // permuted to the nibble-pair order: pieces (x[8m+i], x[8m+4+i]) for this
-        // lane's m = 4(4c+j)+tid
+        // B fragments straight from the activations (L1-cached) or the normalised
+        // slice: this lane's 8 consecutive k of chunk j are k 0-7 of its code word
         if constexpr (norm) s4_unit_gx<NT, true>(acc, lo[u], hi[u], sc[u], xs_norm, K, n_vec, c * 128, klen, kc0);
         else s4_unit_gx<NT>(acc, lo[u], hi[u], sc[u], x, K, n_vec, c * 128);
       }
@@ -452,8 +452,8 @@ __global__ void pack_s4g32_kernel(const uint8_t *__restrict__ codes,
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const uint8_t *g = src + (c * 4 + j) * 16 + tid * 4;
-      words[j] = static_cast<uint32_t>(g[0]) | (static_cast<uint32_t>(g[1]) << 8) |
-                 (static_cast<uint32_t>(g[2]) << 16) | (static_cast<uint32_t>(g[3]) << 24);
+      words[j] = s4_word_pack(static_cast<uint32_t>(g[0]) | (static_cast<uint32_t>(g[1]) << 8) |
+                              (static_cast<uint32_t>(g[2]) << 16) | (static_cast<uint32_t>(g[3]) << 24));
     }
   } else {
     const int gid = piece - 64;
@@ -554,9 +554,8 @@ __global__ void unpack_s4g32_kernel(const uint8_t *__restrict__ packed, uint16_t
     uint32_t o[4];
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-      const uint32_t byte = (words[j] >> (8 * b)) & 0xffu;
-      const float lo = static_cast<float>(static_cast<int>((byte & 0xfu) ^ 8u) - 8) * scale;
-      const float hi = static_cast<float>(static_cast<int>((byte >> 4) ^ 8u) - 8) * scale;
+      const float lo = static_cast<float>(static_cast<int>(s4_word_nibble(words[j], 2 * b) ^ 8u) - 8) * scale;
+      const float hi = static_cast<float>(static_cast<int>(s4_word_nibble(words[j], 2 * b + 1) ^ 8u) - 8) * scale;
       o[b] = pack_bf16x2(lo, hi);
     }
     *reinterpret_cast<uint4 *>(dst + j * 32) = make_uint4(o[0], o[1], o[2], o[3]);

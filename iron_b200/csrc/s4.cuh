@@ -28,4 +28,23 @@ __device__ __forceinline__ uint32_t s4x2_dequant_(uint32_t w, uint32_t scale2) {
   return r;
 }
 
+// Nibble order of a packed 32-bit code word. Natural order (4 code bytes of one row,
+// element 2b in the low nibble of byte b) holds k_i at bits 4i; the packed word holds
+// k_2q at bits 4q and k_2q+1 at bits 16 + 4q, so that s4x2_dequant_(w >> 4q) is the
+// bf16x2 pair (k_2q, k_2q+1): two consecutive k, which is how the activations sit in
+// memory -- their 16-byte loads are the MMA B fragments without any permute.
+__host__ __device__ __forceinline__ uint32_t s4_word_pack(uint32_t natural) {
+  uint32_t r = 0;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    r |= ((natural >> (8 * q)) & 0xfu) << (4 * q);             // k_2q
+    r |= ((natural >> (8 * q + 4)) & 0xfu) << (16 + 4 * q);    // k_2q+1
+  }
+  return r;
+}
+// Nibble of element k_i (i in 0..7) of a packed word.
+__device__ __forceinline__ uint32_t s4_word_nibble(uint32_t packed, int i) {
+  return (packed >> ((i & 1) ? 16 + 4 * (i >> 1) : 4 * (i >> 1))) & 0xfu;
+}
+
 }  // namespace iron

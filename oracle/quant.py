@@ -86,9 +86,11 @@ def pack_s4g32_units(codes: np.ndarray, scale_bits: np.ndarray) -> np.ndarray:
     """Streaming layout of the int4g32 GEMV (the unit format iron_pack_int4g32 writes).
 
     Unit (t, c) covers rows 16t..16t+15 and k 128c..128c+127 and is 1152 bytes:
-    bytes [h*512 + lane*16 + 4j, +4) = code bytes [(4c+j)*16 + 4*tid, +4) of row
-    16t + gid + 8h (lane = 4*gid + tid); bytes [1024 + 16*gid, +16) = the bf16
-    scales of groups 4c..4c+3 of row 16t+gid, then of row 16t+gid+8.
+    the 32-bit word at bytes [h*512 + lane*16 + 4j, +4) holds the 8 codes of row
+    16t + gid + 8h (lane = 4*gid + tid) at k (4c+j)*32 + 8*tid + i, i = 0..7, the
+    code of k_i at bits 4*(i//2) for even i and 16 + 4*(i//2) for odd i (pairs of
+    consecutive k share a bf16x2 after dequantization); bytes [1024 + 16*gid, +16) =
+    the bf16 scales of groups 4c..4c+3 of row 16t+gid, then of row 16t+gid+8.
     """
     codes = np.asarray(codes, dtype=np.uint8)
     sb = np.asarray(scale_bits, dtype=np.uint16)
@@ -97,7 +99,28 @@ def pack_s4g32_units(codes: np.ndarray, scale_bits: np.ndarray) -> np.ndarray:
     T, C = M // 16, K // 128
     # codes: row = 16t + gid + 8h ; byte = (4c + j)*16 + 4*tid + b
     cc = codes.reshape(T, 2, 8, C, 4, 4, 4)  # t, h, gid, c, j, tid, b
-    cc = cc.transpose(0, 3, 1, 2, 5, 4, 6).reshape(T, C, 1024)  # t, c, h, gid, tid, j, b
+    cc = cc.transpose(0, 3, 1, 2, 5, 4, 6)  # t, c, h, gid, tid, j, b
+    # the word's nibble order: low nibbles of the 4 natural bytes into bits 0-15, high
+    # nibbles into bits 16-31 (byte 0 = lo(b0) | lo(b1) << 4, byte 2 = hi(b0) | hi(b1) << 4)
+    lo, hi = cc & 0x0F, cc >> 4
+    cc = np.stack([lo[..., 0] | (lo[..., 1] << 4), lo[..., 2] | (lo[..., 3] << 4),
+                   hi[..., 0] | (hi[..., 1] << 4), hi[..., 2] | (hi[..., 3] << 4)], axis=-1)
+    cc = cc.astype(np.uint8).reshape(T, C, 1024)
     ss = sb.reshape(T, 2, 8, C, 4).transpose(0, 3, 2, 1, 4).reshape(T, C, 64)  # t,c,gid,h,j
     units = np.concatenate([cc, ss.view(np.uint8).reshape(T, C, 128)], axis=2)
     return units.reshape(-1)
+
+
+def unpack_s4g32_units(units: np.ndarray, M: int, K: int):
+    """Inverse of pack_s4g32_units: natural codes [M, K/2] and scale bits [M, K/32]."""
+    T, C = M // 16, K // 128
+    u = np.asarray(units, dtype=np.uint8).reshape(T, C, 1152)
+    cc = u[:, :, :1024].reshape(T, C, 2, 8, 4, 4, 4)  # t, c, h, gid, tid, j, packed byte
+    p0, p1, p2, p3 = (cc[..., i] for i in range(4))
+    lo = np.stack([p0 & 0x0F, p0 >> 4, p1 & 0x0F, p1 >> 4], axis=-1)  # low nibbles of natural bytes 0..3
+    hi = np.stack([p2 & 0x0F, p2 >> 4, p3 & 0x0F, p3 >> 4], axis=-1)
+    nat = (lo | (hi << 4)).astype(np.uint8)  # t, c, h, gid, tid, j, b
+    codes = nat.transpose(0, 2, 3, 1, 5, 4, 6).reshape(M, K // 2)  # t, h, gid, c, j, tid, b
+    ss = u[:, :, 1024:].copy().view(np.uint16).reshape(T, C, 8, 2, 4)  # t, c, gid, h, j
+    scales = ss.transpose(0, 3, 2, 1, 4).reshape(M, K // 32)
+    return codes, scales

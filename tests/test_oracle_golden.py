@@ -50,6 +50,22 @@ def test_s4g32_roundtrip_exact():
     np.testing.assert_array_equal(deq, expect)
 
 
+def test_s4g32_unit_packing_roundtrip_and_nibble_order():
+    """The GEMV's packed unit layout: unpacking restores codes and scales exactly, and
+    a word's even / odd k sit in its low / high halves (consecutive k share a pair)."""
+    codes, sbits, _ = quant.make_s4g32(64, 512, seed=3)
+    units = quant.pack_s4g32_units(codes, sbits)
+    assert units.size == (64 // 16) * (512 // 128) * 1152
+    c2, s2 = quant.unpack_s4g32_units(units, 64, 512)
+    np.testing.assert_array_equal(c2, codes)
+    np.testing.assert_array_equal(s2, sbits)
+    # unit (0, 0), lane 0 (row 0), word j = 0: natural k 0..7 of row 0
+    w = int(units[:4].view(np.uint32)[0])
+    nat = [(int(codes[0, i // 2]) >> (4 * (i % 2))) & 15 for i in range(8)]
+    got = [(w >> ((16 if i % 2 else 0) + 4 * (i // 2))) & 15 for i in range(8)]
+    assert got == nat
+
+
 def test_f32_to_bf16_rounding_matches_torch():
     x = torch.randn(100000) * 10
     x[:5] = torch.tensor([0.0, -0.0, float("inf"), float("-inf"), 1e-40])
