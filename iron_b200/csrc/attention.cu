@@ -26,7 +26,8 @@ namespace iron {
 // 128 (the Llama-3-8B block).
 constexpr int kAWarps = 4;
 constexpr int kABlk = 16;     // tokens per warp step
-constexpr int kAMinChunk = 256;  // tokens per split at least (B200, batch 1: 64 / 128 / 512 tokens measured slower)
+constexpr int kAMinChunk = 64;   // tokens per split at least
+constexpr int kAMaxSplits = 64;  // splits per sequence at most (the combine holds one value per split)
 
 struct AttnArgs {
   const uint16_t *q;    // [B, Hq, D]
@@ -47,6 +48,8 @@ struct AttnArgs {
   const float *lut;
 };
 
+// cache rows: written by earlier steps, or (row p) by the RoPE + append kernel that
+// precedes this one and lets it launch only at its end -- constant while this runs
 __device__ __forceinline__ uint4 ldg16(const uint16_t *p) {
   return __ldg(reinterpret_cast<const uint4 *>(p));
 }
@@ -86,13 +89,13 @@ attn_decode_kernel(AttnArgs a) {
     // pos is final before this launch (written by the previous step, which the step's
     // first kernel waits for), so it and the cached rows below it are read before the
     // wait for the QKV projection
-    p = a.pos[b];
+    p = ld_act_i32(a.pos + b);
     valid = p >= 0 && p < a.maxlen;
     if (!valid) p = 0;
     len = valid ? p + 1 : 0;
   } else {
     pdl_wait();
-    len = min(max(a.lens[b], 0), a.maxlen);
+    len = min(max(ld_act_i32(a.lens + b), 0), a.maxlen);
   }
   const int t_begin = split * a.chunk;
   const int t_end = min(len, t_begin + a.chunk);
@@ -168,16 +171,16 @@ attn_decode_kernel(AttnArgs a) {
       uint16_t q1 = 0, q2 = 0, k1r = 0, k2r = 0, v1 = 0, v2 = 0;
       float cq = 0.f, sq = 0.f, ck = 0.f, sk = 0.f;
       if (hq_) {
-        q1 = xq[jq];
-        q2 = xq[jq + half];
+        q1 = ld_act_u16(xq + jq);
+        q2 = ld_act_u16(xq + jq + half);
         cq = ang[2 * jq];
         sq = ang[2 * jq + 1];
       }
       if (hk_) {
-        k1r = xk[i];
-        k2r = xk[i + half];
-        v1 = xv[i];
-        v2 = xv[i + half];
+        k1r = ld_act_u16(xk + i);
+        k2r = ld_act_u16(xk + i + half);
+        v1 = ld_act_u16(xv + i);
+        v2 = ld_act_u16(xv + i + half);
         ck = ang[2 * i];
         sk = ang[2 * i + 1];
       }
@@ -219,10 +222,11 @@ attn_decode_kernel(AttnArgs a) {
     const uint16_t *qr8 = kFused ? qrow + (gid + 8) * kAD : qrow + (static_cast<int64_t>(b) * a.Hq + hq0 + gid + 8) * qstride;
     const uint32_t *q0 = reinterpret_cast<const uint32_t *>(qr0 + d);
     const uint32_t *q8 = reinterpret_cast<const uint32_t *>(qr8 + d);
-    qa[ks][0] = gid < g ? q0[0] : 0u;
-    qa[ks][1] = gid + 8 < g ? q8[0] : 0u;
-    qa[ks][2] = gid < g ? q0[1] : 0u;
-    qa[ks][3] = gid + 8 < g ? q8[1] : 0u;
+    // fused: the staged q tile in shared memory; else q from the RoPE kernel's output
+    qa[ks][0] = gid < g ? (kFused ? q0[0] : ld_act_u32(q0)) : 0u;
+    qa[ks][1] = gid + 8 < g ? (kFused ? q8[0] : ld_act_u32(q8)) : 0u;
+    qa[ks][2] = gid < g ? (kFused ? q0[1] : ld_act_u32(q0 + 1)) : 0u;
+    qa[ks][3] = gid + 8 < g ? (kFused ? q8[1] : ld_act_u32(q8 + 1)) : 0u;
   }
 
   float o[kAD / 8][4];
@@ -360,32 +364,48 @@ attn_decode_kernel(AttnArgs a) {
 }
 
 // Merge the splits of each (sequence, q head): out = sum_s O_s 2^(m_s - M) / sum_s L_s 2^(m_s - M).
+// Every load is issued before any is used -- this thread's output column of every
+// split into registers, one split's (m, l) per thread into shared memory -- so the
+// merge costs one L2 round trip whatever the split count (<= kAMaxSplits). The sums
+// run in split order, as before.
 template <int kAD>
 __global__ void attn_combine_kernel(const float *__restrict__ ws, uint16_t *__restrict__ out, int splits) {
+  static_assert(kAD >= kAMaxSplits, "one (m, l) pair per thread");
+  __shared__ float sm_m[kAMaxSplits], sm_l[kAMaxSplits];
   pdl_launch_dependents();  // at entry: the next kernel may start its weight / cache loads
   pdl_wait();
   const int64_t hq = blockIdx.x;
   const int d = threadIdx.x;
   const float *p = ws + hq * splits * (2 + kAD);
+  float ov[kAMaxSplits];
+#pragma unroll
+  for (int s = 0; s < kAMaxSplits; ++s) ov[s] = s < splits ? ld_act_f32(p + s * (2 + kAD) + 2 + d) : 0.f;
+  if (d < splits) {
+    sm_m[d] = ld_act_f32(p + d * (2 + kAD));
+    sm_l[d] = ld_act_f32(p + d * (2 + kAD) + 1);
+  }
+  __syncthreads();
   float M = -INFINITY;
-#pragma unroll 8
-  for (int s = 0; s < splits; ++s) M = fmaxf(M, p[s * (2 + kAD)]);
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, sm_m[s]);
   float L = 0.f, O = 0.f;
   if (M != -INFINITY) {
-#pragma unroll 8
-    for (int s = 0; s < splits; ++s) {
-      const float *q = p + s * (2 + kAD);
-      const float f = exp2f(q[0] - M);
-      L += q[1] * f;
-      O += q[2 + d] * f;
+#pragma unroll
+    for (int s = 0; s < kAMaxSplits; ++s) {
+      if (s < splits) {
+        const float f = exp2f(sm_m[s] - M);
+        L += sm_l[s] * f;
+        O += ov[s] * f;
+      }
     }
   }
   out[hq * kAD + d] = float_to_bf16_bits(L > 0.f ? O / L : 0.f);
 }
 
-// Split count: enough CTAs for two waves of 148 SMs, chunks of >= 256 tokens.
+// Split count: enough CTAs for two waves of 148 SMs, chunks of >= kAMinChunk tokens,
+// at most kAMaxSplits.
 __host__ __device__ inline int attn_splits(int B, int Hkv, int Lmax, int sms) {
-  const int max_splits = (Lmax + kAMinChunk - 1) / kAMinChunk;
+  int max_splits = (Lmax + kAMinChunk - 1) / kAMinChunk;
+  if (max_splits > kAMaxSplits) max_splits = kAMaxSplits;
   int s = 1;
   while (s < max_splits && static_cast<int64_t>(B) * Hkv * s < 2LL * sms) s *= 2;
   return s < max_splits ? s : max_splits;

@@ -73,10 +73,10 @@ __global__ void __launch_bounds__(kPThreads) attn_prefill_kernel(PrefillArgs a) 
       const int d = kk * 16 + 2 * tid;
       const uint32_t *p0 = reinterpret_cast<const uint32_t *>(qp + r0 * a.qs + d);
       const uint32_t *p1 = reinterpret_cast<const uint32_t *>(qp + r1 * a.qs + d);
-      qa[kk][0] = r0 < a.S ? p0[0] : 0u;
-      qa[kk][1] = r1 < a.S ? p1[0] : 0u;
-      qa[kk][2] = r0 < a.S ? p0[4] : 0u;
-      qa[kk][3] = r1 < a.S ? p1[4] : 0u;
+      qa[kk][0] = r0 < a.S ? ld_act_u32(p0) : 0u;
+      qa[kk][1] = r1 < a.S ? ld_act_u32(p1) : 0u;
+      qa[kk][2] = r0 < a.S ? ld_act_u32(p0 + 4) : 0u;
+      qa[kk][3] = r1 < a.S ? ld_act_u32(p1 + 4) : 0u;
     }
   }
 
@@ -97,8 +97,8 @@ __global__ void __launch_bounds__(kPThreads) attn_prefill_kernel(PrefillArgs a) 
       const int idx = i * kPThreads + threadIdx.x, row = idx >> 3, c = (idx & 7) * 8;
       const int t = blk * kPBlk + row;
       const bool in = t < a.S_kv;
-      kr[i] = in ? __ldg(reinterpret_cast<const uint4 *>(kp + t * a.ks + c)) : make_uint4(0, 0, 0, 0);
-      vr[i] = in ? __ldg(reinterpret_cast<const uint4 *>(vp + t * a.ks + c)) : make_uint4(0, 0, 0, 0);
+      kr[i] = in ? ld_act_v4(kp + t * a.ks + c) : make_uint4(0, 0, 0, 0);
+      vr[i] = in ? ld_act_v4(vp + t * a.ks + c) : make_uint4(0, 0, 0, 0);
     }
   };
   if (nblk > 0) fetch(0);

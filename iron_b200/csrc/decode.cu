@@ -17,10 +17,10 @@ __global__ void rope_kv_append_kernel(const uint16_t *__restrict__ qkv, const in
                                       uint16_t *__restrict__ k_cache, uint16_t *__restrict__ v_cache,
                                       int *__restrict__ lens, int Hq, int Hkv, int D,
                                       int64_t kv_bstride, int64_t kv_hstride) {
-  pdl_launch_dependents();  // at entry: the next kernel may start its weight / cache loads
   pdl_wait();
+  pdl_launch_dependents();  // after the wait: bounds a window (the attention reads the new rows as cache rows)
   const int b = blockIdx.x;
-  const int p = pos[b];
+  const int p = ld_act_i32(pos + b);
   const int half = D / 2;
   const int rows = Hq + 2 * Hkv;  // q heads, k heads, v heads
   const uint16_t *src = qkv + static_cast<int64_t>(b) * rows * D;
@@ -30,7 +30,7 @@ __global__ void rope_kv_append_kernel(const uint16_t *__restrict__ qkv, const in
     const uint16_t *x = src + r * D;
     if (r < Hq + Hkv) {
       const float c = ang[2 * j], sn = ang[2 * j + 1];
-      const float x1 = bf16_bits_to_float(x[j]), x2 = bf16_bits_to_float(x[j + half]);
+      const float x1 = bf16_bits_to_float(ld_act_u16(x + j)), x2 = bf16_bits_to_float(ld_act_u16(x + j + half));
       const uint16_t y1 = float_to_bf16_bits(x1 * c - x2 * sn);
       const uint16_t y2 = float_to_bf16_bits(x1 * sn + x2 * c);
       if (r < Hq) {
@@ -44,8 +44,8 @@ __global__ void rope_kv_append_kernel(const uint16_t *__restrict__ qkv, const in
       }
     } else {
       uint16_t *vc = v_cache + b * kv_bstride + (r - Hq - Hkv) * kv_hstride + static_cast<int64_t>(p) * D;
-      vc[j] = x[j];
-      vc[j + half] = x[j + half];
+      vc[j] = ld_act_u16(x + j);
+      vc[j + half] = ld_act_u16(x + j + half);
     }
   }
   if (threadIdx.x == 0 && lens) lens[b] = p + 1;
@@ -61,7 +61,7 @@ __global__ void embed_kernel(const int *__restrict__ tokens, const uint4 *__rest
   pdl_wait();
   pdl_launch_dependents();
   const int b = blockIdx.x;
-  const int64_t t = tokens[b];
+  const int64_t t = ld_act_i32(tokens + b);
   const bool ok = t >= 0 && t < V;
   for (int i = threadIdx.x; i < row_vecs; i += blockDim.x)
     x[static_cast<int64_t>(b) * row_vecs + i] = ok ? table[t * row_vecs + i] : make_uint4(0u, 0u, 0u, 0u);
@@ -79,7 +79,7 @@ __global__ void argmax_kernel(const uint16_t *__restrict__ logits, int *__restri
   float best = -INFINITY;
   int bi = 0x7fffffff;
   for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = bf16_bits_to_float(row[i]);
+    const float v = bf16_bits_to_float(ld_act_u16(row + i));
     if (v > best || (v == best && i < bi)) {
       best = v;
       bi = i;

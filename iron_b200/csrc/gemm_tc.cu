@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               v.z = pack_bf16x2(apply_epi(__uint_as_float(r[8 * g + 4]), epi), apply_epi(__uint_as_float(r[8 * g + 5]), epi));
               v.w = pack_bf16x2(apply_epi(__uint_as_float(r[8 * g + 6]), epi), apply_epi(__uint_as_float(r[8 * g + 7]), epi));
               if (res) {
-                const uint4 rv = *reinterpret_cast<const uint4 *>(res + 8 * g);
+                const uint4 rv = ld_act_v4(res + 8 * g);
                 v.x = add_res2(v.x, rv.x);
                 v.y = add_res2(v.y, rv.y);
                 v.z = add_res2(v.z, rv.z);

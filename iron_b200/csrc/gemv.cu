@@ -24,10 +24,6 @@ constexpr int kGemvThreads = 32 * kGemvWarps;
 
 __device__ __forceinline__ uint4 zero4() { return make_uint4(0u, 0u, 0u, 0u); }
 
-// Cached (L1-allocating) 16-byte load for activations, which every CTA re-reads.
-__device__ __forceinline__ uint4 ld_act_v4(const uint16_t *p) {
-  return __ldg(reinterpret_cast<const uint4 *>(p));
-}
 
 __device__ __forceinline__ uint16_t ld_stream_u16(const uint16_t *p) {
   uint16_t r;
@@ -134,7 +130,7 @@ __device__ __forceinline__ void gemv_reduce_store(float (&acc)[NT][4], float *re
         float r = acc[t][e];
         if (epilogue == IRON_EPI_GELU) r = gelu_tanh(r);
         const int64_t o = static_cast<int64_t>(v) * M + row;
-        if (residual) r = __bfloat162float(__float2bfloat16_rn(r)) + bf16_bits_to_float(residual[o]);
+        if (residual) r = __bfloat162float(__float2bfloat16_rn(r)) + bf16_bits_to_float(ld_act_u16(residual + o));
         y[o] = float_to_bf16_bits(r);
       }
     }

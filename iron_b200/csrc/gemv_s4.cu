@@ -155,10 +155,31 @@ __device__ __forceinline__ unsigned long long s4_argmax_key(float v, int row) {
 // a residual add or the SwiGLU of interleaved gate/up rows on the output, and the
 // greedy argmax of each output vector (amax != null: 64-bit keys, larger value then
 // lower row wins).
+// The residual values a store adds (C-fragment layout), loaded early: they were
+// written before this kernel's wait returned, so warp 0 fetches them right after it.
+template <int NT>
+__device__ __forceinline__ void s4_load_residual(float (&r)[NT][4], int tile, int N, int n_vec,
+                                                 const uint16_t *__restrict__ residual) {
+  const int lane = threadIdx.x & 31, gid = lane >> 2, tid = lane & 3;
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int row = tile * 16 + gid + ((e >> 1) << 3);
+      const int vv = t * 8 + tid * 2 + (e & 1);
+      r[t][e] = (residual && vv < n_vec) ? bf16_bits_to_float(ld_act_u16(residual + static_cast<int64_t>(vv) * N + row)) : 0.f;
+    }
+}
+
+// Up to 16 vectors the residual is preloaded (res); wider tiles read it here, where
+// 4 x NT more live registers would spill.
+template <int NT>
+constexpr bool s4_preload_residual() { return NT <= 2; }
+
 template <int NT>
 __device__ __forceinline__ void s4_store(const float (&v)[NT][4], int tile, int N, int n_vec,
-                                         uint16_t *__restrict__ y,
-                                         const uint16_t *__restrict__ residual, int swiglu,
+                                         uint16_t *__restrict__ y, const uint16_t *residual,
+                                         const float (&res)[NT][4], int swiglu,
                                          unsigned long long *amax = nullptr) {
   const int lane = threadIdx.x & 31, gid = lane >> 2, tid = lane & 3;
   const int row0 = tile * 16;
@@ -190,7 +211,9 @@ __device__ __forceinline__ void s4_store(const float (&v)[NT][4], int tile, int 
         float r = v[t][e];
         // the residual is added to the bf16-rounded projection, as IRON adds two
         // bf16 buffers (iron/operators/elementwise_add/reference.py:7-9)
-        if (residual) r = __bfloat162float(__float2bfloat16_rn(r)) + bf16_bits_to_float(residual[o]);
+        if (residual)
+          r = __bfloat162float(__float2bfloat16_rn(r)) +
+              (s4_preload_residual<NT>() ? res[t][e] : bf16_bits_to_float(ld_act_u16(residual + o)));
         const uint16_t yb = float_to_bf16_bits(r);
         y[o] = yb;
         if (amax) {
@@ -327,8 +350,15 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
       if (k < klen) wreg[j] = __ldg(reinterpret_cast<const uint4 *>(epi.norm_w + kc0 + k));
     }
   }
-  pdl_launch_dependents();
+  // with the RMSNorm prologue this GEMV bounds a window (see ld_act_v4): it lets its
+  // dependents launch only after its wait
+  if constexpr (!norm) pdl_launch_dependents();
   pdl_wait();
+  if constexpr (norm) pdl_launch_dependents();
+  float res[NT][4];
+  if constexpr (s4_preload_residual<NT>()) {
+    if (warp == 0 && rank == 0) s4_load_residual<NT>(res, tile, N, n_vec, epi.residual);
+  }
   if constexpr (norm) {
     // RMSNorm (rmsnorm_kernel's arithmetic): one pass over the whole x for the sums of
     // squares that also parks this CTA's k range in shared memory, then the range
@@ -339,7 +369,7 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
       ss[v] = 0.f;
       if (v < n_vec)
         for (int k = threadIdx.x * 8; k < K; k += kThr * 8) {
-          const uint4 r = __ldg(reinterpret_cast<const uint4 *>(x + static_cast<int64_t>(v) * K + k));
+          const uint4 r = ld_act_v4(x + static_cast<int64_t>(v) * K + k);
           const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
           for (int i = 0; i < 4; ++i) ss[v] += bf16_lo(w4[i]) * bf16_lo(w4[i]) + bf16_hi(w4[i]) * bf16_hi(w4[i]);
@@ -428,7 +458,7 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
   if constexpr (kAR && NT == 1) {
     if (warp == 0) s4_allreduce_tile(v[0], tile, N, n_vec, epi.ar);
   }
-  if (warp == 0) s4_store<NT>(v, tile, N, n_vec, y, epi.residual, epi.swiglu, epi.amax);
+  if (warp == 0) s4_store<NT>(v, tile, N, n_vec, y, epi.residual, res, epi.swiglu, epi.amax);
 }
 
 // Repack natural-layout codes [N, K/2] + scales [N, K/32] into GEMV units.
@@ -688,7 +718,7 @@ __global__ void argmax_finalize_kernel(unsigned long long *keys, int *tokens, in
   pdl_launch_dependents();  // at entry: the next kernel may start its weight / cache loads
   pdl_wait();
   const int b = blockIdx.x, lane = threadIdx.x;  // one warp per vector, a lane per slot
-  unsigned long long k = keys[b * kS4ArgmaxSlots + lane];
+  unsigned long long k = ld_act(keys + b * kS4ArgmaxSlots + lane);  // the lm-head GEMV's atomics
   keys[b * kS4ArgmaxSlots + lane] = 0ull;
 #pragma unroll
   for (int x = 16; x > 0; x >>= 1) {

@@ -49,24 +49,34 @@ __global__ void rmsnorm_kernel(const uint16_t *__restrict__ x, const uint16_t *_
                                uint16_t *__restrict__ x_out, const uint16_t *__restrict__ w,
                                uint16_t *__restrict__ y, int cols, float eps) {
   __shared__ float scratch[32];
-  pdl_launch_dependents();  // at entry: the next kernel may start its weight / cache loads
-  pdl_wait();
   const int64_t row = blockIdx.x;
   const uint16_t *xr = x + row * cols;
   const uint16_t *rr = r ? r + row * cols : nullptr;
   uint16_t *yr = y + row * cols;
   uint16_t *xo = x_out ? x_out + row * cols : nullptr;
+  const int stride = blockDim.x * 8;
+  // vector path: each thread keeps up to 4 chunks of 8 in registers (cols <= 8192 at 256 thr)
+  const bool vec = (cols & 7) == 0 && cols <= 4 * stride;
+  // the weights never depend on the previous kernel: requested before waiting for it
+  uint4 wv[4];
+#pragma unroll
+  for (int n = 0; n < 4; ++n) {
+    const int c = threadIdx.x * 8 + n * stride;
+    wv[n] = (vec && w && c < cols) ? *reinterpret_cast<const uint4 *>(w + c) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  pdl_wait();
+  pdl_launch_dependents();  // after the wait: this kernel bounds a window (see ld_act_v4)
   float ss = 0.f;
-  if ((cols & 7) == 0) {
-    // vector path: each thread keeps up to 4 chunks of 8 in registers (cols <= 8192 at 256 thr)
+  if (vec) {
     float v[4][8];
-    int n = 0;
-    for (int c = threadIdx.x * 8; c < cols; c += blockDim.x * 8, ++n) {
-      if (n < 4) {
-        unpack8(*reinterpret_cast<const uint4 *>(xr + c), v[n]);
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+      const int c = threadIdx.x * 8 + n * stride;
+      if (c < cols) {
+        unpack8(ld_act_v4(xr + c), v[n]);
         if (rr) {
           float q[8];
-          unpack8(*reinterpret_cast<const uint4 *>(rr + c), q);
+          unpack8(ld_act_v4(rr + c), q);
 #pragma unroll
           for (int i = 0; i < 8; ++i) v[n][i] = __bfloat162float(__float2bfloat16_rn(v[n][i] + q[i]));
           if (xo) *reinterpret_cast<uint4 *>(xo + c) = pack8(v[n]);
@@ -75,14 +85,15 @@ __global__ void rmsnorm_kernel(const uint16_t *__restrict__ x, const uint16_t *_
         for (int i = 0; i < 8; ++i) ss += v[n][i] * v[n][i];
       }
     }
-    if (n <= 4) {
-      const float inv = rsqrtf(block_sum(ss, scratch) / cols + eps);
-      n = 0;
-      for (int c = threadIdx.x * 8; c < cols; c += blockDim.x * 8, ++n) {
+    const float inv = rsqrtf(block_sum(ss, scratch) / cols + eps);
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+      const int c = threadIdx.x * 8 + n * stride;
+      if (c < cols) {
         float o[8];
         if (w) {
           float ww[8];
-          unpack8(*reinterpret_cast<const uint4 *>(w + c), ww);
+          unpack8(wv[n], ww);
 #pragma unroll
           for (int i = 0; i < 8; ++i) o[i] = v[n][i] * inv * ww[i];
         } else {
@@ -91,14 +102,14 @@ __global__ void rmsnorm_kernel(const uint16_t *__restrict__ x, const uint16_t *_
         }
         *reinterpret_cast<uint4 *>(yr + c) = pack8(o);
       }
-      return;
     }
-    ss = 0.f;  // row longer than the register cache: fall through to the scalar path
+    return;
   }
+  // scalar path: odd widths, or rows longer than the register cache
   for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-    float a = bf16_bits_to_float(xr[c]);
+    float a = bf16_bits_to_float(ld_act_u16(xr + c));
     if (rr) {
-      a = __bfloat162float(__float2bfloat16_rn(a + bf16_bits_to_float(rr[c])));
+      a = __bfloat162float(__float2bfloat16_rn(a + bf16_bits_to_float(ld_act_u16(rr + c))));
       if (xo) xo[c] = float_to_bf16_bits(a);
     }
     ss += a * a;
@@ -106,9 +117,10 @@ __global__ void rmsnorm_kernel(const uint16_t *__restrict__ x, const uint16_t *_
   const float inv = rsqrtf(block_sum(ss, scratch) / cols + eps);
   __syncthreads();  // x_out writes visible before re-reading them
   for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-    float a = rr ? bf16_bits_to_float(xo ? xo[c] : float_to_bf16_bits(bf16_bits_to_float(xr[c]) +
-                                                                     bf16_bits_to_float(rr[c])))
-                 : bf16_bits_to_float(xr[c]);
+    float a = rr ? bf16_bits_to_float(xo ? xo[c]
+                                         : float_to_bf16_bits(bf16_bits_to_float(ld_act_u16(xr + c)) +
+                                                              bf16_bits_to_float(ld_act_u16(rr + c))))
+                 : bf16_bits_to_float(ld_act_u16(xr + c));
     float o = a * inv;
     if (w) o *= bf16_bits_to_float(w[c]);
     yr[c] = float_to_bf16_bits(o);
@@ -133,7 +145,7 @@ __global__ void rope_kernel(const uint16_t *__restrict__ x, const uint16_t *__re
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int r = static_cast<int>(i / half), j = static_cast<int>(i % half);
     int arow = r / rows_per_angle;
-    if (pos) arow = pos[arow];
+    if (pos) arow = ld_act_i32(pos + arow);
     float c, s;
     if (angles_f32) {
       c = angles_f32[static_cast<int64_t>(arow) * cols + 2 * j];
@@ -145,11 +157,11 @@ __global__ void rope_kernel(const uint16_t *__restrict__ x, const uint16_t *__re
     const uint16_t *xr = x + static_cast<int64_t>(r) * cols;
     uint16_t *yr = y + static_cast<int64_t>(r) * cols;
     if (method == 0) {
-      const float x1 = bf16_bits_to_float(xr[j]), x2 = bf16_bits_to_float(xr[j + half]);
+      const float x1 = bf16_bits_to_float(ld_act_u16(xr + j)), x2 = bf16_bits_to_float(ld_act_u16(xr + j + half));
       yr[j] = float_to_bf16_bits(x1 * c - x2 * s);
       yr[j + half] = float_to_bf16_bits(x2 * c + x1 * s);
     } else {
-      const float xe = bf16_bits_to_float(xr[2 * j]), xo = bf16_bits_to_float(xr[2 * j + 1]);
+      const float xe = bf16_bits_to_float(ld_act_u16(xr + 2 * j)), xo = bf16_bits_to_float(ld_act_u16(xr + 2 * j + 1));
       yr[2 * j] = float_to_bf16_bits(xe * c - xo * s);
       yr[2 * j + 1] = float_to_bf16_bits(xe * s + xo * c);
     }
@@ -165,20 +177,20 @@ __global__ void softmax_kernel(const uint16_t *__restrict__ x, uint16_t *__restr
   __shared__ float scratch[32];
   pdl_launch_dependents();  // at entry: the next kernel may start its weight / cache loads
   pdl_wait();
-  if (valid_dev) valid = *valid_dev;
+  if (valid_dev) valid = ld_act_i32(valid_dev);
   valid = max(0, min(valid, cols));
   const int64_t row = blockIdx.x;
   const uint16_t *xr = x + row * cols;
   uint16_t *yr = y + row * cols;
   float m = -INFINITY;
-  for (int c = threadIdx.x; c < valid; c += blockDim.x) m = fmaxf(m, bf16_bits_to_float(xr[c]));
+  for (int c = threadIdx.x; c < valid; c += blockDim.x) m = fmaxf(m, bf16_bits_to_float(ld_act_u16(xr + c)));
   m = block_max(m, scratch);
   float s = 0.f;
-  for (int c = threadIdx.x; c < valid; c += blockDim.x) s += __expf(bf16_bits_to_float(xr[c]) - m);
+  for (int c = threadIdx.x; c < valid; c += blockDim.x) s += __expf(bf16_bits_to_float(ld_act_u16(xr + c)) - m);
   s = block_sum(s, scratch);
   const float inv = 1.f / s;
   for (int c = threadIdx.x; c < cols; c += blockDim.x)
-    yr[c] = float_to_bf16_bits(c < valid ? __expf(bf16_bits_to_float(xr[c]) - m) * inv : 0.f);
+    yr[c] = float_to_bf16_bits(c < valid ? __expf(bf16_bits_to_float(ld_act_u16(xr + c)) - m) * inv : 0.f);
 }
 
 // ---------------------------------------------------------------------------
@@ -194,8 +206,8 @@ __global__ void eltwise_kernel(const uint16_t *__restrict__ a, const uint16_t *_
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8; i += stride) {
     float fa[8], fb[8] = {0, 0, 0, 0, 0, 0, 0, 0}, o[8];
-    unpack8(reinterpret_cast<const uint4 *>(a)[i], fa);
-    if (op != 0) unpack8(reinterpret_cast<const uint4 *>(b)[i], fb);
+    unpack8(ld_act_v4(a + 8 * i), fa);
+    if (op != 0) unpack8(ld_act_v4(b + 8 * i), fb);
 #pragma unroll
     for (int k = 0; k < 8; ++k)
       o[k] = op == 0 ? silu_f(fa[k]) : op == 1 ? fa[k] * fb[k] : op == 2 ? fa[k] + fb[k]
@@ -203,8 +215,8 @@ __global__ void eltwise_kernel(const uint16_t *__restrict__ a, const uint16_t *_
     reinterpret_cast<uint4 *>(y)[i] = pack8(o);
   }
   for (int64_t i = n8 * 8 + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n; i += stride) {
-    const float fa = bf16_bits_to_float(a[i]);
-    const float fb = op != 0 ? bf16_bits_to_float(b[i]) : 0.f;
+    const float fa = bf16_bits_to_float(ld_act_u16(a + i));
+    const float fb = op != 0 ? bf16_bits_to_float(ld_act_u16(b + i)) : 0.f;
     const float o = op == 0 ? silu_f(fa) : op == 1 ? fa * fb : op == 2 ? fa + fb : silu_f(fa) * fb;
     y[i] = float_to_bf16_bits(o);
   }
@@ -239,7 +251,7 @@ __global__ void strided_copy_kernel(const T *__restrict__ in, T *__restrict__ ou
                                     int64_t out_size) {
   pdl_launch_dependents();  // at entry: the next kernel may start its weight / cache loads
   pdl_wait();
-  const int64_t ia = in_add ? *in_add : 0, oa = out_add ? *out_add : 0;
+  const int64_t ia = in_add ? ld_act_i32(in_add) : 0, oa = out_add ? ld_act_i32(out_add) : 0;
   const int64_t total = per_channel * channels;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -247,7 +259,7 @@ __global__ void strided_copy_kernel(const T *__restrict__ in, T *__restrict__ ou
     const int64_t j = i - c * per_channel;
     const int64_t so = tap_offset(src, src_split3, c, j) + ia;
     const int64_t d = tap_offset(dst, dst_split3, c, j) + oa;
-    if (so >= 0 && so < in_size && d >= 0 && d < out_size) out[d] = in[so];
+    if (so >= 0 && so < in_size && d >= 0 && d < out_size) out[d] = ld_act(in + so);
   }
 }
 
@@ -261,7 +273,7 @@ __global__ void repeat_kernel(const uint4 *__restrict__ in, uint4 *__restrict__ 
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t orow = i / row_vecs, v = i - orow * row_vecs;
-    out[i] = in[(orow / repeat) * row_vecs + v];
+    out[i] = ld_act(in + (orow / repeat) * row_vecs + v);
   }
 }
 
@@ -277,7 +289,7 @@ __global__ void transpose_kernel(const T *__restrict__ in, T *__restrict__ out, 
   const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
     const int r = r0 + i, c = c0 + threadIdx.x;
-    if (r < M && c < N) tile[i][threadIdx.x] = src[static_cast<int64_t>(r) * N + c];
+    if (r < M && c < N) tile[i][threadIdx.x] = ld_act(src + static_cast<int64_t>(r) * N + c);
   }
   __syncthreads();
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
