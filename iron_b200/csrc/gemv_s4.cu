@@ -155,31 +155,41 @@ __device__ __forceinline__ unsigned long long s4_argmax_key(float v, int row) {
 // a residual add or the SwiGLU of interleaved gate/up rows on the output, and the
 // greedy argmax of each output vector (amax != null: 64-bit keys, larger value then
 // lower row wins).
-// The residual values a store adds (C-fragment layout), loaded early: they were
-// written before this kernel's wait returned, so warp 0 fetches them right after it.
-template <int NT>
-__device__ __forceinline__ void s4_load_residual(float (&r)[NT][4], int tile, int N, int n_vec,
-                                                 const uint16_t *__restrict__ residual) {
-  const int lane = threadIdx.x & 31, gid = lane >> 2, tid = lane & 3;
+// The residual a tile's store adds, res_s[v * 16 + r] = residual[v, 16 tile + r]:
+// every thread requests its share right after griddepcontrol.wait (it was written
+// before the wait returned). Up to 16 vectors (one value per thread) it stays in a
+// register until the thread's dot products are done, so nothing waits on it early;
+// wider tiles park it at once (8 values per thread would spill).
+template <int NT, int kThreads>
+struct S4Residual {
+  static constexpr int kPer = (16 * 8 * NT + kThreads - 1) / kThreads;
+  static constexpr bool kHold = NT <= 2;
+  float r[kHold ? kPer : 1];
+  __device__ __forceinline__ void load(float *res_s, int tile, int N, int n_vec, const uint16_t *residual) {
 #pragma unroll
-  for (int t = 0; t < NT; ++t)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int row = tile * 16 + gid + ((e >> 1) << 3);
-      const int vv = t * 8 + tid * 2 + (e & 1);
-      r[t][e] = (residual && vv < n_vec) ? bf16_bits_to_float(ld_act_u16(residual + static_cast<int64_t>(vv) * N + row)) : 0.f;
+    for (int k = 0; k < kPer; ++k) {
+      const int i = threadIdx.x + k * kThreads;
+      const float v = i < 16 * n_vec
+                          ? bf16_bits_to_float(ld_act_u16(residual + static_cast<int64_t>(i >> 4) * N + tile * 16 + (i & 15)))
+                          : 0.f;
+      if constexpr (kHold) r[k] = v;
+      else if (i < 16 * n_vec) res_s[i] = v;
     }
-}
-
-// Up to 16 vectors the residual is preloaded (res); wider tiles read it here, where
-// 4 x NT more live registers would spill.
-template <int NT>
-constexpr bool s4_preload_residual() { return NT <= 2; }
+  }
+  __device__ __forceinline__ void park(float *res_s, int n_vec) const {
+    if constexpr (kHold) {
+#pragma unroll
+      for (int k = 0; k < kPer; ++k) {
+        const int i = threadIdx.x + k * kThreads;
+        if (i < 16 * n_vec) res_s[i] = r[k];
+      }
+    }
+  }
+};
 
 template <int NT>
 __device__ __forceinline__ void s4_store(const float (&v)[NT][4], int tile, int N, int n_vec,
-                                         uint16_t *__restrict__ y, const uint16_t *residual,
-                                         const float (&res)[NT][4], int swiglu,
+                                         uint16_t *__restrict__ y, const float *res_s, int swiglu,
                                          unsigned long long *amax = nullptr) {
   const int lane = threadIdx.x & 31, gid = lane >> 2, tid = lane & 3;
   const int row0 = tile * 16;
@@ -211,9 +221,7 @@ __device__ __forceinline__ void s4_store(const float (&v)[NT][4], int tile, int 
         float r = v[t][e];
         // the residual is added to the bf16-rounded projection, as IRON adds two
         // bf16 buffers (iron/operators/elementwise_add/reference.py:7-9)
-        if (residual)
-          r = __bfloat162float(__float2bfloat16_rn(r)) +
-              (s4_preload_residual<NT>() ? res[t][e] : bf16_bits_to_float(ld_act_u16(residual + o)));
+        if (res_s) r = __bfloat162float(__float2bfloat16_rn(r)) + res_s[vv * 16 + (row - row0)];
         const uint16_t yb = float_to_bf16_bits(r);
         y[o] = yb;
         if (amax) {
@@ -355,10 +363,10 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
   if constexpr (!norm) pdl_launch_dependents();
   pdl_wait();
   if constexpr (norm) pdl_launch_dependents();
-  float res[NT][4];
-  if constexpr (s4_preload_residual<NT>()) {
-    if (warp == 0 && rank == 0) s4_load_residual<NT>(res, tile, N, n_vec, epi.residual);
-  }
+  __shared__ float res_s[16 * 8 * NT];
+  const bool has_res = epi.residual != nullptr && rank == 0;
+  S4Residual<NT, 32 * kT4Warps> rres;
+  if (has_res) rres.load(res_s, tile, N, n_vec, epi.residual);
   if constexpr (norm) {
     // RMSNorm (rmsnorm_kernel's arithmetic): one pass over the whole x for the sums of
     // squares that also parks this CTA's k range in shared memory, then the range
@@ -416,6 +424,7 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
     }
     if (c0 + kT4Units < kr.e) load(c0 + kT4Units);
   }
+  if (has_res) rres.park(res_s, n_vec);
   // reduce over warps (and cluster ranks) in fixed order
 #pragma unroll
   for (int t = 0; t < NT; ++t)
@@ -458,7 +467,7 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
   if constexpr (kAR && NT == 1) {
     if (warp == 0) s4_allreduce_tile(v[0], tile, N, n_vec, epi.ar);
   }
-  if (warp == 0) s4_store<NT>(v, tile, N, n_vec, y, epi.residual, res, epi.swiglu, epi.amax);
+  if (warp == 0) s4_store<NT>(v, tile, N, n_vec, y, epi.residual ? res_s : nullptr, epi.swiglu, epi.amax);
 }
 
 // Repack natural-layout codes [N, K/2] + scales [N, K/32] into GEMV units.
@@ -546,14 +555,19 @@ template <int NT>
 static int launch_s4_tile_cs(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,
                              int n_vec, const S4Epi &res, bool pdl, cudaStream_t s) {
   // split K over a cluster until every SM holds >= 2 CTAs (and each warp >= 1 chunk)
+  // (64-vector tiles stop at clusters of 4: their reduction slots and residual fill
+  // the static shared memory)
+  constexpr int kMaxCS = NT >= 8 ? 4 : 8;
   const int tiles = N / 16, cpt = K / 128;
   int cs = 1;
-  while (cs < 8 && tiles * cs < 2 * sm_count() && cpt >= s4_warps<NT>() * cs * 2) cs *= 2;
+  while (cs < kMaxCS && tiles * cs < 2 * sm_count() && cpt >= s4_warps<NT>() * cs * 2) cs *= 2;
   switch (cs) {
     case 1: return launch_s4_tile<NT, 1>(packed, x, y, N, K, n_vec, res, pdl, s);
     case 2: return launch_s4_tile<NT, 2>(packed, x, y, N, K, n_vec, res, pdl, s);
     case 4: return launch_s4_tile<NT, 4>(packed, x, y, N, K, n_vec, res, pdl, s);
-    default: return launch_s4_tile<NT, 8>(packed, x, y, N, K, n_vec, res, pdl, s);
+    default:
+      if constexpr (kMaxCS == 8) return launch_s4_tile<NT, 8>(packed, x, y, N, K, n_vec, res, pdl, s);
+      else return launch_s4_tile<NT, 4>(packed, x, y, N, K, n_vec, res, pdl, s);
   }
 }
 
