@@ -517,7 +517,8 @@ def _int4_gemv_figure(pdl: bool, n_vec: int = 1, launches: int = 4096):
     packed = torch.stack([GEMV.pack_int4g32(codes[j], scales[j]) for j in range(copies)])
     del codes, scales
     lib, cap = _lib.load(), torch.cuda.Stream()
-    flags = _lib.IRON_FLAG_PDL if pdl else 0
+    # x is written by none of the chained launches: the read-only activation path holds
+    flags = (_lib.IRON_FLAG_PDL if pdl else 0) | _lib.IRON_FLAG_X_READONLY
     pstride = packed[0].numel()
     per = copies * max(1, 256 // copies)
     graph = torch.cuda.CUDAGraph()

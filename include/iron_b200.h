@@ -49,6 +49,15 @@ typedef enum {
  * 8 matching up rows; y gets N/2 columns: bf16(silu(gate)) * up, IRON's
  * SwiGLUDecode rounding (iron/operators/swiglu_decode/reference.py:49-53). */
 #define IRON_FLAG_SWIGLU 0x2u
+/* int4 GEMVs: x is written by no kernel that can still run while this one does, so
+ * it may be read through the read-only (non-coherent) path. Without the flag x is read
+ * with L2-coherent loads. With programmatic dependent launch a kernel starts before
+ * its predecessors end, so the flag is only for callers that bound their windows: a
+ * GEMV that adds a residual lets its dependents launch only after its own wait, and
+ * every activation buffer is rewritten only in a later window than its last reader
+ * (the Llama decode step and tensor-parallel block: o_proj and down_proj bound each
+ * layer's two windows). */
+#define IRON_FLAG_X_READONLY 0x4u
 
 /* GEMV epilogues (applied in fp32 to each output before the bf16 store). */
 #define IRON_EPI_NONE 0

@@ -17,6 +17,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libiron_b200.so"
 IRON_OK = 0
 IRON_FLAG_PDL = 0x1
 IRON_FLAG_SWIGLU = 0x2
+IRON_FLAG_X_READONLY = 0x4
 (IRON_OK, IRON_ERR_NULL, IRON_ERR_SHAPE, IRON_ERR_ALIGN, IRON_ERR_UNSUPPORTED, IRON_ERR_CUDA,
  IRON_ERR_WORKSPACE, IRON_ERR_TIMEOUT, IRON_ERR_ARG) = (0, -1, -2, -3, -4, -5, -6, -7, -8)
 IRON_EPI_NONE = 0

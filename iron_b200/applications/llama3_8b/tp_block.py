@@ -111,6 +111,10 @@ class TPDecoderBlock:
         self.group = group
         self.dev = torch.device("cuda", torch.cuda.current_device())
         self.flags = _lib.IRON_FLAG_PDL if pdl else 0
+        # GEMVs read activations through the read-only path: the block keeps the PDL
+        # windows that needs (o_proj / down_proj add residuals and bound them; with NCCL
+        # the all-reduce kernels, which start only after their predecessor ends, do)
+        self.gflags = self.flags | _lib.IRON_FLAG_X_READONLY
         self.sh = shard_of(shape, tp, rank)
         W = random_block_weights(shape, seed, self.dev)
         self.full = W if keep_full else None
@@ -181,18 +185,18 @@ class TPDecoderBlock:
         call, p = _lib.call, (lambda t: t.data_ptr())
         hd, E = s.head_dim, s.hidden
         call("iron_rmsnorm", p(self.x), None, None, p(self.n1), p(self.xn), B, E, s.eps, f, stream)
-        call("iron_gemv_int4g32", p(self.w["qkv"]), p(self.xn), p(self.qkv), self.dims["qkv"][0], E, B, None, f,
-             stream)
+        call("iron_gemv_int4g32", p(self.w["qkv"]), p(self.xn), p(self.qkv), self.dims["qkv"][0], E, B, None,
+             self.gflags, stream)
         kv_b, kv_h = self.hk * self.L * hd, self.L * hd
         # RoPE + KV append inside the attention kernel (q, k, v of the local heads)
         call("iron_attn_decode_qkv", p(self.qkv), p(self.pos), p(self.lut), p(self.kc), p(self.vc), p(self.attn), B,
              self.hq, self.hk, hd, self.L, kv_b, kv_h, 1.0 / math.sqrt(hd), p(self.ws), self.ws.numel(), f, stream)
         if self.fused:
             call("iron_gemv_int4g32_allreduce", p(self.w["o"]), p(self.attn), p(self.h), E, self.dims["o"][1], B,
-                 p(self.x), ctypes.addressof(self.site_o.peers), f, stream)
+                 p(self.x), ctypes.addressof(self.site_o.peers), self.gflags, stream)
         else:
             call("iron_gemv_int4g32", p(self.w["o"]), p(self.attn), p(self.h), E, self.dims["o"][1], B,
-                 p(self.x) if self.rank == 0 else None, f, stream)
+                 p(self.x) if self.rank == 0 else None, self.gflags, stream)
 
     def _mlp_half(self, stream: int):
         """RMSNorm -> gate/up + SwiGLU -> down_proj: x (partial / sum as above)."""
@@ -201,13 +205,13 @@ class TPDecoderBlock:
         E = s.hidden
         call("iron_rmsnorm", p(self.h), None, None, p(self.n2), p(self.xn), B, E, s.eps, f, stream)
         call("iron_gemv_int4g32", p(self.w["gu"]), p(self.xn), p(self.act), self.dims["gu"][0], E, B, None,
-             f | _lib.IRON_FLAG_SWIGLU, stream)
+             self.gflags | _lib.IRON_FLAG_SWIGLU, stream)
         if self.fused:
             call("iron_gemv_int4g32_allreduce", p(self.w["d"]), p(self.act), p(self.x), E, self.dims["d"][1], B,
-                 p(self.h), ctypes.addressof(self.site_d.peers), f, stream)
+                 p(self.h), ctypes.addressof(self.site_d.peers), self.gflags, stream)
         else:
             call("iron_gemv_int4g32", p(self.w["d"]), p(self.act), p(self.x), E, self.dims["d"][1], B,
-                 p(self.h) if self.rank == 0 else None, f, stream)
+                 p(self.h) if self.rank == 0 else None, self.gflags, stream)
 
     def step(self):
         """x <- block(x) for every sequence at its position pos[b] (caches updated)."""

@@ -215,6 +215,9 @@ class LlamaDecodeEngine:
         the lm-head GEMV with the final RMSNorm and the argmax fused, and the token
         update."""
         s, B, f = self.s, self.B, self.flags
+        # the step keeps the PDL windows the read-only activation path needs (its o_proj
+        # and down_proj GEMVs add residuals and so bound each layer's two windows)
+        fg = f | _lib.IRON_FLAG_X_READONLY
         call, p = _lib.call, (lambda t: t.data_ptr())
         E, Hd, L = s.emb_dim, s.head_dim, self.L
         kv_b, kv_h = s.n_kv_groups * L * Hd, L * Hd
@@ -224,11 +227,11 @@ class LlamaDecodeEngine:
             kc, vc = self.kc[li], self.vc[li]
             if fuse_norm:
                 call("iron_gemv_int4g32_ex", p(lay["qkv"].packed), p(self.x), p(self.qkv), s.qkv_dim, E, B, None,
-                     p(lay["n1"]), s.eps, None, f, stream)
+                     p(lay["n1"]), s.eps, None, fg, stream)
             else:
                 call("iron_rmsnorm", p(self.x), None, None, p(lay["n1"]), p(self.xn), B, E, s.eps, f, stream)
                 call("iron_gemv_int4g32", p(lay["qkv"].packed), p(self.xn), p(self.qkv), s.qkv_dim, E, B,
-                     None, f, stream)
+                     None, fg, stream)
             if self.fuse_rope:
                 call("iron_attn_decode_qkv", p(self.qkv), p(self.pos), p(self.lut), p(kc), p(vc), p(self.attn), B,
                      s.n_heads, s.n_kv_groups, Hd, L, kv_b, kv_h, 1.0 / math.sqrt(Hd), p(self.attn_ws),
@@ -240,23 +243,23 @@ class LlamaDecodeEngine:
                      s.n_kv_groups, Hd, L, kv_b, kv_h, 1.0 / math.sqrt(Hd), p(self.attn_ws),
                      self.attn_ws.numel(), f, stream)
             call("iron_gemv_int4g32", p(lay["o"].packed), p(self.attn), p(self.h), E, s.n_heads * Hd, B,
-                 p(self.x), f, stream)
+                 p(self.x), fg, stream)
             if fuse_norm:
                 call("iron_gemv_int4g32_ex", p(lay["gu"].packed), p(self.h), p(self.act), 2 * s.hidden_dim, E, B,
-                     None, p(lay["n2"]), s.eps, None, f | _lib.IRON_FLAG_SWIGLU, stream)
+                     None, p(lay["n2"]), s.eps, None, fg | _lib.IRON_FLAG_SWIGLU, stream)
             else:
                 call("iron_rmsnorm", p(self.h), None, None, p(lay["n2"]), p(self.xn), B, E, s.eps, f, stream)
                 call("iron_gemv_int4g32", p(lay["gu"].packed), p(self.xn), p(self.act), 2 * s.hidden_dim, E,
-                     B, None, f | _lib.IRON_FLAG_SWIGLU, stream)
+                     B, None, fg | _lib.IRON_FLAG_SWIGLU, stream)
             call("iron_gemv_int4g32", p(lay["d"].packed), p(self.act), p(self.x), E, s.hidden_dim, B,
-                 p(self.h), f, stream)
+                 p(self.h), fg, stream)
         if self.fuse_norm == "all":
             call("iron_gemv_int4g32_ex", p(self.lm.packed), p(self.x), p(self.logits), s.vocab_size, E, B, None,
-                 p(self.nf), s.eps, p(self.amax), f, stream)
+                 p(self.nf), s.eps, p(self.amax), fg, stream)
         else:
             call("iron_rmsnorm", p(self.x), None, None, p(self.nf), p(self.xn), B, E, s.eps, f, stream)
             call("iron_gemv_int4g32_ex", p(self.lm.packed), p(self.xn), p(self.logits), s.vocab_size, E, B, None,
-                 None, 0.0, p(self.amax), f, stream)
+                 None, 0.0, p(self.amax), fg, stream)
         call("iron_argmax_finalize", p(self.amax), p(self.tokens), p(self.pos), B, f, stream)
 
     # -- prefill: a whole prompt through the tensor-core GEMMs -----------------------------

@@ -84,46 +84,31 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 // so a kernel can start -- and its SM's L1 be refilled by other kernels still running
 // there -- before the data it reads after griddepcontrol.wait is written. Two rules
 // keep every read fresh:
-//  - kernels that bound a window trigger their dependents only after their own wait
-//    (the RMSNorm kernels, two per decode layer; RoPE + KV append; a GEMV with the
-//    RMSNorm prologue; the embedding gather that starts a step), so every reader of a
-//    buffer's previous contents has finished before any kernel that reads its next
-//    contents is launched;
-//  - small kernels read such data with these loads (cached in L2 only; volatile
-//    keeps them after the wait), while the bandwidth-heavy GEMV activations and cache
-//    rows, written in the same window before their readers' wait, use the read-only
-//    path.
-__device__ __forceinline__ uint4 ld_act_v4(const void *p) {
-  uint4 r;
-  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
-  return r;
-}
-__device__ __forceinline__ uint2 ld_act_v2(const void *p) {
-  uint2 r;
-  asm volatile("ld.global.cg.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
-  return r;
-}
-__device__ __forceinline__ uint32_t ld_act_u32(const void *p) {
-  uint32_t r;
-  asm volatile("ld.global.cg.u32 %0, [%1];" : "=r"(r) : "l"(p));
-  return r;
-}
+//  - kernels that bound a window trigger their dependents only after their own wait:
+//    the int4 GEMVs that add a residual (o_proj and down_proj, two per decoder layer),
+//    RoPE + KV append and the embedding gather that starts a step. Between two bounds
+//    every activation buffer is written once, and every reader of its previous
+//    contents sits before the earlier bound, so it has finished before any kernel
+//    that reads the new contents is launched;
+//  - small kernels read such data with these loads (ld.global.cg: cached in L2 only;
+//    the wait's memory clobber keeps them after it), while the bandwidth-heavy GEMV
+//    activations and cache rows, written in the same window before their readers'
+//    wait, use the read-only path where the caller keeps these windows.
+__device__ __forceinline__ uint4 ld_act_v4(const void *p) { return __ldcg(reinterpret_cast<const uint4 *>(p)); }
+__device__ __forceinline__ uint2 ld_act_v2(const void *p) { return __ldcg(reinterpret_cast<const uint2 *>(p)); }
+__device__ __forceinline__ uint32_t ld_act_u32(const void *p) { return __ldcg(reinterpret_cast<const unsigned *>(p)); }
 __device__ __forceinline__ uint16_t ld_act_u16(const void *p) {
-  uint16_t r;
-  asm volatile("ld.global.cg.u16 %0, [%1];" : "=h"(r) : "l"(p));
-  return r;
+  return __ldcg(reinterpret_cast<const unsigned short *>(p));
 }
-__device__ __forceinline__ float ld_act_f32(const float *p) { return __uint_as_float(ld_act_u32(p)); }
-__device__ __forceinline__ int ld_act_i32(const int *p) { return static_cast<int>(ld_act_u32(p)); }
+__device__ __forceinline__ float ld_act_f32(const float *p) { return __ldcg(p); }
+__device__ __forceinline__ int ld_act_i32(const int *p) { return __ldcg(p); }
 template <typename T>
 __device__ __forceinline__ T ld_act(const T *p) {
   static_assert(sizeof(T) == 1 || sizeof(T) == 2 || sizeof(T) == 4 || sizeof(T) == 8 || sizeof(T) == 16,
                 "1/2/4/8/16-byte elements");
   T r;
   if constexpr (sizeof(T) == 1) {
-    uint16_t v;
-    asm volatile("ld.global.cg.u8 %0, [%1];" : "=h"(v) : "l"(p));
-    const uint8_t b = static_cast<uint8_t>(v);
+    const unsigned char b = __ldcg(reinterpret_cast<const unsigned char *>(p));
     memcpy(&r, &b, 1);
   } else if constexpr (sizeof(T) == 2) {
     const uint16_t v = ld_act_u16(p);

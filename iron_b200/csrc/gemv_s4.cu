@@ -63,6 +63,7 @@ struct S4Epi {
   float eps;
   unsigned long long *amax;
   S4AllReduce ar;  // ar.world > 1: all-reduce the output over the ranks first
+  int x_ro;        // IRON_FLAG_X_READONLY: x through the read-only path, else L2-coherent loads
 };
 
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
@@ -251,7 +252,7 @@ __device__ __forceinline__ void s4_store(const float (&v)[NT][4], int tile, int 
   }
 }
 
-template <int NT, bool kShared = false>
+template <int NT, bool kShared = false, bool kRO = false>
 __device__ __forceinline__ void s4_unit_gx(float (&d)[2][NT][4], const uint4 &clo, const uint4 &chi,
                                            const uint4 &sc, const uint16_t *__restrict__ x, int K,
                                            int n_vec, int kbase, int ldx = -1, int xoff = 0) {
@@ -270,7 +271,11 @@ __device__ __forceinline__ void s4_unit_gx(float (&d)[2][NT][4], const uint4 &cl
         if constexpr (kShared)
           xr[j][t] = *reinterpret_cast<const uint4 *>(x + vv * ldx + kbase - xoff + j * 32 + tid * 8);
         else
-          xr[j][t] = __ldg(reinterpret_cast<const uint4 *>(x + static_cast<int64_t>(vv) * K + kbase + j * 32 + tid * 8));
+        {
+          const uint16_t *px = x + static_cast<int64_t>(vv) * K + kbase + j * 32 + tid * 8;
+          if constexpr (kRO) xr[j][t] = __ldg(reinterpret_cast<const uint4 *>(px));
+          else xr[j][t] = ld_act_v4(px);
+        }
       }
     }
 #pragma unroll
@@ -311,7 +316,7 @@ constexpr int s4_units() { return NT <= 2 ? 2 : 4; }
 // kNorm: the RMSNorm prologue (n_vec <= 8) -- x normalised into shared memory first.
 // (Staging a plain x the same way measured slower on B200: 4.16 against 3.77 us per
 // config-2 launch; the per-unit L1 reads overlap better than one synchronised copy.)
-template <int NT, int CS, bool kNorm = false, bool kAR = false>
+template <int NT, int CS, bool kNorm = false, bool kAR = false, bool kRO = false>
 __global__ void __launch_bounds__(32 * s4_warps<NT>())
 gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__restrict__ x,
                        uint16_t *__restrict__ y, int N, int K, int n_vec, S4Epi epi) {
@@ -358,11 +363,12 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
       if (k < klen) wreg[j] = __ldg(reinterpret_cast<const uint4 *>(epi.norm_w + kc0 + k));
     }
   }
-  // with the RMSNorm prologue this GEMV bounds a window (see ld_act_v4): it lets its
-  // dependents launch only after its wait
-  if constexpr (!norm) pdl_launch_dependents();
+  // a GEMV that adds a residual (a decoder block's o_proj and down_proj) bounds a
+  // window (see ld_act_v4): its dependents launch only after its wait
+  const bool bound = epi.residual != nullptr;
+  if (!bound) pdl_launch_dependents();
   pdl_wait();
-  if constexpr (norm) pdl_launch_dependents();
+  if (bound) pdl_launch_dependents();
   __shared__ float res_s[16 * 8 * NT];
   const bool has_res = epi.residual != nullptr && rank == 0;
   S4Residual<NT, 32 * kT4Warps> rres;
@@ -419,7 +425,7 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
         // B fragments straight from the activations (L1-cached) or the normalised
         // slice: this lane's 8 consecutive k of chunk j are k 0-7 of its code word
         if constexpr (norm) s4_unit_gx<NT, true>(acc, lo[u], hi[u], sc[u], xs_norm, K, n_vec, c * 128, klen, kc0);
-        else s4_unit_gx<NT>(acc, lo[u], hi[u], sc[u], x, K, n_vec, c * 128);
+        else s4_unit_gx<NT, false, kRO>(acc, lo[u], hi[u], sc[u], x, K, n_vec, c * 128);
       }
     }
     if (c0 + kT4Units < kr.e) load(c0 + kT4Units);
@@ -538,10 +544,13 @@ static int launch_s4_tile(const uint8_t *packed, const uint16_t *x, uint16_t *y,
   cudaError_t e;
   if (epi.ar.world > 1) {
     if constexpr (NT != 1) return IRON_ERR_SHAPE;
-    e = cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, true>, packed, x, y, N, K, n_vec, epi);
+    e = epi.x_ro ? cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, true, true>, packed, x, y, N, K, n_vec, epi)
+                 : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, true, false>, packed, x, y, N, K, n_vec, epi);
+  } else if (epi.norm_w) {
+    e = cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, true>, packed, x, y, N, K, n_vec, epi);
   } else {
-    e = epi.norm_w ? cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, true>, packed, x, y, N, K, n_vec, epi)
-                   : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, false>, packed, x, y, N, K, n_vec, epi);
+    e = epi.x_ro ? cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, false, false, true>, packed, x, y, N, K, n_vec, epi)
+                 : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, false, false, false>, packed, x, y, N, K, n_vec, epi);
   }
   if (e != cudaSuccess) {
     set_last_cuda_error(e);
@@ -649,7 +658,7 @@ extern "C" int iron_gemv_int4g32_ex(const uint8_t *packed, const uint16_t *x, ui
     if (n_vec > 8 || K > 2048) return IRON_ERR_SHAPE;  // the fused prologue's shared slice and registers
     if (!aligned16(norm_weight)) return IRON_ERR_ALIGN;
   }
-  S4Epi epi{residual, swiglu, norm_weight, eps, argmax_keys, {}};
+  S4Epi epi{residual, swiglu, norm_weight, eps, argmax_keys, {}, (flags & IRON_FLAG_X_READONLY) ? 1 : 0};
   epi.ar.world = 1;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (n_vec <= 8) return launch_s4_tile_cs<1>(packed, x, y, N, K, n_vec, epi, pdl, s);
@@ -669,7 +678,7 @@ extern "C" int iron_gemv_int4g32_allreduce(const uint8_t *packed, const uint16_t
   if (N <= 0 || K <= 0 || n_vec <= 0 || n_vec > 8 || K % 128 || N % 16) return IRON_ERR_SHAPE;
   if (!aligned16(packed) || !aligned16(x)) return IRON_ERR_ALIGN;
   if (flags & IRON_FLAG_SWIGLU) return IRON_ERR_ARG;
-  S4Epi epi{residual, 0, nullptr, 0.f, nullptr, {}};
+  S4Epi epi{residual, 0, nullptr, 0.f, nullptr, {}, (flags & IRON_FLAG_X_READONLY) ? 1 : 0};
   std::memcpy(&epi.ar, peers, sizeof(S4AllReduce));
   if (epi.ar.world < 1 || epi.ar.world > kS4MaxWorld || epi.ar.rank < 0 || epi.ar.rank >= epi.ar.world ||
       !epi.ar.status)

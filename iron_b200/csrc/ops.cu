@@ -64,8 +64,8 @@ __global__ void rmsnorm_kernel(const uint16_t *__restrict__ x, const uint16_t *_
     const int c = threadIdx.x * 8 + n * stride;
     wv[n] = (vec && w && c < cols) ? *reinterpret_cast<const uint4 *>(w + c) : make_uint4(0u, 0u, 0u, 0u);
   }
+  pdl_launch_dependents();  // at entry: the next kernel may start its weight loads
   pdl_wait();
-  pdl_launch_dependents();  // after the wait: this kernel bounds a window (see ld_act_v4)
   float ss = 0.f;
   if (vec) {
     float v[4][8];
