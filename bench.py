@@ -232,7 +232,8 @@ def run_ours(args, world, rank, local):
     from iron_b200.operators import GEMV
 
     lib = _lib.load()
-    pdl_flag = 0 if args.no_pdl else _lib.IRON_FLAG_PDL
+    # x is written by none of the chained launches: the read-only activation path holds
+    pdl_flag = (0 if args.no_pdl else _lib.IRON_FLAG_PDL) | _lib.IRON_FLAG_X_READONLY
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     sp = stream.cuda_stream

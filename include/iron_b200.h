@@ -49,7 +49,7 @@ typedef enum {
  * 8 matching up rows; y gets N/2 columns: bf16(silu(gate)) * up, IRON's
  * SwiGLUDecode rounding (iron/operators/swiglu_decode/reference.py:49-53). */
 #define IRON_FLAG_SWIGLU 0x2u
-/* int4 GEMVs: x is written by no kernel that can still run while this one does, so
+/* GEMVs (int4 and bf16): x is written by no kernel that can still run while this one does, so
  * it may be read through the read-only (non-coherent) path. Without the flag x is read
  * with L2-coherent loads. With programmatic dependent launch a kernel starts before
  * its predecessors end, so the flag is only for callers that bound their windows: a

@@ -140,7 +140,8 @@ __device__ __forceinline__ void gemv_reduce_store(float (&acc)[NT][4], float *re
 // bf16 GEMV. Chunk = 32 k of a 16-row tile: lane (gid, tid) loads elements
 // [32c + 8 tid, +8) of rows gid and gid+8 (two 16-byte loads) and feeds them as
 // two k16 MMA steps; B is the matching 16 bytes of each vector, unpermuted.
-template <int NT, int CS, int U>
+// kRO: x through the read-only path (IRON_FLAG_X_READONLY), else L2-coherent loads.
+template <int NT, int CS, int U, bool kRO>
 __global__ void __launch_bounds__(kGemvThreads)
 gemv_bf16_kernel(const uint16_t *__restrict__ W, const uint16_t *__restrict__ x,
                  uint16_t *__restrict__ y, int M, int K, int64_t ldw, int64_t w_bstride,
@@ -199,7 +200,10 @@ gemv_bf16_kernel(const uint16_t *__restrict__ W, const uint16_t *__restrict__ x,
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
         const int v = t * 8 + gid;
-        const uint4 xb = (ok && v < n_vec) ? ld_act_v4(x + static_cast<int64_t>(v) * K + k) : zero4();
+        const uint4 xb = (ok && v < n_vec)
+                             ? (kRO ? __ldg(reinterpret_cast<const uint4 *>(x + static_cast<int64_t>(v) * K + k))
+                                    : ld_act_v4(x + static_cast<int64_t>(v) * K + k))
+                             : zero4();
         const uint32_t A0[4] = {n_lo[u].x, n_hi[u].x, n_lo[u].y, n_hi[u].y};
         mma_bf16_16816(acc[t], A0, xb.x, xb.y);
         const uint32_t A1[4] = {n_lo[u].z, n_hi[u].z, n_lo[u].w, n_hi[u].w};
@@ -234,7 +238,7 @@ __global__ void dequant_s4g32_rows_kernel(const uint8_t *__restrict__ Wq,
 template <int NT, int CS>
 static int launch_bf16(const uint16_t *W, const uint16_t *x, uint16_t *y, int M, int K,
                        int64_t ldw, int nb, int64_t wb, int64_t xb, int64_t yb, int n_vec,
-                       const uint16_t *res, int epi, bool pdl, cudaStream_t s) {
+                       const uint16_t *res, int epi, bool pdl, bool ro, cudaStream_t s) {
   dim3 grid(CS, (M + 15) / 16, nb);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -256,8 +260,10 @@ static int launch_bf16(const uint16_t *W, const uint16_t *x, uint16_t *y, int M,
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_bf16_kernel<NT, CS, 4>, W, x, y, M, K, ldw, wb,
-                                     xb, yb, n_vec, res, epi);
+  cudaError_t e = ro ? cudaLaunchKernelEx(&cfg, gemv_bf16_kernel<NT, CS, 4, true>, W, x, y, M, K, ldw, wb, xb, yb,
+                                          n_vec, res, epi)
+                     : cudaLaunchKernelEx(&cfg, gemv_bf16_kernel<NT, CS, 4, false>, W, x, y, M, K, ldw, wb, xb, yb,
+                                          n_vec, res, epi);
   if (e != cudaSuccess) {
     set_last_cuda_error(e);
     (void)cudaGetLastError();
@@ -317,7 +323,7 @@ extern "C" int iron_gemv_bf16(const uint16_t *W, const uint16_t *x, uint16_t *y,
   IRON_DISPATCH_NT(n_vec, IRON_DISPATCH_CS(cs, st = (launch_bf16<NT, CS>(
                                                W, x, y, M, K, ldw, num_batches, w_bstride,
                                                x_bstride, y_bstride, n_vec, residual,
-                                               epilogue, pdl, s))));
+                                               epilogue, pdl, (flags & IRON_FLAG_X_READONLY) != 0, s))));
   return st;
 }
 
