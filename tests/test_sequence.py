@@ -12,7 +12,7 @@ from iron_b200.common.sequence import (CompareDispatch, FusedDispatch, OperatorS
                                        ReferenceDispatch)
 from iron_b200.common.tensor import CPUOnlyTensor, _Intervals
 from iron_b200.common.test_utils import verify_buffer
-from iron_b200.operators import ElementwiseAdd, GEMV, SiLU, Softmax, StridedCopy, SwiGLUDecode
+from iron_b200.operators import ElementwiseAdd, GEMV, SiLU, Softmax, StridedCopy, SwiGLUDecode, SwiGLUPrefill
 
 N = 1024
 NB = 2 * N
@@ -107,6 +107,41 @@ def test_swiglu_decode_reference_dispatch_matches_golden():
     assert not verify_buffer(inter, "intermediate", ls * right, rel_tol=0.04, abs_tol=0.4)
     out = run.get_buffer("out").torch_view().reshape(1, E)
     assert not verify_buffer(out, "out", inter @ d["w_down"], rel_tol=0.04, abs_tol=0.4)
+
+
+def test_swiglu_prefill_reference_dispatch_and_buffers():
+    """SwiGLUPrefill's runlist on the CPU reference dispatch: IRON's buffer names and
+    layouts, both weight layouts, intermediates chained as IRON checks them."""
+    S, E, H = 256, 512, 512
+    for b_col_maj in (False, True):
+        g = torch.Generator().manual_seed(7)
+        x = torch.randn(S, E, generator=g).to(torch.bfloat16)
+        w_gate = (torch.randn(E, H, generator=g) * 0.1).to(torch.bfloat16)  # (K, N)
+        w_up = (torch.randn(E, H, generator=g) * 0.1).to(torch.bfloat16)
+        w_down = (torch.randn(H, E, generator=g) * 0.1).to(torch.bfloat16)
+        seq = SwiGLUPrefill(seq_len=S, embedding_dim=E, hidden_dim=H, b_col_maj=b_col_maj,
+                            dispatch=ReferenceDispatch()).compile()
+        assert seq.name == f"swiglu_prefill_s{S}_e{E}_h{H}" + ("_bc" if b_col_maj else "")
+        run = seq.get_callable()
+
+        def stored(w):
+            return (w.T if b_col_maj else w).contiguous().reshape(-1)
+
+        run.get_buffer("w_gate").torch_view()[:] = stored(w_gate)
+        run.get_buffer("w_up").torch_view()[:] = stored(w_up)
+        run.get_buffer("w_down").torch_view()[:] = stored(w_down)
+        run.get_buffer("in").torch_view()[:] = x.reshape(-1)
+        run()
+        left = run.get_buffer("left").torch_view().reshape(S, H)
+        assert not verify_buffer(left, "left", (x.float() @ w_gate.float()).to(torch.bfloat16), rel_tol=0.04,
+                                 abs_tol=0.4)
+        ls = run.get_buffer("left_swished").torch_view().reshape(S, H)
+        right = run.get_buffer("right").torch_view().reshape(S, H)
+        inter = run.get_buffer("intermediate").torch_view().reshape(S, H)
+        assert not verify_buffer(inter, "intermediate", ls * right, rel_tol=0.04, abs_tol=0.4)
+        out = run.get_buffer("out").torch_view().reshape(S, E)
+        assert not verify_buffer(out, "out", (inter.float() @ w_down.float()).to(torch.bfloat16), rel_tol=0.08,
+                                 abs_tol=0.4, max_error_rate=0.05)
 
 
 def test_intervals():

@@ -11,7 +11,7 @@ from helpers import bf16, load
 from iron_b200.common.sequence import CompareDispatch, OperatorSequence
 from iron_b200.common.test_utils import verify_buffer
 from iron_b200.common.verify import Tolerance
-from iron_b200.operators import ElementwiseAdd, GEMV, SiLU, Softmax, StridedCopy, SwiGLUDecode
+from iron_b200.operators import ElementwiseAdd, GEMV, SiLU, Softmax, StridedCopy, SwiGLUDecode, SwiGLUPrefill
 
 pytestmark = pytest.mark.gpu
 
@@ -182,3 +182,37 @@ def test_swiglu_decode_golden_fixture():
     inter = run.get_buffer("intermediate").to_torch().reshape(1, 512)
     out = run.get_buffer("out").to_torch().reshape(1, 256)
     assert not verify_buffer(out, "output", inter @ d["w_down"], rel_tol=0.04, abs_tol=0.4)
+
+
+@pytest.mark.parametrize("b_col_maj", [False, True])
+def test_swiglu_prefill(b_col_maj):
+    """IRON's swiglu_prefill/test.py on the B200 (seq 256, 2048 / 2048, both weight
+    layouts): IRON's golden recipe, intermediates chained as IRON checks them
+    (gate rel 0.04 / abs 0.4, output rel 0.08 / abs 0.4 with 5 % allowed misses)."""
+    S, E, H = 256, 2048, 2048
+    g = torch.Generator().manual_seed(42)
+    x = torch.randn(S, E, generator=g).to(torch.bfloat16) * 4
+    w_gate = (torch.randn(H, E, generator=g).to(torch.bfloat16) * 4).T  # (K, N)
+    w_up = (torch.randn(H, E, generator=g).to(torch.bfloat16) * 4).T
+    w_down = torch.randn(H, E, generator=g).to(torch.bfloat16) * 4
+    seq = SwiGLUPrefill(seq_len=S, embedding_dim=E, hidden_dim=H, b_col_maj=b_col_maj).compile()
+    run = seq.get_callable()
+
+    def stored(w):
+        return (w.T if b_col_maj else w).contiguous().reshape(-1)
+
+    run.get_buffer("w_gate").torch_view()[:] = stored(w_gate)
+    run.get_buffer("w_up").torch_view()[:] = stored(w_up)
+    run.get_buffer("w_down").torch_view()[:] = stored(w_down)
+    run.get_buffer("in").torch_view()[:] = x.reshape(-1)
+    run()
+    left = run.get_buffer("left").to_torch().reshape(S, H)
+    assert not verify_buffer(left, "left", (x.float() @ w_gate.float()).to(torch.bfloat16), rel_tol=0.04,
+                             abs_tol=0.4)
+    ls = run.get_buffer("left_swished").to_torch().reshape(S, H)
+    right = run.get_buffer("right").to_torch().reshape(S, H)
+    inter = run.get_buffer("intermediate").to_torch().reshape(S, H)
+    assert not verify_buffer(inter, "intermediate", ls * right, rel_tol=0.04, abs_tol=0.4)
+    out = run.get_buffer("out").to_torch().reshape(S, E)
+    assert not verify_buffer(out, "output", (inter.float() @ w_down.float()).to(torch.bfloat16), rel_tol=0.08,
+                             abs_tol=0.4, max_error_rate=0.05)
