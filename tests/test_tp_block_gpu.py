@@ -60,7 +60,7 @@ def test_attention_head_dim_128_ragged():
     lens = torch.tensor([1, 1777, 3000], dtype=torch.int32)
     out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device="cuda")
     wsb = _lib.load().iron_attn_decode_workspace_bytes_d(B, Hq, Hkv, L, D)
-    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(max(wsb, 16), dtype=torch.uint8, device="cuda")
     qd, kd, vd, ld = q.cuda(), k.cuda(), v.cuda(), lens.cuda()
     _lib.call("iron_attn_decode", qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), ld.data_ptr(), out.data_ptr(), B,
               Hq, Hkv, D, L, Hkv * L * D, L * D, 1 / np.sqrt(D), ws.data_ptr(), ws.numel(), 0,

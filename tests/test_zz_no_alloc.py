@@ -52,7 +52,7 @@ def test_noalloc_matches_workspace_entry_point_twice():
         q, k, v, lens = _inputs(B, L, seed)
         need = lib.iron_attn_decode_workspace_bytes(B, 32, 8, L)
         assert 0 < need <= 1 << 20, "case must use split partials within the fixed array"
-        ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+        ws = torch.zeros(need, dtype=torch.uint8, device="cuda")
         ref = _call("iron_attn_decode", q, k, v, lens, ws)
         got = _call("iron_attn_decode_noalloc", q, k, v, lens)
         torch.cuda.synchronize()
