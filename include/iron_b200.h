@@ -124,6 +124,11 @@ int iron_unpack_int4g32(const uint8_t *packed, uint16_t *out, int N, int K, void
 int iron_gemv_int4g32_ex(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K, int n_vec,
                          const uint16_t *residual, const uint16_t *norm_weight, float eps,
                          unsigned long long *argmax_keys, unsigned flags, void *stream);
+/* iron_l2_prefetch (no reference counterpart): requests [ptr, ptr + bytes) into L2
+ * (cp.async.bulk.prefetch.L2 in 64 KB pieces; ptr 16-byte aligned) and returns once
+ * the requests are issued. The decode engine runs it on a side branch of its graph so
+ * later GEMVs' weights stream in while the chain is latency-bound. */
+int iron_l2_prefetch(const void *ptr, size_t bytes, unsigned flags, void *stream);
 int iron_argmax_finalize(unsigned long long *keys, int32_t *tokens, int32_t *pos, int B, unsigned flags,
                          void *stream);
 /* iron_gemv_int4g32_allreduce (no reference counterpart as one call: it replaces a

@@ -64,6 +64,7 @@ SIGNATURES: dict[str, list] = {
     "iron_llama_decode_persistent_scratch_bytes": [c_int, c_int],
     "iron_gemv_int4g32_ex": [P, P, P, c_int, c_int, c_int, P, P, c_float, P, c_uint, P],
     "iron_argmax_finalize": [P, P, P, c_int, c_uint, P],
+    "iron_l2_prefetch": [P, c_size_t, c_uint, P],
     "iron_gemv_int4g32_allreduce": [P, P, P, c_int, c_int, c_int, P, P, c_uint, P],
     "iron_ipc_alloc": [c_size_t, P],
     "iron_ipc_free": [P],

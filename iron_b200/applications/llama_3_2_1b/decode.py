@@ -98,7 +98,7 @@ class LlamaDecodeEngine:
 
     def __init__(self, shape: LlamaShape, batch: int, max_seq: int, seed: int = 0,
                  keep_natural: bool = False, pdl: bool = True, persistent: bool | None = None,
-                 fuse_norm: str | None = None, fuse_rope: bool | None = None):
+                 fuse_norm: str | None = None, fuse_rope: bool | None = None, l2_prefetch: bool | None = None):
         self.s, self.B, self.L = shape, batch, max_seq
         self.dev = torch.device("cuda", torch.cuda.current_device())
         self.flags = _lib.IRON_FLAG_PDL if pdl else 0
@@ -163,6 +163,10 @@ class LlamaDecodeEngine:
             raise ValueError("the fused RMSNorm prologue serves B <= 8")
         # RoPE + KV append inside the attention kernel (else the rope_kv_append kernel)
         self.fuse_rope = fuse_rope if fuse_rope is not None else True
+        # each layer's gate/up and down weights requested into L2 on a side branch of
+        # the step (off the dependent chain) when the layer starts
+        self.l2_prefetch = bool(l2_prefetch) if l2_prefetch is not None else False
+        self._side = torch.cuda.Stream() if self.l2_prefetch else None
         if self.persistent:
             if not fits:
                 raise ValueError("the persistent decode step needs the Llama-3.2-1B layer shape and batch <= 2")
@@ -222,9 +226,16 @@ class LlamaDecodeEngine:
         E, Hd, L = s.emb_dim, s.head_dim, self.L
         kv_b, kv_h = s.n_kv_groups * L * Hd, L * Hd
         fuse_norm = self.fuse_norm != "none"
+        main = torch.cuda.ExternalStream(stream) if self.l2_prefetch else None
         call("iron_embed", p(self.tokens), p(self.embed_table), p(self.x), B, E, s.vocab_size, f, stream)
         for li, lay in enumerate(self.layers):
             kc, vc = self.kc[li], self.vc[li]
+            if self.l2_prefetch:
+                fork = torch.cuda.Event()
+                fork.record(main)
+                self._side.wait_event(fork)
+                for m in ("gu", "d"):
+                    call("iron_l2_prefetch", p(lay[m].packed), lay[m].packed.numel(), 0, self._side.cuda_stream)
             if fuse_norm:
                 call("iron_gemv_int4g32_ex", p(lay["qkv"].packed), p(self.x), p(self.qkv), s.qkv_dim, E, B, None,
                      p(lay["n1"]), s.eps, None, fg, stream)
@@ -261,6 +272,10 @@ class LlamaDecodeEngine:
             call("iron_gemv_int4g32_ex", p(self.lm.packed), p(self.xn), p(self.logits), s.vocab_size, E, B, None,
                  None, 0.0, p(self.amax), fg, stream)
         call("iron_argmax_finalize", p(self.amax), p(self.tokens), p(self.pos), B, f, stream)
+        if self.l2_prefetch:
+            join = torch.cuda.Event()
+            join.record(self._side)
+            main.wait_event(join)
 
     # -- prefill: a whole prompt through the tensor-core GEMMs -----------------------------
     def _prefill_buffers(self, S: int):
@@ -347,7 +362,7 @@ class LlamaDecodeEngine:
         if self.persistent:
             return 1
         per_layer = ((5 if self.fuse_norm != "none" else 7) + (1 if self.attn_ws.numel() > 16 else 0)  # + combine
-                     + (0 if self.fuse_rope else 1))
+                     + (0 if self.fuse_rope else 1) + (2 if self.l2_prefetch else 0))
         return 1 + self.s.n_layers * per_layer + (2 if self.fuse_norm == "all" else 3)
 
     def set_state(self, tokens, positions):

@@ -754,6 +754,30 @@ __global__ void argmax_finalize_kernel(unsigned long long *keys, int *tokens, in
   }
 }
 
+// Bring [ptr, ptr + bytes) into L2 ahead of its readers: each CTA's thread 0 issues
+// cp.async.bulk.prefetch.L2 for one 64 KB piece (fire and forget: the kernel ends
+// when the requests are issued). Meant for a side branch of a decode graph, so the
+// weights of a later GEMV stream in while the main chain is latency-bound.
+constexpr uint32_t kL2PrefetchPiece = 64 * 1024;
+__global__ void l2_prefetch_kernel(const uint8_t *__restrict__ p, size_t bytes) {
+  const size_t off = static_cast<size_t>(blockIdx.x) * kL2PrefetchPiece;
+  if (threadIdx.x != 0 || off >= bytes) return;
+  const size_t left = bytes - off;
+  const uint32_t n = static_cast<uint32_t>(left < kL2PrefetchPiece ? left : kL2PrefetchPiece) & ~15u;
+  if (n) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p + off), "r"(n) : "memory");
+}
+
+extern "C" int iron_l2_prefetch(const void *ptr, size_t bytes, unsigned flags, void *stream) {
+  if (!ptr) return IRON_ERR_NULL;
+  if (bytes == 0) return IRON_OK;
+  if (!aligned16(ptr)) return IRON_ERR_ALIGN;
+  const size_t pieces = (bytes + kL2PrefetchPiece - 1) / kL2PrefetchPiece;
+  if (pieces > 0x7fffffffu) return IRON_ERR_SHAPE;
+  return launch(l2_prefetch_kernel, dim3(static_cast<unsigned>(pieces)), dim3(32), 0,
+                static_cast<cudaStream_t>(stream), (flags & IRON_FLAG_PDL) != 0,
+                static_cast<const uint8_t *>(ptr), bytes);
+}
+
 extern "C" int iron_argmax_finalize(unsigned long long *keys, int32_t *tokens, int32_t *pos, int B, unsigned flags,
                                     void *stream) {
   if (!keys || !tokens) return IRON_ERR_NULL;

@@ -188,3 +188,22 @@ def test_gemv_ex_fused_rmsnorm_and_argmax(n_vec):
     got = y.cpu().float()
     assert torch.equal(tok.cpu().long(), got.argmax(1))  # first index of the max of what it wrote
     assert int(keys.abs().sum()) == 0  # keys reset for the next step
+
+
+def test_l2_prefetch_option_leaves_results_unchanged():
+    """The side-branch L2 prefetch (an option, off by default) changes no result: the
+    same tokens and logits over three graph-replayed steps."""
+    shape = LlamaShape(n_layers=2, vocab_size=4096)
+    runs = []
+    for pf in (False, True):
+        eng = LlamaDecodeEngine(shape, 2, 64, seed=3, l2_prefetch=pf)
+        eng.set_state([11, 12], [4, 9])
+        eng.capture()
+        outs = []
+        for _ in range(3):
+            eng.step()
+            outs.append((eng.tokens.clone(), eng.logits.clone()))
+        torch.cuda.synchronize()
+        runs.append(outs)
+    for (ta, la), (tb, lb) in zip(*runs):
+        assert torch.equal(ta, tb) and torch.equal(la, lb)
