@@ -65,6 +65,7 @@ SIGNATURES: dict[str, list] = {
     "iron_gemv_int4g32_ex": [P, P, P, c_int, c_int, c_int, P, P, c_float, P, c_uint, P],
     "iron_argmax_finalize": [P, P, P, c_int, c_uint, P],
     "iron_l2_prefetch": [P, c_size_t, c_uint, P],
+    "iron_attn_decode_kernels": [c_int, c_int, c_int, c_int],
     "iron_gemv_int4g32_allreduce": [P, P, P, c_int, c_int, c_int, P, P, c_uint, P],
     "iron_ipc_alloc": [c_size_t, P],
     "iron_ipc_free": [P],

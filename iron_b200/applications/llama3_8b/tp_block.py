@@ -158,8 +158,8 @@ class TPDecoderBlock:
         return sum(r * c * 9 // 16 for r, c in self.dims.values())
 
     def kernels_per_step(self) -> int:
-        """Launches of one step: 2 RMSNorm, 4 GEMVs, attention (+ its split combine)."""
-        return 7 + int(self.ws.numel() > 16)
+        """Launches of one step: 2 RMSNorm, 4 GEMVs, attention (+ a split combine)."""
+        return 6 + _lib.load().iron_attn_decode_kernels(self.B, self.hq, self.hk, self.L)
 
     def kv_bytes(self, positions) -> int:
         return int(sum(int(p) + 1 for p in positions)) * self.hk * self.s.head_dim * 2 * 2

@@ -361,8 +361,9 @@ class LlamaDecodeEngine:
     def kernels_per_step(self) -> int:
         if self.persistent:
             return 1
-        per_layer = ((5 if self.fuse_norm != "none" else 7) + (1 if self.attn_ws.numel() > 16 else 0)  # + combine
-                     + (0 if self.fuse_rope else 1) + (2 if self.l2_prefetch else 0))
+        attn = _lib.load().iron_attn_decode_kernels(self.B, self.s.n_heads, self.s.n_kv_groups, self.L)
+        per_layer = ((4 if self.fuse_norm != "none" else 6) + attn + (0 if self.fuse_rope else 1)
+                     + (2 if self.l2_prefetch else 0))
         return 1 + self.s.n_layers * per_layer + (2 if self.fuse_norm == "all" else 3)
 
     def set_state(self, tokens, positions):

@@ -18,9 +18,13 @@
 // Memory-bound: each cache row is read once per kv head, not once per q head.
 #include <mutex>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace iron {
+
+namespace cg = cooperative_groups;
 
 // Head dims: 64 (Llama-3.2-1B; IRON's MHA supports d = 64 only, mha/op.py:39-41) and
 // 128 (the Llama-3-8B block).
@@ -61,7 +65,11 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void *smem
                : "r"(a));
 }
 
-template <int kAD, bool kFused = false>
+// kCS > 1: the splits of one (sequence, kv head) are a thread-block cluster of kCS
+// CTAs (gridDim.x == kCS); each CTA writes its (max, sum, output) rows into rank 0's
+// shared memory and rank 0 merges them in rank order after one cluster barrier -- no
+// workspace, no second kernel.
+template <int kAD, bool kFused = false, int kCS = 1>
 __global__ void __launch_bounds__(32 * kAWarps)
 attn_decode_kernel(AttnArgs a) {
   constexpr int kAVStride = kAD + 8;  // padded V tile row: an odd number of 16-byte chunks
@@ -70,6 +78,7 @@ attn_decode_kernel(AttnArgs a) {
   // the V tiles (loop) and the warp-merge buffer (after it) share the storage
   __shared__ __align__(16) uint8_t smem[kVBytes > kOBytes ? kVBytes : kOBytes];
   __shared__ float red_m[kAWarps][16], red_l[kAWarps][16];
+  extern __shared__ __align__(16) float cbuf[];  // kCS > 1 (rank 0): [kCS][g][2 + kAD]
   uint16_t (*vtile)[kABlk * kAVStride] = reinterpret_cast<uint16_t (*)[kABlk * kAVStride]>(smem);
   float (*red_o)[16][kAD] = reinterpret_cast<float (*)[16][kAD]>(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -350,7 +359,14 @@ attn_decode_kernel(AttnArgs a) {
       }
     }
     const int64_t hq = static_cast<int64_t>(b) * a.Hq + hq0 + r;
-    if (a.splits == 1) {
+    if constexpr (kCS > 1) {
+      float *dst = cg::this_cluster().map_shared_rank(cbuf, 0) + (split * g + r) * (2 + kAD);
+      if (d == 0) {
+        dst[0] = M;
+        dst[1] = L;
+      }
+      dst[2 + d] = O;
+    } else if (a.splits == 1) {
       a.out[hq * kAD + d] = float_to_bf16_bits(L > 0.f ? O / L : 0.f);
     } else {
       float *pw = a.ws + (hq * a.splits + split) * (2 + kAD);
@@ -359,6 +375,28 @@ attn_decode_kernel(AttnArgs a) {
         pw[1] = L;
       }
       pw[2 + d] = O;
+    }
+  }
+  if constexpr (kCS > 1) {
+    // out = sum_q O_q 2^(m_q - M) / sum_q L_q 2^(m_q - M) over the cluster's ranks
+    cg::this_cluster().sync();
+    if (split != 0) return;
+    for (int idx = threadIdx.x; idx < g * kAD; idx += blockDim.x) {
+      const int r = idx / kAD, d = idx % kAD;
+      float M = -INFINITY;
+#pragma unroll
+      for (int q = 0; q < kCS; ++q) M = fmaxf(M, cbuf[(q * g + r) * (2 + kAD)]);
+      float L = 0.f, O = 0.f;
+      if (M != -INFINITY) {
+#pragma unroll
+        for (int q = 0; q < kCS; ++q) {
+          const float *c = cbuf + (q * g + r) * (2 + kAD);
+          const float f = exp2f(c[0] - M);
+          L += c[1] * f;
+          O += c[2 + d] * f;
+        }
+      }
+      a.out[(static_cast<int64_t>(b) * a.Hq + hq0 + r) * kAD + d] = float_to_bf16_bits(L > 0.f ? O / L : 0.f);
     }
   }
 }
@@ -452,6 +490,66 @@ static float *attn_scratch_address(int *status) {
 
 using namespace iron;
 
+// Cluster form: the splits of a (sequence, kv head) as one cluster of 8 CTAs that merge
+// through distributed shared memory. It serves GQA groups of <= 4 query heads (rank 0
+// holds 8 x 4 rows of partials) when the sequence would be split and all clusters fit
+// in one wave of the SMs.
+constexpr int kAClusterSplits = 8;
+
+static bool attn_use_cluster(int B, int Hq, int Hkv, int Lmax) {
+  // one wave of clusters (B200: batch 1 gains 21 us per step, batch 8 -- 64 clusters --
+  // loses 42 us against independent splits and the combine kernel)
+  const int sms = sm_count();
+  return Hq / Hkv <= 4 && static_cast<int64_t>(B) * Hkv * kAClusterSplits <= sms &&
+         attn_splits(B, Hkv, Lmax, sms) > 1;
+}
+
+template <int kAD, bool kFused>
+static int launch_attn_cluster(AttnArgs a, int B, int Hkv, int Lmax, bool pdl, cudaStream_t s) {
+  constexpr int kCS = kAClusterSplits;
+  auto kern = attn_decode_kernel<kAD, kFused, kCS>;
+  constexpr size_t kMaxSmem = static_cast<size_t>(kCS) * 4 * (2 + kAD) * sizeof(float);
+  static bool configured = false;  // per instantiation: dynamic shared memory opt-in done
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kMaxSmem));
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e);
+      (void)cudaGetLastError();
+      return IRON_ERR_CUDA;
+    }
+    configured = true;
+  }
+  a.splits = kCS;
+  a.chunk = ((Lmax + kCS - 1) / kCS + kAWarps * kABlk - 1) / (kAWarps * kABlk) * (kAWarps * kABlk);
+  a.ws = nullptr;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kCS, Hkv, B);
+  cfg.blockDim = dim3(32 * kAWarps);
+  cfg.dynamicSmemBytes = static_cast<size_t>(kCS) * (a.Hq / a.Hkv) * (2 + kAD) * sizeof(float);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeClusterDimension;
+  attr[na].val.clusterDim.x = kCS;
+  attr[na].val.clusterDim.y = 1;
+  attr[na].val.clusterDim.z = 1;
+  ++na;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    (void)cudaGetLastError();
+    return IRON_ERR_CUDA;
+  }
+  return IRON_OK;
+}
+
 static size_t attn_ws_bytes(int B, int Hq, int Hkv, int Lmax, int D) {
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Lmax <= 0) return 0;
   const int s = attn_splits(B, Hkv, Lmax, sm_count());
@@ -494,12 +592,15 @@ extern "C" int iron_attn_decode(const uint16_t *q, const uint16_t *k_cache, cons
   a.maxlen = Lmax;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.ws = static_cast<float *>(workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool pdl = (flags & IRON_FLAG_PDL) != 0;
+  if (attn_use_cluster(B, Hq, Hkv, Lmax))
+    return D == 64 ? launch_attn_cluster<64, false>(a, B, Hkv, Lmax, pdl, s)
+                   : launch_attn_cluster<128, false>(a, B, Hkv, Lmax, pdl, s);
   if (a.splits > 1) {
     if (!workspace) return IRON_ERR_NULL;
     if (workspace_bytes < attn_ws_bytes(B, Hq, Hkv, Lmax, D)) return IRON_ERR_WORKSPACE;
   }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const bool pdl = (flags & IRON_FLAG_PDL) != 0;
   int st = D == 64 ? launch(attn_decode_kernel<64>, dim3(a.splits, Hkv, B), dim3(32 * kAWarps), 0, s, pdl, a)
                    : launch(attn_decode_kernel<128>, dim3(a.splits, Hkv, B), dim3(32 * kAWarps), 0, s, pdl, a);
   if (st != IRON_OK || a.splits == 1) return st;
@@ -518,6 +619,9 @@ extern "C" int iron_attn_decode_noalloc(const uint16_t *q, const uint16_t *k_cac
                                         unsigned flags, void *stream) {
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Lmax <= 0) return IRON_ERR_SHAPE;
   if (D != 64 && D != 128) return IRON_ERR_UNSUPPORTED;
+  if (Hkv > 0 && Hq % Hkv == 0 && attn_use_cluster(B, Hq, Hkv, Lmax))  // merges in the cluster: no partials
+    return iron_attn_decode(q, k_cache, v_cache, lens, out, B, Hq, Hkv, D, Lmax, kv_batch_stride, kv_head_stride,
+                            scale, nullptr, 0, flags, stream);
   const size_t need = attn_ws_bytes(B, Hq, Hkv, Lmax, D);
   if (need > kAttnScratchBytes) return IRON_ERR_WORKSPACE;  // beyond the fixed array
   void *ws = nullptr;
@@ -559,13 +663,16 @@ extern "C" int iron_attn_decode_qkv(const uint16_t *qkv, const int32_t *pos, con
   a.qkv = qkv;
   a.pos = pos;
   a.lut = lut;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool pdl = (flags & IRON_FLAG_PDL) != 0;
+  if (attn_use_cluster(B, Hq, Hkv, Lmax))
+    return D == 64 ? launch_attn_cluster<64, true>(a, B, Hkv, Lmax, pdl, s)
+                   : launch_attn_cluster<128, true>(a, B, Hkv, Lmax, pdl, s);
   if (a.splits > 1) {
     if (!workspace) return IRON_ERR_NULL;
     if (workspace_bytes < attn_ws_bytes(B, Hq, Hkv, Lmax, D)) return IRON_ERR_WORKSPACE;
     a.ws = static_cast<float *>(workspace);
   }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const bool pdl = (flags & IRON_FLAG_PDL) != 0;
   // the splits merge in the combine kernel, which PDL overlaps with this one's tail
   // (measured faster on B200 than merging in the last split CTA)
   int st = D == 64 ? launch(attn_decode_kernel<64, true>, dim3(a.splits, Hkv, B), dim3(32 * kAWarps), 0, s, pdl, a)
@@ -575,6 +682,12 @@ extern "C" int iron_attn_decode_qkv(const uint16_t *qkv, const int32_t *pos, con
                           out, a.splits)
                  : launch(attn_combine_kernel<128>, dim3(B * Hq), dim3(128), 0, s, pdl,
                           static_cast<const float *>(a.ws), out, a.splits);
+}
+
+extern "C" int iron_attn_decode_kernels(int B, int Hq, int Hkv, int Lmax) {
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Lmax <= 0 || Hq % Hkv) return 0;
+  if (attn_use_cluster(B, Hq, Hkv, Lmax)) return 1;
+  return attn_splits(B, Hkv, Lmax, sm_count()) > 1 ? 2 : 1;
 }
 
 extern "C" size_t iron_attn_decode_qkv_workspace_bytes(int B, int Hq, int Hkv, int Lmax, int D) {
