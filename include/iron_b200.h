@@ -295,10 +295,10 @@ int iron_attn_decode_noalloc(const uint16_t *q, const uint16_t *k_cache, const u
  */
 size_t iron_attn_decode_qkv_workspace_bytes(int B, int Hq, int Hkv, int Lmax, int D);
 /* iron_attn_decode_kernels: launches one decode-attention call makes (1, or 2 when a
- * split-combine kernel follows). With GQA groups of <= 4 query heads the splits of a
- * (sequence, kv head) run as one cluster of 8 CTAs that merge through distributed
- * shared memory (one launch, no workspace use); otherwise the partials go through
- * `workspace` and a combine kernel. */
+ * split-combine kernel follows). With GQA groups of <= 4 query heads, when all of them
+ * fit in one wave of the SMs, the splits of a (sequence, kv head) run as one cluster of
+ * 16 or 8 CTAs that merge through distributed shared memory (one launch, no workspace
+ * use); otherwise the partials go through `workspace` and a combine kernel. */
 int iron_attn_decode_kernels(int B, int Hq, int Hkv, int Lmax);
 int iron_attn_decode_qkv(const uint16_t *qkv, const int32_t *pos, const float *lut, uint16_t *k_cache,
                          uint16_t *v_cache, uint16_t *out, int B, int Hq, int Hkv, int D, int Lmax,

@@ -490,27 +490,36 @@ static float *attn_scratch_address(int *status) {
 
 using namespace iron;
 
-// Cluster form: the splits of a (sequence, kv head) as one cluster of 8 CTAs that merge
-// through distributed shared memory. It serves GQA groups of <= 4 query heads (rank 0
-// holds 8 x 4 rows of partials) when the sequence would be split and all clusters fit
-// in one wave of the SMs.
-constexpr int kAClusterSplits = 8;
-
-static bool attn_use_cluster(int B, int Hq, int Hkv, int Lmax) {
-  // one wave of clusters (B200: batch 1 gains 21 us per step, batch 8 -- 64 clusters --
-  // loses 42 us against independent splits and the combine kernel)
+// Cluster form: the splits of a (sequence, kv head) as one cluster of 16 or 8 CTAs
+// that merge through distributed shared memory. It serves GQA groups of <= 4 query
+// heads (rank 0 holds cluster x 4 rows of partials) when the sequence would be split
+// and all clusters fit in one wave of the SMs: the largest such size (B200, batch 1:
+// 16 -> 484 us per step, 8 -> 499, no cluster 516; batch 2: 8 -> 522, none 542; batch
+// 8, 64 clusters of 8: 42 us slower than independent splits and a combine kernel).
+static int attn_cluster_size(int B, int Hq, int Hkv, int Lmax) {
   const int sms = sm_count();
-  return Hq / Hkv <= 4 && static_cast<int64_t>(B) * Hkv * kAClusterSplits <= sms &&
-         attn_splits(B, Hkv, Lmax, sms) > 1;
+  if (Hq / Hkv > 4 || attn_splits(B, Hkv, Lmax, sms) <= 1) return 0;
+  for (int cs = 16; cs >= 8; cs /= 2)
+    if (static_cast<int64_t>(B) * Hkv * cs <= sms) return cs;
+  return 0;
 }
 
-template <int kAD, bool kFused>
-static int launch_attn_cluster(AttnArgs a, int B, int Hkv, int Lmax, bool pdl, cudaStream_t s) {
-  constexpr int kCS = kAClusterSplits;
+static bool attn_use_cluster(int B, int Hq, int Hkv, int Lmax) { return attn_cluster_size(B, Hq, Hkv, Lmax) > 0; }
+
+template <int kAD, bool kFused, int kCS>
+static int launch_attn_cluster_cs(AttnArgs a, int B, int Hkv, int Lmax, bool pdl, cudaStream_t s) {
   auto kern = attn_decode_kernel<kAD, kFused, kCS>;
   constexpr size_t kMaxSmem = static_cast<size_t>(kCS) * 4 * (2 + kAD) * sizeof(float);
   static bool configured = false;  // per instantiation: dynamic shared memory opt-in done
   if (!configured) {
+    if (kCS > 8) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        (void)cudaGetLastError();
+        return IRON_ERR_CUDA;
+      }
+    }
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kMaxSmem));
     if (e != cudaSuccess) {
       set_last_cuda_error(e);
@@ -548,6 +557,12 @@ static int launch_attn_cluster(AttnArgs a, int B, int Hkv, int Lmax, bool pdl, c
     return IRON_ERR_CUDA;
   }
   return IRON_OK;
+}
+
+template <int kAD, bool kFused>
+static int launch_attn_cluster(AttnArgs a, int B, int Hq, int Hkv, int Lmax, bool pdl, cudaStream_t s) {
+  return attn_cluster_size(B, Hq, Hkv, Lmax) == 16 ? launch_attn_cluster_cs<kAD, kFused, 16>(a, B, Hkv, Lmax, pdl, s)
+                                                   : launch_attn_cluster_cs<kAD, kFused, 8>(a, B, Hkv, Lmax, pdl, s);
 }
 
 static size_t attn_ws_bytes(int B, int Hq, int Hkv, int Lmax, int D) {
@@ -595,8 +610,8 @@ extern "C" int iron_attn_decode(const uint16_t *q, const uint16_t *k_cache, cons
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool pdl = (flags & IRON_FLAG_PDL) != 0;
   if (attn_use_cluster(B, Hq, Hkv, Lmax))
-    return D == 64 ? launch_attn_cluster<64, false>(a, B, Hkv, Lmax, pdl, s)
-                   : launch_attn_cluster<128, false>(a, B, Hkv, Lmax, pdl, s);
+    return D == 64 ? launch_attn_cluster<64, false>(a, B, Hq, Hkv, Lmax, pdl, s)
+                   : launch_attn_cluster<128, false>(a, B, Hq, Hkv, Lmax, pdl, s);
   if (a.splits > 1) {
     if (!workspace) return IRON_ERR_NULL;
     if (workspace_bytes < attn_ws_bytes(B, Hq, Hkv, Lmax, D)) return IRON_ERR_WORKSPACE;
@@ -666,8 +681,8 @@ extern "C" int iron_attn_decode_qkv(const uint16_t *qkv, const int32_t *pos, con
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool pdl = (flags & IRON_FLAG_PDL) != 0;
   if (attn_use_cluster(B, Hq, Hkv, Lmax))
-    return D == 64 ? launch_attn_cluster<64, true>(a, B, Hkv, Lmax, pdl, s)
-                   : launch_attn_cluster<128, true>(a, B, Hkv, Lmax, pdl, s);
+    return D == 64 ? launch_attn_cluster<64, true>(a, B, Hq, Hkv, Lmax, pdl, s)
+                   : launch_attn_cluster<128, true>(a, B, Hq, Hkv, Lmax, pdl, s);
   if (a.splits > 1) {
     if (!workspace) return IRON_ERR_NULL;
     if (workspace_bytes < attn_ws_bytes(B, Hq, Hkv, Lmax, D)) return IRON_ERR_WORKSPACE;
