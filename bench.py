@@ -10,13 +10,16 @@ Workloads:
       model (16 layers, vocab 128256, int4 group-32 weights, bf16 activations)
       decodes B sequences greedily from position 2048 (the 2048-token prompt's
       KV cache is synthetic). One step = one decode step of the batch = one
-      CUDA-graph replay (embedding, 16 x [RMSNorm, QKV GEMV, RoPE+KV append,
-      attention (+combine), O GEMV+residual, RMSNorm, gate/up GEMV+SwiGLU, down
+      CUDA-graph replay (embedding, 16 x [RMSNorm, QKV GEMV, attention with
+      RoPE + KV append and its split merge (a cluster at batch <= 2, else a
+      combine kernel), O GEMV+residual, RMSNorm, gate/up GEMV+SwiGLU, down
       GEMV+residual], final RMSNorm, lm-head GEMV, argmax). value = tokens/s.
       The line also carries the config-2 int4 GEMV figure under "int4_gemv".
   int4_gemv (config 2): y = dequant(W) x, W [8192 x 2048] signed int4 with a
       bf16 scale per 32 k, x [V x 2048] bf16. One step = one GEMV call.
   bf16_gemv (config 1): W [2048 x 8192] bf16, x [8192].
+  gemm: the tcgen05 GEMM (--gemm-shape M,K,N). tp_block: one Llama-3-8B decoder
+      block, tensor-parallel over the ranks (--allreduce fused|nccl).
 
 Timing: W warm-up steps, then exactly K steps bracketed by a barrier and
 cuda.synchronize, timed with CUDA events on the launching stream. Every step
