@@ -2,7 +2,7 @@
 """Benchmark of IRON's LLM-operator hot path on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|int4_gemv|bf16_gemv] [--batch B] [--n-vec V]
+                    [--workload decode|int4_gemv|bf16_gemv|gemm|tp_block|block|attention] [--batch B] [--n-vec V]
 
 Metric: "Llama-3.2-1B-shape decode tok/s; int4 GEMV achieved HBM GB/s".
 Workloads:
@@ -20,6 +20,11 @@ Workloads:
   bf16_gemv (config 1): W [2048 x 8192] bf16, x [8192].
   gemm: the tcgen05 GEMM (--gemm-shape M,K,N). tp_block: one Llama-3-8B decoder
       block, tensor-parallel over the ranks (--allreduce fused|nccl).
+  block (config 3): one Llama-3.2-1B decoder block with bf16 weights at batch
+      --batch (1 or 16), positions in 0..4095: RMSNorm, QKV GEMV, RoPE + KV
+      append, SwiGLU MLP; the full block (attention, o_proj, residuals) too.
+  attention (config 4): the decode attention at batch 1/16/64 x L_max
+      512/4096/32768 with ragged lengths; value = the batch-64, 32768 case.
 
 Timing: W warm-up steps, then exactly K steps bracketed by a barrier and
 cuda.synchronize, timed with CUDA events on the launching stream. Every step
@@ -60,7 +65,8 @@ def _args():
                     help="timed steps (default: 256 decode steps, 20000 GEMVs)")
     ap.add_argument("--warmup", type=int, default=None, help="warm-up steps (default: 5 decode, 200 GEMV)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "int4_gemv", "bf16_gemv", "gemm", "tp_block"],
+    ap.add_argument("--workload", choices=["decode", "int4_gemv", "bf16_gemv", "gemm", "tp_block", "block",
+                                                   "attention"],
                     default="decode")
     ap.add_argument("--gemm-shape", default="2048,2048,8192", help="M,K,N of the gemm workload")
     ap.add_argument("--batch", type=int, default=1, help="decode batch per GPU")
@@ -71,9 +77,10 @@ def _args():
                     help="tp_block: the all-reduce inside the GEMVs (fused, batch <= 8) or NCCL calls")
     a = ap.parse_args()
     if a.steps is None:
-        a.steps = {"decode": 256, "gemm": 200, "tp_block": 2000}.get(a.workload, 20000)
+        a.steps = {"decode": 256, "gemm": 200, "tp_block": 2000, "block": 3000, "attention": 200}.get(
+            a.workload, 20000)
     if a.warmup is None:
-        a.warmup = {"decode": 5, "gemm": 10, "tp_block": 20}.get(a.workload, 200)
+        a.warmup = {"decode": 5, "gemm": 10, "tp_block": 20, "block": 30, "attention": 3}.get(a.workload, 200)
     if a.warmup < 3:
         ap.error("--warmup must be >= 3")
     return a
@@ -961,6 +968,308 @@ def run_tp_block(args, world, rank, local):
         dist.destroy_process_group()
 
 
+# ---- decoder block with bf16 weights (config 3) --------------------------------------------
+BLOCK_CTX = 4096  # cache rows per sequence; positions are drawn from 0..4095
+
+
+def _block_positions(B: int, seed: int = 11):
+    g = torch.Generator()
+    g.manual_seed(seed)
+    return torch.randint(0, BLOCK_CTX, (B,), generator=g, dtype=torch.int32)
+
+
+def _time_block_form(args, world, local, full: bool, pos, rank):
+    """Device time per step of one block form over rotating weight copies (> 2.5x L2)."""
+    from iron_b200.applications.llama_3_2_1b.block_bf16 import DecoderBlockBF16
+
+    B = args.batch
+    blocks = []
+    for c in range(3):
+        blk = DecoderBlockBF16(batch=B, max_seq=BLOCK_CTX, seed=13 + 7 * c + 101 * rank, full=full,
+                               pdl=not args.no_pdl)
+        g = torch.Generator(device="cuda")
+        g.manual_seed(5 + c)
+        blk.x.normal_(generator=g)
+        if full:
+            blk.kc.normal_(generator=g)
+            blk.vc.normal_(generator=g)
+        blk.pos.copy_(pos)
+        blocks.append(blk)
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        for blk in blocks:
+            blk._launch(st.cuda_stream)  # outside capture: first-call attribute setup
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
+        for blk in blocks:
+            blk._launch(st.cuda_stream)
+    torch.cuda.synchronize()
+    reps = max(1, args.steps // len(blocks))
+    for _ in range(max(1, args.warmup // len(blocks))):
+        graph.replay()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if (rank == 0 and not full) else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    _barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if sampler:
+        sampler.mark("t0")
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    e1.synchronize()
+    if sampler:
+        sampler.mark("t1")
+    torch.cuda.synchronize()
+    _barrier(world)
+    ms = _max_over_ranks(e0.elapsed_time(e1), world)
+    clocks = sampler.stop() if sampler else None
+    steps = reps * len(blocks)
+    blk = blocks[0]
+    out = {"steps": steps, "ms_per_step": ms / steps, "bytes_per_step": blk.step_bytes(pos.tolist()),
+           "kernels_per_step": blk.kernels_per_step(), "clocks": clocks}
+    del graph, blocks
+    torch.cuda.synchronize()
+    return out
+
+
+def run_block(args, world, rank, local):
+    """RMSNorm -> QKV GEMV -> RoPE -> KV append -> SwiGLU MLP of one
+    Llama-3.2-1B block with bf16 weights, batch --batch (1 or 16) at positions drawn
+    from 0..4095; the full block (attention, o_proj, second norm, residuals) rides along
+    under "full_block". Each rank runs its own copy (replicas)."""
+    B = args.batch
+    pos = _block_positions(B)
+    chain = _time_block_form(args, world, local, False, pos, rank)
+    full = _time_block_form(args, world, local, True, pos, rank)
+    peak, psrc = _peak_hbm()
+    gbs = chain["bytes_per_step"] / (chain["ms_per_step"] * 1e-3) / 1e9
+    fgbs = full["bytes_per_step"] / (full["ms_per_step"] * 1e-3) / 1e9
+    line = {"metric": "Llama-3.2-1B decoder block (bf16 weights) achieved HBM GB/s",
+            "value": round(gbs * world, 1), "unit": "GB/s", "n_gpus": world, "steps": chain["steps"],
+            "warmup": args.warmup, "ms_per_step": chain["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp32 accumulate)",
+            "data": "synthetic (random-init bf16 weights ~ N(0, 0.02), norm weights ~ N(1, 0.02); seeded)",
+            "config": {"workload": "block (BASELINE config 3)", "batch": B, "positions": pos.tolist(),
+                       "ops": "RMSNorm, QKV GEMV, RoPE + KV append, gate GEMV, up GEMV, silu*mul, down GEMV",
+                       "l2": "3 weight copies (340 MB) rotated inside one graph", "parallelism": f"dp{world}"},
+            "us_per_step": round(chain["ms_per_step"] * 1e3, 2),
+            "tok_s_through_block": round(world * B / (chain["ms_per_step"] * 1e-3), 1),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "traffic": None, "scope": "one step of the operator chain",
+                         "algorithmic_bytes_per_step": chain["bytes_per_step"], "peak_source": psrc},
+            "full_block": {"us_per_step": round(full["ms_per_step"] * 1e3, 2), "achieved_gbs": round(fgbs, 1),
+                           "frac": round(fgbs / peak, 4), "algorithmic_bytes_per_step": full["bytes_per_step"],
+                           "kernels_per_step": full["kernels_per_step"]},
+            "gpu_launches": chain["kernels_per_step"] * chain["steps"], "clocks": chain["clocks"], "e2e": None}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = _cpu_block(B, pos, budget_s=10.0)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def _cpu_block(B, pos, budget_s=10.0, steps=None):
+    """IRON's CPU golden of the config-3 chain (the oracle's restatement of llama_cpu.py's
+    block pieces, torch bf16 weights) on all host threads."""
+    from iron_b200.applications.llama_3_2_1b.decode import LlamaShape, rope_table
+    from oracle import llama as ollama
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    s = LlamaShape()
+    E, H, Hd = s.emb_dim, s.hidden_dim, s.head_dim
+    g = torch.Generator()
+    g.manual_seed(13)
+    lin = lambda r, c: (0.02 * torch.randn(r, c, generator=g)).to(torch.bfloat16)
+    W = {"n1": (1 + 0.02 * torch.randn(E, generator=g)).to(torch.bfloat16), "q": lin(s.n_heads * Hd, E),
+         "k": lin(s.n_kv_groups * Hd, E), "v": lin(s.n_kv_groups * Hd, E), "g": lin(H, E), "u": lin(H, E),
+         "d": lin(E, H)}
+    x = torch.randn(B, E, generator=g).to(torch.bfloat16)
+    kc = torch.zeros(B, s.n_kv_groups, BLOCK_CTX, Hd, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    lut = rope_table(Hd, BLOCK_CTX, s.rope_base, "cpu")
+    P = pos.tolist()
+    step = lambda: ollama.block_mlp_half(x, kc, vc, P, W, lut, s.n_heads, s.n_kv_groups, Hd, s.eps)
+    step()
+    n, t0 = 0, time.perf_counter()
+    while (steps is None and time.perf_counter() - t0 < budget_s) or (steps is not None and n < steps):
+        step()
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    nbytes = 2 * sum(w.numel() for w in W.values()) + 2 * B * E * 2 + B * 2 * s.n_kv_groups * Hd * 2
+    return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} steps of the config-3 chain at batch {B}: the oracle's block_mlp_half "
+                      f"(llama_cpu.py's pieces restated in torch, bf16 weights)", "ms_per_step": dt * 1e3}
+
+
+# ---- GQA decode attention (config 4) ------------------------------------------------------
+ATTN_CASES = [(b, l) for b in (1, 16, 64) for l in (512, 4096, 32768)]
+
+
+def _attn_case_inputs(B, L, seed):
+    g = torch.Generator()
+    g.manual_seed(seed)
+    lens = torch.randint(1, L + 1, (B,), generator=g, dtype=torch.int32)
+    return lens
+
+
+def _time_attention(B, L, args, max_alloc=12 << 30):
+    """Device time per iron_attn_decode launch at (B, L_max) with ragged lengths, over
+    rotating cache copies whose read bytes exceed 3x L2."""
+    from iron_b200 import _lib
+
+    Hq, Hkv, D = 32, 8, 64
+    lens = _attn_case_inputs(B, L, seed=1000 * B + L)
+    read = int(lens.sum()) * Hkv * D * 2 * 2
+    alloc = B * Hkv * L * D * 2 * 2
+    copies = max(2, min(1024, -(-3 * L2_BYTES // read), max_alloc // alloc))
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev)
+    g.manual_seed(B + L)
+    kc = torch.randn(copies, B, Hkv, L, D, device=dev, generator=g, dtype=torch.bfloat16)
+    vc = torch.randn(copies, B, Hkv, L, D, device=dev, generator=g, dtype=torch.bfloat16)
+    q = torch.randn(B, Hq, D, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=dev)
+    ld = lens.to(dev)
+    lib = _lib.load()
+    wsb = lib.iron_attn_decode_workspace_bytes_d(B, Hq, Hkv, L, D)
+    ws = torch.zeros(max(wsb, 16), dtype=torch.uint8, device=dev)
+    flags = 0 if args.no_pdl else _lib.IRON_FLAG_PDL
+    cstride = kc[0].numel() * 2
+    st = torch.cuda.Stream()
+
+    def launch_all(stream):
+        for c in range(copies):
+            r = lib.iron_attn_decode(q.data_ptr(), kc.data_ptr() + c * cstride, vc.data_ptr() + c * cstride,
+                                     ld.data_ptr(), out.data_ptr(), B, Hq, Hkv, D, L, Hkv * L * D, L * D,
+                                     1.0 / D ** 0.5, ws.data_ptr(), ws.numel(), flags, stream)
+            if r != 0:
+                raise RuntimeError(_lib.strerror(r))
+
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        launch_all(st.cuda_stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
+        launch_all(st.cuda_stream)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    reps = max(3, -(-200 // copies))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
+    nbytes = read + B * Hq * D * 2 * 2
+    launches = reps * copies * lib.iron_attn_decode_kernels(B, Hq, Hkv, L)
+    del graph, kc, vc
+    torch.cuda.synchronize()
+    return {"B": B, "L_max": L, "sum_len": int(lens.sum()), "us": round(us, 2),
+            "gbs": round(nbytes / (us * 1e-6) / 1e9, 1), "bytes": nbytes, "copies": copies}, launches
+
+
+def run_attention(args, world, rank, local):
+    """iron_attn_decode (32 q / 8 kv heads, d 64) at batch 1/16/64 x
+    L_max 512/4096/32768, per-sequence lengths ~ U[1, L_max] (seeded). value = the
+    achieved GB/s of the largest case (batch 64, 32768); every case under "cases"."""
+    peak, psrc = _peak_hbm()
+    cases, launches = [], 0
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+        sampler.mark("t0")
+    for B, L in ATTN_CASES:
+        c, n = _time_attention(B, L, args)
+        c["frac"] = round(c["gbs"] / peak, 4)
+        cases.append(c)
+        launches += n
+    if sampler:
+        sampler.mark("t1")
+    clocks = sampler.stop() if sampler else None
+    head = cases[-1]
+    line = {"metric": "GQA decode attention achieved HBM GB/s", "value": round(head["gbs"] * world, 1),
+            "unit": "GB/s", "n_gpus": world, "steps": None, "warmup": 3, "ms_per_step": head["us"] / 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 (fp32 softmax and accumulate)",
+            "data": "synthetic (K/V ~ N(0, 1), lengths ~ U[1, L_max]; seeded)",
+            "config": {"workload": "attention (BASELINE config 4)", "heads": "32 q / 8 kv, d 64",
+                       "headline_case": {"B": 64, "L_max": 32768},
+                       "l2": "cache copies rotated so each round reads > 3x L2", "parallelism": f"dp{world}"},
+            "roofline": {"bound": "hbm", "achieved": head["gbs"], "peak": peak, "unit": "GB/s",
+                         "frac": head["frac"], "traffic": None,
+                         "scope": "one iron_attn_decode call (split kernel + combine)",
+                         "algorithmic_bytes_per_step": head["bytes"], "peak_source": psrc},
+            "cases": cases, "gpu_launches": launches, "clocks": clocks, "e2e": None}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def _cpu_attention(B, L, steps):
+    """IRON's CPU truth of decode attention (llama_cpu.py:118-140 restated by the oracle)."""
+    from oracle import ops
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    lens = _attn_case_inputs(B, L, seed=1000 * B + L)
+    g = torch.Generator()
+    g.manual_seed(B + L)
+    q = torch.randn(B, 32, 64, generator=g).to(torch.bfloat16)
+    kc = torch.randn(B, 8, L, 64, generator=g).to(torch.bfloat16)
+    vc = torch.randn(B, 8, L, 64, generator=g).to(torch.bfloat16)
+    ops.attn_decode(q, kc, vc, lens.tolist())
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        ops.attn_decode(q, kc, vc, lens.tolist())
+    dt = (time.perf_counter() - t0) / steps
+    nbytes = int(lens.sum()) * 8 * 64 * 4 + B * 32 * 64 * 4
+    return nbytes / dt / 1e9, dt, threads
+
+
+def run_reference_extra(args, world, rank):
+    """--impl reference for the block and attention workloads (rank 0 only)."""
+    if rank != 0:
+        return
+    steps = max(1, min(args.steps, 5))
+    if args.workload == "block":
+        cb = _cpu_block(args.batch, _block_positions(args.batch), steps=steps)
+        value, unit, ms = cb["value"], "GB/s", cb["ms_per_step"]
+        cfg = {"workload": "block (BASELINE config 3)", "batch": args.batch}
+        sample, threads = cb["sample"], cb["cores"]
+        metric = "Llama-3.2-1B decoder block (bf16 weights) achieved HBM GB/s"
+    else:
+        B, L = 64, 4096  # a bounded sample of the config (the 32768 case takes minutes per call on the host)
+        gbs, dt, threads = _cpu_attention(B, L, steps)
+        value, unit, ms = round(gbs, 3), "GB/s", dt * 1e3
+        cfg = {"workload": "attention (BASELINE config 4)", "B": B, "L_max": L}
+        sample = f"{steps} calls at batch {B}, L_max {L} (ragged): the oracle's attn_decode"
+        metric = "GQA decode attention achieved HBM GB/s"
+    line = {"impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": world,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)", "config": cfg,
+            "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = _args()
     if args.impl == "reference":
@@ -968,6 +1277,8 @@ def main():
         rank = int(os.environ.get("RANK", "0"))
         if args.workload == "decode":
             run_reference_decode(args, world, rank)
+        elif args.workload in ("block", "attention"):
+            run_reference_extra(args, world, rank)
         else:
             run_reference(args, world, rank)
         return
@@ -978,6 +1289,10 @@ def main():
         run_gemm(args, world, rank, local)
     elif args.workload == "tp_block":
         run_tp_block(args, world, rank, local)
+    elif args.workload == "block":
+        run_block(args, world, rank, local)
+    elif args.workload == "attention":
+        run_attention(args, world, rank, local)
     else:
         run_ours(args, world, rank, local)
 
