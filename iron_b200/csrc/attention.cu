@@ -32,6 +32,13 @@ constexpr int kAWarps = 4;
 constexpr int kABlk = 16;     // tokens per warp step
 constexpr int kAMinChunk = 64;   // tokens per split at least
 constexpr int kAMaxSplits = 64;  // splits per sequence at most (the combine holds one value per split)
+// tokens per CTA at most (while splits are left): one CTA streams about one 16-token
+// block per warp per memory round trip, so in a ragged batch the CTA of the longest
+// sequence would otherwise set the time (B200, batch 64 at up to 32768 tokens)
+constexpr int kAMaxChunk = 4096;
+// tokens per CTA at most in the cluster form (16 or 8 CTAs per (sequence, kv head)):
+// beyond it the few clusters cannot keep enough rows in flight
+constexpr int kAClusterMaxChunk = 512;
 
 struct AttnArgs {
   const uint16_t *q;    // [B, Hq, D]
@@ -440,13 +447,16 @@ __global__ void attn_combine_kernel(const float *__restrict__ ws, uint16_t *__re
   out[hq * kAD + d] = float_to_bf16_bits(L > 0.f ? O / L : 0.f);
 }
 
-// Split count: enough CTAs for two waves of 148 SMs, chunks of >= kAMinChunk tokens,
-// at most kAMaxSplits.
-__host__ __device__ inline int attn_splits(int B, int Hkv, int Lmax, int sms) {
+// Split count: enough CTAs for two waves of the SMs and chunks of at most `max_chunk`
+// tokens, with chunks of >= kAMinChunk tokens and at most `limit` (<= kAMaxSplits) splits.
+__host__ __device__ inline int attn_splits(int B, int Hkv, int Lmax, int sms, int limit = kAMaxSplits,
+                                           int max_chunk = kAMaxChunk) {
   int max_splits = (Lmax + kAMinChunk - 1) / kAMinChunk;
-  if (max_splits > kAMaxSplits) max_splits = kAMaxSplits;
+  if (max_splits > limit) max_splits = limit;
+  if (max_splits < 1) max_splits = 1;
   int s = 1;
-  while (s < max_splits && static_cast<int64_t>(B) * Hkv * s < 2LL * sms) s *= 2;
+  while (s < max_splits && (static_cast<int64_t>(B) * Hkv * s < 2LL * sms || (Lmax + s - 1) / s > max_chunk))
+    s *= 2;
   return s < max_splits ? s : max_splits;
 }
 
@@ -501,7 +511,7 @@ static int attn_cluster_size(int B, int Hq, int Hkv, int Lmax) {
   const int sms = sm_count();
   if (Hq / Hkv > 4 || attn_splits(B, Hkv, Lmax, sms) <= 1) return 0;
   for (int cs = 16; cs >= 8; cs /= 2)
-    if (static_cast<int64_t>(B) * Hkv * cs <= sms) return cs;
+    if (static_cast<int64_t>(B) * Hkv * cs <= sms) return (Lmax + cs - 1) / cs <= kAClusterMaxChunk ? cs : 0;
   return 0;
 }
 
@@ -566,9 +576,9 @@ static int launch_attn_cluster(AttnArgs a, int B, int Hq, int Hkv, int Lmax, boo
                                                    : launch_attn_cluster_cs<kAD, kFused, 8>(a, B, Hkv, Lmax, pdl, s);
 }
 
-static size_t attn_ws_bytes(int B, int Hq, int Hkv, int Lmax, int D) {
+static size_t attn_ws_bytes(int B, int Hq, int Hkv, int Lmax, int D, int limit = kAMaxSplits) {
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Lmax <= 0) return 0;
-  const int s = attn_splits(B, Hkv, Lmax, sm_count());
+  const int s = attn_splits(B, Hkv, Lmax, sm_count(), limit);
   if (s == 1) return 0;
   return static_cast<size_t>(B) * Hq * s * (2 + D) * sizeof(float);
 }
@@ -581,11 +591,11 @@ extern "C" size_t iron_attn_decode_workspace_bytes_d(int B, int Hq, int Hkv, int
   return (D == 64 || D == 128) ? attn_ws_bytes(B, Hq, Hkv, Lmax, D) : 0;
 }
 
-extern "C" int iron_attn_decode(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
-                                const int32_t *lens, uint16_t *out, int B, int Hq, int Hkv, int D,
-                                int Lmax, int64_t kv_batch_stride, int64_t kv_head_stride,
-                                float scale, void *workspace, size_t workspace_bytes,
-                                unsigned flags, void *stream) {
+// iron_attn_decode with at most `limit` splits per sequence
+static int attn_decode_impl(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                            const int32_t *lens, uint16_t *out, int B, int Hq, int Hkv, int D, int Lmax,
+                            int64_t kv_batch_stride, int64_t kv_head_stride, float scale, void *workspace,
+                            size_t workspace_bytes, unsigned flags, void *stream, int limit) {
   if (!q || !k_cache || !v_cache || !lens || !out) return IRON_ERR_NULL;
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Lmax <= 0 || B > 65535 || Hkv > 65535) return IRON_ERR_SHAPE;
   if (D != 64 && D != 128) return IRON_ERR_UNSUPPORTED;
@@ -603,7 +613,7 @@ extern "C" int iron_attn_decode(const uint16_t *q, const uint16_t *k_cache, cons
   a.hstride = kv_head_stride;
   a.Hq = Hq;
   a.Hkv = Hkv;
-  a.splits = attn_splits(B, Hkv, Lmax, sm_count());
+  a.splits = attn_splits(B, Hkv, Lmax, sm_count(), limit);
   a.chunk = ((Lmax + a.splits - 1) / a.splits + kAWarps * kABlk - 1) / (kAWarps * kABlk) * (kAWarps * kABlk);
   a.maxlen = Lmax;
   a.scale_log2 = scale * 1.4426950408889634f;
@@ -615,7 +625,7 @@ extern "C" int iron_attn_decode(const uint16_t *q, const uint16_t *k_cache, cons
                    : launch_attn_cluster<128, false>(a, B, Hq, Hkv, Lmax, pdl, s);
   if (a.splits > 1) {
     if (!workspace) return IRON_ERR_NULL;
-    if (workspace_bytes < attn_ws_bytes(B, Hq, Hkv, Lmax, D)) return IRON_ERR_WORKSPACE;
+    if (workspace_bytes < attn_ws_bytes(B, Hq, Hkv, Lmax, D, limit)) return IRON_ERR_WORKSPACE;
   }
   int st = D == 64 ? launch(attn_decode_kernel<64>, dim3(a.splits, Hkv, B), dim3(32 * kAWarps), 0, s, pdl, a)
                    : launch(attn_decode_kernel<128>, dim3(a.splits, Hkv, B), dim3(32 * kAWarps), 0, s, pdl, a);
@@ -626,8 +636,18 @@ extern "C" int iron_attn_decode(const uint16_t *q, const uint16_t *k_cache, cons
                           static_cast<const float *>(a.ws), out, a.splits);
 }
 
+extern "C" int iron_attn_decode(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                                const int32_t *lens, uint16_t *out, int B, int Hq, int Hkv, int D,
+                                int Lmax, int64_t kv_batch_stride, int64_t kv_head_stride,
+                                float scale, void *workspace, size_t workspace_bytes,
+                                unsigned flags, void *stream) {
+  return attn_decode_impl(q, k_cache, v_cache, lens, out, B, Hq, Hkv, D, Lmax, kv_batch_stride, kv_head_stride,
+                          scale, workspace, workspace_bytes, flags, stream, kAMaxSplits);
+}
+
 // Same computation as iron_attn_decode, for callers that cannot allocate the
-// workspace: the split partials go to the library's fixed per-device array.
+// workspace: the split partials go to the library's fixed per-device array (with
+// fewer splits where the usual count's partials would not fit it).
 extern "C" int iron_attn_decode_noalloc(const uint16_t *q, const uint16_t *k_cache,
                                         const uint16_t *v_cache, const int32_t *lens, uint16_t *out,
                                         int B, int Hq, int Hkv, int D, int Lmax,
@@ -638,7 +658,12 @@ extern "C" int iron_attn_decode_noalloc(const uint16_t *q, const uint16_t *k_cac
   if (Hkv > 0 && Hq % Hkv == 0 && attn_use_cluster(B, Hq, Hkv, Lmax))  // merges in the cluster: no partials
     return iron_attn_decode(q, k_cache, v_cache, lens, out, B, Hq, Hkv, D, Lmax, kv_batch_stride, kv_head_stride,
                             scale, nullptr, 0, flags, stream);
-  const size_t need = attn_ws_bytes(B, Hq, Hkv, Lmax, D);
+  // the splits that the chunk cap adds come off where their partials would not fit the
+  // array (down to the two-wave count, whose partials must fit)
+  const int waves = attn_splits(B, Hkv, Lmax, sm_count(), kAMaxSplits, 0x7fffffff);
+  int limit = kAMaxSplits;
+  while (limit / 2 >= waves && attn_ws_bytes(B, Hq, Hkv, Lmax, D, limit) > kAttnScratchBytes) limit /= 2;
+  const size_t need = attn_ws_bytes(B, Hq, Hkv, Lmax, D, limit);
   if (need > kAttnScratchBytes) return IRON_ERR_WORKSPACE;  // beyond the fixed array
   void *ws = nullptr;
   if (need > 0) {
@@ -646,8 +671,8 @@ extern "C" int iron_attn_decode_noalloc(const uint16_t *q, const uint16_t *k_cac
     ws = attn_scratch_address(&st);
     if (st != IRON_OK) return st;
   }
-  return iron_attn_decode(q, k_cache, v_cache, lens, out, B, Hq, Hkv, D, Lmax, kv_batch_stride,
-                          kv_head_stride, scale, ws, need, flags, stream);
+  return attn_decode_impl(q, k_cache, v_cache, lens, out, B, Hq, Hkv, D, Lmax, kv_batch_stride, kv_head_stride,
+                          scale, ws, need, flags, stream, limit);
 }
 
 // Fused decode attention: q, k, v of the new token from the QKV projection, RoPE at
