@@ -71,6 +71,7 @@ def _args():
     ap.add_argument("--gemm-shape", default="2048,2048,8192", help="M,K,N of the gemm workload")
     ap.add_argument("--batch", type=int, default=1, help="decode batch per GPU")
     ap.add_argument("--n-vec", type=int, default=1, help="vectors per GEMV call (int4_gemv)")
+    ap.add_argument("--attn-case", default=None, help="attention: one case B,L_max instead of all nine")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--allreduce", choices=["auto", "fused", "nccl"], default="auto",
@@ -1185,7 +1186,8 @@ def _time_attention(B, L, args, max_alloc=12 << 30):
 def run_attention(args, world, rank, local):
     """iron_attn_decode (32 q / 8 kv heads, d 64) at batch 1/16/64 x
     L_max 512/4096/32768, per-sequence lengths ~ U[1, L_max] (seeded). value = the
-    achieved GB/s of the largest case (batch 64, 32768); every case under "cases"."""
+    achieved GB/s of the largest case (batch 64, 32768; or the one --attn-case names);
+    every case under "cases"."""
     peak, psrc = _peak_hbm()
     cases, launches = [], 0
     sampler = ClockSampler(local) if rank == 0 else None
@@ -1193,7 +1195,8 @@ def run_attention(args, world, rank, local):
         sampler.start()
         time.sleep(0.3)
         sampler.mark("t0")
-    for B, L in ATTN_CASES:
+    todo = [tuple(int(v) for v in args.attn_case.split(","))] if args.attn_case else ATTN_CASES
+    for B, L in todo:
         c, n = _time_attention(B, L, args)
         c["frac"] = round(c["gbs"] / peak, 4)
         cases.append(c)
@@ -1202,16 +1205,25 @@ def run_attention(args, world, rank, local):
         sampler.mark("t1")
     clocks = sampler.stop() if sampler else None
     head = cases[-1]
+    # DRAM traffic from the ncu capture of the batch-64 x 4096 case (profiles/), scaled to
+    # this case by algorithmic bytes (the capture's traffic equals its algorithmic bytes)
+    t_small = _profile_traffic("attention:B64L4096")
+    traffic = None
+    if t_small is not None:
+        lens = _attn_case_inputs(64, 4096, seed=1000 * 64 + 4096)
+        small = int(lens.sum()) * 8 * 64 * 4 + 64 * 32 * 64 * 4
+        traffic = int(round(t_small / small * head["bytes"]))
     line = {"metric": "GQA decode attention achieved HBM GB/s", "value": round(head["gbs"] * world, 1),
             "unit": "GB/s", "n_gpus": world, "steps": None, "warmup": 3, "ms_per_step": head["us"] / 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16 (fp32 softmax and accumulate)",
             "data": "synthetic (K/V ~ N(0, 1), lengths ~ U[1, L_max]; seeded)",
             "config": {"workload": "attention (BASELINE config 4)", "heads": "32 q / 8 kv, d 64",
-                       "headline_case": {"B": 64, "L_max": 32768},
+                       "headline_case": {"B": head["B"], "L_max": head["L_max"]},
                        "l2": "cache copies rotated so each round reads > 3x L2", "parallelism": f"dp{world}"},
             "roofline": {"bound": "hbm", "achieved": head["gbs"], "peak": peak, "unit": "GB/s",
-                         "frac": head["frac"], "traffic": None,
+                         "frac": head["frac"], "traffic": traffic,
+                         "traffic_source": "ncu capture of the batch-64 x 4096 case, scaled by algorithmic bytes",
                          "scope": "one iron_attn_decode call (split kernel + combine)",
                          "algorithmic_bytes_per_step": head["bytes"], "peak_source": psrc},
             "cases": cases, "gpu_launches": launches, "clocks": clocks, "e2e": None}
