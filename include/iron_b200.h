@@ -271,8 +271,10 @@ int iron_attn_decode(const uint16_t *q, const uint16_t *k_cache, const uint16_t 
  * not acceptable. Same arguments and results as iron_attn_decode minus the
  * workspace: the split partials go to a fixed 1 MiB array inside the library
  * (per device, held until the process exits; enough for 32 query / 8 kv heads up
- * to 32768 tokens at any batch). Requests needing more than 1 MiB
- * (iron_attn_decode_workspace_bytes > 1 MiB) return IRON_ERR_WORKSPACE. The
+ * to 32768 tokens at any batch). Where the usual split count's partials would not fit
+ * it, the extra splits that long caches get (at most 4096 tokens per CTA) are dropped,
+ * down to the count that fills two waves of the SMs; requests whose partials exceed
+ * 1 MiB even then return IRON_ERR_WORKSPACE. The
  * first call on a device looks up the array's device address (with that device
  * current) and caches it, so make that first call before any stream capture.
  * Nothing is allocated: no cudaMalloc or cudaFree. Every call uses the same
@@ -296,7 +298,8 @@ int iron_attn_decode_noalloc(const uint16_t *q, const uint16_t *k_cache, const u
 size_t iron_attn_decode_qkv_workspace_bytes(int B, int Hq, int Hkv, int Lmax, int D);
 /* iron_attn_decode_kernels: launches one decode-attention call makes (1, or 2 when a
  * split-combine kernel follows). With GQA groups of <= 4 query heads, when all of them
- * fit in one wave of the SMs, the splits of a (sequence, kv head) run as one cluster of
+ * fit in one wave of the SMs and no CTA gets more than 512 of the Lmax tokens, the
+ * splits of a (sequence, kv head) run as one cluster of
  * 16 or 8 CTAs that merge through distributed shared memory (one launch, no workspace
  * use); otherwise the partials go through `workspace` and a combine kernel. */
 int iron_attn_decode_kernels(int B, int Hq, int Hkv, int Lmax);
