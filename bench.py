@@ -1180,7 +1180,8 @@ def _time_attention(B, L, args, max_alloc=12 << 30):
     del graph, kc, vc
     torch.cuda.synchronize()
     return {"B": B, "L_max": L, "sum_len": int(lens.sum()), "us": round(us, 2),
-            "gbs": round(nbytes / (us * 1e-6) / 1e9, 1), "bytes": nbytes, "copies": copies}, launches
+            "gbs": round(nbytes / (us * 1e-6) / 1e9, 1), "bytes": nbytes, "copies": copies,
+            "calls_timed": reps * copies}, launches
 
 
 def run_attention(args, world, rank, local):
@@ -1214,7 +1215,8 @@ def run_attention(args, world, rank, local):
         small = int(lens.sum()) * 8 * 64 * 4 + 64 * 32 * 64 * 4
         traffic = int(round(t_small / small * head["bytes"]))
     line = {"metric": "GQA decode attention achieved HBM GB/s", "value": round(head["gbs"] * world, 1),
-            "unit": "GB/s", "n_gpus": world, "steps": None, "warmup": 3, "ms_per_step": head["us"] / 1e3,
+            "unit": "GB/s", "n_gpus": world, "steps": head["calls_timed"], "warmup": 3 * head["copies"],
+            "ms_per_step": head["us"] / 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16 (fp32 softmax and accumulate)",
             "data": "synthetic (K/V ~ N(0, 1), lengths ~ U[1, L_max]; seeded)",
