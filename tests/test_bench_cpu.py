@@ -1,6 +1,7 @@
 """bench.py's contract on the CPU: the reference arm (IRON's CPU path, timed on the host
 cores) prints one JSON line with the keys the driver reads, only rank 0 prints under a
-multi-rank launch, and fewer than 3 warm-up steps are refused."""
+multi-rank launch, and fewer than 3 warm-up steps are refused; the GPU arms' block and
+attention lines carry the contract keys (device timing stubbed)."""
 
 import json
 import os
@@ -45,3 +46,49 @@ def test_fewer_than_three_warmup_steps_refused():
     r = _bench("--impl", "reference", "--workload", "bf16_gemv", "--steps", "1", "--warmup", "2")
     assert r.returncode != 0
     assert "warmup" in r.stderr
+
+
+OURS_KEYS = {"metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+             "scaling", "vs_baseline", "dtype", "data", "config", "roofline", "gpu_launches", "clocks", "e2e"}
+
+
+def _run_line(fn, args, monkeypatch, capsys):
+    import bench
+
+    monkeypatch.setattr(bench, "ClockSampler", lambda local: None)
+    fn(bench)(args, 1, 0, 0)
+    return json.loads(capsys.readouterr().out.strip())
+
+
+def test_attention_line_keys_and_scaled_traffic(monkeypatch, capsys):
+    """The attention line's contract keys, with the device timing replaced by a stub: the
+    headline is the last case, its traffic the profiled ratio times its bytes."""
+    import bench
+
+    def fake(B, L, args, max_alloc=0):
+        return {"B": B, "L_max": L, "sum_len": 1, "us": 10.0, "gbs": 100.0, "bytes": 10 ** 9, "copies": 2,
+                "calls_timed": 200}, 200
+
+    monkeypatch.setattr(bench, "_time_attention", fake)
+    args = type("A", (), {"attn_case": None, "no_pdl": False})()
+    d = _run_line(lambda b: b.run_attention, args, monkeypatch, capsys)
+    assert OURS_KEYS <= set(d), OURS_KEYS - set(d)
+    assert len(d["cases"]) == 9 and d["config"]["headline_case"] == {"B": 64, "L_max": 32768}
+    assert d["gpu_launches"] == 9 * 200 and d["steps"] == 200
+    assert abs(d["roofline"]["traffic"] / 10 ** 9 - 1) < 1e-3  # the capture's traffic equals its bytes
+
+
+def test_block_line_keys(monkeypatch, capsys):
+    import bench
+
+    def fake(args, world, local, full, pos, rank):
+        return {"steps": 3000, "ms_per_step": 0.04, "bytes_per_step": 113260544,
+                "kernels_per_step": 9 if full else 7, "clocks": None}
+
+    monkeypatch.setattr(bench, "_time_block_form", fake)
+    args = type("A", (), {"batch": 16, "no_cpu_baseline": True, "warmup": 30})()
+    d = _run_line(lambda b: b.run_block, args, monkeypatch, capsys)
+    assert OURS_KEYS <= set(d), OURS_KEYS - set(d)
+    assert d["gpu_launches"] == 7 * 3000 and len(d["config"]["positions"]) == 16
+    assert all(0 <= p < 4096 for p in d["config"]["positions"])
+    assert abs(d["value"] - 113260544 / 40e-6 / 1e9) < 0.1
