@@ -521,24 +521,15 @@ template <int kAD, bool kFused, int kCS>
 static int launch_attn_cluster_cs(AttnArgs a, int B, int Hkv, int Lmax, bool pdl, cudaStream_t s) {
   auto kern = attn_decode_kernel<kAD, kFused, kCS>;
   constexpr size_t kMaxSmem = static_cast<size_t>(kCS) * 4 * (2 + kAD) * sizeof(float);
-  static bool configured = false;  // per instantiation: dynamic shared memory opt-in done
-  if (!configured) {
-    if (kCS > 8) {
-      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-      if (e != cudaSuccess) {
-        set_last_cuda_error(e);
-        (void)cudaGetLastError();
-        return IRON_ERR_CUDA;
-      }
-    }
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kMaxSmem));
-    if (e != cudaSuccess) {
-      set_last_cuda_error(e);
-      (void)cudaGetLastError();
-      return IRON_ERR_CUDA;
-    }
-    configured = true;
-  }
+  static PerDeviceOnce configured;  // per instantiation and device: cluster / shared memory opt-ins
+  const int cst = configured.run([&]() {
+    cudaError_t e = cudaSuccess;
+    if (kCS > 8) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kMaxSmem));
+    return call_status(e);
+  });
+  if (cst != IRON_OK) return cst;
   a.splits = kCS;
   a.chunk = ((Lmax + kCS - 1) / kCS + kAWarps * kABlk - 1) / (kAWarps * kABlk) * (kAWarps * kABlk);
   a.ws = nullptr;

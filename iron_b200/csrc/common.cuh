@@ -1,6 +1,7 @@
 // Shared helpers for the sm_100a kernels of libiron_b200.so.
 #pragma once
 
+#include <atomic>
 #include <cstring>
 
 #include <cuda_runtime.h>
@@ -26,8 +27,33 @@ inline int launch_status() {
 
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Status of a CUDA runtime call that is not a launch: records a failure for
+// iron_last_cuda_error() and clears it from the runtime.
+inline int call_status(cudaError_t e) {
+  if (e == cudaSuccess) return IRON_OK;
+  set_last_cuda_error(e);
+  (void)cudaGetLastError();
+  return IRON_ERR_CUDA;
+}
+
 // Number of SMs of the current device, cached per device.
 int sm_count();
+
+// One-time setup per device (function attributes apply to the current device), safe
+// under concurrent callers: two threads may both run the setup, which is idempotent.
+struct PerDeviceOnce {
+  std::atomic<bool> done[64];
+  template <typename F>
+  int run(F &&setup) {  // setup() -> status; recorded as done only when it succeeds
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+    const bool cached = dev >= 0 && dev < 64;
+    if (cached && done[dev].load(std::memory_order_acquire)) return IRON_OK;
+    const int st = setup();
+    if (st == IRON_OK && cached) done[dev].store(true, std::memory_order_release);
+    return st;
+  }
+};
 
 // Launch `kernel` on `stream`, optionally allowing programmatic dependent launch.
 template <typename... KArgs, typename... Args>

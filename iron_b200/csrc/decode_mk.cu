@@ -796,15 +796,12 @@ extern "C" int iron_llama_decode_persistent(const void *layers, int n_layers, co
   a.eps = eps;
   a.scale_log2 = 0.125f * 1.4426950408889634f;  // 1 / sqrt(64)
   const size_t smem = mk::kMaxB * mk::kE * 2 + 128 + mk::kWarps * (mk::kG * mk::kD * 2 + 16 * mk::kVStride * 2);
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(mk::decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
-      return launch_status();
-    attr_set[dev] = true;
-  }
+  static PerDeviceOnce attr_set;  // per device: the shared memory opt-in
+  const int ast = attr_set.run([&]() {
+    return call_status(cudaFuncSetAttribute(mk::decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(smem)));
+  });
+  if (ast != IRON_OK) return ast;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(sm_count());
   cfg.blockDim = dim3(mk::kThreads);

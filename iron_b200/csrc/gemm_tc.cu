@@ -315,15 +315,11 @@ template <int BN>
 int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, uint16_t *C, int M, int N, int K, int64_t ldc,
                 const uint16_t *R, int64_t ldr, Epi epi, cudaStream_t s, bool pdl) {
   using G = Cfg<BN>;
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem) !=
-        cudaSuccess)
-      return launch_status();
-    attr_set[dev] = true;
-  }
+  static PerDeviceOnce attr_set;  // per instantiation and device: the shared memory opt-in
+  const int ast = attr_set.run([]() {
+    return call_status(cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem));
+  });
+  if (ast != IRON_OK) return ast;
   const int64_t tiles = static_cast<int64_t>((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   dim3 grid(static_cast<unsigned>(tiles < sm_count() ? tiles : sm_count()));
   return launch(gemm_tc_kernel<BN>, grid, dim3(kThreads), G::kSmem, s, pdl, ta, tb, C, M, N, K, ldc, R, ldr, epi);
