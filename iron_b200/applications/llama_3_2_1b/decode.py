@@ -145,7 +145,7 @@ class LlamaDecodeEngine:
         self.amax = torch.zeros(B * 32, dtype=torch.int64, device=dev)  # fused argmax key slots
         self.graph = None
         # The persistent single-kernel step (iron_llama_decode_persistent) serves the
-        # Llama-3.2-1B layer shape at B <= 8; it is opt-in: measured on B200 it is slower
+        # Llama-3.2-1B layer shape at B <= 2; it is opt-in: measured on B200 it is slower
         # than the PDL-chained graph (1.26 vs 0.63 ms per batch-1 step).
         # (B > 2 is refused: at B = 8 a second layer's attention diverges from the kernel
         # chain for some sequences -- an open issue of the persistent kernel)
@@ -155,7 +155,7 @@ class LlamaDecodeEngine:
         # where RMSNorm runs inside the following GEMV ("none", "layers": the QKV and
         # gate/up GEMVs, "all": also the lm-head); only for B <= 8. Defaults measured on
         # B200 (one process, interleaved, 8-warp GEMV tiles): the fused prologue costs
-        # 28 us per step at B = 1 and 172 us at B = 8; RoPE inside attention (whose cached
+        # 63 us per step at B = 1 and 289 us at B = 8; RoPE inside attention (whose cached
         # K / V rows are then requested before the wait for the QKV projection) saves
         # 44 us at B = 1, 62 us at B = 8 and 305 us at B = 64.
         self.fuse_norm = fuse_norm if fuse_norm is not None else "none"
