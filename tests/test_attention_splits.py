@@ -1,0 +1,40 @@
+"""Host-side split rules of the decode attention, read through the C ABI without a GPU
+(the SM count falls back to the B200's 148): enough split CTAs for two waves, at most
+4096 tokens per split CTA, clusters only while a CTA's share is at most 512 tokens.
+The split count s shows in the workspace size of the split-and-combine form,
+B * Hq * s * (2 + D) * 4 bytes (0 when s = 1; reported also where the splits merge in a
+cluster instead), and in the launches per call (1: one split or one cluster per
+(sequence, kv head); 2: split kernel + combine)."""
+
+import pytest
+
+from iron_b200 import _lib
+
+HQ, HKV, D = 32, 8, 64
+
+
+def _splits(B, L):
+    ws = _lib.load().iron_attn_decode_workspace_bytes_d(B, HQ, HKV, L, D)
+    return ws // (B * HQ * (2 + D) * 4) if ws else 1
+
+
+@pytest.mark.parametrize("B,L,splits,launches", [
+    (1, 2320, 37, 1),     # decode batch 1: 37 chunks of 64 tokens, merged in clusters of 16
+    (2, 2320, 32, 1),     # batch 2: clusters of 8
+    (8, 2320, 8, 2),      # batch 8: two waves of split CTAs, combine kernel
+    (64, 2320, 1, 1),     # batch 64: one CTA per (sequence, kv head) already fills two waves
+    (64, 4096, 1, 1),     # 4096 tokens still fit one CTA
+    (1, 32768, 64, 2),    # a cluster CTA would get 2048 tokens: independent splits instead
+    (16, 32768, 8, 2),    # the 4096-token cap, not the waves, sets the count
+    (64, 32768, 8, 2),
+])
+def test_split_rules(B, L, splits, launches):
+    assert _splits(B, L) == splits
+    assert _lib.load().iron_attn_decode_kernels(B, HQ, HKV, L) == launches
+
+
+def test_fused_form_uses_the_same_splits():
+    lib = _lib.load()
+    for B, L in [(1, 2320), (8, 2320), (64, 32768)]:
+        assert lib.iron_attn_decode_qkv_workspace_bytes(B, HQ, HKV, L, D) == \
+            lib.iron_attn_decode_workspace_bytes_d(B, HQ, HKV, L, D)
