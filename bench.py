@@ -117,7 +117,9 @@ def _max_over_ranks(x: float, world: int) -> float:
         return x
     import torch.distributed as dist
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    # NCCL reduces device tensors; a gloo group (the CPU tests) host tensors
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 

@@ -1,7 +1,8 @@
 """bench.py's contract on the CPU: the reference arm (IRON's CPU path, timed on the host
 cores) prints one JSON line with the keys the driver reads, only rank 0 prints under a
 multi-rank launch, and fewer than 3 warm-up steps are refused; the GPU arms' block and
-attention lines carry the contract keys (device timing stubbed)."""
+attention lines carry the contract keys (device timing stubbed); with two gloo ranks
+every rank's reported time is the max over ranks."""
 
 import json
 import os
@@ -92,3 +93,34 @@ def test_block_line_keys(monkeypatch, capsys):
     assert d["gpu_launches"] == 7 * 3000 and len(d["config"]["positions"]) == 16
     assert all(0 <= p < 4096 for p in d["config"]["positions"])
     assert abs(d["value"] - 113260544 / 40e-6 / 1e9) < 0.1
+
+
+def _rank_max(rank, world, port, out):
+    import torch.distributed as dist
+
+    sys.path.insert(0, REPO)
+    import bench
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        bench._barrier(world)
+        out[rank] = bench._max_over_ranks(1.5 + rank, world)  # each rank's "device time"
+        bench._barrier(world)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_multi_rank_time_is_the_max_over_ranks():
+    """With N > 1 ranks the step time every rank reports is the slowest rank's (two gloo
+    ranks standing in for the NCCL group of a GPU run)."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s_:
+        s_.bind(("127.0.0.1", 0))
+        port = s_.getsockname()[1]
+    out = mp.get_context("spawn").Manager().dict()
+    mp.spawn(_rank_max, args=(2, port, out), nprocs=2, join=True)
+    assert dict(out) == {0: 2.5, 1: 2.5}
