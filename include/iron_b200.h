@@ -140,14 +140,16 @@ int iron_argmax_finalize(unsigned long long *keys, int32_t *tokens, int32_t *pos
  * and, with `residual`, y = bf16(bf16(sum) + residual) on every rank. `peers` points to
  * an iron_allreduce_peers in host memory; recv[r] is rank r's buffer ([world, N, n_vec]
  * 8-byte slots, zero before first use and left zero), mapped into this process with
- * iron_ipc_open for r != rank. All ranks launch it for the same shape; a wait for a peer's tile gives up after 1 s and sets
- * *status. iron_ipc_alloc / iron_ipc_free give these buffers their own zero-filled
+ * iron_ipc_open for r != rank. All ranks launch it for the same shape; a wait for a peer's tile gives up after
+ * wait_us microseconds (0: one second), sets *status and goes on with the values it has
+ * (later waits of the same launch give up at once). iron_ipc_alloc / iron_ipc_free give these buffers their own zero-filled
  * allocations (an IPC handle maps the start of an allocation); iron_ipc_handle /
  * iron_ipc_open / iron_ipc_close wrap CUDA IPC (64-byte handles). */
 typedef struct {
   int world, rank;
   float *recv[8];
   unsigned *status;
+  unsigned wait_us;
 } iron_allreduce_peers;
 int iron_gemv_int4g32_allreduce(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K, int n_vec,
                                 const uint16_t *residual, const void *peers, unsigned flags, void *stream);
@@ -270,13 +272,16 @@ int iron_attn_decode(const uint16_t *q, const uint16_t *k_cache, const uint16_t 
  * latency-critical path where cudaMalloc's implicit device synchronisation is
  * not acceptable. Same arguments and results as iron_attn_decode minus the
  * workspace: the split partials go to a fixed 1 MiB array inside the library
- * (per device, held until the process exits; enough for 32 query / 8 kv heads up
- * to 32768 tokens at any batch). Where the usual split count's partials would not fit
- * it, the extra splits that long caches get (at most 4096 tokens per CTA) are dropped,
- * down to the count that fills two waves of the SMs; requests whose partials exceed
- * 1 MiB even then return IRON_ERR_WORKSPACE. The
+ * (per device, held until the process exits). At head_dim 64 with 32 query / 8 kv
+ * heads on a 148-SM B200 that holds the partials of every batch up to 32768 tokens; at
+ * head_dim 128 some batches do not fit (at 32768 tokens: 1, 2, 4, 8, 9, 16-18 and
+ * 32-36). Where the usual split count's partials would not fit it, the extra splits
+ * that long caches get (at most 4096 tokens per CTA) are dropped, down to the count
+ * that fills two waves of the SMs; requests whose partials exceed 1 MiB even then
+ * return IRON_ERR_WORKSPACE (after the same argument checks as iron_attn_decode). The
  * first call on a device looks up the array's device address (with that device
- * current) and caches it, so make that first call before any stream capture.
+ * current) and caches it with the CUDA context it belongs to, so make that first call
+ * before any stream capture; after cudaDeviceReset the next call looks it up again.
  * Nothing is allocated: no cudaMalloc or cudaFree. Every call uses the same
  * array, so calls that overlap on the GPU (other streams, other threads) race;
  * each call writes every partial it reads, so no clearing is needed.

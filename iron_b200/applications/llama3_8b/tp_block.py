@@ -35,7 +35,7 @@ class AllReducePeers(ctypes.Structure):
     """iron_allreduce_peers (include/iron_b200.h)."""
 
     _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int), ("recv", ctypes.c_void_p * 8),
-                ("status", ctypes.c_void_p)]
+                ("status", ctypes.c_void_p), ("wait_us", ctypes.c_uint)]
 
 
 class _DeviceBuffer:

@@ -469,11 +469,29 @@ constexpr size_t kAttnScratchBytes = static_cast<size_t>(1) << 20;
 static __device__ __align__(256) float g_attn_scratch[kAttnScratchBytes / sizeof(float)];
 
 // Device address of g_attn_scratch on the current device. In host code the
-// symbol names a host-side stand-in, not device memory, so the address is
-// looked up once per device (with that device current) and cached.
+// symbol names a host-side stand-in, not device memory, so the address is looked up
+// with the device current (cudaGetSymbolAddress) at the first call on each device and
+// cached together with the CUDA context it belongs to: after cudaDeviceReset (or any
+// teardown of the device's primary context) the module is loaded again, the current
+// context differs, and the address is looked up again instead of reusing a stale one.
+typedef int (*CtxGetCurrentFn)(void **);  // cuCtxGetCurrent (CUresult, CUcontext *)
+static CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
+
 static float *attn_scratch_address(int *status) {
   static std::mutex mu;
   static float *cache[64] = {nullptr};
+  static void *cache_ctx[64] = {nullptr};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess || dev < 0 || dev >= 64) {
@@ -481,8 +499,13 @@ static float *attn_scratch_address(int *status) {
     *status = IRON_ERR_CUDA;
     return nullptr;
   }
+  // the context current on this thread; null before the runtime has made the device's
+  // primary context current here (the lookup below does that)
+  const CtxGetCurrentFn get_ctx = ctx_get_current();
+  void *ctx = nullptr;
+  if (get_ctx && get_ctx(&ctx) != 0) ctx = nullptr;
   std::lock_guard<std::mutex> lock(mu);
-  if (!cache[dev]) {
+  if (!cache[dev] || !ctx || cache_ctx[dev] != ctx) {
     void *p = nullptr;
     e = cudaGetSymbolAddress(&p, g_attn_scratch);
     if (e != cudaSuccess || !p) {
@@ -491,7 +514,9 @@ static float *attn_scratch_address(int *status) {
       *status = IRON_ERR_CUDA;
       return nullptr;
     }
+    if (get_ctx && get_ctx(&ctx) != 0) ctx = nullptr;
     cache[dev] = static_cast<float *>(p);
+    cache_ctx[dev] = ctx;
   }
   *status = IRON_OK;
   return cache[dev];
@@ -584,11 +609,11 @@ extern "C" size_t iron_attn_decode_workspace_bytes_d(int B, int Hq, int Hkv, int
   return (D == 64 || D == 128) ? attn_ws_bytes(B, Hq, Hkv, Lmax, D) : 0;
 }
 
-// iron_attn_decode with at most `limit` splits per sequence
-static int attn_decode_impl(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
-                            const int32_t *lens, uint16_t *out, int B, int Hq, int Hkv, int D, int Lmax,
-                            int64_t kv_batch_stride, int64_t kv_head_stride, float scale, void *workspace,
-                            size_t workspace_bytes, unsigned flags, void *stream, int limit) {
+// Argument checks of iron_attn_decode and iron_attn_decode_noalloc (same order, same
+// statuses): pointers, shape, head size, GQA grouping, alignment.
+static int attn_decode_check(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                             const int32_t *lens, const uint16_t *out, int B, int Hq, int Hkv, int D, int Lmax,
+                             int64_t kv_batch_stride, int64_t kv_head_stride) {
   if (!q || !k_cache || !v_cache || !lens || !out) return IRON_ERR_NULL;
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Lmax <= 0 || B > 65535 || Hkv > 65535) return IRON_ERR_SHAPE;
   if (D != 64 && D != 128) return IRON_ERR_UNSUPPORTED;
@@ -596,6 +621,17 @@ static int attn_decode_impl(const uint16_t *q, const uint16_t *k_cache, const ui
   if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || (kv_batch_stride % 8) ||
       (kv_head_stride % 8))
     return IRON_ERR_ALIGN;
+  return IRON_OK;
+}
+
+// iron_attn_decode with at most `limit` splits per sequence
+static int attn_decode_impl(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                            const int32_t *lens, uint16_t *out, int B, int Hq, int Hkv, int D, int Lmax,
+                            int64_t kv_batch_stride, int64_t kv_head_stride, float scale, void *workspace,
+                            size_t workspace_bytes, unsigned flags, void *stream, int limit) {
+  const int chk = attn_decode_check(q, k_cache, v_cache, lens, out, B, Hq, Hkv, D, Lmax, kv_batch_stride,
+                                    kv_head_stride);
+  if (chk != IRON_OK) return chk;
   AttnArgs a;
   a.q = q;
   a.k = k_cache;
@@ -646,9 +682,10 @@ extern "C" int iron_attn_decode_noalloc(const uint16_t *q, const uint16_t *k_cac
                                         int B, int Hq, int Hkv, int D, int Lmax,
                                         int64_t kv_batch_stride, int64_t kv_head_stride, float scale,
                                         unsigned flags, void *stream) {
-  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Lmax <= 0) return IRON_ERR_SHAPE;
-  if (D != 64 && D != 128) return IRON_ERR_UNSUPPORTED;
-  if (Hkv > 0 && Hq % Hkv == 0 && attn_use_cluster(B, Hq, Hkv, Lmax))  // merges in the cluster: no partials
+  const int chk = attn_decode_check(q, k_cache, v_cache, lens, out, B, Hq, Hkv, D, Lmax, kv_batch_stride,
+                                    kv_head_stride);
+  if (chk != IRON_OK) return chk;
+  if (attn_use_cluster(B, Hq, Hkv, Lmax))  // merges in the cluster: no partials
     return iron_attn_decode(q, k_cache, v_cache, lens, out, B, Hq, Hkv, D, Lmax, kv_batch_stride, kv_head_stride,
                             scale, nullptr, 0, flags, stream);
   // the splits that the chunk cap adds come off where their partials would not fit the

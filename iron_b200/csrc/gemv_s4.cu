@@ -54,6 +54,7 @@ struct S4AllReduce {
   int world, rank;
   float *recv[kS4MaxWorld];       // [world (source), N, n_vec] x (fp32 value, flag) 8-byte slots, zero between uses
   unsigned *status;               // non-zero: a wait for a peer's tile gave up
+  unsigned wait_us;               // give-up time of a wait for a peer's value (0: 1 s)
 };
 
 struct S4Epi {
@@ -110,6 +111,7 @@ __device__ __forceinline__ void s4_allreduce_tile(float (&v)[4], int tile, int N
     }
   }
   unsigned long long *mine = reinterpret_cast<unsigned long long *>(own);
+  const uint64_t limit_ns = ar.wait_us ? static_cast<uint64_t>(ar.wait_us) * 1000ull : 1000000000ull;
   bool gave_up = false;
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
@@ -125,7 +127,7 @@ __device__ __forceinline__ void s4_allreduce_tile(float (&v)[4], int tile, int N
             if (ld_acquire_sys(ar.status) != 0u) gave_up = true;  // an earlier wait gave up: fail fast
             const uint64_t t = s4_now_ns();
             if (start == 0) start = t;
-            else if (t - start > 1000000000ull) {  // 1 s without the peer's value
+            else if (t - start > limit_ns) {  // no value from the peer within the limit
               atomicOr(ar.status, 1u);
               gave_up = true;
             }

@@ -38,3 +38,21 @@ def test_fused_form_uses_the_same_splits():
     for B, L in [(1, 2320), (8, 2320), (64, 32768)]:
         assert lib.iron_attn_decode_qkv_workspace_bytes(B, HQ, HKV, L, D) == \
             lib.iron_attn_decode_workspace_bytes_d(B, HQ, HKV, L, D)
+
+
+def test_noalloc_argument_checks_and_capacity_on_the_host():
+    """iron_attn_decode_noalloc runs iron_attn_decode's argument checks first, then sizes
+    its fixed 1 MiB array; every status below is returned before any CUDA call."""
+    lib = _lib.load()
+    ok = 16  # any non-null, 16-byte aligned stand-in: nothing is launched
+    L = 32768
+
+    def call(q=ok, B=18, Hq=32, Hkv=8, D=128, kv_b=8 * L * 128, kv_h=L * 128):
+        return lib.iron_attn_decode_noalloc(q, ok, ok, ok, ok, B, Hq, Hkv, D, L, kv_b, kv_h, 0.088, 0, None)
+
+    assert call() == -6                   # head_dim 128, batch 18: 1,198,080 B of partials even at 4 splits
+    assert call(q=None) == -1             # null pointer
+    assert call(Hq=30) == -2              # query heads not a multiple of kv heads
+    assert call(D=96) == -4               # head size not served
+    assert call(q=24) == -3               # misaligned q
+    assert call(kv_h=L * 128 + 4) == -3   # misaligned head stride
