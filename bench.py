@@ -571,6 +571,18 @@ def _decode_bytes(eng, positions):
             + B * s.emb_dim * 2 + 2 * B * s.vocab_size * 2)
 
 
+def _decode_config(B, world, K):
+    """The decode workload's config, shared by both arms (same keys, same values)."""
+    from iron_b200.applications.llama_3_2_1b.decode import LlamaShape
+
+    wbytes = LlamaShape().weight_params() * 9 // 16
+    return {"workload": "decode (BASELINE config 5)", "model": "Llama-3.2-1B shape, random init",
+            "weights": "int4 group-32 (bf16 scales)", "batch_per_gpu": B, "global_batch": B * world,
+            "context_start": PREFIX, "seq_len": PREFIX + K,
+            "l2": "no flush: each step streams %.0f MB of weights (> L2)" % (wbytes / 1e6),
+            "parallelism": f"dp{world} (independent replicas)"}
+
+
 def run_decode(args, world, rank, local):
     from iron_b200.applications.llama_3_2_1b.decode import LlamaDecodeEngine, LlamaShape
 
@@ -634,11 +646,7 @@ def run_decode(args, world, rank, local):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16 (int4 g32 weights dequantized exactly to bf16, fp32 accumulate)",
         "data": "synthetic (random-init weights, random prompt KV cache; seeded)",
-        "config": {"workload": "decode (BASELINE config 5)", "model": "Llama-3.2-1B shape, random init",
-                   "weights": "int4 group-32 (bf16 scales)", "batch_per_gpu": B, "global_batch": B * world,
-                   "context_start": PREFIX, "seq_len": PREFIX + K,
-                   "l2": "no flush: each step streams %.0f MB of weights (> L2)" % (eng.weight_bytes() / 1e6),
-                   "parallelism": f"dp{world} (independent replicas)"},
+        "config": _decode_config(B, world, K),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4),
                      "traffic": _profile_traffic(f"decode:B{B}"),
@@ -698,35 +706,49 @@ def _prefill_figure(eng, S, reps=3):
 
 
 def _decode_e2e(eng, B, steps):
-    """tok/s through the engine API with host token ids: each step copies the
-    batch's input tokens from pinned host memory, replays the decode graph and
-    reads the sampled tokens back to pinned host memory."""
+    """tok/s through the engine API with host token ids, as IRON's decode loop runs
+    (iron/common/sequence.py:721-730 reads the result back every token): each step
+    copies the batch's input tokens from pinned host memory, replays the decode graph,
+    reads the sampled tokens back to pinned host memory and waits for them on the host.
+    The same loop without the per-step host wait (steps pipelined) is reported beside it."""
     host_in = eng.tokens.cpu().pin_memory()
     host_out = torch.empty(B, dtype=torch.int32).pin_memory()
-    eng.set_state(host_in, [PREFIX] * B)
-    for _ in range(3):
-        eng.tokens.copy_(host_in, non_blocking=True)
-        eng.step()
-        host_out.copy_(eng.tokens, non_blocking=True)
-    torch.cuda.synchronize()
-    eng.set_state(host_in, [PREFIX] * B)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        eng.tokens.copy_(host_in, non_blocking=True)
-        eng.step()
-        host_out.copy_(eng.tokens, non_blocking=True)
-    e1.record()
-    e1.synchronize()
-    ms = e0.elapsed_time(e1)
+    stream = torch.cuda.current_stream()
+
+    def loop(n, sync):
+        for _ in range(n):
+            eng.tokens.copy_(host_in, non_blocking=True)
+            eng.step()
+            host_out.copy_(eng.tokens, non_blocking=True)
+            if sync:
+                stream.synchronize()
+
+    res = {}
+    for sync in (True, False):
+        eng.set_state(host_in, [PREFIX] * B)
+        loop(3, sync)
+        torch.cuda.synchronize()
+        eng.set_state(host_in, [PREFIX] * B)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        loop(steps, sync)
+        e1.record()
+        e1.synchronize()
+        res[sync] = e0.elapsed_time(e1)
+    ms, ms_pipe = res[True], res[False]
     return {"value": round(B * steps / (ms * 1e-3), 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
             "d2h_bytes_per_step": 4 * B, "steps": steps, "ms_per_step": ms / steps,
-            "path": "LlamaDecodeEngine.step (CUDA graph of C-ABI kernels), pinned host token ids in and out"}
+            "path": "LlamaDecodeEngine.step (CUDA graph of C-ABI kernels), pinned host token ids in and out, "
+                    "host waits for each step's tokens",
+            "pipelined": {"value": round(B * steps / (ms_pipe * 1e-3), 1), "ms_per_step": ms_pipe / steps,
+                          "note": "same loop without the per-step host wait"}}
 
 
 def _cpu_decode_model(B, layers, seed=5):
-    """bf16 weights (N(0, 0.02)-scaled) and a 2048-token KV cache for the CPU decode step."""
+    """The CPU decode step's model: int4 group-32 weights (codes ~ U{-8..7}, bf16 group
+    scales in the GPU engine's ranges) dequantized exactly to bf16 -- the values the GPU
+    kernels multiply -- and a 2048-token KV cache."""
     from iron_b200.applications.llama_3_2_1b.decode import LlamaShape
 
     s = LlamaShape()
@@ -734,12 +756,15 @@ def _cpu_decode_model(B, layers, seed=5):
     gen.manual_seed(seed)
     E, H, Hd = s.emb_dim, s.hidden_dim, s.head_dim
 
-    def w(o, i):
-        return (torch.randn(o, i, generator=gen) * 0.02).to(torch.bfloat16)
+    def w(o, i, smin=0.001, smax=0.004):
+        q = torch.randint(-8, 8, (o, i), generator=gen, dtype=torch.int8).float()
+        sc = (torch.rand(o, i // 32, generator=gen) * (smax - smin) + smin).to(torch.bfloat16).float()
+        return (q * sc.repeat_interleave(32, dim=1)).to(torch.bfloat16)
 
     Ws = [{"n1": torch.ones(E, dtype=torch.bfloat16), "n2": torch.ones(E, dtype=torch.bfloat16),
            "q": w(s.n_heads * Hd, E), "k": w(s.n_kv_groups * Hd, E), "v": w(s.n_kv_groups * Hd, E),
-           "o": w(E, s.n_heads * Hd), "g": w(H, E), "u": w(H, E), "d": w(E, H)} for _ in range(layers)]
+           "o": w(E, s.n_heads * Hd), "g": w(H, E), "u": w(H, E), "d": w(E, H, 0.0005, 0.002)}
+          for _ in range(layers)]
     lm = w(s.vocab_size, E)
     kcs = [torch.randn(B, s.n_kv_groups, PREFIX + 8, Hd, generator=gen).to(torch.bfloat16) for _ in range(layers)]
     vcs = [torch.randn(B, s.n_kv_groups, PREFIX + 8, Hd, generator=gen).to(torch.bfloat16) for _ in range(layers)]
@@ -784,9 +809,14 @@ def run_reference_decode(args, world, rank):
         return
     B = args.batch
     step, layers = _cpu_decode_timer(B)
-    steps = max(1, min(args.steps, 8))
     for _ in range(min(args.warmup, 1)):
         step()
+    # every requested step, unless the CPU would take more than ~3 minutes for them
+    # (large batches): then a bounded sample of them, said so in `sample`
+    t0 = time.perf_counter()
+    step()
+    first = time.perf_counter() - t0
+    steps = max(1, min(args.steps, int(180.0 / max(first, 1e-3))))
     t0 = time.perf_counter()
     for _ in range(steps):
         step()
@@ -794,13 +824,14 @@ def run_reference_decode(args, world, rank):
     value = round(B / dt, 3)
     threads = torch.get_num_threads()
     sample = (f"{steps} decode steps (of {args.steps} requested) of batch {B} at context {PREFIX}, "
-              f"all {layers} layers + lm-head, llama_cpu.py restated in torch, bf16 weights")
+              f"all {layers} layers + lm-head, llama_cpu.py restated in torch on the bf16 values of "
+              f"int4 group-32 weights (what the GPU multiplies)")
     line = {"impl": "reference", "metric": "Llama-3.2-1B-shape decode tok/s", "value": value, "unit": "tok/s",
             "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (random-init weights; seeded)",
-            "config": {"workload": "decode (BASELINE config 5)", "model": "Llama-3.2-1B shape, random init",
-                       "batch_per_gpu": B, "context_start": PREFIX},
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 (int4 g32 weights dequantized exactly to bf16, fp32 accumulate)",
+            "data": "synthetic (random-init weights, random prompt KV cache; seeded)",
+            "config": _decode_config(B, world, args.steps),
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)

@@ -334,33 +334,19 @@ int iron_embed(const int32_t *tokens, const uint16_t *table, uint16_t *x, int B,
 int iron_argmax(const uint16_t *logits, int32_t *out, int B, int V, int32_t *pos, unsigned flags,
                 void *stream);
 
-/* ---- persistent decode step ---------------------------------------------------------
- * One whole Llama-3.2-1B-shape decode step (hidden 2048, 32/8 heads of 64, FFN 8192,
- * int4 g32 weights; llama_npu.py:1156-1195's step, llama_cpu.py:170-285's math) in a
- * single cooperative launch of one CTA per SM, phases separated by a bounded grid
- * barrier. `layers` is a DEVICE array of n_layers iron_decode_layer. The batch
- * (B <= 8) decodes tokens[b] at position pos[b]; afterwards tokens[b] holds the
- * greedy next token, pos[b] += 1, and the caches hold the new rows. x, h [B, 2048],
- * qkv [B, 3072], attn [B, 2048], act [B, 8192] are activation buffers; logits
- * [B, vocab] is optional. scratch (>= iron_llama_decode_persistent_scratch_bytes,
- * zero-filled before the first call; the kernel leaves it zeroed) holds partials,
- * counters and the grid barrier. *status (device) gets bit 0 if a barrier wait gave
- * up (after 1 s without progress; then re-zero the scratch) and bit 1 if a position
- * is outside [0, max_seq) or a token outside [0, vocab) (nothing is computed then).
- */
-typedef struct {
-  const uint8_t *qkv, *o, *gu, *d; /* packed int4 g32 (iron_pack_int4g32) */
-  const uint16_t *n1, *n2;         /* RMSNorm weights [2048] */
-  uint16_t *k_cache, *v_cache;     /* [B, 8, max_seq, 64] */
-} iron_decode_layer;
-size_t iron_llama_decode_persistent_scratch_bytes(int B, int max_seq);
-int iron_llama_decode_persistent(const void *layers, int n_layers, const uint16_t *embed,
-                                 const uint16_t *final_norm, const uint8_t *lm_head, int vocab,
-                                 const float *rope_lut, int32_t *tokens, int32_t *pos, uint16_t *x,
-                                 uint16_t *h, uint16_t *qkv, uint16_t *attn, uint16_t *act,
-                                 uint16_t *logits, int B, int max_seq, int64_t kv_batch_stride,
-                                 int64_t kv_head_stride, float eps, void *scratch, size_t scratch_bytes,
-                                 unsigned *status, unsigned flags, void *stream);
+/* Next-token sampling on the device, replacing the per-token logits read-back and the
+ * CPU sampling of IRON's generate_token (iron/applications/llama_3.2_1b/
+ * llama_inference_harness.py:146-169; its decode loop reads the logits at
+ * iron/common/sequence.py:721-730). For each of the B rows of logits (bf16 [B, V]):
+ * divide by `temperature` (> 0; 0 leaves the logits as they are, as the harness
+ * does), keep the logits >= the top_k-th largest (ties kept; top_k <= 0 or >= V keeps
+ * all), softmax, and draw one index with probability proportional to its weight.
+ * The uniform draw is a function of (seed, row b, pos[b]) (SplitMix64), so the result
+ * is bitwise reproducible and a replayed decode graph draws afresh as positions
+ * advance. tokens[b] gets the index; with `pos`, pos[b] += 1 afterwards (pos NULL:
+ * position 0 for every row). */
+int iron_sample_topk(const uint16_t *logits, int B, int V, float temperature, int top_k,
+                     unsigned long long seed, int32_t *tokens, int32_t *pos, unsigned flags, void *stream);
 
 /* ---- prefill attention ------------------------------------------------------------
  * Causal (or full) grouped-query attention over a sequence, replacing IRON's MHA

@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import ctypes
 import threading
-from ctypes import c_float, c_int, c_int64, c_uint, c_void_p, c_char_p, c_size_t
+from ctypes import c_float, c_int, c_int64, c_uint, c_uint64, c_void_p, c_char_p, c_size_t
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libiron_b200.so"
@@ -61,9 +61,9 @@ SIGNATURES: dict[str, list] = {
                        c_float, c_float, c_int, c_uint, P],
     "iron_gemm_status": [c_int],
     "iron_unpack_int4g32": [P, P, c_int, c_int, P],
-    "iron_llama_decode_persistent_scratch_bytes": [c_int, c_int],
     "iron_gemv_int4g32_ex": [P, P, P, c_int, c_int, c_int, P, P, c_float, P, c_uint, P],
     "iron_argmax_finalize": [P, P, P, c_int, c_uint, P],
+    "iron_sample_topk": [P, c_int, c_int, c_float, c_int, c_uint64, P, P, c_uint, P],
     "iron_l2_prefetch": [P, c_size_t, c_uint, P],
     "iron_attn_decode_kernels": [c_int, c_int, c_int, c_int],
     "iron_gemv_int4g32_allreduce": [P, P, P, c_int, c_int, c_int, P, P, c_uint, P],
@@ -75,14 +75,11 @@ SIGNATURES: dict[str, list] = {
     "iron_attn_decode_qkv_workspace_bytes": [c_int, c_int, c_int, c_int, c_int],
     "iron_attn_decode_qkv": [P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int64, c_int64, c_float, P,
                              c_size_t, c_uint, P],
-    "iron_llama_decode_persistent": [P, c_int, P, P, P, c_int, P, P, P, P, P, P, P, P, P, c_int, c_int, c_int64,
-                                     c_int64, c_float, P, c_size_t, P, c_uint, P],
     "iron_attn_prefill": [P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, c_float, c_int,
                           c_uint, P],
 }
 _RESTYPES = {"iron_strerror": c_char_p, "iron_attn_decode_workspace_bytes": c_size_t,
              "iron_attn_decode_workspace_bytes_d": c_size_t,
-             "iron_llama_decode_persistent_scratch_bytes": c_size_t,
              "iron_attn_decode_qkv_workspace_bytes": c_size_t}
 
 _lock = threading.Lock()

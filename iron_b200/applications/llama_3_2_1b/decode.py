@@ -93,13 +93,28 @@ def interleave_gate_up(gate_rows: int) -> torch.Tensor:
     return idx.reshape(-1)
 
 
+@dataclass
+class SamplingConfig:
+    """Next-token sampling of IRON's harness (llama_inference_harness.py:44-45 defaults,
+    :146-169 steps): logits / temperature, top-k filter, softmax, multinomial draw.
+    Runs on the device; the draw is a function of (seed, sequence, position)."""
+
+    temperature: float = 0.7
+    top_k: int = 50
+    seed: int = 0
+
+
 class LlamaDecodeEngine:
     """Batched greedy decode of a random-init int4 Llama-3.2-1B-shape model."""
 
     def __init__(self, shape: LlamaShape, batch: int, max_seq: int, seed: int = 0,
-                 keep_natural: bool = False, pdl: bool = True, persistent: bool | None = None,
-                 fuse_norm: str | None = None, fuse_rope: bool | None = None, l2_prefetch: bool | None = None):
+                 keep_natural: bool = False, pdl: bool = True, fuse_norm: str | None = None,
+                 fuse_rope: bool | None = None, l2_prefetch: bool | None = None,
+                 sampling: "SamplingConfig | None" = None):
         self.s, self.B, self.L = shape, batch, max_seq
+        # None: greedy argmax fused into the lm-head GEMV; else temperature / top-k /
+        # multinomial on the device (iron_sample_topk)
+        self.sampling = sampling
         self.dev = torch.device("cuda", torch.cuda.current_device())
         self.flags = _lib.IRON_FLAG_PDL if pdl else 0
         s, dev = shape, self.dev
@@ -144,14 +159,6 @@ class LlamaDecodeEngine:
         self.attn_ws = torch.zeros(max(wsb, 16), dtype=torch.uint8, device=dev)
         self.amax = torch.zeros(B * 32, dtype=torch.int64, device=dev)  # fused argmax key slots
         self.graph = None
-        # The persistent single-kernel step (iron_llama_decode_persistent) serves the
-        # Llama-3.2-1B layer shape at B <= 2; it is opt-in: measured on B200 it is slower
-        # than the PDL-chained graph (1.26 vs 0.63 ms per batch-1 step).
-        # (B > 2 is refused: at B = 8 a second layer's attention diverges from the kernel
-        # chain for some sequences -- an open issue of the persistent kernel)
-        fits = (B <= 2 and (s.emb_dim, s.n_heads, s.n_kv_groups, s.head_dim, s.hidden_dim)
-                == (2048, 32, 8, 64, 8192))
-        self.persistent = bool(persistent)
         # where RMSNorm runs inside the following GEMV ("none", "layers": the QKV and
         # gate/up GEMVs, "all": also the lm-head); only for B <= 8. Defaults measured on
         # B200 (one process, interleaved, 8-warp GEMV tiles): the fused prologue costs
@@ -167,16 +174,6 @@ class LlamaDecodeEngine:
         # the step (off the dependent chain) when the layer starts
         self.l2_prefetch = bool(l2_prefetch) if l2_prefetch is not None else False
         self._side = torch.cuda.Stream() if self.l2_prefetch else None
-        if self.persistent:
-            if not fits:
-                raise ValueError("the persistent decode step needs the Llama-3.2-1B layer shape and batch <= 2")
-            ptrs = [[lay[k].packed.data_ptr() for k in ("qkv", "o", "gu", "d")]
-                    + [lay["n1"].data_ptr(), lay["n2"].data_ptr(), self.kc[i].data_ptr(), self.vc[i].data_ptr()]
-                    for i, lay in enumerate(self.layers)]
-            self._mk_layers = torch.tensor(ptrs, dtype=torch.int64, device=dev)
-            nb = _lib.load().iron_llama_decode_persistent_scratch_bytes(B, max_seq)
-            self._mk_scratch = torch.zeros(nb, dtype=torch.uint8, device=dev)
-            self._mk_status = torch.zeros(4, dtype=torch.int32, device=dev)
 
     # -- bytes moved per step (the roofline numerator) ---------------------------------
     def weight_bytes(self) -> int:
@@ -189,28 +186,11 @@ class LlamaDecodeEngine:
 
     # -- one decode step ----------------------------------------------------------------
     def _launch_step(self, stream: int):
-        if self.persistent:
-            self._launch_step_persistent(stream)
-        else:
-            self._launch_step_graph_kernels(stream)
-
-    def _launch_step_persistent(self, stream: int):
-        s, B, p = self.s, self.B, (lambda t: t.data_ptr())
-        L, Hd = self.L, s.head_dim
-        _lib.call("iron_llama_decode_persistent", p(self._mk_layers), s.n_layers, p(self.embed_table), p(self.nf),
-                  p(self.lm.packed), s.vocab_size, p(self.lut), p(self.tokens), p(self.pos), p(self.x), p(self.h),
-                  p(self.qkv), p(self.attn), p(self.act), p(self.logits), B, L, s.n_kv_groups * L * Hd, L * Hd,
-                  s.eps, p(self._mk_scratch), self._mk_scratch.numel(), p(self._mk_status), self.flags, stream)
+        self._launch_step_graph_kernels(stream)
 
     def check_status(self):
-        """Raise if a persistent step's grid barrier gave up (then re-arm its scratch)."""
-        if self.persistent:
-            st = int(self._mk_status[0])
-            if st:
-                self._mk_scratch.zero_()
-                self._mk_status.zero_()
-                what = "a grid barrier wait timed out" if st & 1 else "a position or token is out of range"
-                raise RuntimeError(f"persistent decode step: {what}")
+        """The step's kernels have no device-side waits to report on (kept for callers
+        that check every engine after a step)."""
 
     def _launch_step_graph_kernels(self, stream: int):
         """The step as a chain of kernels: per layer QKV GEMV (RMSNorm fused for
@@ -264,14 +244,20 @@ class LlamaDecodeEngine:
                      B, None, fg | _lib.IRON_FLAG_SWIGLU, stream)
             call("iron_gemv_int4g32", p(lay["d"].packed), p(self.act), p(self.x), E, s.hidden_dim, B,
                  p(self.h), fg, stream)
+        amax = None if self.sampling is not None else p(self.amax)
         if self.fuse_norm == "all":
             call("iron_gemv_int4g32_ex", p(self.lm.packed), p(self.x), p(self.logits), s.vocab_size, E, B, None,
-                 p(self.nf), s.eps, p(self.amax), fg, stream)
+                 p(self.nf), s.eps, amax, fg, stream)
         else:
             call("iron_rmsnorm", p(self.x), None, None, p(self.nf), p(self.xn), B, E, s.eps, f, stream)
             call("iron_gemv_int4g32_ex", p(self.lm.packed), p(self.xn), p(self.logits), s.vocab_size, E, B, None,
-                 None, 0.0, p(self.amax), fg, stream)
-        call("iron_argmax_finalize", p(self.amax), p(self.tokens), p(self.pos), B, f, stream)
+                 None, 0.0, amax, fg, stream)
+        if self.sampling is None:
+            call("iron_argmax_finalize", p(self.amax), p(self.tokens), p(self.pos), B, f, stream)
+        else:
+            sp = self.sampling
+            call("iron_sample_topk", p(self.logits), B, s.vocab_size, sp.temperature, sp.top_k, sp.seed,
+                 p(self.tokens), p(self.pos), f, stream)
         if self.l2_prefetch:
             join = torch.cuda.Event()
             join.record(self._side)
@@ -333,8 +319,14 @@ class LlamaDecodeEngine:
         call("iron_rmsnorm", p(last), None, None, p(self.nf), p(xn1), 1, E, s.eps, f, stream)
         call("iron_gemv_int4g32", p(self.lm.packed), p(xn1), p(self.logits[seq : seq + 1]), s.vocab_size, E, 1,
              None, f, stream)
-        call("iron_argmax", p(self.logits[seq : seq + 1]), p(self.tokens[seq : seq + 1]), 1, s.vocab_size, None,
-             f, stream)
+        if self.sampling is None:
+            call("iron_argmax", p(self.logits[seq : seq + 1]), p(self.tokens[seq : seq + 1]), 1, s.vocab_size,
+                 None, f, stream)
+        else:  # the draw for the prompt's last position S - 1 (the word is advanced, then dropped)
+            self._pf_draw_pos = torch.full((1,), S - 1, dtype=torch.int32, device=self.dev)
+            sp = self.sampling
+            call("iron_sample_topk", p(self.logits[seq : seq + 1]), 1, s.vocab_size, sp.temperature, sp.top_k,
+                 sp.seed, p(self.tokens[seq : seq + 1]), p(self._pf_draw_pos), f, stream)
 
     def prefill(self, tokens, seq: int = 0):
         """Run a prompt through the model for sequence `seq`: fills its KV cache at
@@ -359,8 +351,6 @@ class LlamaDecodeEngine:
         return s.n_layers * (gemm + attn)
 
     def kernels_per_step(self) -> int:
-        if self.persistent:
-            return 1
         attn = _lib.load().iron_attn_decode_kernels(self.B, self.s.n_heads, self.s.n_kv_groups, self.L)
         per_layer = ((4 if self.fuse_norm != "none" else 6) + attn + (0 if self.fuse_rope else 1)
                      + (2 if self.l2_prefetch else 0))

@@ -133,7 +133,8 @@ class Tensor:
     its range is uploaded by the next ``to("npu")``. Ranges that kernels wrote
     (``mark_device_written``, done by the sequence callables after a run) are
     downloaded before the host view is handed out, so host reads never see
-    stale data and a host write never clobbers newer device data.
+    stale data and a host write never clobbers newer device data; ``to("cpu")``
+    likewise keeps host-written ranges that have not been uploaded yet.
     """
 
     _host_only = False
@@ -216,9 +217,18 @@ class Tensor:
                 dev[s:e].copy_(st.host[s:e], non_blocking=False)
             self.device = "npu"
         elif where == "cpu":
+            # refresh the host copy from HBM, except the ranges written on the host since
+            # the last upload: those are newer and stay for the next to("npu") (IRON's
+            # decode pass writes x and the angles, then calls input_buffer.to("cpu"),
+            # then runs: llama_npu.py:1177-1188)
             if st.allocated:
-                self._bytes(st.host).copy_(self._bytes(st.dev), non_blocking=False)
-            st.host_dirty.take(*self._range)
+                s0, e0 = self._range
+                cur = s0
+                for a, b in [iv for iv in st.host_dirty.iv if iv[1] > s0 and iv[0] < e0] + [(e0, e0)]:
+                    a, b = max(a, s0), min(b, e0)
+                    if a > cur:
+                        st.host[cur:a].copy_(st.dev[cur:a], non_blocking=False)
+                    cur = max(cur, b)
             st.dev_dirty.take(*self._range)
             self.device = "cpu"
         else:

@@ -1,9 +1,8 @@
-// mbarrier + bulk-copy (TMA engine, non-tensor) helpers with bounded waits.
+// mbarrier helpers with bounded waits.
 //
 // Every wait spins a bounded number of times; on exhaustion it returns false and
 // the caller records IRON_ERR_TIMEOUT in the error word and leaves. A wait never
-// runs forever. Every bulk copy here reads this
-// GPU's global memory into the issuing CTA's own shared memory.
+// runs forever.
 #pragma once
 
 #include "common.cuh"
@@ -52,16 +51,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
     if (done) return true;
   }
   return false;
-}
-
-// Bulk global -> shared copy of `bytes` (multiple of 16, both addresses 16-byte
-// aligned), completing transaction bytes on `bar`.
-__device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, uint32_t bytes,
-                                         uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-      ::"r"(smem_addr(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_addr(bar))
-      : "memory");
 }
 
 // Named barrier among `threads` threads (id 1..15; id 0 is __syncthreads).

@@ -1,4 +1,4 @@
-// int4 group-32 weight helpers shared by the GEMV and the persistent decode kernel:
+// int4 group-32 weight helpers of the GEMV kernels:
 // exact dequantization of a signed nibble pair to bf16x2 (bf16(q * s), the value
 // IRON's Dequant produces) and the byte-permute / LOP3 primitives it uses.
 #pragma once

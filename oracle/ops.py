@@ -184,6 +184,20 @@ def attn_decode(q, k_cache, v_cache, lens):
     return out
 
 
+def sample_probs(logits: torch.Tensor, temperature: float, top_k: int | None) -> torch.Tensor:
+    """Next-token probabilities of IRON's generate_token
+    (iron/applications/llama_3.2_1b/llama_inference_harness.py:146-169): logits /
+    temperature (when > 0), then every logit below the top_k-th largest set to -inf
+    (ties kept), then softmax; fp64 here. logits [B, V] -> probabilities [B, V]."""
+    lf = logits.double()
+    if temperature > 0:
+        lf = lf / temperature
+    if top_k is not None and 0 < top_k < lf.shape[-1]:
+        kth = torch.topk(lf, top_k, dim=-1).values[..., -1:]
+        lf = torch.where(lf < kth, torch.tensor(float("-inf"), dtype=lf.dtype), lf)
+    return torch.softmax(lf, dim=-1)
+
+
 # ---- Llama pieces ------------------------------------------------------------
 def rope_angles(head_dim: int, context_length: int, base: float = 500000.0) -> torch.Tensor:
     """Interleaved cos/sin table (iron/applications/llama_3.2_1b/llama_inference_harness.py:109-123)."""

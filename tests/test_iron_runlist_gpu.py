@@ -1,0 +1,254 @@
+"""IRON's own Llama decode pipeline, run on these operators without other changes.
+
+The decode runlist below is built exactly as IRON builds it
+(iron/applications/llama_3.2_1b/llama_npu.py:280-447 constructs the operators,
+:459-557 the runlist, :559-584 the OperatorSequence, :588-642 binds the weights) --
+the same constructors and arguments, the same buffer names and slices, the batched
+scores / context GEMVs (num_batches = n_heads), Repeat x4 of the caches, one Transpose
+per head, the scale multiply and the runtime-length Softmax -- with
+`iron_b200.operators` in place of `iron.operators`. It is then driven the way
+`llama_forward_pass_decode` drives it (:1156-1195): `params.write("cache_offset")`,
+`params.write("softmax_vector_size")`, `params.sync()`, the `rope_angles` and `x`
+buffer writes, `input_buffer.to("cpu")`, the call, and the `logits` read-back.
+
+Reduced to 2 layers, vocab 4096 and a 256-token context (the largest reduction whose
+operator shapes IRON's own divisibility rules accept); every layer dimension is
+Llama-3.2-1B's. Checks, over 5 consecutive positions:
+  - fused (CUDA graph), separate and compare dispatch agree bitwise;
+  - logits against the oracle's decode step (oracle.llama.model_decode on the same
+    bf16 weights, caches and bf16 angle table) at rtol 2e-2 / atol 1e-2 and IRON's
+    decode KL bound (iron/applications/llama_3.2_1b/test.py:77-97).
+"""
+
+import math
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_close
+from oracle import llama as ollama
+from oracle import ops as oops
+
+pytestmark = pytest.mark.gpu
+
+from iron_b200.common.sequence import CompareDispatch, OperatorSequence
+from iron_b200.operators import (GEMV, ElementwiseAdd, ElementwiseMul, Repeat, RMSNorm, RoPE, SiLU, Softmax,
+                                 StridedCopy, Transpose)
+
+CFG = SimpleNamespace(n_layers=2, vocab_size=4096, emb_dim=2048, n_heads=32, n_kv_groups=8, head_dim=64,
+                      hidden_dim=8192)
+PROMPT_LEN = 256  # the decode runlist's maximum context (IRON's prompt_len)
+POSITIONS = [200, 201, 202, 203, 204]
+
+
+def build_decode_sequence(config, prompt_len, dispatch):
+    """llama_npu.py:280-584, operator for operator."""
+    gemv_attn_query_op = GEMV(M=config.n_heads * config.head_dim, K=config.emb_dim, num_aie_columns=8,
+                              tile_size_input=4, tile_size_output=config.head_dim // 2)
+    gemv_attn_key_value_op = GEMV(M=config.n_kv_groups * config.head_dim, K=config.emb_dim, num_aie_columns=8,
+                                  tile_size_input=4, tile_size_output=config.head_dim // 2)
+    rope_queries_op = RoPE(rows=config.n_heads, cols=config.head_dim, angle_rows=1)
+    rope_keys_op = RoPE(rows=config.n_kv_groups, cols=config.head_dim, angle_rows=1)
+    strided_copy_cache_op = StridedCopy(
+        input_sizes=(config.n_kv_groups, config.head_dim), input_strides=(config.head_dim, 1), input_offset=0,
+        output_sizes=(1, config.n_kv_groups, config.head_dim), output_strides=(0, prompt_len * config.head_dim, 1),
+        output_offset=0, input_buffer_size=1 * config.n_kv_groups * config.head_dim,
+        output_buffer_size=config.n_kv_groups * prompt_len * config.head_dim, num_aie_channels=1,
+        output_offset_parameter="cache_offset")
+    gemv_attn_scores_op = GEMV(M=prompt_len, K=config.head_dim, num_aie_columns=8, tile_size_input=4,
+                               tile_size_output=prompt_len // 8, num_batches=config.n_heads)
+    attn_scale_op = ElementwiseMul(size=config.n_heads * prompt_len, tile_size=prompt_len // 8, num_aie_columns=8)
+    softmax_op = Softmax(rows=config.n_heads, cols=prompt_len, num_aie_columns=1, num_channels=1,
+                         rtp_vector_size=prompt_len, vector_size_parameter="softmax_vector_size")
+    transpose_values_op = Transpose(M=prompt_len, N=config.head_dim, num_aie_columns=2, num_channels=1, m=256,
+                                    n=32, s=8)
+    gemv_attn_context_op = GEMV(M=config.head_dim, K=prompt_len, num_aie_columns=8, tile_size_input=4,
+                                tile_size_output=4, num_batches=config.n_heads)
+    gemv_attn_output_op = GEMV(M=config.emb_dim, K=config.n_heads * config.head_dim, num_aie_columns=8,
+                               tile_size_input=4, tile_size_output=config.emb_dim // 8)
+    rms_norm_op = RMSNorm(size=config.emb_dim, num_aie_columns=1, num_channels=1, tile_size=config.emb_dim,
+                          weighted=True)
+    gemv_ffn_up_gate_op = GEMV(M=config.hidden_dim, K=config.emb_dim, num_aie_columns=8, tile_size_input=4,
+                               tile_size_output=config.hidden_dim // 8)
+    gemv_ffn_down_op = GEMV(M=config.emb_dim, K=config.hidden_dim, num_aie_columns=8, tile_size_input=1,
+                            tile_size_output=config.emb_dim // 8)
+    silu_ffn_op = SiLU(size=config.hidden_dim, tile_size=config.hidden_dim // 8, num_aie_columns=8)
+    eltwise_mul_ffn_op = ElementwiseMul(size=config.hidden_dim, tile_size=config.hidden_dim // 8, num_aie_columns=8)
+    residual_add_op = ElementwiseAdd(size=config.emb_dim, tile_size=config.emb_dim // 8)
+    repeat_interleave_op = Repeat(rows=config.n_kv_groups, cols=prompt_len * config.head_dim,
+                                  repeat=config.n_heads // config.n_kv_groups, transfer_size=config.head_dim)
+    gemv_out_head_op = GEMV(M=config.vocab_size, K=config.emb_dim, num_aie_columns=8, tile_size_input=4,
+                            tile_size_output=32)
+
+    cache_buffer_size = config.n_kv_groups * prompt_len * config.head_dim * 2
+    values_per_head_buffer_size = prompt_len * config.head_dim * 2
+    values_buffer_size = config.n_heads * values_per_head_buffer_size
+    vp = values_per_head_buffer_size
+
+    runlist = []
+    for i in range(config.n_layers):
+        runlist.extend(
+            [(rms_norm_op, "x", f"W_norm1_{i}", "x_norm"),
+             (gemv_attn_query_op, f"W_attn_query_{i}", "x_norm", "queries"),
+             (gemv_attn_key_value_op, f"W_attn_key_{i}", "x_norm", "keys"),
+             (gemv_attn_key_value_op, f"W_attn_value_{i}", "x_norm", "values"),
+             (rope_queries_op, "queries", "rope_angles", "queries"),
+             (rope_keys_op, "keys", "rope_angles", "keys"),
+             (strided_copy_cache_op, "keys", f"keys_cache_{i}"),
+             (strided_copy_cache_op, "values", f"values_cache_{i}"),
+             (repeat_interleave_op, f"keys_cache_{i}", "attn_scores_keys"),
+             (repeat_interleave_op, f"values_cache_{i}", "attn_scores_values"),
+             (gemv_attn_scores_op, "attn_scores_keys", "queries", "attn_scores"),
+             (attn_scale_op, "attn_scores", "attn_scale_factor", "attn_scores"),
+             (softmax_op, "attn_scores", "attn_weights")]
+            + [(transpose_values_op, f"attn_scores_values[{h * vp}:{(h + 1) * vp}]",
+                f"attn_scores_values_transposed[{h * vp}:{(h + 1) * vp}]") for h in range(config.n_heads)]
+            + [(gemv_attn_context_op, "attn_scores_values_transposed", "attn_weights", "attn_context"),
+               (gemv_attn_output_op, f"W_attn_output_decode_{i}", "attn_context", "attn_output"),
+               (residual_add_op, "x", "attn_output", "x"),
+               (rms_norm_op, "x", f"W_norm2_{i}", "x_norm"),
+               (gemv_ffn_up_gate_op, f"W_ffn_gate_{i}", "x_norm", "ffn_gate"),
+               (gemv_ffn_up_gate_op, f"W_ffn_up_{i}", "x_norm", "ffn_up"),
+               (silu_ffn_op, "ffn_gate", "ffn_gate"),
+               (eltwise_mul_ffn_op, "ffn_gate", "ffn_up", "ffn_hidden"),
+               (gemv_ffn_down_op, f"W_ffn_down_{i}", "ffn_hidden", "ffn_output"),
+               (residual_add_op, "x", "ffn_output", "x")])
+    runlist += [(rms_norm_op, "x", "W_final_norm", "x"), (gemv_out_head_op, "W_out_head", "x", "logits")]
+    return OperatorSequence(
+        "fused_op", runlist, input_args=["x", "rope_angles"], output_args=["logits"],
+        buffer_sizes={**{f"keys_cache_{i}": cache_buffer_size for i in range(config.n_layers)},
+                      **{f"values_cache_{i}": cache_buffer_size for i in range(config.n_layers)},
+                      "attn_scores_values": values_buffer_size,
+                      "attn_scores_values_transposed": values_buffer_size},
+        dispatch=dispatch).compile()
+
+
+def _weights(config, seed=0):
+    """Random bf16 weights under IRON's HF names (llama_npu.py:588-639)."""
+    g = torch.Generator().manual_seed(seed)
+    E, H, D = config.emb_dim, config.hidden_dim, config.head_dim
+
+    def w(o, i, std=0.02):
+        return (torch.randn(o, i, generator=g) * std).to(torch.bfloat16)
+
+    W = {}
+    for i in range(config.n_layers):
+        p = f"model.layers.{i}."
+        W[p + "input_layernorm.weight"] = (1 + 0.02 * torch.randn(E, generator=g)).to(torch.bfloat16)
+        W[p + "post_attention_layernorm.weight"] = (1 + 0.02 * torch.randn(E, generator=g)).to(torch.bfloat16)
+        W[p + "self_attn.q_proj.weight"] = w(config.n_heads * D, E)
+        W[p + "self_attn.k_proj.weight"] = w(config.n_kv_groups * D, E)
+        W[p + "self_attn.v_proj.weight"] = w(config.n_kv_groups * D, E)
+        W[p + "self_attn.o_proj.weight"] = w(E, config.n_heads * D)
+        W[p + "mlp.gate_proj.weight"] = w(H, E)
+        W[p + "mlp.up_proj.weight"] = w(H, E)
+        W[p + "mlp.down_proj.weight"] = w(E, H)
+    W["model.norm.weight"] = (1 + 0.02 * torch.randn(E, generator=g)).to(torch.bfloat16)
+    W["model.embed_tokens.weight"] = w(config.vocab_size, E, 0.5)
+    return W
+
+
+def _bind_weights(fused, config, W, caches):
+    """llama_npu.py:588-642: weights into their buffers, the scale factor, the head."""
+    for i in range(config.n_layers):
+        p = f"model.layers.{i}."
+        names = {f"W_norm1_{i}": "input_layernorm", f"W_attn_query_{i}": "self_attn.q_proj",
+                 f"W_attn_key_{i}": "self_attn.k_proj", f"W_attn_value_{i}": "self_attn.v_proj",
+                 f"W_attn_output_decode_{i}": "self_attn.o_proj", f"W_norm2_{i}": "post_attention_layernorm",
+                 f"W_ffn_gate_{i}": "mlp.gate_proj", f"W_ffn_up_{i}": "mlp.up_proj",
+                 f"W_ffn_down_{i}": "mlp.down_proj"}
+        for buf, hf in names.items():
+            fused.get_buffer(buf).torch_view()[:] = W[p + hf + ".weight"].flatten()
+        # the prompt's KV cache (what IRON's prefill leaves there)
+        fused.get_buffer(f"keys_cache_{i}").torch_view()[:] = caches[0][i].flatten()
+        fused.get_buffer(f"values_cache_{i}").torch_view()[:] = caches[1][i].flatten()
+    fused.get_buffer("attn_scale_factor").fill_(1.0 / math.sqrt(config.head_dim))
+    fused.get_buffer("W_final_norm").torch_view()[:] = W["model.norm.weight"].flatten()
+    fused.get_buffer("W_out_head").torch_view()[:] = W["model.embed_tokens.weight"].flatten()
+    if hasattr(fused, "input_buffer"):  # the arenas of the fused callable, which llama_npu.py uses
+        fused.input_buffer.to("npu")
+        fused.scratch_buffer.to("npu")
+        fused.output_buffer.to("npu")
+
+
+def _decode_pass(fused, config, angles, W, token, num_preceding_tokens):
+    """llama_forward_pass_decode (llama_npu.py:1156-1195) for one token."""
+    context_len = num_preceding_tokens + 1
+    cache_offset = num_preceding_tokens * config.head_dim
+    params = fused.params
+    params.write("cache_offset", np.int32(cache_offset))
+    params.write("softmax_vector_size", np.int32(context_len))
+    params.sync()
+    fused.get_buffer("rope_angles").torch_view()[:] = angles[num_preceding_tokens:num_preceding_tokens + 1].flatten()
+    x = torch.nn.functional.embedding(torch.tensor([[token]]), W["model.embed_tokens.weight"])
+    fused.get_buffer("x").torch_view().view(-1, config.emb_dim)[:1, :] = x[0]
+    if hasattr(fused, "input_buffer"):  # per-buffer callables (separate, compare) have no arenas
+        fused.input_buffer.to("cpu")
+    fused()
+    return fused.get_buffer("logits").to_torch().view(1, 1, config.vocab_size).clone()
+
+
+def _run(dispatch, W, caches, angles, tokens):
+    if dispatch == "compare":  # report, do not raise: see the check of the step statistics below
+        dispatch = CompareDispatch(raise_on_mismatch=False)
+    seq = build_decode_sequence(CFG, PROMPT_LEN, dispatch)
+    fused = seq.get_callable()
+    _bind_weights(fused, CFG, W, caches)
+    out, stats = [], []
+    for t, p in zip(tokens, POSITIONS):
+        out.append(_decode_pass(fused, CFG, angles, W, t, p))
+        stats.append(list(getattr(fused, "last_step_stats", [])))
+    return out, stats
+
+
+def test_iron_decode_runlist_runs_as_written():
+    W = _weights(CFG, seed=3)
+    g = torch.Generator().manual_seed(4)
+    shape = (CFG.n_layers, CFG.n_kv_groups, PROMPT_LEN, CFG.head_dim)
+    kc = torch.randn(shape, generator=g).to(torch.bfloat16)
+    vc = torch.randn(shape, generator=g).to(torch.bfloat16)
+    kc[:, :, POSITIONS[0]:] = 0  # slots past the prompt: never written yet
+    vc[:, :, POSITIONS[0]:] = 0
+    angles = oops.rope_angles(CFG.head_dim, PROMPT_LEN).to(torch.bfloat16)  # bf16 like IRON's rope_angles buffer
+    tokens = [17, 4000, 5, 123, 2048]
+
+    runs, stats = {}, {}
+    for d in ("fused", "separate", "compare"):
+        runs[d], stats[d] = _run(d, W, (kc, vc), angles, tokens)
+    for d in ("separate", "compare"):
+        for t, (a, b) in enumerate(zip(runs["fused"], runs[d])):
+            assert torch.equal(a, b), f"{d} differs from fused at step {t}"
+    # compare mode held every step to its operator's reference(): all agree except the
+    # two whose IRON goldens ignore the runtime parameters -- the cache StridedCopy (the
+    # golden scatters into a zero buffer, not at cache_offset) and the masked Softmax
+    # (the golden softmaxes the whole row: iron/operators/softmax/op.py:88-97)
+    per_pos = stats["compare"]
+    assert all(len(s) == len(per_pos[0]) > 100 for s in per_pos)
+    bad = {st["op"] for s in per_pos for st in s if st["mismatch"]}
+    assert bad <= {"StridedCopy", "Softmax"}, bad
+
+    # the oracle's decode step on the same weights, caches and angles
+    E, D = CFG.emb_dim, CFG.head_dim
+    layers = []
+    for i in range(CFG.n_layers):
+        p = f"model.layers.{i}."
+        layers.append({"n1": W[p + "input_layernorm.weight"], "n2": W[p + "post_attention_layernorm.weight"],
+                       "q": W[p + "self_attn.q_proj.weight"], "k": W[p + "self_attn.k_proj.weight"],
+                       "v": W[p + "self_attn.v_proj.weight"], "o": W[p + "self_attn.o_proj.weight"],
+                       "g": W[p + "mlp.gate_proj.weight"], "u": W[p + "mlp.up_proj.weight"],
+                       "d": W[p + "mlp.down_proj.weight"]})
+    kcs = [kc[i][None].clone() for i in range(CFG.n_layers)]
+    vcs = [vc[i][None].clone() for i in range(CFG.n_layers)]
+    emb = W["model.embed_tokens.weight"]
+    for t, (tok, pos) in enumerate(zip(tokens, POSITIONS)):
+        ref = ollama.model_decode([tok], [pos], layers, W["model.norm.weight"], emb, emb, kcs, vcs, angles,
+                                  CFG.n_heads, CFG.n_kv_groups, D)
+        got = runs["fused"][t].view(1, -1)
+        d = (got.float() - ref.float()).abs()
+        print(f"position {pos}: max |diff| {float(d.max()):.3g}")
+        assert_close(got, ref, 2e-2, 1e-2, what=f"logits at position {pos}")
+        lp = torch.log_softmax(ref.float(), -1)
+        kl = float((lp.exp() * (lp - torch.log_softmax(got.float(), -1))).sum())
+        assert kl <= 0.05, kl

@@ -32,20 +32,17 @@ def _oracle_weights(eng):
     return out
 
 
-@pytest.mark.parametrize("persistent,fuse", [(False, None), (True, None), (False, ("layers", True)),
-                                             (False, ("none", False))])
+@pytest.mark.parametrize("fuse", [None, ("layers", True), ("none", False)])
 @pytest.mark.parametrize("batch,prefix", [(1, [9]), (2, [63, 65]), (3, [0, 5, 40]),
                                           (8, [1, 2, 3, 63, 64, 65, 100, 127]),
                                           (12, [0, 1, 2, 3, 5, 8, 13, 21, 34, 55, 89, 144])])
-def test_decode_step_matches_oracle(batch, prefix, persistent, fuse):
-    if persistent and batch > 2:
-        pytest.skip("the persistent step serves batch <= 2")
+def test_decode_step_matches_oracle(batch, prefix, fuse):
     if fuse and fuse[0] != "none" and batch > 8:
         pytest.skip("the fused RMSNorm prologue serves batch <= 8")
     shape = LlamaShape(n_layers=2, vocab_size=4096)
     L = 160
     kw = dict(fuse_norm=fuse[0], fuse_rope=fuse[1]) if fuse else {}
-    eng = LlamaDecodeEngine(shape, batch, L, seed=7, keep_natural=True, persistent=persistent, **kw)
+    eng = LlamaDecodeEngine(shape, batch, L, seed=7, keep_natural=True, **kw)
     g = torch.Generator(device="cuda").manual_seed(1)
     eng.kc.copy_(torch.randn(eng.kc.shape, generator=g, device="cuda").to(torch.bfloat16))
     eng.vc.copy_(torch.randn(eng.vc.shape, generator=g, device="cuda").to(torch.bfloat16))
@@ -61,11 +58,12 @@ def test_decode_step_matches_oracle(batch, prefix, persistent, fuse):
     logits = ollama.model_decode(toks, prefix, W, eng.nf.cpu(), eng.embed_table.cpu(),
                                  eng.lm.dequant().cpu(), kcs, vcs, eng.lut.cpu(), shape.n_heads,
                                  shape.n_kv_groups, shape.head_dim)
-    # two random-init layers amplify rounding differences between the fused and the
-    # reference composition: up to 3 % of the logits may fall outside 2e-2 (a few ulp),
-    # and the distributions must agree (KL, the app-level check of
-    # iron/applications/llama_3.2_1b/test.py:77-113)
-    assert_close(eng.logits.cpu(), logits, 2e-2, 2e-2, max_mismatch_frac=3e-2, what="logits")
+    # every logit within the north star's bar, and the distributions agree (KL, the
+    # app-level check of iron/applications/llama_3.2_1b/test.py:77-113)
+    d = (eng.logits.cpu().float() - logits.float()).abs()
+    bad = d >= torch.maximum(torch.full_like(d, 1e-2), 2e-2 * (eng.logits.cpu().float().abs() + logits.float().abs()))
+    print(f"batch {batch} {fuse}: outside 2e-2 / 1e-2: {int(bad.sum())}/{bad.numel()}, max |diff| {float(d.max()):.3g}")
+    assert_close(eng.logits.cpu(), logits, 2e-2, 1e-2, what="logits")
     lp = torch.log_softmax(logits.float(), -1)
     kl = (lp.exp() * (lp - torch.log_softmax(eng.logits.cpu().float(), -1))).sum(-1)
     assert float(kl.max()) < 1e-3, kl
@@ -82,12 +80,11 @@ def test_decode_step_matches_oracle(batch, prefix, persistent, fuse):
     assert torch.all(got.gather(1, top[:, None])[:, 0] == got.max(1).values)
 
 
-@pytest.mark.parametrize("persistent", [False, True])
-def test_graph_replay_matches_eager_steps(persistent):
+def test_graph_replay_matches_eager_steps():
     shape = LlamaShape(n_layers=2, vocab_size=4096)
     runs = []
     for use_graph in (False, True):
-        eng = LlamaDecodeEngine(shape, 2, 64, seed=3, persistent=persistent)
+        eng = LlamaDecodeEngine(shape, 2, 64, seed=3)
         eng.set_state([11, 12], [4, 9])
         if use_graph:
             eng.capture()
@@ -135,31 +132,6 @@ def test_prefill_matches_oracle_then_decodes(S):
     lg2 = ollama.model_decode([0, nxt], [0, S], W, eng.nf.cpu(), eng.embed_table.cpu(), lm, kcs2, vcs2,
                               eng.lut.cpu(), shape.n_heads, shape.n_kv_groups, shape.head_dim)
     assert_close(eng.logits[1:2].cpu(), lg2[1:2], 3e-2, 3e-2, what="decode after prefill")
-
-
-def test_persistent_step_matches_kernel_chain_full_model():
-    """The single-kernel step against the 148-kernel graph on the full 16-layer model:
-    same weights, same state, several chained steps (tokens fed back)."""
-    shape = LlamaShape()
-    outs = []
-    for persistent in (False, True):
-        eng = LlamaDecodeEngine(shape, 2, 96, seed=21, persistent=persistent)
-        g = torch.Generator(device="cuda").manual_seed(4)
-        eng.kc[:, :, :, :64].normal_(generator=g)
-        eng.vc[:, :, :, :64].normal_(generator=g)
-        eng.set_state([17, 4242], [64, 31])
-        eng.capture()
-        logits = []
-        for _ in range(4):
-            eng.step()
-            logits.append(eng.logits.clone())
-        torch.cuda.synchronize()
-        eng.check_status()
-        outs.append((eng.tokens.cpu(), eng.pos.cpu(), logits, eng.kc[:, :, :, :70].cpu()))
-    (t0, p0, l0, k0), (t1, p1, l1, k1) = outs
-    assert p0.tolist() == p1.tolist() == [68, 35]
-    assert_close(l1[0].cpu(), l0[0].cpu(), 2e-2, 2e-2, what="first-step logits")
-    assert_close(k1, k0, 2e-2, 2e-2, max_mismatch_frac=1e-3, what="caches")
 
 
 @pytest.mark.parametrize("n_vec", [1, 3, 8])

