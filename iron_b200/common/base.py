@@ -144,6 +144,11 @@ class MLIROperator(AIEOperatorBase):
         def call(*bufs):
             self._check_buffers(bufs)
             self._launch(*bufs, stream=_lib.current_stream())
+            # the kernel rewrote its outputs in HBM: their device copies are now the
+            # authoritative ones (a later to("cpu") / to_torch() pulls them)
+            for b, spec in zip(bufs, self.get_arg_spec()):
+                if spec.direction in ("out", "inout") and hasattr(b, "mark_device_written"):
+                    b.mark_device_written()
 
         return call
 

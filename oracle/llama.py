@@ -10,6 +10,8 @@ golden (llama_cpu run in fp32) is the accuracy reference.
 
 from __future__ import annotations
 
+import math
+
 import torch
 
 from . import ops
@@ -44,6 +46,46 @@ def block_decode(x, k_cache, v_cache, pos, W, angles, n_heads, n_kv, head_dim, e
     hn = ops.rms_norm(h, W["n2"], eps)
     act = ops.swiglu_act(ops.gemv_multi(W["g"], hn), ops.gemv_multi(W["u"], hn))
     return ops.add(h, ops.gemv_multi(W["d"], act))
+
+
+def block_decode_runlist(x, k_cache, v_cache, pos, W, angles, n_heads, n_kv, head_dim, eps=1e-5):
+    """One decode step of one block for ONE sequence, rounded to bf16 at the operator
+    boundaries of IRON's fused decode runlist
+    (iron/applications/llama_3.2_1b/llama_npu.py:459-557): the scores GEMV, the scale
+    multiply, the masked Softmax and the context GEMV each round their output, and SiLU
+    rounds before the ElementwiseMul. x [1, E]; caches [n_kv, Lmax, hd] (row pos written).
+    Each step is the operator's own golden (gemv, mul, softmax with its mask, silu, add).
+    """
+    xn = ops.rms_norm(x, W["n1"], eps)
+    q = ops.gemv_multi(W["q"], xn).view(n_heads, head_dim)
+    k = ops.gemv_multi(W["k"], xn).view(n_kv, head_dim)
+    v = ops.gemv_multi(W["v"], xn).view(n_kv, head_dim)
+    ang = angles[pos : pos + 1]
+    q, k = ops.rope(q, ang), ops.rope(k, ang)
+    k_cache[:, pos] = k
+    v_cache[:, pos] = v
+    g = n_heads // n_kv
+    K = ops.repeat_interleave(k_cache, g)                       # Repeat
+    V = ops.repeat_interleave(v_cache, g)
+    scores = ops.gemv(K, q)                                     # batched GEMV, [h, Lmax]
+    scale = torch.full_like(scores, 1.0 / math.sqrt(head_dim))
+    scores = ops.mul(scores, scale)                             # ElementwiseMul by the scale buffer
+    w = ops.softmax(scores, pos + 1)                            # Softmax masked past the context
+    ctx = ops.gemv(ops.transpose(V), w).reshape(1, n_heads * head_dim)  # Transpose + batched GEMV
+    h = ops.add(x, ops.gemv_multi(W["o"], ctx))
+    hn = ops.rms_norm(h, W["n2"], eps)
+    act = ops.mul(ops.silu(ops.gemv_multi(W["g"], hn)), ops.gemv_multi(W["u"], hn))
+    return ops.add(h, ops.gemv_multi(W["d"], act))
+
+
+def model_decode_runlist(token, pos, layers, nf, embed, lm, k_caches, v_caches, angles, n_heads, n_kv,
+                         head_dim, eps=1e-5):
+    """IRON's decode runlist for one token (block_decode_runlist per layer, then the
+    final RMSNorm and the head GEMV). Caches [n_kv, Lmax, hd] per layer. Returns [1, V]."""
+    x = embed[int(token)][None].clone()
+    for li, W in enumerate(layers):
+        x = block_decode_runlist(x, k_caches[li], v_caches[li], int(pos), W, angles, n_heads, n_kv, head_dim, eps)
+    return ops.gemv_multi(lm, ops.rms_norm(x, nf, eps))
 
 
 def block_mlp_half(x, k_cache, v_cache, pos, W, angles, n_heads, n_kv, head_dim, eps=1e-5):

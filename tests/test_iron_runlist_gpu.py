@@ -15,9 +15,16 @@ Reduced to 2 layers, vocab 4096 and a 256-token context (the largest reduction w
 operator shapes IRON's own divisibility rules accept); every layer dimension is
 Llama-3.2-1B's. Checks, over 5 consecutive positions:
   - fused (CUDA graph), separate and compare dispatch agree bitwise;
-  - logits against the oracle's decode step (oracle.llama.model_decode on the same
-    bf16 weights, caches and bf16 angle table) at rtol 2e-2 / atol 1e-2 and IRON's
-    decode KL bound (iron/applications/llama_3.2_1b/test.py:77-97).
+  - logits against the runlist restated on the CPU (oracle.llama.model_decode_runlist:
+    every step the operator's own golden, rounded to bf16 where the runlist's operators
+    write their buffers) at rtol 2e-2 / atol 1e-2;
+  - the next-token distribution against the Llama CPU decode step
+    (oracle.llama.model_decode, llama_cpu.py's math with one rounding per attention)
+    within IRON's decode KL bound (iron/applications/llama_3.2_1b/test.py:77-97). The
+    runlist rounds the scores, the scaled scores, the softmax and the context to bf16
+    on the way, so its logits differ from that single-rounding form by more than the
+    elementwise bar (hundreds of the 4096 logits, on the CPU alone), which is
+    why IRON's own app-level check is a KL bound.
 """
 
 import math
@@ -146,7 +153,7 @@ def _weights(config, seed=0):
         W[p + "mlp.up_proj.weight"] = w(H, E)
         W[p + "mlp.down_proj.weight"] = w(E, H)
     W["model.norm.weight"] = (1 + 0.02 * torch.randn(E, generator=g)).to(torch.bfloat16)
-    W["model.embed_tokens.weight"] = w(config.vocab_size, E, 0.5)
+    W["model.embed_tokens.weight"] = w(config.vocab_size, E)
     return W
 
 
@@ -241,14 +248,19 @@ def test_iron_decode_runlist_runs_as_written():
                        "d": W[p + "mlp.down_proj.weight"]})
     kcs = [kc[i][None].clone() for i in range(CFG.n_layers)]
     vcs = [vc[i][None].clone() for i in range(CFG.n_layers)]
+    kcr = [kc[i].clone() for i in range(CFG.n_layers)]
+    vcr = [vc[i].clone() for i in range(CFG.n_layers)]
     emb = W["model.embed_tokens.weight"]
+    nf = W["model.norm.weight"]
     for t, (tok, pos) in enumerate(zip(tokens, POSITIONS)):
-        ref = ollama.model_decode([tok], [pos], layers, W["model.norm.weight"], emb, emb, kcs, vcs, angles,
-                                  CFG.n_heads, CFG.n_kv_groups, D)
+        ref_chain = ollama.model_decode_runlist(tok, pos, layers, nf, emb, emb, kcr, vcr, angles, CFG.n_heads,
+                                                CFG.n_kv_groups, D)
+        ref = ollama.model_decode([tok], [pos], layers, nf, emb, emb, kcs, vcs, angles, CFG.n_heads,
+                                  CFG.n_kv_groups, D)
         got = runs["fused"][t].view(1, -1)
-        d = (got.float() - ref.float()).abs()
-        print(f"position {pos}: max |diff| {float(d.max()):.3g}")
-        assert_close(got, ref, 2e-2, 1e-2, what=f"logits at position {pos}")
+        d = (got.float() - ref_chain.float()).abs()
         lp = torch.log_softmax(ref.float(), -1)
         kl = float((lp.exp() * (lp - torch.log_softmax(got.float(), -1))).sum())
+        print(f"position {pos}: max |diff| to the runlist oracle {float(d.max()):.3g}, KL to llama_cpu {kl:.3g}")
+        assert_close(got, ref_chain, 2e-2, 1e-2, what=f"logits at position {pos}")
         assert kl <= 0.05, kl

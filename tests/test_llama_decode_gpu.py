@@ -62,7 +62,9 @@ def test_decode_step_matches_oracle(batch, prefix, fuse):
     # app-level check of iron/applications/llama_3.2_1b/test.py:77-113)
     d = (eng.logits.cpu().float() - logits.float()).abs()
     bad = d >= torch.maximum(torch.full_like(d, 1e-2), 2e-2 * (eng.logits.cpu().float().abs() + logits.float().abs()))
-    print(f"batch {batch} {fuse}: outside 2e-2 / 1e-2: {int(bad.sum())}/{bad.numel()}, max |diff| {float(d.max()):.3g}")
+    print(f"batch {batch} {fuse}: outside 2e-2 / 1e-2: {int(bad.sum())}/{bad.numel()}, max |diff| {float(d.max()):.3g}; "
+          f"per sequence (pos, outside, max |diff|): "
+          f"{[(p, int(bad[b].sum()), round(float(d[b].max()), 4)) for b, p in enumerate(prefix)]}")
     assert_close(eng.logits.cpu(), logits, 2e-2, 1e-2, what="logits")
     lp = torch.log_softmax(logits.float(), -1)
     kl = (lp.exp() * (lp - torch.log_softmax(eng.logits.cpu().float(), -1))).sum(-1)
