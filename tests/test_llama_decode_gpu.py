@@ -58,14 +58,37 @@ def test_decode_step_matches_oracle(batch, prefix, fuse):
     logits = ollama.model_decode(toks, prefix, W, eng.nf.cpu(), eng.embed_table.cpu(),
                                  eng.lm.dequant().cpu(), kcs, vcs, eng.lut.cpu(), shape.n_heads,
                                  shape.n_kv_groups, shape.head_dim)
-    # every logit within the north star's bar, and the distributions agree (KL, the
-    # app-level check of iron/applications/llama_3.2_1b/test.py:77-113)
+    # 1. The last layer's attention and the lm-head recomputed by the oracle on the
+    # engine's OWN inputs (its QKV projection and caches; its final hidden state): every
+    # output within the north star's bar, no exceptions -- the kernels' parity, free of
+    # the chain's amplification.
+    from oracle import ops
+    Hq, Hd = shape.n_heads, shape.head_dim
+    lut = eng.lut.cpu()
+    q_raw = eng.qkv.cpu()[:, :Hq * Hd].reshape(batch, Hq, Hd)
+    q_rot = torch.stack([ops.rope(q_raw[b], lut[p:p + 1]) for b, p in enumerate(prefix)])
+    att = ops.attn_decode(q_rot, eng.kc[-1].cpu(), eng.vc[-1].cpu(), [p + 1 for p in prefix])
+    assert_close(eng.attn.cpu().reshape(batch, Hq, Hd), att, 2e-2, 1e-2, what="attention on the engine's inputs")
+    lm = eng.lm.dequant().cpu()
+    head = ops.gemv_multi(lm, ops.rms_norm(eng.x.cpu(), eng.nf.cpu(), shape.eps))
+    assert_close(eng.logits.cpu(), head, 2e-2, 1e-2, what="lm-head on the engine's hidden state")
+    # 2. End to end against the oracle's own chain. Two random-init layers can amplify
+    # one-ulp differences (fp32 sums in other orders) far past the bar for some inputs;
+    # measured on B200 at batch 8, all in two sequences: at position 63 the hidden state
+    # after layer 1 is a near-cancellation (RMS 0.25 against ~40 for the others), so a
+    # 0.016 difference is 6 % of it and 555 of that sequence's 4096 logits fell outside
+    # 2e-2 / 1e-2 (1.7 % of the batch's); at position 65 the new token takes 63-93 % of
+    # every head's attention weight with scores near 6, so its attention output moved by
+    # up to 0.10 while the attention kernel matched the oracle to 0.008 on its own
+    # inputs. Hence: at most 2 % of the batch's logits outside, and the distributions
+    # within KL 1e-3 (IRON's app-level check is a KL bound:
+    # iron/applications/llama_3.2_1b/test.py:77-113).
     d = (eng.logits.cpu().float() - logits.float()).abs()
     bad = d >= torch.maximum(torch.full_like(d, 1e-2), 2e-2 * (eng.logits.cpu().float().abs() + logits.float().abs()))
     print(f"batch {batch} {fuse}: outside 2e-2 / 1e-2: {int(bad.sum())}/{bad.numel()}, max |diff| {float(d.max()):.3g}; "
           f"per sequence (pos, outside, max |diff|): "
           f"{[(p, int(bad[b].sum()), round(float(d[b].max()), 4)) for b, p in enumerate(prefix)]}")
-    assert_close(eng.logits.cpu(), logits, 2e-2, 1e-2, what="logits")
+    assert_close(eng.logits.cpu(), logits, 2e-2, 1e-2, max_mismatch_frac=2e-2, what="logits")
     lp = torch.log_softmax(logits.float(), -1)
     kl = (lp.exp() * (lp - torch.log_softmax(eng.logits.cpu().float(), -1))).sum(-1)
     assert float(kl.max()) < 1e-3, kl
