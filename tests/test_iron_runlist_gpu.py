@@ -206,11 +206,14 @@ def _run(dispatch, W, caches, angles, tokens):
     seq = build_decode_sequence(CFG, PROMPT_LEN, dispatch)
     fused = seq.get_callable()
     _bind_weights(fused, CFG, W, caches)
-    out, stats = [], []
+    out, stats, caches_before = [], [], []
     for t, p in zip(tokens, POSITIONS):
+        caches_before.append([(fused.get_buffer(f"keys_cache_{i}").to_torch().view(CFG.n_kv_groups, PROMPT_LEN, -1),
+                               fused.get_buffer(f"values_cache_{i}").to_torch().view(CFG.n_kv_groups, PROMPT_LEN, -1))
+                              for i in range(CFG.n_layers)])
         out.append(_decode_pass(fused, CFG, angles, W, t, p))
         stats.append(list(getattr(fused, "last_step_stats", [])))
-    return out, stats
+    return out, stats, caches_before
 
 
 def test_iron_decode_runlist_runs_as_written():
@@ -224,9 +227,9 @@ def test_iron_decode_runlist_runs_as_written():
     angles = oops.rope_angles(CFG.head_dim, PROMPT_LEN).to(torch.bfloat16)  # bf16 like IRON's rope_angles buffer
     tokens = [17, 4000, 5, 123, 2048]
 
-    runs, stats = {}, {}
+    runs, stats, before = {}, {}, {}
     for d in ("fused", "separate", "compare"):
-        runs[d], stats[d] = _run(d, W, (kc, vc), angles, tokens)
+        runs[d], stats[d], before[d] = _run(d, W, (kc, vc), angles, tokens)
     for d in ("separate", "compare"):
         for t, (a, b) in enumerate(zip(runs["fused"], runs[d])):
             assert torch.equal(a, b), f"{d} differs from fused at step {t}"
@@ -249,15 +252,17 @@ def test_iron_decode_runlist_runs_as_written():
                        "v": W[p + "self_attn.v_proj.weight"], "o": W[p + "self_attn.o_proj.weight"],
                        "g": W[p + "mlp.gate_proj.weight"], "u": W[p + "mlp.up_proj.weight"],
                        "d": W[p + "mlp.down_proj.weight"]})
-    kcs = [kc[i][None].clone() for i in range(CFG.n_layers)]
-    vcs = [vc[i][None].clone() for i in range(CFG.n_layers)]
-    kcr = [kc[i].clone() for i in range(CFG.n_layers)]
-    vcr = [vc[i].clone() for i in range(CFG.n_layers)]
     emb = W["model.embed_tokens.weight"]
     nf = W["model.norm.weight"]
     for t, (tok, pos) in enumerate(zip(tokens, POSITIONS)):
+        # each position from the caches the runlist held before it (teacher-forced state:
+        # one step's deviation, not the drift of the CPU's own earlier rows)
+        kcr = [before["fused"][t][i][0].clone() for i in range(CFG.n_layers)]
+        vcr = [before["fused"][t][i][1].clone() for i in range(CFG.n_layers)]
         ref_chain = ollama.model_decode_runlist(tok, pos, layers, nf, emb, emb, kcr, vcr, angles, CFG.n_heads,
                                                 CFG.n_kv_groups, D)
+        kcs = [before["fused"][t][i][0][None].clone() for i in range(CFG.n_layers)]
+        vcs = [before["fused"][t][i][1][None].clone() for i in range(CFG.n_layers)]
         ref = ollama.model_decode([tok], [pos], layers, nf, emb, emb, kcs, vcs, angles, CFG.n_heads,
                                   CFG.n_kv_groups, D)
         got = runs["fused"][t].view(1, -1)
