@@ -254,50 +254,85 @@ __device__ __forceinline__ void s4_store(const float (&v)[NT][4], int tile, int 
   }
 }
 
+// m16n8k16 bf16 MMA of one 32-k group into fresh accumulators: D = A * B (C = 0).
+__device__ __forceinline__ void mma_bf16_16816_zc(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  const float z = 0.f;
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(z));
+}
+
+// One 16-row x 128-k unit against the activations. The B fragments are x's 16-byte
+// loads as they sit in memory (this lane's 8 consecutive k of a group); lanes of vectors
+// past n_vec read the last vector (their columns are never stored), so no load is
+// predicated. Up to 8 vectors (NT == 1) the codes become the exact integers q as bf16x2
+// pairs (s4x2_int_: LOP3 magic number + one exact subtract), two MMAs give each 32-k
+// group's integer dot products sum_k q x in fp32 and the group scale multiplies them in
+// fp32 (acc += s * D): 6 instructions per group for the scales against 10 for scaling
+// every weight pair. Wider tiles (NT >= 2) scale the pairs instead (s4x2_dequant_: the
+// exact bf16(q * s) of IRON's Dequant), which costs the same for any NT, and feed the
+// MMAs' accumulators directly.
 template <int NT, bool kShared = false, bool kRO = false>
-__device__ __forceinline__ void s4_unit_gx(float (&d)[2][NT][4], const uint4 &clo, const uint4 &chi,
+__device__ __forceinline__ void s4_unit_gx(float (&acc)[NT][4], const uint4 &clo, const uint4 &chi,
                                            const uint4 &sc, const uint16_t *__restrict__ x, int K,
                                            int n_vec, int kbase, int ldx = -1, int xoff = 0) {
   const int lane = threadIdx.x & 31, gid = lane >> 2, tid = lane & 3;
   const uint32_t wl[4] = {clo.x, clo.y, clo.z, clo.w};
   const uint32_t wh[4] = {chi.x, chi.y, chi.z, chi.w};
   const uint32_t sl2[2] = {sc.x, sc.y}, sh2[2] = {sc.z, sc.w};
-  uint4 xr[4][NT];
+  auto xload = [&](int j, int t) -> uint4 {
+    const int vv = min(t * 8 + gid, n_vec - 1);
+    if constexpr (kShared) {
+      return *reinterpret_cast<const uint4 *>(x + vv * ldx + kbase - xoff + tid * 8 + j * 32);
+    } else {
+      const uint16_t *px = x + static_cast<int64_t>(vv) * K + kbase + tid * 8 + j * 32;
+      if constexpr (kRO) return __ldg(reinterpret_cast<const uint4 *>(px));
+      else return ld_act_v4(px);
+    }
+  };
+  if constexpr (NT == 1) {
+    uint4 xr[4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < 4; ++j) xr[j] = xload(j, 0);
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      const int vv = t * 8 + gid;
-      xr[j][t] = make_uint4(0u, 0u, 0u, 0u);
-      if (vv < n_vec) {
-        if constexpr (kShared)
-          xr[j][t] = *reinterpret_cast<const uint4 *>(x + vv * ldx + kbase - xoff + j * 32 + tid * 8);
-        else
-        {
-          const uint16_t *px = x + static_cast<int64_t>(vv) * K + kbase + j * 32 + tid * 8;
-          if constexpr (kRO) xr[j][t] = __ldg(reinterpret_cast<const uint4 *>(px));
-          else xr[j][t] = ld_act_v4(px);
-        }
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t A0[4] = {s4x2_int_(wl[j]), s4x2_int_(wh[j]), s4x2_int_(wl[j] >> 4), s4x2_int_(wh[j] >> 4)};
+      const uint32_t A1[4] = {s4x2_int_(wl[j] >> 8), s4x2_int_(wh[j] >> 8), s4x2_int_(wl[j] >> 12),
+                              s4x2_int_(wh[j] >> 12)};
+      const float s_lo = (j & 1) ? bf16_hi(sl2[j >> 1]) : bf16_lo(sl2[j >> 1]);  // row gid, group j
+      const float s_hi = (j & 1) ? bf16_hi(sh2[j >> 1]) : bf16_lo(sh2[j >> 1]);  // row gid + 8
+      float d[4];
+      mma_bf16_16816_zc(d, A0, xr[j].x, xr[j].y);  // k (0,1) / (2,3) of this lane's 8
+      mma_bf16_16816(d, A1, xr[j].z, xr[j].w);     // k (4,5) / (6,7)
+      acc[0][0] = fmaf(s_lo, d[0], acc[0][0]);
+      acc[0][1] = fmaf(s_lo, d[1], acc[0][1]);
+      acc[0][2] = fmaf(s_hi, d[2], acc[0][2]);
+      acc[0][3] = fmaf(s_hi, d[3], acc[0][3]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 xr[NT];
+#pragma unroll
+      for (int t = 0; t < NT; ++t) xr[t] = xload(j, t);
+      const uint32_t sel = (j & 1) ? 0x3232u : 0x1010u;
+      const uint32_t s2_lo = prmt_(sl2[j >> 1], sl2[j >> 1], sel);
+      const uint32_t s2_hi = prmt_(sh2[j >> 1], sh2[j >> 1], sel);
+      uint32_t pl[4], ph[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        pl[q] = s4x2_dequant_(wl[j] >> (4 * q), s2_lo);
+        ph[q] = s4x2_dequant_(wh[j] >> (4 * q), s2_hi);
       }
-    }
+      const uint32_t A0[4] = {pl[0], ph[0], pl[1], ph[1]};
+      const uint32_t A1[4] = {pl[2], ph[2], pl[3], ph[3]};
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t sel = (j & 1) ? 0x3232u : 0x1010u;
-    const uint32_t s2_lo = prmt_(sl2[j >> 1], sl2[j >> 1], sel);
-    const uint32_t s2_hi = prmt_(sh2[j >> 1], sh2[j >> 1], sel);
-    uint32_t pl[4], ph[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      pl[q] = s4x2_dequant_(wl[j] >> (4 * q), s2_lo);
-      ph[q] = s4x2_dequant_(wh[j] >> (4 * q), s2_hi);
-    }
-    const uint32_t A0[4] = {pl[0], ph[0], pl[1], ph[1]};
-    const uint32_t A1[4] = {pl[2], ph[2], pl[3], ph[3]};
-#pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      const uint4 e = xr[j][t];
-      mma_bf16_16816(d[j & 1][t], A0, e.x, e.y);  // k (0,1) / (2,3) of this lane's 8
-      mma_bf16_16816(d[j & 1][t], A1, e.z, e.w);  // k (4,5) / (6,7)
+      for (int t = 0; t < NT; ++t) {
+        mma_bf16_16816(acc[t], A0, xr[t].x, xr[t].y);
+        mma_bf16_16816(acc[t], A1, xr[t].z, xr[t].w);
+      }
     }
   }
 }
@@ -313,10 +348,11 @@ __device__ __forceinline__ void s4_unit_gx(float (&d)[2][NT][4], const uint4 &cl
 template <int NT>
 constexpr int s4_warps() { return NT <= 2 ? 8 : 4; }
 // CTAs per SM the register budget must allow: single-tile (<= 8 vector) kernels keep
-// four 8-warp CTAs per SM (<= 64 registers a thread); above that the occupancy cliff
-// (3 CTAs per SM) put config 2's 512 CTAs into two waves: 5.8 against 3.5 us per launch.
+// four 8-warp CTAs per SM (<= 64 registers a thread; at 66 registers the occupancy cliff
+// to 3 CTAs per SM put config 2's 512 CTAs into two waves: 5.8 against 3.5 us per
+// launch), 16-vector tiles three.
 template <int NT, bool kNorm>
-constexpr int s4_min_ctas() { return (NT == 1 && !kNorm) ? 4 : 1; }
+constexpr int s4_min_ctas() { return (NT == 1 && !kNorm) ? 4 : NT == 2 ? 3 : 1; }
 template <int NT>
 constexpr int s4_units() { return NT <= 2 ? 2 : 4; }
 
@@ -339,11 +375,9 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
   const S4Range kr = s4_split(0, cpt, CS * kT4Warps, rank * kT4Warps + warp);  // my chunks
   const uint8_t *base = packed + (static_cast<int64_t>(tile) * cpt) * kS4UnitBytes;
 
-  float acc[2][NT][4];
+  float acc[NT][4];
 #pragma unroll
-  for (int a = 0; a < 2; ++a)
-#pragma unroll
-    for (int t = 0; t < NT; ++t) acc[a][t][0] = acc[a][t][1] = acc[a][t][2] = acc[a][t][3] = 0.f;
+  for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
 
   uint4 lo[kT4Units], hi[kT4Units], sc[kT4Units];
   auto load = [&](int c0) {
@@ -442,7 +476,7 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
 #pragma unroll
   for (int t = 0; t < NT; ++t)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) red[((warp * NT + t) * 4 + e) * 32 + lane] = acc[0][t][e] + acc[1][t][e];
+    for (int e = 0; e < 4; ++e) red[((warp * NT + t) * 4 + e) * 32 + lane] = acc[t][e];
   __syncthreads();
   float v[NT][4];
   if (warp == 0) {
