@@ -480,7 +480,7 @@ def cpu_baseline(args, wl, budget_s=10.0):
         step()
         n += 1
     dt = (time.perf_counter() - t0) / n
-    return {"value": round(wl.bytes_per_step / dt / 1e9, 3), "unit": "GB/s", "cores": threads,
+    return {"value": float(f"{wl.bytes_per_step / dt / 1e9:.4g}"), "unit": "GB/s", "cores": threads,
             "kind": "port", "sample": f"{n} steps in {budget_s:.0f} s: {desc}",
             "ms_per_step": dt * 1e3}
 
@@ -501,7 +501,7 @@ def run_reference(args, world, rank):
     for _ in range(steps):
         step()
     dt = (time.perf_counter() - t0) / steps
-    value = round(wl.bytes_per_step / dt / 1e9, 3)
+    value = float(f"{wl.bytes_per_step / dt / 1e9:.4g}")  # 4 significant digits (a slow host stays > 0)
     line = {
         "impl": "reference",
         "metric": "int4 GEMV achieved HBM GB/s" if args.workload == "int4_gemv" else "bf16 GEMV achieved HBM GB/s",
@@ -799,7 +799,7 @@ def cpu_baseline_decode(B, budget_s=15.0):
         step()
         n += 1
     dt = (time.perf_counter() - t0) / n
-    return {"value": round(B / dt, 3), "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+    return {"value": float(f"{B / dt:.4g}"), "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
             "sample": f"{n} full decode steps (all {layers} layers + lm-head) of batch {B} at context {PREFIX}: "
                       f"llama_cpu.py restated in torch, bf16 weights", "s_per_step": round(dt, 4)}
 
@@ -821,7 +821,7 @@ def run_reference_decode(args, world, rank):
     for _ in range(steps):
         step()
     dt = (time.perf_counter() - t0) / steps
-    value = round(B / dt, 3)
+    value = float(f"{B / dt:.4g}")
     threads = torch.get_num_threads()
     sample = (f"{steps} decode steps (of {args.steps} requested) of batch {B} at context {PREFIX}, "
               f"all {layers} layers + lm-head, llama_cpu.py restated in torch on the bf16 values of "
@@ -1141,7 +1141,7 @@ def _cpu_block(B, pos, budget_s=10.0, steps=None):
         n += 1
     dt = (time.perf_counter() - t0) / n
     nbytes = 2 * sum(w.numel() for w in W.values()) + 2 * B * E * 2 + B * 2 * s.n_kv_groups * Hd * 2
-    return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+    return {"value": float(f"{nbytes / dt / 1e9:.4g}"), "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"{n} steps of the config-3 chain at batch {B}: the oracle's block_mlp_half "
                       f"(llama_cpu.py's pieces restated in torch, bf16 weights)", "ms_per_step": dt * 1e3}
 

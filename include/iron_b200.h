@@ -131,6 +131,39 @@ int iron_gemv_int4g32_ex(const uint8_t *packed, const uint16_t *x, uint16_t *y, 
 int iron_l2_prefetch(const void *ptr, size_t bytes, unsigned flags, void *stream);
 int iron_argmax_finalize(unsigned long long *keys, int32_t *tokens, int32_t *pos, int B, unsigned flags,
                          void *stream);
+/* iron_gemv_int4g32_chain (no reference counterpart as one call: it folds the weighted
+ * RMSNorm steps of IRON's decode runlist, iron/applications/llama_3.2_1b/llama_npu.py:
+ * 463-470 and :536, into the GEMVs around them). The int4 GEMV of iron_gemv_int4g32
+ * (n_vec <= 8) with the decode chain's extras, all optional (NULL / 0: off):
+ *   - residual [n_vec, N]: y = bf16(bf16(W x) + residual) (as iron_gemv_int4g32);
+ *   - ss_in [n_vec, K / 16] fp32 with eps (K 2048 or 4096): x holds bf16(h * w) for some
+ *     rows h whose per-16-element sums of squares are ss_in; the output is scaled by
+ *     inv = 1 / sqrt(sum(ss_in[v]) / K + eps) before rounding (and before SwiGLU), i.e.
+ *     y = W . rmsnorm(h) * w up to the rounding of x -- the RMSNorm without its kernel;
+ *   - ss_out [n_vec, N / 16], y_weighted [n_vec, N], weight [N] (all three or none): the
+ *     producer side -- y_weighted = bf16(y * weight) and the per-16-row sums of squares
+ *     of the stored y, the next chained GEMV's x and ss_in;
+ *   - argmax_keys [n_vec * 32]: the greedy argmax epilogue (as iron_gemv_int4g32_ex).
+ * IRON_FLAG_SWIGLU excludes residual, argmax and the producer side. The partial sums are
+ * combined in a fixed order, so results are bitwise reproducible. */
+typedef struct {
+  const uint16_t *residual;
+  const float *ss_in;
+  float eps;
+  float *ss_out;
+  uint16_t *y_weighted;
+  const uint16_t *weight;
+  unsigned long long *argmax_keys;
+} iron_gemv_chain;
+int iron_gemv_int4g32_chain(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K, int n_vec,
+                            const iron_gemv_chain *c, unsigned flags, void *stream);
+/* iron_embed_chain (no reference counterpart as one call: IRON embeds on the CPU,
+ * llama_npu.py:1177-1183, and normalises in the runlist): x[b] = table[tokens[b]] (a
+ * zero row for a token outside [0, V)), xw[b] = bf16(x[b] * weight) and ss[b, E / 16]
+ * the per-16-element sums of squares of x[b] -- the first layer's chained RMSNorm input
+ * for iron_gemv_int4g32_chain. E % 16 == 0. */
+int iron_embed_chain(const int32_t *tokens, const uint16_t *table, uint16_t *x, uint16_t *xw, const uint16_t *weight,
+                     float *ss, int B, int E, int V, unsigned flags, void *stream);
 /* iron_gemv_int4g32_allreduce (no reference counterpart as one call: it replaces a
  * row-parallel projection followed by the NCCL all-reduce of the tensor-parallel
  * block): the int4 GEMV of this rank's input columns (n_vec <= 8), whose output tiles

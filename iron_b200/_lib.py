@@ -64,6 +64,8 @@ SIGNATURES: dict[str, list] = {
     "iron_gemv_int4g32_ex": [P, P, P, c_int, c_int, c_int, P, P, c_float, P, c_uint, P],
     "iron_argmax_finalize": [P, P, P, c_int, c_uint, P],
     "iron_sample_topk": [P, c_int, c_int, c_float, c_int, c_uint64, P, P, c_uint, P],
+    "iron_gemv_int4g32_chain": [P, P, P, c_int, c_int, c_int, P, c_uint, P],
+    "iron_embed_chain": [P, P, P, P, P, P, c_int, c_int, c_int, c_uint, P],
     "iron_l2_prefetch": [P, c_size_t, c_uint, P],
     "iron_attn_decode_kernels": [c_int, c_int, c_int, c_int],
     "iron_gemv_int4g32_allreduce": [P, P, P, c_int, c_int, c_int, P, P, c_uint, P],
@@ -81,6 +83,14 @@ SIGNATURES: dict[str, list] = {
 _RESTYPES = {"iron_strerror": c_char_p, "iron_attn_decode_workspace_bytes": c_size_t,
              "iron_attn_decode_workspace_bytes_d": c_size_t,
              "iron_attn_decode_qkv_workspace_bytes": c_size_t}
+
+class GemvChain(ctypes.Structure):
+    """iron_gemv_chain (include/iron_b200.h): the decode-chain extras of
+    iron_gemv_int4g32_chain (pointers as ints, NULL = off)."""
+
+    _fields_ = [("residual", c_void_p), ("ss_in", c_void_p), ("eps", c_float), ("ss_out", c_void_p),
+                ("y_weighted", c_void_p), ("weight", c_void_p), ("argmax_keys", c_void_p)]
+
 
 _lock = threading.Lock()
 _lib = None

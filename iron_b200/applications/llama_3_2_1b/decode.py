@@ -159,15 +159,23 @@ class LlamaDecodeEngine:
         self.attn_ws = torch.zeros(max(wsb, 16), dtype=torch.uint8, device=dev)
         self.amax = torch.zeros(B * 32, dtype=torch.int64, device=dev)  # fused argmax key slots
         self.graph = None
-        # where RMSNorm runs inside the following GEMV ("none", "layers": the QKV and
-        # gate/up GEMVs, "all": also the lm-head); only for B <= 8. Defaults measured on
-        # B200 (one process, interleaved, 8-warp GEMV tiles): the fused prologue costs
-        # 63 us per step at B = 1 and 289 us at B = 8; RoPE inside attention (whose cached
-        # K / V rows are then requested before the wait for the QKV projection) saves
-        # 44 us at B = 1, 62 us at B = 8 and 305 us at B = 64.
-        self.fuse_norm = fuse_norm if fuse_norm is not None else "none"
+        # where the RMSNorms run: "chain" (B <= 8) folds them into the GEMVs around them
+        # (iron_gemv_int4g32_chain: the residual GEMVs write bf16(h * w) and per-16-row
+        # sums of squares, the next GEMV scales its output by 1 / rms -- no norm kernels);
+        # "none": RMSNorm kernels; "layers" / "all": RMSNorm recomputed in the QKV and
+        # gate/up (and lm-head) GEMVs' prologue. RoPE inside attention (whose cached K / V
+        # rows are then requested before the wait for the QKV projection) saves 44 us per
+        # step at B = 1, 62 us at B = 8 and 305 us at B = 64 (B200).
+        self.fuse_norm = fuse_norm if fuse_norm is not None else ("chain" if B <= 8 else "none")
+        if self.fuse_norm not in ("chain", "none", "layers", "all"):
+            raise ValueError(f"unknown fuse_norm {self.fuse_norm!r}")
         if self.fuse_norm != "none" and B > 8:
-            raise ValueError("the fused RMSNorm prologue serves B <= 8")
+            raise ValueError("the fused RMSNorm forms serve B <= 8")
+        if self.fuse_norm == "chain":
+            self.xw = torch.zeros(B, E, dtype=torch.bfloat16, device=dev)  # bf16(x * w) inputs
+            self.hw = torch.zeros(B, E, dtype=torch.bfloat16, device=dev)
+            self.ss_x = torch.zeros(B, E // 16, dtype=torch.float32, device=dev)  # their sums of squares
+            self.ss_h = torch.zeros(B, E // 16, dtype=torch.float32, device=dev)
         # RoPE + KV append inside the attention kernel (else the rope_kv_append kernel)
         self.fuse_rope = fuse_rope if fuse_rope is not None else True
         # each layer's gate/up and down weights requested into L2 on a side branch of
@@ -198,6 +206,8 @@ class LlamaDecodeEngine:
         residual, gate/up GEMV (RMSNorm fused) + SwiGLU, down GEMV + residual; then
         the lm-head GEMV with the final RMSNorm and the argmax fused, and the token
         update."""
+        if self.fuse_norm == "chain":
+            return self._launch_step_chain(stream)
         s, B, f = self.s, self.B, self.flags
         # the step keeps the PDL windows the read-only activation path needs (its o_proj
         # and down_proj GEMVs add residuals and so bound each layer's two windows)
@@ -262,6 +272,49 @@ class LlamaDecodeEngine:
             join = torch.cuda.Event()
             join.record(self._side)
             main.wait_event(join)
+
+    def _launch_step_chain(self, stream: int):
+        """The step with the RMSNorms folded into the GEMVs (5 kernels per layer at batch 1
+        and 2): the embedding gather writes x, bf16(x * n1) and x's sums of squares; per
+        layer the QKV GEMV scales by 1 / rms(x), attention (RoPE + append + splits), the O
+        GEMV adds the residual and writes h, bf16(h * n2) and h's sums of squares, the
+        gate/up GEMV scales by 1 / rms(h) before SwiGLU, the down GEMV adds the residual and
+        writes the next layer's inputs (with n1 of the next layer, or the final norm's
+        weights); the lm-head scales by 1 / rms and picks the token."""
+        s, B, f = self.s, self.B, self.flags
+        fg = f | _lib.IRON_FLAG_X_READONLY  # the windows hold as in _launch_step_graph_kernels
+        call, p = _lib.call, (lambda t: t.data_ptr())
+        E, Hd, L = s.emb_dim, s.head_dim, self.L
+        kv_b, kv_h = s.n_kv_groups * L * Hd, L * Hd
+        C = _lib.GemvChain
+
+        def chain(packed, x, y, N, K, c, flags):
+            call("iron_gemv_int4g32_chain", p(packed), p(x), p(y), N, K, B, ctypes.byref(c), flags, stream)
+
+        call("iron_embed_chain", p(self.tokens), p(self.embed_table), p(self.x), p(self.xw),
+             p(self.layers[0]["n1"]), p(self.ss_x), B, E, s.vocab_size, f, stream)
+        for li, lay in enumerate(self.layers):
+            kc, vc = self.kc[li], self.vc[li]
+            nxt = self.layers[li + 1]["n1"] if li + 1 < len(self.layers) else self.nf
+            chain(lay["qkv"].packed, self.xw, self.qkv, s.qkv_dim, E, C(ss_in=p(self.ss_x), eps=s.eps), fg)
+            call("iron_attn_decode_qkv", p(self.qkv), p(self.pos), p(self.lut), p(kc), p(vc), p(self.attn), B,
+                 s.n_heads, s.n_kv_groups, Hd, L, kv_b, kv_h, 1.0 / math.sqrt(Hd), p(self.attn_ws),
+                 self.attn_ws.numel(), f, stream)
+            chain(lay["o"].packed, self.attn, self.h, E, s.n_heads * Hd,
+                  C(residual=p(self.x), ss_out=p(self.ss_h), y_weighted=p(self.hw), weight=p(lay["n2"])), fg)
+            chain(lay["gu"].packed, self.hw, self.act, 2 * s.hidden_dim, E, C(ss_in=p(self.ss_h), eps=s.eps),
+                  fg | _lib.IRON_FLAG_SWIGLU)
+            chain(lay["d"].packed, self.act, self.x, E, s.hidden_dim,
+                  C(residual=p(self.h), ss_out=p(self.ss_x), y_weighted=p(self.xw), weight=p(nxt)), fg)
+        amax = p(self.amax) if self.sampling is None else None
+        chain(self.lm.packed, self.xw, self.logits, s.vocab_size, E,
+              C(ss_in=p(self.ss_x), eps=s.eps, argmax_keys=amax), fg)
+        if self.sampling is None:
+            call("iron_argmax_finalize", p(self.amax), p(self.tokens), p(self.pos), B, f, stream)
+        else:
+            sp = self.sampling
+            call("iron_sample_topk", p(self.logits), B, s.vocab_size, sp.temperature, sp.top_k, sp.seed,
+                 p(self.tokens), p(self.pos), f, stream)
 
     # -- prefill: a whole prompt through the tensor-core GEMMs -----------------------------
     def _prefill_buffers(self, S: int):
@@ -352,6 +405,8 @@ class LlamaDecodeEngine:
 
     def kernels_per_step(self) -> int:
         attn = _lib.load().iron_attn_decode_kernels(self.B, self.s.n_heads, self.s.n_kv_groups, self.L)
+        if self.fuse_norm == "chain":
+            return 1 + self.s.n_layers * (4 + attn) + 2
         per_layer = ((4 if self.fuse_norm != "none" else 6) + attn + (0 if self.fuse_rope else 1)
                      + (2 if self.l2_prefetch else 0))
         return 1 + self.s.n_layers * per_layer + (2 if self.fuse_norm == "all" else 3)

@@ -152,6 +152,16 @@ __device__ __forceinline__ T ld_act(const T *p) {
   return r;
 }
 
+// Asynchronous 16-byte global -> shared copy (both addresses 16-byte aligned), L2 only;
+// completes for the issuing thread at cp_async_wait_all() after cp_async_commit().
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // 16-byte streaming load that bypasses L1 allocation (weights are read once).
 __device__ __forceinline__ uint4 ld_stream_v4(const void *p) {
   uint4 r;

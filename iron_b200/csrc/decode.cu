@@ -67,6 +67,39 @@ __global__ void embed_kernel(const int *__restrict__ tokens, const uint4 *__rest
     x[static_cast<int64_t>(b) * row_vecs + i] = ok ? table[t * row_vecs + i] : make_uint4(0u, 0u, 0u, 0u);
 }
 
+// The embedding gather plus the first layer's chained RMSNorm input: xw = bf16(x * w)
+// and per 16 elements the sum of squares of x (two threads' 8 elements each, summed
+// through one shuffle: a fixed order).
+__global__ void embed_chain_kernel(const int *__restrict__ tokens, const uint4 *__restrict__ table,
+                                   uint4 *__restrict__ x, uint4 *__restrict__ xw, const uint4 *__restrict__ w,
+                                   float *__restrict__ ss, int row_vecs, int V) {
+  pdl_wait();  // as embed_kernel: the step's first kernel waits for the previous step
+  pdl_launch_dependents();
+  const int b = blockIdx.x;
+  const int64_t t = ld_act_i32(tokens + b);
+  const bool ok = t >= 0 && t < V;
+  for (int i0 = 0; i0 < row_vecs; i0 += blockDim.x) {  // uniform trip count (the shuffle)
+    const int i = i0 + threadIdx.x;
+    float q = 0.f;
+    if (i < row_vecs) {
+      const uint4 r = ok ? table[t * row_vecs + i] : make_uint4(0u, 0u, 0u, 0u);
+      const uint4 wv = __ldg(w + i);
+      x[static_cast<int64_t>(b) * row_vecs + i] = r;
+      const uint32_t a[4] = {r.x, r.y, r.z, r.w}, c[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float lo = bf16_lo(a[k]), hi = bf16_hi(a[k]);
+        q += lo * lo + hi * hi;
+        o[k] = pack_bf16x2(lo * bf16_lo(c[k]), hi * bf16_hi(c[k]));
+      }
+      xw[static_cast<int64_t>(b) * row_vecs + i] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    q += __shfl_xor_sync(0xffffffffu, q, 1);
+    if (i < row_vecs && (i & 1) == 0) ss[static_cast<int64_t>(b) * (row_vecs / 2) + i / 2] = q;
+  }
+}
+
 // First index of the maximum of each row (NaN never wins).
 __global__ void argmax_kernel(const uint16_t *__restrict__ logits, int *__restrict__ out, int V,
                               int *__restrict__ pos) {
@@ -144,6 +177,19 @@ extern "C" int iron_embed(const int32_t *tokens, const uint16_t *table, uint16_t
   return launch(embed_kernel, dim3(B), dim3(256), 0, static_cast<cudaStream_t>(stream),
                 (flags & IRON_FLAG_PDL) != 0, tokens, reinterpret_cast<const uint4 *>(table),
                 reinterpret_cast<uint4 *>(x), E / 8, V);
+}
+
+extern "C" int iron_embed_chain(const int32_t *tokens, const uint16_t *table, uint16_t *x, uint16_t *xw,
+                                const uint16_t *weight, float *ss, int B, int E, int V, unsigned flags,
+                                void *stream) {
+  if (!tokens || !table || !x || !xw || !weight || !ss) return IRON_ERR_NULL;
+  if (B <= 0 || E <= 0 || V <= 0 || B > 65535) return IRON_ERR_SHAPE;
+  if (E % 16) return IRON_ERR_SHAPE;
+  if (!aligned16(table) || !aligned16(x) || !aligned16(xw) || !aligned16(weight)) return IRON_ERR_ALIGN;
+  return launch(embed_chain_kernel, dim3(B), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                (flags & IRON_FLAG_PDL) != 0, tokens, reinterpret_cast<const uint4 *>(table),
+                reinterpret_cast<uint4 *>(x), reinterpret_cast<uint4 *>(xw), reinterpret_cast<const uint4 *>(weight),
+                ss, E / 8, V);
 }
 
 extern "C" int iron_argmax(const uint16_t *logits, int32_t *out, int B, int V, int32_t *pos,

@@ -65,6 +65,11 @@ struct S4Epi {
   unsigned long long *amax;
   S4AllReduce ar;  // ar.world > 1: all-reduce the output over the ranks first
   int x_ro;        // IRON_FLAG_X_READONLY: x through the read-only path, else L2-coherent loads
+  // RMSNorm folded into the decode chain (single-tile kernels, n_vec <= 8):
+  const float *ss_in;    // [n_vec, K/16] partial sums of squares of the unweighted input rows
+  float *ss_out;         // [n_vec, N/16] partial sums of squares of y (per 16-row tile)
+  uint16_t *yw;          // [n_vec, N] bf16(y * yw_w): the next GEMV's input
+  const uint16_t *yw_w;  // [N] the next RMSNorm's weights
 };
 
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
@@ -190,10 +195,15 @@ struct S4Residual {
   }
 };
 
+// The chain writer (yw != null): y2 = bf16(y * w[row]) into yw and, per vector, the sum
+// of squares of the tile's 16 stored (bf16) y values into ss_out[v, tile] -- summed over
+// the rows in a fixed order (shuffles), so the RMSNorm scale built from them downstream
+// is bitwise reproducible. w_lo / w_hi: w of rows gid / gid + 8.
 template <int NT>
 __device__ __forceinline__ void s4_store(const float (&v)[NT][4], int tile, int N, int n_vec,
                                          uint16_t *__restrict__ y, const float *res_s, int swiglu,
-                                         unsigned long long *amax = nullptr) {
+                                         unsigned long long *amax = nullptr, uint16_t *yw = nullptr,
+                                         float *ss_out = nullptr, float w_lo = 0.f, float w_hi = 0.f) {
   const int lane = threadIdx.x & 31, gid = lane >> 2, tid = lane & 3;
   const int row0 = tile * 16;
   if (swiglu) {
@@ -215,6 +225,7 @@ __device__ __forceinline__ void s4_store(const float (&v)[NT][4], int tile, int 
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
     unsigned long long best[2] = {0ull, 0ull};  // per vector 2tid + (e & 1)
+    float sq[2] = {0.f, 0.f};                   // per vector 2tid + (e & 1): chain writer
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int row = row0 + gid + ((e >> 1) << 3);
@@ -227,11 +238,28 @@ __device__ __forceinline__ void s4_store(const float (&v)[NT][4], int tile, int 
         if (res_s) r = __bfloat162float(__float2bfloat16_rn(r)) + res_s[vv * 16 + (row - row0)];
         const uint16_t yb = float_to_bf16_bits(r);
         y[o] = yb;
+        if (yw) {
+          const float yf = bf16_bits_to_float(yb);
+          yw[o] = float_to_bf16_bits(yf * ((e >> 1) ? w_hi : w_lo));
+          sq[e & 1] += yf * yf;
+        }
         if (amax) {
           const unsigned long long k = s4_argmax_key(bf16_bits_to_float(yb), row);
           best[e & 1] = k > best[e & 1] ? k : best[e & 1];
         }
       }
+    }
+    if (yw) {
+#pragma unroll
+      for (int q = 0; q < 2; ++q)
+#pragma unroll
+        for (int x = 4; x <= 16; x <<= 1) sq[q] += __shfl_xor_sync(0xffffffffu, sq[q], x);
+      if (gid == 0)
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const int vv = t * 8 + tid * 2 + q;
+          if (vv < n_vec) ss_out[static_cast<int64_t>(vv) * (N / 16) + tile] = sq[q];
+        }
     }
     if (amax) {
       // best (value, then lowest row) of the tile's 16 rows per vector: reduce over the
@@ -254,85 +282,61 @@ __device__ __forceinline__ void s4_store(const float (&v)[NT][4], int tile, int 
   }
 }
 
-// m16n8k16 bf16 MMA of one 32-k group into fresh accumulators: D = A * B (C = 0).
-__device__ __forceinline__ void mma_bf16_16816_zc(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  const float z = 0.f;
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
-      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(z));
-}
-
-// One 16-row x 128-k unit against the activations. The B fragments are x's 16-byte
-// loads as they sit in memory (this lane's 8 consecutive k of a group); lanes of vectors
-// past n_vec read the last vector (their columns are never stored), so no load is
-// predicated. Up to 8 vectors (NT == 1) the codes become the exact integers q as bf16x2
-// pairs (s4x2_int_: LOP3 magic number + one exact subtract), two MMAs give each 32-k
-// group's integer dot products sum_k q x in fp32 and the group scale multiplies them in
-// fp32 (acc += s * D): 6 instructions per group for the scales against 10 for scaling
-// every weight pair. Wider tiles (NT >= 2) scale the pairs instead (s4x2_dequant_: the
-// exact bf16(q * s) of IRON's Dequant), which costs the same for any NT, and feed the
-// MMAs' accumulators directly.
+// One 16-row x 128-k unit against the activations: per 32-k group the codes become the
+// exact dequantized weights bf16(q * s) -- IRON's Dequant values -- as bf16x2 pairs (LOP3
+// magic number, exact subtract, one rounding multiply by the group scale) and two MMAs
+// accumulate them against x in fp32. The B fragments are x's 16-byte loads as they sit
+// in memory (this lane's 8 consecutive k of a group); lanes of vectors past n_vec read
+// the last vector (their columns are never stored), so up to 8 vectors no load is
+// predicated. (Applying
+// the group scale to the MMA's fp32 group sums instead measured no faster on B200 and
+// would change the results from IRON's dequantize-then-GEMV by up to ~1e-2.)
 template <int NT, bool kShared = false, bool kRO = false>
-__device__ __forceinline__ void s4_unit_gx(float (&acc)[NT][4], const uint4 &clo, const uint4 &chi,
+__device__ __forceinline__ void s4_unit_gx(float (&acc)[2][NT][4], const uint4 &clo, const uint4 &chi,
                                            const uint4 &sc, const uint16_t *__restrict__ x, int K,
                                            int n_vec, int kbase, int ldx = -1, int xoff = 0) {
   const int lane = threadIdx.x & 31, gid = lane >> 2, tid = lane & 3;
   const uint32_t wl[4] = {clo.x, clo.y, clo.z, clo.w};
   const uint32_t wh[4] = {chi.x, chi.y, chi.z, chi.w};
   const uint32_t sl2[2] = {sc.x, sc.y}, sh2[2] = {sc.z, sc.w};
-  auto xload = [&](int j, int t) -> uint4 {
-    const int vv = min(t * 8 + gid, n_vec - 1);
-    if constexpr (kShared) {
-      return *reinterpret_cast<const uint4 *>(x + vv * ldx + kbase - xoff + tid * 8 + j * 32);
-    } else {
-      const uint16_t *px = x + static_cast<int64_t>(vv) * K + kbase + tid * 8 + j * 32;
-      if constexpr (kRO) return __ldg(reinterpret_cast<const uint4 *>(px));
-      else return ld_act_v4(px);
-    }
-  };
-  if constexpr (NT == 1) {
-    uint4 xr[4];
+  uint4 xr[4][NT];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) xr[j] = xload(j, 0);
+  for (int j = 0; j < 4; ++j)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t A0[4] = {s4x2_int_(wl[j]), s4x2_int_(wh[j]), s4x2_int_(wl[j] >> 4), s4x2_int_(wh[j] >> 4)};
-      const uint32_t A1[4] = {s4x2_int_(wl[j] >> 8), s4x2_int_(wh[j] >> 8), s4x2_int_(wl[j] >> 12),
-                              s4x2_int_(wh[j] >> 12)};
-      const float s_lo = (j & 1) ? bf16_hi(sl2[j >> 1]) : bf16_lo(sl2[j >> 1]);  // row gid, group j
-      const float s_hi = (j & 1) ? bf16_hi(sh2[j >> 1]) : bf16_lo(sh2[j >> 1]);  // row gid + 8
-      float d[4];
-      mma_bf16_16816_zc(d, A0, xr[j].x, xr[j].y);  // k (0,1) / (2,3) of this lane's 8
-      mma_bf16_16816(d, A1, xr[j].z, xr[j].w);     // k (4,5) / (6,7)
-      acc[0][0] = fmaf(s_lo, d[0], acc[0][0]);
-      acc[0][1] = fmaf(s_lo, d[1], acc[0][1]);
-      acc[0][2] = fmaf(s_hi, d[2], acc[0][2]);
-      acc[0][3] = fmaf(s_hi, d[3], acc[0][3]);
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint4 xr[NT];
-#pragma unroll
-      for (int t = 0; t < NT; ++t) xr[t] = xload(j, t);
-      const uint32_t sel = (j & 1) ? 0x3232u : 0x1010u;
-      const uint32_t s2_lo = prmt_(sl2[j >> 1], sl2[j >> 1], sel);
-      const uint32_t s2_hi = prmt_(sh2[j >> 1], sh2[j >> 1], sel);
-      uint32_t pl[4], ph[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        pl[q] = s4x2_dequant_(wl[j] >> (4 * q), s2_lo);
-        ph[q] = s4x2_dequant_(wh[j] >> (4 * q), s2_hi);
+    for (int t = 0; t < NT; ++t) {
+      // single-tile form: every lane loads (lanes past n_vec the last vector); wider
+      // tiles predicate (their register budget has no room for the extra addresses)
+      const int vv = NT == 1 ? min(gid, n_vec - 1) : t * 8 + gid;
+      if (NT == 1 || vv < n_vec) {
+        if constexpr (kShared)
+          xr[j][t] = *reinterpret_cast<const uint4 *>(x + vv * ldx + kbase - xoff + j * 32 + tid * 8);
+        else {
+          const uint16_t *px = x + static_cast<int64_t>(vv) * K + kbase + j * 32 + tid * 8;
+          if constexpr (kRO) xr[j][t] = __ldg(reinterpret_cast<const uint4 *>(px));
+          else xr[j][t] = ld_act_v4(px);
+        }
+      } else {
+        xr[j][t] = make_uint4(0u, 0u, 0u, 0u);
       }
-      const uint32_t A0[4] = {pl[0], ph[0], pl[1], ph[1]};
-      const uint32_t A1[4] = {pl[2], ph[2], pl[3], ph[3]};
+    }
 #pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        mma_bf16_16816(acc[t], A0, xr[t].x, xr[t].y);
-        mma_bf16_16816(acc[t], A1, xr[t].z, xr[t].w);
-      }
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t sel = (j & 1) ? 0x3232u : 0x1010u;
+    const uint32_t s2_lo = prmt_(sl2[j >> 1], sl2[j >> 1], sel);
+    const uint32_t s2_hi = prmt_(sh2[j >> 1], sh2[j >> 1], sel);
+    uint32_t pl[4], ph[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      pl[q] = s4x2_dequant_(wl[j] >> (4 * q), s2_lo);
+      ph[q] = s4x2_dequant_(wh[j] >> (4 * q), s2_hi);
+    }
+    const uint32_t A0[4] = {pl[0], ph[0], pl[1], ph[1]};
+    const uint32_t A1[4] = {pl[2], ph[2], pl[3], ph[3]};
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const uint4 e = xr[j][t];
+      mma_bf16_16816(acc[j & 1][t], A0, e.x, e.y);  // k (0,1) / (2,3) of this lane's 8
+      mma_bf16_16816(acc[j & 1][t], A1, e.z, e.w);  // k (4,5) / (6,7)
     }
   }
 }
@@ -350,9 +354,9 @@ constexpr int s4_warps() { return NT <= 2 ? 8 : 4; }
 // CTAs per SM the register budget must allow: single-tile (<= 8 vector) kernels keep
 // four 8-warp CTAs per SM (<= 64 registers a thread; at 66 registers the occupancy cliff
 // to 3 CTAs per SM put config 2's 512 CTAs into two waves: 5.8 against 3.5 us per
-// launch), 16-vector tiles three.
+// launch); the wider tiles (and the fused-norm form) keep the compiler's own choice (0).
 template <int NT, bool kNorm>
-constexpr int s4_min_ctas() { return (NT == 1 && !kNorm) ? 4 : NT == 2 ? 3 : 1; }
+constexpr int s4_min_ctas() { return (NT == 1 && !kNorm) ? 4 : 0; }
 template <int NT>
 constexpr int s4_units() { return NT <= 2 ? 2 : 4; }
 
@@ -375,9 +379,11 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
   const S4Range kr = s4_split(0, cpt, CS * kT4Warps, rank * kT4Warps + warp);  // my chunks
   const uint8_t *base = packed + (static_cast<int64_t>(tile) * cpt) * kS4UnitBytes;
 
-  float acc[NT][4];
+  float acc[2][NT][4];  // two accumulator sets (even / odd groups): two independent MMA chains
 #pragma unroll
-  for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+  for (int a = 0; a < 2; ++a)
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc[a][t][0] = acc[a][t][1] = acc[a][t][2] = acc[a][t][3] = 0.f;
 
   uint4 lo[kT4Units], hi[kT4Units], sc[kT4Units];
   auto load = [&](int c0) {
@@ -404,12 +410,30 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
       if (k < klen) wreg[j] = __ldg(reinterpret_cast<const uint4 *>(epi.norm_w + kc0 + k));
     }
   }
+  // the chain's small inputs land in shared memory by asynchronous copies (no registers
+  // held across the main loop): the writer's RMSNorm weights of this tile's 16 rows
+  // (before the wait: they never depend on the previous kernel) and, after the wait,
+  // warp v's vector-v partial sums of squares (K / 16 floats)
+  __shared__ __align__(16) uint16_t w_s[16];
+  __shared__ __align__(16) float pss_s[NT == 1 ? 8 * 256 : 4];
+  if (NT == 1 && epi.yw && warp == 0 && rank == 0 && lane < 2) cp_async16(w_s + lane * 8, epi.yw_w + tile * 16 + lane * 8);
   // a GEMV that adds a residual (a decoder block's o_proj and down_proj) bounds a
   // window (see ld_act_v4): its dependents launch only after its wait
   const bool bound = epi.residual != nullptr;
   if (!bound) pdl_launch_dependents();
   pdl_wait();
   if (bound) pdl_launch_dependents();
+  // chain prologue: warp v requests vector v's partial sums of squares now and sums them
+  // after its units (K / 16 partials: K / 2048 16-byte pieces per lane)
+  __shared__ float inv_s[8];
+  const bool ss_warp = NT == 1 && epi.ss_in != nullptr && rank == 0 && warp < n_vec;
+  if (ss_warp) {
+    const float *ps = epi.ss_in + static_cast<int64_t>(warp) * (K / 16) + lane * 4;
+    float *pd = pss_s + warp * 256 + lane * 4;
+    cp_async16(pd, ps);
+    if (K == 4096) cp_async16(pd + 128, ps + 128);
+  }
+  cp_async_commit();
   __shared__ float res_s[16 * 8 * NT];
   const bool has_res = epi.residual != nullptr && rank == 0;
   S4Residual<NT, 32 * kT4Warps> rres;
@@ -472,11 +496,22 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
     if (c0 + kT4Units < kr.e) load(c0 + kT4Units);
   }
   if (has_res) rres.park(res_s, n_vec);
+  cp_async_wait_all();  // this thread's chain copies (if any) have landed
+  if (ss_warp) {  // inv_s[v] = 1 / sqrt(mean(x_v^2) + eps), the partials summed in a fixed order
+    const float4 a = *reinterpret_cast<const float4 *>(pss_s + warp * 256 + lane * 4);
+    float t = (a.x + a.y) + (a.z + a.w);
+    if (K == 4096) {
+      const float4 c = *reinterpret_cast<const float4 *>(pss_s + warp * 256 + 128 + lane * 4);
+      t += (c.x + c.y) + (c.z + c.w);
+    }
+    t = warp_sum(t);
+    if (lane == 0) inv_s[warp] = rsqrtf(t / K + epi.eps);
+  }
   // reduce over warps (and cluster ranks) in fixed order
 #pragma unroll
   for (int t = 0; t < NT; ++t)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) red[((warp * NT + t) * 4 + e) * 32 + lane] = acc[t][e];
+    for (int e = 0; e < 4; ++e) red[((warp * NT + t) * 4 + e) * 32 + lane] = acc[0][t][e] + acc[1][t][e];
   __syncthreads();
   float v[NT][4];
   if (warp == 0) {
@@ -514,7 +549,24 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
   if constexpr (kAR && NT == 1) {
     if (warp == 0) s4_allreduce_tile(v[0], tile, N, n_vec, epi.ar);
   }
-  if (warp == 0) s4_store<NT>(v, tile, N, n_vec, y, epi.residual ? res_s : nullptr, epi.swiglu, epi.amax);
+  if constexpr (NT == 1) {
+    if (epi.ss_in && warp == 0) {  // the folded RMSNorm: y = inv * (W . (x * w))
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int vv = tid * 2 + (e & 1);
+        if (vv < n_vec) v[0][e] *= inv_s[vv];
+      }
+    }
+  }
+  if (warp == 0) {
+    float w_lo = 0.f, w_hi = 0.f;  // (w_s landed before the block barrier above)
+    if (NT == 1 && epi.yw) {
+      w_lo = bf16_bits_to_float(w_s[gid]);
+      w_hi = bf16_bits_to_float(w_s[gid + 8]);
+    }
+    s4_store<NT>(v, tile, N, n_vec, y, epi.residual ? res_s : nullptr, epi.swiglu, epi.amax, NT == 1 ? epi.yw : nullptr,
+                 epi.ss_out, w_lo, w_hi);
+  }
 }
 
 // Repack natural-layout codes [N, K/2] + scales [N, K/32] into GEMV units.
@@ -710,6 +762,31 @@ extern "C" int iron_gemv_int4g32_ex(const uint8_t *packed, const uint16_t *x, ui
   if (n_vec <= 32) return launch_s4_tile_cs<4>(packed, x, y, N, K, n_vec, epi, pdl, s);
   return launch_s4_tile_cs<8>(packed, x, y, N, K, n_vec, epi, pdl, s);
 #endif
+}
+
+extern "C" int iron_gemv_int4g32_chain(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K, int n_vec,
+                                       const iron_gemv_chain *c, unsigned flags, void *stream) {
+  if (!packed || !x || !y || !c) return IRON_ERR_NULL;
+  if (N <= 0 || K <= 0 || n_vec <= 0 || n_vec > 8 || K % 128 || N % 16) return IRON_ERR_SHAPE;
+  if (static_cast<int64_t>(N / 16) * (K / 128) > 0x7fffffffLL) return IRON_ERR_SHAPE;
+  if (!aligned16(packed) || !aligned16(x)) return IRON_ERR_ALIGN;
+  const int swiglu = (flags & IRON_FLAG_SWIGLU) ? 1 : 0;
+  const bool writer = c->ss_out || c->y_weighted || c->weight;
+  if (writer && !(c->ss_out && c->y_weighted && c->weight)) return IRON_ERR_NULL;
+  if (swiglu && (c->residual || c->argmax_keys || writer)) return IRON_ERR_ARG;
+  if (c->ss_in) {
+    if (K != 2048 && K != 4096) return IRON_ERR_SHAPE;  // K / 16 partials: one or two float4 per lane
+    if (!aligned16(c->ss_in)) return IRON_ERR_ALIGN;
+    if (!(c->eps >= 0.f)) return IRON_ERR_ARG;
+  }
+  S4Epi epi{c->residual, swiglu, nullptr, c->eps, c->argmax_keys, {}, (flags & IRON_FLAG_X_READONLY) ? 1 : 0};
+  epi.ar.world = 1;
+  epi.ss_in = c->ss_in;
+  epi.ss_out = c->ss_out;
+  epi.yw = c->y_weighted;
+  epi.yw_w = c->weight;
+  return launch_s4_tile_cs<1>(packed, x, y, N, K, n_vec, epi, (flags & IRON_FLAG_PDL) != 0,
+                              static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int iron_gemv_int4g32_allreduce(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,

@@ -28,15 +28,6 @@ __device__ __forceinline__ uint32_t s4x2_dequant_(uint32_t w, uint32_t scale2) {
   return r;
 }
 
-// Signed int4 pair -> bf16x2 of the exact integers (q_lo, q_hi), q in [-8, 7]: the LOP3
-// magic number of s4x2_dequant_ and its exact subtract, without the scale (the GEMV
-// applies the group scale to the MMA's fp32 group sums).
-__device__ __forceinline__ uint32_t s4x2_int_(uint32_t w) {
-  uint32_t biased = lop3_and_xor_(w, 0x000f000fu, 0x43084308u), q;
-  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(biased), "r"(0x43084308u));
-  return q;
-}
-
 // Nibble order of a packed 32-bit code word. Natural order (4 code bytes of one row,
 // element 2b in the low nibble of byte b) holds k_i at bits 4i; the packed word holds
 // k_2q at bits 4q and k_2q+1 at bits 16 + 4q, so that s4x2_dequant_(w >> 4q) is the
