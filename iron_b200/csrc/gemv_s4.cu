@@ -363,7 +363,9 @@ constexpr int s4_units() { return NT <= 2 ? 2 : 4; }
 // kNorm: the RMSNorm prologue (n_vec <= 8) -- x normalised into shared memory first.
 // (Staging a plain x the same way measured slower on B200: 4.16 against 3.77 us per
 // config-2 launch; the per-unit L1 reads overlap better than one synchronised copy.)
-template <int NT, int CS, bool kNorm = false, bool kAR = false, bool kRO = false>
+// kChain (NT == 1): the decode chain's folded RMSNorm (S4Epi ss_in / ss_out / yw); a
+// separate instantiation, so the plain GEMV carries none of its shared memory or code.
+template <int NT, int CS, bool kNorm = false, bool kAR = false, bool kRO = false, bool kChain = false>
 __global__ void __launch_bounds__(32 * s4_warps<NT>(), s4_min_ctas<NT, kNorm>())
 gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__restrict__ x,
                        uint16_t *__restrict__ y, int N, int K, int n_vec, S4Epi epi) {
@@ -414,9 +416,10 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
   // held across the main loop): the writer's RMSNorm weights of this tile's 16 rows
   // (before the wait: they never depend on the previous kernel) and, after the wait,
   // warp v's vector-v partial sums of squares (K / 16 floats)
-  __shared__ __align__(16) uint16_t w_s[16];
-  __shared__ __align__(16) float pss_s[NT == 1 ? 8 * 256 : 4];
-  if (NT == 1 && epi.yw && warp == 0 && rank == 0 && lane < 2) cp_async16(w_s + lane * 8, epi.yw_w + tile * 16 + lane * 8);
+  constexpr bool chain = kChain && NT == 1;
+  __shared__ __align__(16) uint16_t w_s[chain ? 16 : 8];
+  __shared__ __align__(16) float pss_s[chain ? 8 * 256 : 4];
+  if (chain && epi.yw && warp == 0 && rank == 0 && lane < 2) cp_async16(w_s + lane * 8, epi.yw_w + tile * 16 + lane * 8);
   // a GEMV that adds a residual (a decoder block's o_proj and down_proj) bounds a
   // window (see ld_act_v4): its dependents launch only after its wait
   const bool bound = epi.residual != nullptr;
@@ -426,14 +429,14 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
   // chain prologue: warp v requests vector v's partial sums of squares now and sums them
   // after its units (K / 16 partials: K / 2048 16-byte pieces per lane)
   __shared__ float inv_s[8];
-  const bool ss_warp = NT == 1 && epi.ss_in != nullptr && rank == 0 && warp < n_vec;
+  const bool ss_warp = chain && epi.ss_in != nullptr && rank == 0 && warp < n_vec;
   if (ss_warp) {
     const float *ps = epi.ss_in + static_cast<int64_t>(warp) * (K / 16) + lane * 4;
     float *pd = pss_s + warp * 256 + lane * 4;
     cp_async16(pd, ps);
     if (K == 4096) cp_async16(pd + 128, ps + 128);
   }
-  cp_async_commit();
+  if constexpr (chain) cp_async_commit();
   __shared__ float res_s[16 * 8 * NT];
   const bool has_res = epi.residual != nullptr && rank == 0;
   S4Residual<NT, 32 * kT4Warps> rres;
@@ -496,7 +499,7 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
     if (c0 + kT4Units < kr.e) load(c0 + kT4Units);
   }
   if (has_res) rres.park(res_s, n_vec);
-  cp_async_wait_all();  // this thread's chain copies (if any) have landed
+  if constexpr (chain) cp_async_wait_all();  // this thread's chain copies (if any) have landed
   if (ss_warp) {  // inv_s[v] = 1 / sqrt(mean(x_v^2) + eps), the partials summed in a fixed order
     const float4 a = *reinterpret_cast<const float4 *>(pss_s + warp * 256 + lane * 4);
     float t = (a.x + a.y) + (a.z + a.w);
@@ -549,7 +552,7 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
   if constexpr (kAR && NT == 1) {
     if (warp == 0) s4_allreduce_tile(v[0], tile, N, n_vec, epi.ar);
   }
-  if constexpr (NT == 1) {
+  if constexpr (chain) {
     if (epi.ss_in && warp == 0) {  // the folded RMSNorm: y = inv * (W . (x * w))
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -560,11 +563,11 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
   }
   if (warp == 0) {
     float w_lo = 0.f, w_hi = 0.f;  // (w_s landed before the block barrier above)
-    if (NT == 1 && epi.yw) {
+    if (chain && epi.yw) {
       w_lo = bf16_bits_to_float(w_s[gid]);
       w_hi = bf16_bits_to_float(w_s[gid + 8]);
     }
-    s4_store<NT>(v, tile, N, n_vec, y, epi.residual ? res_s : nullptr, epi.swiglu, epi.amax, NT == 1 ? epi.yw : nullptr,
+    s4_store<NT>(v, tile, N, n_vec, y, epi.residual ? res_s : nullptr, epi.swiglu, epi.amax, chain ? epi.yw : nullptr,
                  epi.ss_out, w_lo, w_hi);
   }
 }
@@ -639,6 +642,10 @@ static int launch_s4_tile(const uint8_t *packed, const uint16_t *x, uint16_t *y,
     if constexpr (NT != 1) return IRON_ERR_SHAPE;
     e = epi.x_ro ? cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, true, true>, packed, x, y, N, K, n_vec, epi)
                  : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, true, false>, packed, x, y, N, K, n_vec, epi);
+  } else if (epi.ss_in || epi.yw) {
+    if constexpr (NT != 1) return IRON_ERR_SHAPE;
+    e = epi.x_ro ? cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, false, true, true>, packed, x, y, N, K, n_vec, epi)
+                 : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, false, false, true>, packed, x, y, N, K, n_vec, epi);
   } else if (epi.norm_w) {
     e = cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, true>, packed, x, y, N, K, n_vec, epi);
   } else {

@@ -7,6 +7,7 @@ those goldens do or tolerate. Inputs and outputs are torch CPU tensors.
 
 from __future__ import annotations
 
+import contextlib
 import math
 
 import numpy as np
@@ -14,11 +15,31 @@ import torch
 
 BF16 = torch.bfloat16
 
+# The arithmetic type of the restated goldens: fp32, as IRON's goldens compute. A test
+# may rerun the oracle in fp64 (same bf16 rounding points) to measure how sensitive a
+# result is to the precision of its sums -- the spread a correct fp32 implementation
+# with another summation order can show.
+_ACC = [torch.float32]
+
+
+@contextlib.contextmanager
+def accumulate(dtype):
+    """Run the oracle's arithmetic in `dtype` inside the block (rounding points unchanged)."""
+    old, _ACC[0] = _ACC[0], dtype
+    try:
+        yield
+    finally:
+        _ACC[0] = old
+
+
+def _f(t: torch.Tensor) -> torch.Tensor:
+    return t.to(_ACC[0])
+
 
 def gemv(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
     """C = A @ B, fp32 accumulate, bf16 out (iron/operators/gemv/reference.py:9-11).
     A [M, K] or [b, M, K]; B [K] or [b, K]."""
-    Af, Bf = A.float(), B.float()
+    Af, Bf = _f(A), _f(B)
     if A.dim() == 3:
         return torch.einsum("bmk,bk->bm", Af, Bf).to(BF16)
     return (Af @ Bf).to(BF16)
@@ -26,21 +47,21 @@ def gemv(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
 
 def gemv_multi(A: torch.Tensor, X: torch.Tensor) -> torch.Tensor:
     """One matrix, a batch of vectors: Y[v] = A @ X[v] (decode batch)."""
-    return (X.float() @ A.float().T).to(BF16)
+    return (_f(X) @ _f(A).T).to(BF16)
 
 
 def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
     """Tanh-approximation GELU (iron/operators/gemv/reference.py:59-66)."""
-    xf = x.float()
+    xf = _f(x)
     return 0.5 * xf * (1.0 + torch.tanh(0.7978845608028654 * (xf + 0.044715 * xf**3)))
 
 
 def rms_norm(x: torch.Tensor, w: torch.Tensor | None = None, eps: float = 1e-5) -> torch.Tensor:
     """x / sqrt(mean(x^2) + eps) [* w] row-wise (iron/operators/rms_norm/reference.py:7-16)."""
-    xf = x.float()
+    xf = _f(x)
     out = xf / torch.sqrt(torch.mean(xf * xf, dim=-1, keepdim=True) + eps)
     if w is not None:
-        out = out * w.float()
+        out = out * _f(w)
     return out.to(BF16)
 
 
@@ -50,9 +71,9 @@ def rope(x: torch.Tensor, angles: torch.Tensor, method_type: int = 0) -> torch.T
     (iron/operators/rope/reference.py:69-102)."""
     rows = x.shape[0]
     rep = rows // angles.shape[0]
-    cos = angles[..., 0::2].float().repeat_interleave(rep, dim=0)
-    sin = angles[..., 1::2].float().repeat_interleave(rep, dim=0)
-    xf = x.float()
+    cos = _f(angles[..., 0::2]).repeat_interleave(rep, dim=0)
+    sin = _f(angles[..., 1::2]).repeat_interleave(rep, dim=0)
+    xf = _f(x)
     if method_type == 0:
         half = x.shape[-1] // 2
         x1, x2 = xf[..., :half], xf[..., half:]
@@ -69,7 +90,7 @@ def softmax(x: torch.Tensor, valid: int | None = None) -> torch.Tensor:
     """Row softmax in fp32 (iron/operators/softmax/reference.py:9-11). With
     ``valid``, columns >= valid are first set to -inf as the device's mask_bf16
     does (iron/operators/softmax/design.py:85-91)."""
-    xf = x.float()
+    xf = _f(x)
     if valid is not None:
         xf = xf.clone()
         xf[..., valid:] = -math.inf
@@ -78,24 +99,24 @@ def softmax(x: torch.Tensor, valid: int | None = None) -> torch.Tensor:
 
 def silu(x: torch.Tensor) -> torch.Tensor:
     """iron/operators/silu/reference.py:7-9."""
-    return torch.nn.functional.silu(x.float()).to(BF16)
+    return torch.nn.functional.silu(_f(x)).to(BF16)
 
 
 def mul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     """iron/operators/elementwise_mul/reference.py:7-9."""
-    return (a.float() * b.float()).to(BF16)
+    return (_f(a) * _f(b)).to(BF16)
 
 
 def add(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     """iron/operators/elementwise_add/reference.py:7-9."""
-    return (a.float() + b.float()).to(BF16)
+    return (_f(a) + _f(b)).to(BF16)
 
 
 def swiglu_act(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     """silu(gate) * up, the SiLU + ElementwiseMul steps of SwiGLUDecode
     (iron/operators/swiglu_decode/op.py:56-62), fused."""
-    g = gate.float()
-    return (g * torch.sigmoid(g) * up.float()).to(BF16)
+    g = _f(gate)
+    return (g * torch.sigmoid(g) * _f(up)).to(BF16)
 
 
 def repeat_interleave(x: torch.Tensor, repeat: int) -> torch.Tensor:
@@ -153,10 +174,10 @@ def mha_prefill(Q, K, V, causal=True, chunk=1024):
     H, S, d = Q.shape
     out = torch.empty(H, S, V.shape[-1], dtype=BF16)
     for h in range(H):
-        Kh = K[h // g].float()
-        Vh = V[h // g].float()
+        Kh = _f(K[h // g])
+        Vh = _f(V[h // g])
         for r0 in range(0, S, chunk):
-            q = Q[h, r0 : r0 + chunk].float()
+            q = _f(Q[h, r0 : r0 + chunk])
             s = q @ Kh.T / math.sqrt(d)
             if causal:
                 rows = torch.arange(r0, r0 + q.shape[0]).unsqueeze(1)
@@ -177,9 +198,9 @@ def attn_decode(q, k_cache, v_cache, lens):
     out = torch.empty(B, Hq, d, dtype=BF16)
     for b in range(B):
         L = int(lens[b])
-        K = k_cache[b, :, :L].float().repeat_interleave(g, dim=0)
-        V = v_cache[b, :, :L].float().repeat_interleave(g, dim=0)
-        s = torch.einsum("hd,hld->hl", q[b].float(), K) / math.sqrt(d)
+        K = _f(k_cache[b, :, :L]).repeat_interleave(g, dim=0)
+        V = _f(v_cache[b, :, :L]).repeat_interleave(g, dim=0)
+        s = torch.einsum("hd,hld->hl", _f(q[b]), K) / math.sqrt(d)
         out[b] = torch.einsum("hl,hld->hd", torch.softmax(s, dim=-1), V).to(BF16)
     return out
 
@@ -213,7 +234,7 @@ def gemm(A: torch.Tensor, B: torch.Tensor, b_col_maj: bool = False, c_col_maj: b
     """C = A @ B from stored layouts (iron/operators/gemm/reference.py:7-18), fp32
     accumulation, bf16 out."""
     Bm = B.T if b_col_maj else B
-    C = (A.float() @ Bm.float()).to(BF16)
+    C = (_f(A) @ _f(Bm)).to(BF16)
     return C.T if c_col_maj else C
 
 
@@ -221,7 +242,7 @@ def flm_gemm(A: torch.Tensor, B: torch.Tensor, epilogue: str = "none", clamp=Non
     """flm GEMM (iron/operators/flm/gemm/reference.py:8-57): fp32 accumulation,
     conversion to bf16, then the activation (gelu = x*sigmoid(1.702x)) and the
     clamp, evaluated in bf16 torch ops as the golden does."""
-    C = (A.float() @ B.float()).to(A.dtype)
+    C = (_f(A) @ _f(B)).to(A.dtype)
     if epilogue == "gelu":
         C = C * torch.sigmoid(1.702 * C)
     elif epilogue == "silu":
