@@ -77,6 +77,19 @@ class Int4Matrix:
         if not keep_natural:
             del codes, scales
 
+    @classmethod
+    def from_dense(cls, w: torch.Tensor, keep_natural: bool = False) -> "Int4Matrix":
+        """Quantize bf16 / fp32 weights [rows, cols] (weights.quantize_int4g32) and pack them."""
+        from .weights import quantize_int4g32
+
+        m = cls.__new__(cls)
+        codes, scales = quantize_int4g32(w)
+        m.rows, m.cols = w.shape
+        m.packed = GEMV.pack_int4g32(codes, scales)
+        m.codes = codes if keep_natural else None
+        m.scales = scales if keep_natural else None
+        return m
+
     def dequant(self) -> torch.Tensor:
         """Exact bf16 weights [rows, cols] (needs keep_natural)."""
         out = torch.empty(self.rows, self.cols, dtype=torch.bfloat16, device=self.codes.device)
@@ -110,7 +123,9 @@ class LlamaDecodeEngine:
     def __init__(self, shape: LlamaShape, batch: int, max_seq: int, seed: int = 0,
                  keep_natural: bool = False, pdl: bool = True, fuse_norm: str | None = None,
                  fuse_rope: bool | None = None, l2_prefetch: bool | None = None,
-                 sampling: "SamplingConfig | None" = None):
+                 sampling: "SamplingConfig | None" = None, weights: dict | None = None):
+        """weights: a checkpoint's tensors by Hugging Face name (weights.load_checkpoint),
+        quantized here to int4 group-32; None: random weights from `seed`."""
         self.s, self.B, self.L = shape, batch, max_seq
         # None: greedy argmax fused into the lm-head GEMV; else temperature / top-k /
         # multinomial on the device (iron_sample_topk)
@@ -122,7 +137,9 @@ class LlamaDecodeEngine:
         g.manual_seed(seed)
         E, Hd = s.emb_dim, s.head_dim
         self.layers = []
-        for _ in range(s.n_layers):
+        if weights is not None:
+            self._load_weights(weights, keep_natural)
+        for _ in range(s.n_layers if weights is None else 0):
             lay = {
                 "n1": (1 + 0.02 * torch.randn(E, device=dev, generator=g)).to(torch.bfloat16),
                 "n2": (1 + 0.02 * torch.randn(E, device=dev, generator=g)).to(torch.bfloat16),
@@ -133,11 +150,12 @@ class LlamaDecodeEngine:
                 "d": Int4Matrix(E, s.hidden_dim, g, 0.0005, 0.002, keep_natural),
             }
             self.layers.append(lay)
-        self.nf = (1 + 0.02 * torch.randn(E, device=dev, generator=g)).to(torch.bfloat16)
-        self.lm = Int4Matrix(s.vocab_size, E, g, 0.001, 0.004, keep_natural=True)
-        self.embed_table = self.lm.dequant()  # tied: the embedding is the dequantized lm-head
-        if not keep_natural:
-            self.lm.codes = self.lm.scales = None
+        if weights is None:
+            self.nf = (1 + 0.02 * torch.randn(E, device=dev, generator=g)).to(torch.bfloat16)
+            self.lm = Int4Matrix(s.vocab_size, E, g, 0.001, 0.004, keep_natural=True)
+            self.embed_table = self.lm.dequant()  # tied: the embedding is the dequantized lm-head
+            if not keep_natural:
+                self.lm.codes = self.lm.scales = None
         self.lut = rope_table(Hd, max_seq, s.rope_base, dev)
         B = batch
         self.kc = torch.zeros(s.n_layers, B, s.n_kv_groups, max_seq, Hd, dtype=torch.bfloat16, device=dev)
@@ -182,6 +200,33 @@ class LlamaDecodeEngine:
         # the step (off the dependent chain) when the layer starts
         self.l2_prefetch = bool(l2_prefetch) if l2_prefetch is not None else False
         self._side = torch.cuda.Stream() if self.l2_prefetch else None
+
+    def _load_weights(self, state: dict, keep_natural: bool):
+        """Bind a checkpoint's tensors (IRON's names, llama_npu.py:588-639) and quantize the
+        projections: q / k / v stacked into the QKV matrix, gate and up interleaved per 8
+        rows (interleave_gate_up), the head from lm_head.weight or the tied embedding."""
+        from . import weights as W
+
+        s, dev = self.s, self.dev
+        W.check_checkpoint(state, s)
+
+        def dense(name):
+            return state[name].to(device=dev, dtype=torch.bfloat16)
+
+        perm = interleave_gate_up(s.hidden_dim).to(dev)
+        for i in range(s.n_layers):
+            qkv = torch.cat([dense(W.layer_name(i, k)) for k in ("q", "k", "v")])
+            gu = torch.cat([dense(W.layer_name(i, "g")), dense(W.layer_name(i, "u"))])[perm]
+            self.layers.append({
+                "n1": dense(W.layer_name(i, "n1")), "n2": dense(W.layer_name(i, "n2")),
+                "qkv": Int4Matrix.from_dense(qkv, keep_natural),
+                "o": Int4Matrix.from_dense(dense(W.layer_name(i, "o")), keep_natural),
+                "gu": Int4Matrix.from_dense(gu, keep_natural),
+                "d": Int4Matrix.from_dense(dense(W.layer_name(i, "d")), keep_natural),
+            })
+        self.nf = dense(W.FINAL_NORM)
+        self.embed_table = dense(W.EMBED).contiguous()
+        self.lm = Int4Matrix.from_dense(dense(W.LM_HEAD if W.LM_HEAD in state else W.EMBED), keep_natural)
 
     # -- bytes moved per step (the roofline numerator) ---------------------------------
     def weight_bytes(self) -> int:

@@ -20,6 +20,10 @@ BF16 = torch.bfloat16
 # result is to the precision of its sums -- the spread a correct fp32 implementation
 # with another summation order can show.
 _ACC = [torch.float32]
+# The type every restated operator rounds its output to: bf16 (the operators' buffers).
+# IRON's accuracy reference is the CPU model run in fp32 throughout
+# (iron/applications/llama_3.2_1b/llama_npu.py:1239-1241): fp32 here, no bf16 rounding.
+_OUT = [BF16]
 
 
 @contextlib.contextmanager
@@ -32,6 +36,16 @@ def accumulate(dtype):
         _ACC[0] = old
 
 
+@contextlib.contextmanager
+def fp32_reference():
+    """Inside the block every operator keeps fp32 outputs (IRON's fp32 CPU reference)."""
+    old, _OUT[0] = _OUT[0], torch.float32
+    try:
+        yield
+    finally:
+        _OUT[0] = old
+
+
 def _f(t: torch.Tensor) -> torch.Tensor:
     return t.to(_ACC[0])
 
@@ -41,13 +55,13 @@ def gemv(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
     A [M, K] or [b, M, K]; B [K] or [b, K]."""
     Af, Bf = _f(A), _f(B)
     if A.dim() == 3:
-        return torch.einsum("bmk,bk->bm", Af, Bf).to(BF16)
-    return (Af @ Bf).to(BF16)
+        return torch.einsum("bmk,bk->bm", Af, Bf).to(_OUT[0])
+    return (Af @ Bf).to(_OUT[0])
 
 
 def gemv_multi(A: torch.Tensor, X: torch.Tensor) -> torch.Tensor:
     """One matrix, a batch of vectors: Y[v] = A @ X[v] (decode batch)."""
-    return (_f(X) @ _f(A).T).to(BF16)
+    return (_f(X) @ _f(A).T).to(_OUT[0])
 
 
 def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
@@ -62,7 +76,7 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor | None = None, eps: float = 1e-5) 
     out = xf / torch.sqrt(torch.mean(xf * xf, dim=-1, keepdim=True) + eps)
     if w is not None:
         out = out * _f(w)
-    return out.to(BF16)
+    return out.to(_OUT[0])
 
 
 def rope(x: torch.Tensor, angles: torch.Tensor, method_type: int = 0) -> torch.Tensor:
@@ -83,7 +97,7 @@ def rope(x: torch.Tensor, angles: torch.Tensor, method_type: int = 0) -> torch.T
         y = torch.empty_like(xf)
         y[..., 0::2] = xe * cos - xo * sin
         y[..., 1::2] = xe * sin + xo * cos
-    return y.to(BF16)
+    return y.to(_OUT[0])
 
 
 def softmax(x: torch.Tensor, valid: int | None = None) -> torch.Tensor:
@@ -94,29 +108,29 @@ def softmax(x: torch.Tensor, valid: int | None = None) -> torch.Tensor:
     if valid is not None:
         xf = xf.clone()
         xf[..., valid:] = -math.inf
-    return torch.softmax(xf, dim=-1).to(BF16)
+    return torch.softmax(xf, dim=-1).to(_OUT[0])
 
 
 def silu(x: torch.Tensor) -> torch.Tensor:
     """iron/operators/silu/reference.py:7-9."""
-    return torch.nn.functional.silu(_f(x)).to(BF16)
+    return torch.nn.functional.silu(_f(x)).to(_OUT[0])
 
 
 def mul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     """iron/operators/elementwise_mul/reference.py:7-9."""
-    return (_f(a) * _f(b)).to(BF16)
+    return (_f(a) * _f(b)).to(_OUT[0])
 
 
 def add(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     """iron/operators/elementwise_add/reference.py:7-9."""
-    return (_f(a) + _f(b)).to(BF16)
+    return (_f(a) + _f(b)).to(_OUT[0])
 
 
 def swiglu_act(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     """silu(gate) * up, the SiLU + ElementwiseMul steps of SwiGLUDecode
     (iron/operators/swiglu_decode/op.py:56-62), fused."""
     g = _f(gate)
-    return (g * torch.sigmoid(g) * _f(up)).to(BF16)
+    return (g * torch.sigmoid(g) * _f(up)).to(_OUT[0])
 
 
 def repeat_interleave(x: torch.Tensor, repeat: int) -> torch.Tensor:
@@ -172,7 +186,7 @@ def mha_prefill(Q, K, V, causal=True, chunk=1024):
     Query rows are processed `chunk` at a time (same math, bounded memory)."""
     g = Q.shape[0] // K.shape[0]
     H, S, d = Q.shape
-    out = torch.empty(H, S, V.shape[-1], dtype=BF16)
+    out = torch.empty(H, S, V.shape[-1], dtype=_OUT[0])
     for h in range(H):
         Kh = _f(K[h // g])
         Vh = _f(V[h // g])
@@ -183,7 +197,7 @@ def mha_prefill(Q, K, V, causal=True, chunk=1024):
                 rows = torch.arange(r0, r0 + q.shape[0]).unsqueeze(1)
                 cols = torch.arange(Kh.shape[0]).unsqueeze(0)
                 s = s.masked_fill(cols > rows, -math.inf)
-            out[h, r0 : r0 + chunk] = (torch.softmax(s, dim=-1) @ Vh).to(BF16)
+            out[h, r0 : r0 + chunk] = (torch.softmax(s, dim=-1) @ Vh).to(_OUT[0])
     return out
 
 
@@ -195,13 +209,13 @@ def attn_decode(q, k_cache, v_cache, lens):
     B, Hq, d = q.shape
     Hkv = k_cache.shape[1]
     g = Hq // Hkv
-    out = torch.empty(B, Hq, d, dtype=BF16)
+    out = torch.empty(B, Hq, d, dtype=_OUT[0])
     for b in range(B):
         L = int(lens[b])
         K = _f(k_cache[b, :, :L]).repeat_interleave(g, dim=0)
         V = _f(v_cache[b, :, :L]).repeat_interleave(g, dim=0)
         s = torch.einsum("hd,hld->hl", _f(q[b]), K) / math.sqrt(d)
-        out[b] = torch.einsum("hl,hld->hd", torch.softmax(s, dim=-1), V).to(BF16)
+        out[b] = torch.einsum("hl,hld->hd", torch.softmax(s, dim=-1), V).to(_OUT[0])
     return out
 
 
@@ -234,7 +248,7 @@ def gemm(A: torch.Tensor, B: torch.Tensor, b_col_maj: bool = False, c_col_maj: b
     """C = A @ B from stored layouts (iron/operators/gemm/reference.py:7-18), fp32
     accumulation, bf16 out."""
     Bm = B.T if b_col_maj else B
-    C = (_f(A) @ _f(Bm)).to(BF16)
+    C = (_f(A) @ _f(Bm)).to(_OUT[0])
     return C.T if c_col_maj else C
 
 
