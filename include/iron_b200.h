@@ -131,6 +131,19 @@ int iron_gemv_int4g32_ex(const uint8_t *packed, const uint16_t *x, uint16_t *y, 
 int iron_l2_prefetch(const void *ptr, size_t bytes, unsigned flags, void *stream);
 int iron_argmax_finalize(unsigned long long *keys, int32_t *tokens, int32_t *pos, int B, unsigned flags,
                          void *stream);
+/* q4 weights: IRON's asymmetric int4 q4nx values (min + scale * code per group of 32
+ * along K, unsigned codes; format of iron/operators/flm/dequant/README.md, values of
+ * iron/operators/flm/dequant/reference.py:40-77), replacing flm.DequantBFP followed by
+ * the GEMV. iron_pack_q4g32: natural codes [N, K/2] (even k low nibble), bf16 scales and
+ * mins [N, K/32] -> 1280-byte streaming units (N % 16 == 0, K % 128 == 0). The GEMV
+ * (n_vec <= 8, optional residual as iron_gemv_int4g32) multiplies bf16(min + scale *
+ * code) -- IRON's fp32 value rounded once -- with fp32 accumulate; iron_unpack_q4g32
+ * writes those bf16 weights [N, K] (for checks). */
+int iron_pack_q4g32(const uint8_t *codes, const uint16_t *scales, const uint16_t *mins, uint8_t *packed, int N,
+                    int K, void *stream);
+int iron_unpack_q4g32(const uint8_t *packed, uint16_t *out, int N, int K, void *stream);
+int iron_gemv_q4g32(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K, int n_vec,
+                    const uint16_t *residual, unsigned flags, void *stream);
 /* iron_gemv_int4g32_chain (no reference counterpart as one call: it folds the weighted
  * RMSNorm steps of IRON's decode runlist, iron/applications/llama_3.2_1b/llama_npu.py:
  * 463-470 and :536, into the GEMVs around them). The int4 GEMV of iron_gemv_int4g32

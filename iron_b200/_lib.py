@@ -65,6 +65,9 @@ SIGNATURES: dict[str, list] = {
     "iron_argmax_finalize": [P, P, P, c_int, c_uint, P],
     "iron_sample_topk": [P, c_int, c_int, c_float, c_int, c_uint64, P, P, c_uint, P],
     "iron_gemv_int4g32_chain": [P, P, P, c_int, c_int, c_int, P, c_uint, P],
+    "iron_pack_q4g32": [P, P, P, P, c_int, c_int, P],
+    "iron_unpack_q4g32": [P, P, c_int, c_int, P],
+    "iron_gemv_q4g32": [P, P, P, c_int, c_int, c_int, P, c_uint, P],
     "iron_embed_chain": [P, P, P, P, P, P, c_int, c_int, c_int, c_uint, P],
     "iron_l2_prefetch": [P, c_size_t, c_uint, P],
     "iron_attn_decode_kernels": [c_int, c_int, c_int, c_int],

@@ -30,6 +30,8 @@ namespace cg = cooperative_groups;
 namespace iron {
 
 constexpr int kS4UnitBytes = 1152;
+// q4 (asymmetric) units append 128 bytes of group mins, laid out as the scales: 1280 B.
+constexpr int kQ4UnitBytes = 1280;
 constexpr int kS4CodeBytes = 1024;
 
 struct S4Range {
@@ -70,6 +72,7 @@ struct S4Epi {
   float *ss_out;         // [n_vec, N/16] partial sums of squares of y (per 16-row tile)
   uint16_t *yw;          // [n_vec, N] bf16(y * yw_w): the next GEMV's input
   const uint16_t *yw_w;  // [N] the next RMSNorm's weights
+  int asym;              // q4 units (min + scale * code, 1280 B) instead of int4 g32
 };
 
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
@@ -291,10 +294,13 @@ __device__ __forceinline__ void s4_store(const float (&v)[NT][4], int tile, int 
 // predicated. (Applying
 // the group scale to the MMA's fp32 group sums instead measured no faster on B200 and
 // would change the results from IRON's dequantize-then-GEMV by up to ~1e-2.)
-template <int NT, bool kShared = false, bool kRO = false>
+// kAsym: the q4 (min + scale * code) weights: codes unsigned, mn the row pair's bf16
+// group mins laid out as sc (q4x2_dequant_: bf16(min + scale * code), one rounding).
+template <int NT, bool kShared = false, bool kRO = false, bool kAsym = false>
 __device__ __forceinline__ void s4_unit_gx(float (&acc)[2][NT][4], const uint4 &clo, const uint4 &chi,
                                            const uint4 &sc, const uint16_t *__restrict__ x, int K,
-                                           int n_vec, int kbase, int ldx = -1, int xoff = 0) {
+                                           int n_vec, int kbase, int ldx = -1, int xoff = 0,
+                                           const uint4 &mn = make_uint4(0u, 0u, 0u, 0u)) {
   const int lane = threadIdx.x & 31, gid = lane >> 2, tid = lane & 3;
   const uint32_t wl[4] = {clo.x, clo.y, clo.z, clo.w};
   const uint32_t wh[4] = {chi.x, chi.y, chi.z, chi.w};
@@ -325,10 +331,21 @@ __device__ __forceinline__ void s4_unit_gx(float (&acc)[2][NT][4], const uint4 &
     const uint32_t s2_lo = prmt_(sl2[j >> 1], sl2[j >> 1], sel);
     const uint32_t s2_hi = prmt_(sh2[j >> 1], sh2[j >> 1], sel);
     uint32_t pl[4], ph[4];
+    if constexpr (kAsym) {
+      const uint32_t ml2[2] = {mn.x, mn.y}, mh2[2] = {mn.z, mn.w};
+      const uint32_t m2_lo = prmt_(ml2[j >> 1], ml2[j >> 1], sel);
+      const uint32_t m2_hi = prmt_(mh2[j >> 1], mh2[j >> 1], sel);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      pl[q] = s4x2_dequant_(wl[j] >> (4 * q), s2_lo);
-      ph[q] = s4x2_dequant_(wh[j] >> (4 * q), s2_hi);
+      for (int q = 0; q < 4; ++q) {
+        pl[q] = q4x2_dequant_(wl[j] >> (4 * q), s2_lo, m2_lo);
+        ph[q] = q4x2_dequant_(wh[j] >> (4 * q), s2_hi, m2_hi);
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        pl[q] = s4x2_dequant_(wl[j] >> (4 * q), s2_lo);
+        ph[q] = s4x2_dequant_(wh[j] >> (4 * q), s2_hi);
+      }
     }
     const uint32_t A0[4] = {pl[0], ph[0], pl[1], ph[1]};
     const uint32_t A1[4] = {pl[2], ph[2], pl[3], ph[3]};
@@ -354,7 +371,7 @@ constexpr int s4_warps() { return NT <= 2 ? 8 : 4; }
 // CTAs per SM the register budget must allow: single-tile (<= 8 vector) kernels keep
 // four 8-warp CTAs per SM (<= 64 registers a thread; at 66 registers the occupancy cliff
 // to 3 CTAs per SM put config 2's 512 CTAs into two waves: 5.8 against 3.5 us per
-// launch); the wider tiles (and the fused-norm form) keep the compiler's own choice (0).
+// launch); the wider tiles (and the fused-norm and q4 forms) keep the compiler's own choice (0).
 template <int NT, bool kNorm>
 constexpr int s4_min_ctas() { return (NT == 1 && !kNorm) ? 4 : 0; }
 template <int NT>
@@ -365,8 +382,9 @@ constexpr int s4_units() { return NT <= 2 ? 2 : 4; }
 // config-2 launch; the per-unit L1 reads overlap better than one synchronised copy.)
 // kChain (NT == 1): the decode chain's folded RMSNorm (S4Epi ss_in / ss_out / yw); a
 // separate instantiation, so the plain GEMV carries none of its shared memory or code.
-template <int NT, int CS, bool kNorm = false, bool kAR = false, bool kRO = false, bool kChain = false>
-__global__ void __launch_bounds__(32 * s4_warps<NT>(), s4_min_ctas<NT, kNorm>())
+template <int NT, int CS, bool kNorm = false, bool kAR = false, bool kRO = false, bool kChain = false,
+          bool kAsym = false>
+__global__ void __launch_bounds__(32 * s4_warps<NT>(), s4_min_ctas<NT, kNorm || kAsym>())
 gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__restrict__ x,
                        uint16_t *__restrict__ y, int N, int K, int n_vec, S4Epi epi) {
   constexpr int kT4Warps = s4_warps<NT>();
@@ -379,7 +397,8 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
   const int tile = blockIdx.x / CS;
   const int cpt = K / 128;
   const S4Range kr = s4_split(0, cpt, CS * kT4Warps, rank * kT4Warps + warp);  // my chunks
-  const uint8_t *base = packed + (static_cast<int64_t>(tile) * cpt) * kS4UnitBytes;
+  constexpr int kUnit = kAsym ? kQ4UnitBytes : kS4UnitBytes;
+  const uint8_t *base = packed + (static_cast<int64_t>(tile) * cpt) * kUnit;
 
   float acc[2][NT][4];  // two accumulator sets (even / odd groups): two independent MMA chains
 #pragma unroll
@@ -387,15 +406,16 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc[a][t][0] = acc[a][t][1] = acc[a][t][2] = acc[a][t][3] = 0.f;
 
-  uint4 lo[kT4Units], hi[kT4Units], sc[kT4Units];
+  uint4 lo[kT4Units], hi[kT4Units], sc[kT4Units], mn[kAsym ? kT4Units : 1];
   auto load = [&](int c0) {
 #pragma unroll
     for (int u = 0; u < kT4Units; ++u) {
       if (c0 + u < kr.e) {
-        const uint8_t *p = base + static_cast<int64_t>(c0 + u) * kS4UnitBytes;
+        const uint8_t *p = base + static_cast<int64_t>(c0 + u) * kUnit;
         lo[u] = ld_stream_v4(p + lane * 16);
         hi[u] = ld_stream_v4(p + 512 + lane * 16);
         sc[u] = ld_stream_v4(p + kS4CodeBytes + gid * 16);
+        if constexpr (kAsym) mn[u] = ld_stream_v4(p + kS4UnitBytes + gid * 16);
       }
     }
   };
@@ -493,6 +513,7 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
         // B fragments straight from the activations (L1-cached) or the normalised
         // slice: this lane's 8 consecutive k of chunk j are k 0-7 of its code word
         if constexpr (norm) s4_unit_gx<NT, true>(acc, lo[u], hi[u], sc[u], xs_norm, K, n_vec, c * 128, klen, kc0);
+        else if constexpr (kAsym) s4_unit_gx<NT, false, kRO, true>(acc, lo[u], hi[u], sc[u], x, K, n_vec, c * 128, -1, 0, mn[u]);
         else s4_unit_gx<NT, false, kRO>(acc, lo[u], hi[u], sc[u], x, K, n_vec, c * 128);
       }
     }
@@ -574,14 +595,17 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
 
 // Repack natural-layout codes [N, K/2] + scales [N, K/32] into GEMV units.
 // One thread per 16-byte piece of a unit (72 pieces per unit).
+// (kAsym: q4 units, the group mins in pieces 72..79 laid out as the scales)
+template <bool kAsym = false>
 __global__ void pack_s4g32_kernel(const uint8_t *__restrict__ codes,
                                   const uint16_t *__restrict__ scales, uint8_t *__restrict__ out,
-                                  int N, int K, int64_t pieces) {
+                                  int N, int K, int64_t pieces, const uint16_t *__restrict__ mins = nullptr) {
+  constexpr int kPieces = kAsym ? 80 : 72;
   const int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (p >= pieces) return;
   const int cpt = K / 128;
-  const int64_t unit = p / 72;
-  const int piece = static_cast<int>(p % 72);
+  const int64_t unit = p / kPieces;
+  const int piece = static_cast<int>(p % kPieces);
   const int64_t tile = unit / cpt;
   const int c = static_cast<int>(unit % cpt);
   uint32_t words[4];
@@ -597,10 +621,11 @@ __global__ void pack_s4g32_kernel(const uint8_t *__restrict__ codes,
                               (static_cast<uint32_t>(g[2]) << 16) | (static_cast<uint32_t>(g[3]) << 24));
     }
   } else {
-    const int gid = piece - 64;
+    const int gid = (piece - 64) & 7;
     const int64_t rlo = tile * 16 + gid, rhi = rlo + 8;
-    const uint16_t *slo = scales + rlo * (K / 32) + c * 4;
-    const uint16_t *shi = scales + rhi * (K / 32) + c * 4;
+    const uint16_t *src = (kAsym && piece >= 72) ? mins : scales;
+    const uint16_t *slo = src + rlo * (K / 32) + c * 4;
+    const uint16_t *shi = src + rhi * (K / 32) + c * 4;
     words[0] = slo[0] | (static_cast<uint32_t>(slo[1]) << 16);
     words[1] = slo[2] | (static_cast<uint32_t>(slo[3]) << 16);
     words[2] = shi[0] | (static_cast<uint32_t>(shi[1]) << 16);
@@ -638,7 +663,11 @@ static int launch_s4_tile(const uint8_t *packed, const uint16_t *x, uint16_t *y,
   cfg.attrs = attr;
   cfg.numAttrs = na;
   cudaError_t e;
-  if (epi.ar.world > 1) {
+  if (epi.asym) {
+    if constexpr (NT != 1) return IRON_ERR_SHAPE;
+    e = epi.x_ro ? cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, false, true, false, true>, packed, x, y, N, K, n_vec, epi)
+                 : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, false, false, false, true>, packed, x, y, N, K, n_vec, epi);
+  } else if (epi.ar.world > 1) {
     if constexpr (NT != 1) return IRON_ERR_SHAPE;
     e = epi.x_ro ? cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, true, true>, packed, x, y, N, K, n_vec, epi)
                  : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, true, false>, packed, x, y, N, K, n_vec, epi);
@@ -684,6 +713,7 @@ static int launch_s4_tile_cs(const uint8_t *packed, const uint16_t *x, uint16_t 
 // row's 4 x 8 dequantized weights, bf16(q * s) exactly (the products of a 4-bit
 // integer and a bf16 scale are exact in fp32, so one rounding gives the
 // Dequant golden's value).
+template <bool kAsym = false>
 __global__ void unpack_s4g32_kernel(const uint8_t *__restrict__ packed, uint16_t *__restrict__ out, int K,
                                     int64_t pieces) {
   const int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -694,22 +724,31 @@ __global__ void unpack_s4g32_kernel(const uint8_t *__restrict__ packed, uint16_t
   const int64_t tile = unit / cpt;
   const int c = static_cast<int>(unit % cpt);
   const int h = piece >> 5, lane = piece & 31, gid = lane >> 2, tid = lane & 3;
-  const uint4 *u = reinterpret_cast<const uint4 *>(packed) + unit * 72;
+  const uint4 *u = reinterpret_cast<const uint4 *>(packed) + unit * (kAsym ? 80 : 72);
   const uint4 cw = u[piece];
   const uint4 sw = u[64 + gid];
+  const uint4 mw = kAsym ? u[72 + gid] : make_uint4(0u, 0u, 0u, 0u);
   const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
   const uint32_t sc[2] = {h ? sw.z : sw.x, h ? sw.w : sw.y};  // groups (0,1), (2,3) of the row
+  const uint32_t mc[2] = {h ? mw.z : mw.x, h ? mw.w : mw.y};
   const int64_t row = tile * 16 + gid + 8 * h;
   uint16_t *dst = out + row * K + c * 128 + tid * 8;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const float scale = (j & 1) ? bf16_hi(sc[j >> 1]) : bf16_lo(sc[j >> 1]);
+    const float mn = (j & 1) ? bf16_hi(mc[j >> 1]) : bf16_lo(mc[j >> 1]);
     uint32_t o[4];
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-      const float lo = static_cast<float>(static_cast<int>(s4_word_nibble(words[j], 2 * b) ^ 8u) - 8) * scale;
-      const float hi = static_cast<float>(static_cast<int>(s4_word_nibble(words[j], 2 * b + 1) ^ 8u) - 8) * scale;
-      o[b] = pack_bf16x2(lo, hi);
+      if constexpr (kAsym) {  // min + scale * code (exact in fp32), rounded once
+        const float lo = fmaf(static_cast<float>(s4_word_nibble(words[j], 2 * b)), scale, mn);
+        const float hi = fmaf(static_cast<float>(s4_word_nibble(words[j], 2 * b + 1)), scale, mn);
+        o[b] = pack_bf16x2(lo, hi);
+      } else {
+        const float lo = static_cast<float>(static_cast<int>(s4_word_nibble(words[j], 2 * b) ^ 8u) - 8) * scale;
+        const float hi = static_cast<float>(static_cast<int>(s4_word_nibble(words[j], 2 * b + 1) ^ 8u) - 8) * scale;
+        o[b] = pack_bf16x2(lo, hi);
+      }
     }
     *reinterpret_cast<uint4 *>(dst + j * 32) = make_uint4(o[0], o[1], o[2], o[3]);
   }
@@ -726,7 +765,7 @@ extern "C" int iron_pack_int4g32(const uint8_t *codes, const uint16_t *scales, u
   if (!aligned16(packed)) return IRON_ERR_ALIGN;
   const int64_t pieces = static_cast<int64_t>(N / 16) * (K / 128) * 72;
   const int threads = 256;
-  pack_s4g32_kernel<<<static_cast<unsigned>((pieces + threads - 1) / threads), threads, 0,
+  pack_s4g32_kernel<false><<<static_cast<unsigned>((pieces + threads - 1) / threads), threads, 0,
                       static_cast<cudaStream_t>(stream)>>>(codes, scales, packed, N, K, pieces);
   return launch_status();
 }
@@ -737,9 +776,47 @@ extern "C" int iron_unpack_int4g32(const uint8_t *packed, uint16_t *out, int N, 
   if (!aligned16(packed) || !aligned16(out)) return IRON_ERR_ALIGN;
   const int64_t pieces = static_cast<int64_t>(N / 16) * (K / 128) * 64;
   const int threads = 256;
-  unpack_s4g32_kernel<<<static_cast<unsigned>((pieces + threads - 1) / threads), threads, 0,
+  unpack_s4g32_kernel<false><<<static_cast<unsigned>((pieces + threads - 1) / threads), threads, 0,
                         static_cast<cudaStream_t>(stream)>>>(packed, out, K, pieces);
   return launch_status();
+}
+
+// q4 weights (asymmetric int4: min + scale * code per 32-k group, IRON's q4nx values).
+extern "C" int iron_pack_q4g32(const uint8_t *codes, const uint16_t *scales, const uint16_t *mins, uint8_t *packed,
+                               int N, int K, void *stream) {
+  if (!codes || !scales || !mins || !packed) return IRON_ERR_NULL;
+  if (N <= 0 || K <= 0 || N % 16 || K % 128) return IRON_ERR_SHAPE;
+  if (!aligned16(packed)) return IRON_ERR_ALIGN;
+  const int64_t pieces = static_cast<int64_t>(N / 16) * (K / 128) * 80;
+  const int threads = 256;
+  pack_s4g32_kernel<true><<<static_cast<unsigned>((pieces + threads - 1) / threads), threads, 0,
+                            static_cast<cudaStream_t>(stream)>>>(codes, scales, packed, N, K, pieces, mins);
+  return launch_status();
+}
+
+extern "C" int iron_unpack_q4g32(const uint8_t *packed, uint16_t *out, int N, int K, void *stream) {
+  if (!packed || !out) return IRON_ERR_NULL;
+  if (N <= 0 || K <= 0 || N % 16 || K % 128) return IRON_ERR_SHAPE;
+  if (!aligned16(packed) || !aligned16(out)) return IRON_ERR_ALIGN;
+  const int64_t pieces = static_cast<int64_t>(N / 16) * (K / 128) * 64;
+  const int threads = 256;
+  unpack_s4g32_kernel<true><<<static_cast<unsigned>((pieces + threads - 1) / threads), threads, 0,
+                              static_cast<cudaStream_t>(stream)>>>(packed, out, K, pieces);
+  return launch_status();
+}
+
+extern "C" int iron_gemv_q4g32(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K, int n_vec,
+                               const uint16_t *residual, unsigned flags, void *stream) {
+  if (!packed || !x || !y) return IRON_ERR_NULL;
+  if (N <= 0 || K <= 0 || n_vec <= 0 || n_vec > 8 || K % 128 || N % 16) return IRON_ERR_SHAPE;
+  if (static_cast<int64_t>(N / 16) * (K / 128) > 0x7fffffffLL) return IRON_ERR_SHAPE;
+  if (!aligned16(packed) || !aligned16(x)) return IRON_ERR_ALIGN;
+  if (flags & IRON_FLAG_SWIGLU) return IRON_ERR_ARG;
+  S4Epi epi{residual, 0, nullptr, 0.f, nullptr, {}, (flags & IRON_FLAG_X_READONLY) ? 1 : 0};
+  epi.ar.world = 1;
+  epi.asym = 1;
+  return launch_s4_tile_cs<1>(packed, x, y, N, K, n_vec, epi, (flags & IRON_FLAG_PDL) != 0,
+                              static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int iron_gemv_int4g32_ex(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,

@@ -28,6 +28,17 @@ __device__ __forceinline__ uint32_t s4x2_dequant_(uint32_t w, uint32_t scale2) {
   return r;
 }
 
+// Unsigned int4 pair -> bf16x2 of min + scale * code, rounded once (fma): OR-ing the
+// nibble into the mantissa of bf16 128.0 gives 128 + code exactly, subtracting 128 is
+// exact, and the fma rounds the exact min + scale * code to bf16.
+__device__ __forceinline__ uint32_t q4x2_dequant_(uint32_t w, uint32_t scale2, uint32_t min2) {
+  uint32_t biased, q, r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(biased) : "r"(w), "r"(0x000f000fu), "r"(0x43004300u));
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(biased), "r"(0x43004300u));
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(q), "r"(scale2), "r"(min2));
+  return r;
+}
+
 // Nibble order of a packed 32-bit code word. Natural order (4 code bytes of one row,
 // element 2b in the low nibble of byte b) holds k_i at bits 4i; the packed word holds
 // k_2q at bits 4q and k_2q+1 at bits 16 + 4q, so that s4x2_dequant_(w >> 4q) is the

@@ -70,11 +70,16 @@ class GEMV(MLIROperator):
             raise ValueError(
                 f"gelu epilogue needs tile_size_output % 16 == 0 (got {self.tile_size_output})"
             )
-        if self.weight_dtype not in ("bf16", "int4g32"):
-            raise ValueError(f"weight_dtype must be 'bf16' or 'int4g32', got {self.weight_dtype!r}")
+        if self.weight_dtype not in ("bf16", "int4g32", "q4nx"):
+            raise ValueError(f"weight_dtype must be 'bf16', 'int4g32' or 'q4nx', got {self.weight_dtype!r}")
         if not 1 <= self.n_vec <= 64:
             raise ValueError(f"n_vec must be in [1, 64], got {self.n_vec}")
-        if self.weight_dtype == "int4g32":
+        if self.weight_dtype == "q4nx":
+            if self.K % 512 or self.M % 64:
+                raise ValueError("q4nx GEMV needs K % 512 == 0 and M % 64 == 0")
+            if self.n_vec > 8:
+                raise ValueError("q4nx GEMV takes at most 8 vectors")
+        if self.weight_dtype in ("int4g32", "q4nx"):
             if self.K % 128 or self.M % 16:
                 raise ValueError("int4g32 GEMV needs K % 128 == 0 and M % 16 == 0")
             if self.num_batches != 1:
@@ -96,9 +101,10 @@ class GEMV(MLIROperator):
 
     def get_arg_spec(self):
         vec = (self.n_vec,) if self.n_vec > 1 else ()
-        if self.weight_dtype == "int4g32":
+        if self.weight_dtype in ("int4g32", "q4nx"):
+            nbytes = self.packed_bytes(self.M, self.K) * (1280 if self.weight_dtype == "q4nx" else 1152) // 1152
             return [
-                AIERuntimeArgSpec("in", (self.packed_bytes(self.M, self.K),), dtype=np.uint8),
+                AIERuntimeArgSpec("in", (nbytes,), dtype=np.uint8),
                 AIERuntimeArgSpec("in", vec + (self.K,)),  # vector(s)
                 AIERuntimeArgSpec("out", vec + (self.M,)),  # output
             ]
@@ -126,9 +132,27 @@ class GEMV(MLIROperator):
                   _lib.current_stream())
         return out
 
+    @staticmethod
+    def pack_q4nx(blob, K: int, N: int):
+        """A q4nx blob (IRON's asymmetric int4: min + scale * code; CUDA uint8) for an
+        N x K matrix -> the packed uint8 buffer the q4nx GEMV streams (1280 B units)."""
+        import torch
+
+        from .q4nx import q4nx_natural
+
+        codes, scales, mins = q4nx_natural(blob, K, N)
+        out = torch.empty((N // 16) * (K // 128) * 1280, dtype=torch.uint8, device=blob.device)
+        _lib.call("iron_pack_q4g32", _lib.dptr(codes), _lib.dptr(scales), _lib.dptr(mins), _lib.dptr(out), N, K,
+                  _lib.current_stream())
+        return out
+
     def _launch(self, *bufs, stream, residual=None, flags=0):
         p = _lib.dptr
         res = p(residual) if residual is not None else None
+        if self.weight_dtype == "q4nx":
+            w, x, y = bufs
+            _lib.call("iron_gemv_q4g32", p(w), p(x), p(y), self.M, self.K, self.n_vec, res, flags, stream)
+            return
         if self.weight_dtype == "int4g32":
             w, x, y = bufs
             _lib.call("iron_gemv_int4g32", p(w), p(x), p(y), self.M, self.K, self.n_vec, res,

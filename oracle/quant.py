@@ -124,3 +124,69 @@ def unpack_s4g32_units(units: np.ndarray, M: int, K: int):
     ss = u[:, :, 1024:].copy().view(np.uint16).reshape(T, C, 8, 2, 4)  # t, c, gid, h, j
     scales = ss.transpose(0, 3, 2, 1, 4).reshape(M, K // 32)
     return codes, scales
+
+
+# ---- q4nx: asymmetric int4, min + scale * code ---------------------------------------
+# The input format of IRON's flm.DequantBFP (iron/operators/flm/dequant/README.md, input
+# layers 1-9; reference iron/operators/flm/dequant/reference.py:40-77): blocks of 32
+# out-features x 256 in-features -- 512 B of bf16 scales [8 groups][32 n], 512 B of bf16
+# mins, 4096 B of codes (two n per byte: even n in the low nibble) -- ordered, for block
+# i, as cb, kb, k_half, n_half (i = ((cb * K/512 + kb) * 2 + k_half) * 2 + n_half).
+Q4NX_M, Q4NX_K, Q4NX_G, Q4NX_KB, Q4NX_PAR = 32, 256, 32, 512, 16
+Q4NX_BLOCK = Q4NX_M * Q4NX_K * 5 // 8
+
+
+def q4nx_to_natural(blob: np.ndarray, K: int, N: int):
+    """q4nx blob -> (codes uint8 [N, K] in 0..15, scale bits uint16 [N, K/32], min bits
+    uint16 [N, K/32]): the block walk of reference.py:40-77, per block."""
+    b = np.asarray(blob, dtype=np.uint8).reshape(-1, Q4NX_BLOCK)
+    n_blocks = b.shape[0]
+    ng = Q4NX_K // Q4NX_G
+    sm = ng * Q4NX_M * 2
+    sc = b[:, :sm].copy().view(np.uint16).reshape(n_blocks, ng, Q4NX_M)
+    mn = b[:, sm:2 * sm].copy().view(np.uint16).reshape(n_blocks, ng, Q4NX_M)
+    qs = b[:, 2 * sm:].reshape(n_blocks, Q4NX_M // Q4NX_PAR, Q4NX_K, Q4NX_PAR // 2)
+    q = np.empty((n_blocks, Q4NX_M // Q4NX_PAR, Q4NX_K, Q4NX_PAR), dtype=np.uint8)
+    q[..., 0::2] = qs & 0xF
+    q[..., 1::2] = qs >> 4
+    q = q.transpose(0, 1, 3, 2).reshape(n_blocks, Q4NX_M, Q4NX_K)
+    k_tiles = K // Q4NX_KB
+    codes = np.zeros((N, K), dtype=np.uint8)
+    sbits = np.zeros((N, K // Q4NX_G), dtype=np.uint16)
+    mbits = np.zeros_like(sbits)
+    for i in range(n_blocks):
+        cb, rest = divmod(i, 4 * k_tiles)
+        kb, rest = divmod(rest, 4)
+        k_half, n_half = divmod(rest, 2)
+        r0, c0 = (2 * cb + n_half) * Q4NX_M, (2 * kb + k_half) * Q4NX_K
+        codes[r0:r0 + Q4NX_M, c0:c0 + Q4NX_K] = q[i]
+        sbits[r0:r0 + Q4NX_M, c0 // Q4NX_G:c0 // Q4NX_G + ng] = sc[i].T
+        mbits[r0:r0 + Q4NX_M, c0 // Q4NX_G:c0 // Q4NX_G + ng] = mn[i].T
+    return codes, sbits, mbits
+
+
+def q4nx_dequant(codes: np.ndarray, sbits: np.ndarray, mbits: np.ndarray) -> np.ndarray:
+    """fp32 [N, K] = min + scale * code, as reference.py computes it."""
+    s = np.repeat(bf16_bits_to_f32(sbits), Q4NX_G, axis=1)
+    m = np.repeat(bf16_bits_to_f32(mbits), Q4NX_G, axis=1)
+    return (m + s * codes.astype(np.float32)).astype(np.float32)
+
+
+def q4nx_from_natural(codes: np.ndarray, sbits: np.ndarray, mbits: np.ndarray) -> np.ndarray:
+    """Inverse of q4nx_to_natural (builds blobs for tests)."""
+    N, K = codes.shape
+    k_tiles = K // Q4NX_KB
+    n_blocks = (N // Q4NX_M) * (K // Q4NX_K)
+    ng = Q4NX_K // Q4NX_G
+    out = np.empty((n_blocks, Q4NX_BLOCK), dtype=np.uint8)
+    for i in range(n_blocks):
+        cb, rest = divmod(i, 4 * k_tiles)
+        kb, rest = divmod(rest, 4)
+        k_half, n_half = divmod(rest, 2)
+        r0, c0 = (2 * cb + n_half) * Q4NX_M, (2 * kb + k_half) * Q4NX_K
+        q = codes[r0:r0 + Q4NX_M, c0:c0 + Q4NX_K].reshape(Q4NX_M // Q4NX_PAR, Q4NX_PAR, Q4NX_K).transpose(0, 2, 1)
+        qs = (q[..., 0::2] & 0xF) | ((q[..., 1::2] & 0xF) << 4)
+        s = np.ascontiguousarray(sbits[r0:r0 + Q4NX_M, c0 // Q4NX_G:c0 // Q4NX_G + ng].T).view(np.uint8)
+        m = np.ascontiguousarray(mbits[r0:r0 + Q4NX_M, c0 // Q4NX_G:c0 // Q4NX_G + ng].T).view(np.uint8)
+        out[i] = np.concatenate([s.reshape(-1), m.reshape(-1), qs.astype(np.uint8).reshape(-1)])
+    return out.reshape(-1)

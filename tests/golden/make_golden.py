@@ -228,13 +228,45 @@ def gemm_fixtures(ref: Path):
         _save(f"flm_gemm_{epi}{tag}_M128_K512_N128", A=d["input"], B=d["input_b"], C=d["output"])
 
 
+def q4nx_fixtures(ref: Path):
+    """q4nx goldens (the asymmetric int4 input format: min + scale * code): IRON's own
+    iron/operators/flm/dequant/reference.py generates a blob (random_q4nx) and
+    dequantizes it (dequantize, fp32). Its design module needs mlir_aie; a module holding
+    only the geometry constants it imports stands in (values from
+    iron/operators/flm/dequant/design.py and iron/operators/flm/gemm/design.py:51-67),
+    and pack_b (unused by these two functions) is stubbed."""
+    for mname in ("iron", "iron.operators", "iron.operators.flm", "iron.operators.flm.dequant"):
+        sys.modules.setdefault(mname, types.ModuleType(mname))
+    design = types.ModuleType("iron.operators.flm.dequant.design")
+    design.M_TILE, design.K_TILE, design.GROUP = 32, 256, 32
+    design.K_TILE_B, design.N_TILE, design.S, design.T, design.CT_K = 512, 64, 8, 8, 128
+
+    def qw_bytes_for(K, N, run_out_features=None, run_period_out_features=None):
+        raise RuntimeError("not used by the fixtures")
+
+    design.qw_bytes_for = qw_bytes_for
+    sys.modules["iron.operators.flm.dequant.design"] = design
+    packing = types.ModuleType("iron.operators.flm.packing")
+    packing.pack_b = qw_bytes_for
+    sys.modules["iron.operators.flm.packing"] = packing
+    qm = _load(ref, "iron/operators/flm/dequant/reference.py", "ref_q4nx")
+    for K, N, seed in [(1024, 128, 0), (512, 192, 1)]:
+        blob = qm.random_q4nx(K, N, seed=seed)
+        w = qm.dequantize(blob, K, N)
+        _save(f"q4nx_K{K}_N{N}", blob=blob, w=np.asarray(w, dtype=np.float32), dims=np.array([K, N]))
+
+
 if __name__ == "__main__":
     import os
 
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
     src = args[0] if args else os.environ.get("IRON_REFERENCE_DIR")
     if not src:
-        sys.exit("usage: make_golden.py <path to the IRON checkout> [--only-gemm]")
+        sys.exit("usage: make_golden.py <path to the IRON checkout> [--only-gemm | --only-q4nx]")
+    if "--only-q4nx" in sys.argv:
+        q4nx_fixtures(Path(src))
+        sys.exit(0)
     if "--only-gemm" not in sys.argv:
         main(Path(src))
     gemm_fixtures(Path(src))
+    q4nx_fixtures(Path(src))

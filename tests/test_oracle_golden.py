@@ -214,3 +214,33 @@ def test_flm_gemm_matches_golden(epi, clamp):
     d = {k: bf16(v) for k, v in load(f"flm_gemm_{epi}{tag}_M128_K512_N128").items()}
     got = ops.flm_gemm(d["A"], d["B"], epi, clamp)
     assert_close(got, d["C"], 0.005, 0.005, what=epi)
+
+
+@pytest.mark.parametrize("name", ["q4nx_K1024_N128", "q4nx_K512_N192"])
+def test_q4nx_restatement_matches_iron(name):
+    """The q4nx block walk restated in oracle/quant.py gives IRON's own dequantized values
+    bit for bit (fixture from iron/operators/flm/dequant/reference.py: random_q4nx and
+    dequantize), and its inverse rebuilds the blob byte for byte."""
+    from oracle import quant
+
+    d = load(name)
+    K, N = (int(v) for v in d["dims"])
+    codes, sbits, mbits = quant.q4nx_to_natural(d["blob"], K, N)
+    assert np.array_equal(quant.q4nx_dequant(codes, sbits, mbits), d["w"])
+    assert np.array_equal(quant.q4nx_from_natural(codes, sbits, mbits), d["blob"])
+
+
+@pytest.mark.parametrize("name", ["q4nx_K1024_N128", "q4nx_K512_N192"])
+def test_q4nx_importer_matches_restatement(name):
+    """The product's q4nx importer (torch index arithmetic, run here on the CPU) yields the
+    restatement's natural arrays: codes two per byte, bf16 scales and mins."""
+    from iron_b200.operators.gemv.q4nx import q4nx_natural
+    from oracle import quant
+
+    d = load(name)
+    K, N = (int(v) for v in d["dims"])
+    codes, scales, mins = q4nx_natural(torch.from_numpy(d["blob"]), K, N)
+    oc, osb, omb = quant.q4nx_to_natural(d["blob"], K, N)
+    assert np.array_equal(codes.numpy(), (oc[:, 0::2] | (oc[:, 1::2] << 4)).astype(np.uint8))
+    assert np.array_equal(scales.view(torch.int16).numpy().view(np.uint16), osb)
+    assert np.array_equal(mins.view(torch.int16).numpy().view(np.uint16), omb)
