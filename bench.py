@@ -923,6 +923,20 @@ def run_tp_block(args, world, rank, local):
     fused = world > 1 and B <= 8 and args.allreduce != "nccl"
     if args.allreduce == "fused" and not fused:
         raise SystemExit("--allreduce fused needs more than one GPU and batch <= 8")
+    # with more than one GPU and the default all-reduce, the NCCL form is timed too and
+    # reported beside the fused one (every rank takes the same steps in the same order)
+    other_us = None
+    if world > 1 and fused and args.allreduce == "auto":
+        other_us = _time_tp_block(args, shape, world, rank, B, ctx, fused=False)[0]
+    us, ms_max, ms, clocks, blk = _time_tp_block(args, shape, world, rank, B, ctx, fused=fused, local=local)
+    _tp_block_line(args, shape, world, rank, B, ctx, fused, us, ms_max, ms, clocks, blk, other_us)
+
+
+def _time_tp_block(args, shape, world, rank, B, ctx, fused, local=None):
+    """Build, capture and time one tensor-parallel block form; returns (us per block,
+    max-over-ranks ms, this rank's ms, clocks, block or None once released)."""
+    from iron_b200.applications.llama3_8b.tp_block import TPDecoderBlock
+
     blk = TPDecoderBlock(shape, world, rank, B, ctx + 16, seed=13, pdl=not args.no_pdl, fused_allreduce=fused)
     g = torch.Generator(device="cuda")
     g.manual_seed(7 + rank)
@@ -936,7 +950,7 @@ def run_tp_block(args, world, rank, local):
     for i in range(args.warmup):
         blk.step()
     torch.cuda.synchronize()
-    sampler = ClockSampler(local) if rank == 0 else None
+    sampler = ClockSampler(local) if (rank == 0 and local is not None) else None
     if sampler:
         sampler.start()
         time.sleep(0.3)
@@ -957,6 +971,17 @@ def run_tp_block(args, world, rank, local):
     ms = e0.elapsed_time(e1)
     ms_max = _max_over_ranks(ms, world)
     clocks = sampler.stop() if sampler else None
+    blk.check_status()
+    if local is None:  # the other form: release it before the measured one is built
+        blk.release()
+        torch.cuda.synchronize()
+        return ms_max * 1e3 / args.steps, ms_max, ms, None, None
+    return ms_max * 1e3 / args.steps, ms_max, ms, clocks, blk
+
+
+def _tp_block_line(args, shape, world, rank, B, ctx, fused, us, ms_max, ms, clocks, blk, other_us):
+    import torch.distributed as dist
+
     # the all-reduce alone, same message, same number per step
     ar_us = None
     if world > 1:
@@ -973,7 +998,6 @@ def run_tp_block(args, world, rank, local):
         a1.record()
         a1.synchronize()
         ar_us = _max_over_ranks(a0.elapsed_time(a1) * 1e3 / n, world)
-    us = ms_max * 1e3 / args.steps
     bytes_rank = blk.weight_bytes() + blk.kv_bytes([ctx] * B) + B * blk.hk * shape.head_dim * 2 * 2
     peak, _ = _peak_hbm()
     achieved = bytes_rank / (ms / args.steps * 1e-3) / 1e9
@@ -988,18 +1012,61 @@ def run_tp_block(args, world, rank, local):
                                      if fused else "NCCL bf16 sum of [B, 4096], 2 per block"),
                        "parallelism": f"tp{world}"},
             "us_per_block": round(us, 2),
+            "us_per_block_by_allreduce": ({"fused": round(us, 2), "nccl": round(other_us, 2)}
+                                          if other_us is not None else None),
             "nccl_allreduce_us": round(ar_us, 2) if ar_us is not None else None,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": None,
                          "scope": "one rank's block step (its weight shard + kv heads)",
                          "algorithmic_bytes_per_step": int(bytes_rank)},
             "gpu_launches": blk.kernels_per_step() * args.steps, "clocks": clocks, "e2e": None}
-    blk.check_status()
     blk.release()
+    if rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = _cpu_tp_block(B, ctx, steps=3)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def _cpu_tp_block(B, ctx, steps=3, seed=3):
+    """The Llama-3-8B block's decode step on the host cores: llama_cpu.py's block (restated
+    in oracle/llama.py) on the bf16 values of int4 group-32 weights, KV cache at `ctx`."""
+    from iron_b200.applications.llama3_8b.sharding import BlockShape
+    from oracle import llama as ollama
+    from oracle import ops
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    s = BlockShape()
+    gen = torch.Generator()
+    gen.manual_seed(seed)
+    E, F, Hd = s.hidden, s.ffn, s.head_dim
+
+    def w(o, i):
+        q = torch.randint(-8, 8, (o, i), generator=gen, dtype=torch.int8).float()
+        sc = (torch.rand(o, i // 32, generator=gen) * 0.003 + 0.001).to(torch.bfloat16).float()
+        return (q * sc.repeat_interleave(32, dim=1)).to(torch.bfloat16)
+
+    W = {"n1": torch.ones(E, dtype=torch.bfloat16), "n2": torch.ones(E, dtype=torch.bfloat16),
+         "q": w(s.n_heads * Hd, E), "k": w(s.n_kv * Hd, E), "v": w(s.n_kv * Hd, E), "o": w(E, s.n_heads * Hd),
+         "g": w(F, E), "u": w(F, E), "d": w(E, F)}
+    kc = torch.randn(B, s.n_kv, ctx + 8, Hd, generator=gen).to(torch.bfloat16)
+    vc = torch.randn(B, s.n_kv, ctx + 8, Hd, generator=gen).to(torch.bfloat16)
+    x = torch.randn(B, E, generator=gen).to(torch.bfloat16)
+    angles = ops.rope_angles(Hd, ctx + 8, s.rope_base)
+
+    def step():
+        return ollama.block_decode(x, kc, vc, [ctx] * B, W, angles, s.n_heads, s.n_kv, Hd, s.eps)
+
+    step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = (time.perf_counter() - t0) / steps
+    return {"value": float(f"{B / dt:.4g}"), "unit": "tok/s through one block", "cores": torch.get_num_threads(),
+            "kind": "port", "us_per_block": round(dt * 1e6, 1),
+            "sample": f"{steps} decode steps of the whole (unsharded) Llama-3-8B block at batch {B}, context {ctx}: "
+                      f"llama_cpu.py's block restated in torch on int4-valued bf16 weights"}
 
 
 # ---- decoder block with bf16 weights (config 3) --------------------------------------------
@@ -1296,7 +1363,14 @@ def run_reference_extra(args, world, rank):
     if rank != 0:
         return
     steps = max(1, min(args.steps, 5))
-    if args.workload == "block":
+    if args.workload == "tp_block":
+        cb = _cpu_tp_block(args.batch, PREFIX, steps=steps)
+        value, unit, ms = cb["value"], cb["unit"], cb["us_per_block"] * 1e-3
+        cfg = {"workload": "tp_block (BASELINE config 5, Llama-3-8B block)", "batch": args.batch, "context": PREFIX,
+               "tp": 1}
+        sample, threads = cb["sample"], cb["cores"]
+        metric = "Llama-3-8B block decode step, tensor-parallel"
+    elif args.workload == "block":
         cb = _cpu_block(args.batch, _block_positions(args.batch), steps=steps)
         value, unit, ms = cb["value"], "GB/s", cb["ms_per_step"]
         cfg = {"workload": "block (BASELINE config 3)", "batch": args.batch}
@@ -1311,7 +1385,8 @@ def run_reference_extra(args, world, rank):
         metric = "GQA decode attention achieved HBM GB/s"
     line = {"impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": world,
             "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)", "config": cfg,
+            "scaling": "strong" if args.workload == "tp_block" else "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded)", "config": cfg,
             "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -1324,7 +1399,7 @@ def main():
         rank = int(os.environ.get("RANK", "0"))
         if args.workload == "decode":
             run_reference_decode(args, world, rank)
-        elif args.workload in ("block", "attention"):
+        elif args.workload in ("block", "attention", "tp_block"):
             run_reference_extra(args, world, rank)
         else:
             run_reference(args, world, rank)

@@ -22,7 +22,7 @@ def _bench(*args, env=None, timeout=240):
                           capture_output=True, text=True, timeout=timeout)
 
 
-@pytest.mark.parametrize("workload", ["decode", "bf16_gemv", "int4_gemv", "block", "attention"])
+@pytest.mark.parametrize("workload", ["decode", "bf16_gemv", "int4_gemv", "block", "attention", "tp_block"])
 def test_reference_arm_prints_one_contract_line(workload):
     r = _bench("--impl", "reference", "--workload", workload, "--steps", "1", "--warmup", "3")
     assert r.returncode == 0, r.stderr[-2000:]
