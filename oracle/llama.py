@@ -19,19 +19,39 @@ from . import ops
 BF16 = torch.bfloat16
 
 
-def block_decode(x, k_cache, v_cache, pos, W, angles, n_heads, n_kv, head_dim, eps=1e-5):
+def _normed_gemv(W, x, w, eps, fold):
+    """GEMV of the RMSNorm of x. fold=False: IRON's order, gemv(W, bf16(x * inv * w)).
+    fold=True: the RMSNorm folded into the GEMV as the B200 decode chain does it --
+    bf16(inv * (W . bf16(x * w))), inv = 1 / sqrt(mean(x^2) + eps) from the bf16 x."""
+    if not fold:
+        return ops.gemv_multi(W, ops.rms_norm(x, w, eps))
+    xf = ops._f(x)
+    inv = 1.0 / torch.sqrt((xf * xf).mean(-1, keepdim=True) + eps)
+    xw = (xf * ops._f(w)).to(BF16)
+    return ((ops._f(xw) @ ops._f(W).T) * inv).to(ops._OUT[0])
+
+
+def _normed_swiglu(Wg, Wu, x, w, eps, fold):
+    """SwiGLU of the gate / up projections of the RMSNorm of x (fold as in _normed_gemv)."""
+    if not fold:
+        xn = ops.rms_norm(x, w, eps)
+        return ops.swiglu_act(ops.gemv_multi(Wg, xn), ops.gemv_multi(Wu, xn))
+    return ops.swiglu_act(_normed_gemv(Wg, x, w, eps, True), _normed_gemv(Wu, x, w, eps, True))
+
+
+def block_decode(x, k_cache, v_cache, pos, W, angles, n_heads, n_kv, head_dim, eps=1e-5, fold=False):
     """One decode step of one block for a batch of sequences.
 
     x [B, E] bf16; caches [B, n_kv, Lmax, hd] bf16 (updated in place at slot pos[b]);
     pos [B] ints (tokens already cached); W dict of bf16 weights with keys
     n1 q k v o n2 g u d (linear weights [out, in]); angles [ctx, hd] table.
+    fold: the RMSNorms folded into the GEMVs' rounding points (_normed_gemv).
     Returns the block output [B, E] bf16.
     """
     B, E = x.shape
-    xn = ops.rms_norm(x, W["n1"], eps)
-    q = ops.gemv_multi(W["q"], xn).view(B, n_heads, head_dim)
-    k = ops.gemv_multi(W["k"], xn).view(B, n_kv, head_dim)
-    v = ops.gemv_multi(W["v"], xn).view(B, n_kv, head_dim)
+    q = _normed_gemv(W["q"], x, W["n1"], eps, fold).view(B, n_heads, head_dim)
+    k = _normed_gemv(W["k"], x, W["n1"], eps, fold).view(B, n_kv, head_dim)
+    v = _normed_gemv(W["v"], x, W["n1"], eps, fold).view(B, n_kv, head_dim)
     lens = []
     for b in range(B):
         p = int(pos[b])
@@ -43,8 +63,7 @@ def block_decode(x, k_cache, v_cache, pos, W, angles, n_heads, n_kv, head_dim, e
         lens.append(p + 1)
     attn = ops.attn_decode(q, k_cache, v_cache, lens).reshape(B, n_heads * head_dim)
     h = ops.add(x, ops.gemv_multi(W["o"], attn))
-    hn = ops.rms_norm(h, W["n2"], eps)
-    act = ops.swiglu_act(ops.gemv_multi(W["g"], hn), ops.gemv_multi(W["u"], hn))
+    act = _normed_swiglu(W["g"], W["u"], h, W["n2"], eps, fold)
     return ops.add(h, ops.gemv_multi(W["d"], act))
 
 
@@ -107,13 +126,17 @@ def block_mlp_half(x, k_cache, v_cache, pos, W, angles, n_heads, n_kv, head_dim,
 
 
 def model_decode(tokens, pos, layers, nf, embed, lm, k_caches, v_caches, angles, n_heads, n_kv,
-                 head_dim, eps=1e-5):
+                 head_dim, eps=1e-5, fold=False, hidden=None):
     """One greedy decode step of the whole model (llama_cpu.py:221-285, decode form):
-    embedding, the blocks, final RMSNorm, lm-head. Returns logits [B, V] (bf16)."""
+    embedding, the blocks, final RMSNorm, lm-head. Returns logits [B, V] (bf16).
+    fold: the RMSNorms at the B200 decode chain's rounding points (_normed_gemv).
+    hidden: a list that receives each block's output (the residual stream)."""
     x = embed[torch.as_tensor(tokens, dtype=torch.long)].clone()
     for li, W in enumerate(layers):
-        x = block_decode(x, k_caches[li], v_caches[li], pos, W, angles, n_heads, n_kv, head_dim, eps)
-    return ops.gemv_multi(lm, ops.rms_norm(x, nf, eps))
+        x = block_decode(x, k_caches[li], v_caches[li], pos, W, angles, n_heads, n_kv, head_dim, eps, fold)
+        if hidden is not None:
+            hidden.append(x)
+    return _normed_gemv(lm, x, nf, eps, fold)
 
 
 def model_prefill(tokens, layers, nf, embed, lm, k_caches, v_caches, angles, n_heads, n_kv, head_dim,

@@ -57,14 +57,25 @@ def test_decode_step_matches_oracle(batch, prefix, fuse):
     vcs = [vc0[i].clone() for i in range(shape.n_layers)]
     lm_cpu = eng.lm.dequant().cpu()
 
-    def oracle_step(kc_out=None, vc_out=None):
+    # the chained engine folds the RMSNorms into its GEMVs: the oracle at the same rounding
+    # points (oracle.llama._normed_gemv); IRON's own order is checked by the KL bound below
+    fold = eng.fuse_norm == "chain"
+
+    def oracle_step(kc_out=None, vc_out=None, hidden=None, fold_=fold):
         kk = [k.clone() for k in kcs] if kc_out is None else kc_out
         vv = [v.clone() for v in vcs] if vc_out is None else vc_out
         return ollama.model_decode(toks, prefix, W, eng.nf.cpu(), eng.embed_table.cpu(), lm_cpu, kk, vv,
-                                   eng.lut.cpu(), shape.n_heads, shape.n_kv_groups, shape.head_dim)
+                                   eng.lut.cpu(), shape.n_heads, shape.n_kv_groups, shape.head_dim, fold=fold_,
+                                   hidden=hidden)
 
     logits, well = conditioned_rows(oracle_step, 2e-2, 1e-2)
-    oracle_step(kcs, vcs)  # the oracle's appended cache rows, for the row checks below
+    hid = []
+    oracle_step(kcs, vcs, hidden=hid)  # the oracle's appended cache rows, for the row checks below
+    # a sequence whose residual stream ends as a near-cancellation of far larger terms
+    # (final RMS < 5 % of the largest block output's) turns one-ulp differences of those
+    # terms into errors of its own size: not held to the elementwise bar
+    rms = torch.stack([h.float().pow(2).mean(-1).sqrt() for h in hid])
+    well = well & (rms[-1] > 0.05 * rms.max(0).values)
     # 1. The last layer's attention and the lm-head recomputed by the oracle on the
     # engine's OWN inputs (its QKV projection and caches; its final hidden state): every
     # output within the north star's bar, no exceptions -- the kernels' parity, free of
@@ -80,12 +91,12 @@ def test_decode_step_matches_oracle(batch, prefix, fuse):
     head = ops.gemv_multi(lm, ops.rms_norm(eng.x.cpu(), eng.nf.cpu(), shape.eps))
     assert_close(eng.logits.cpu(), head, 2e-2, 1e-2, what="lm-head on the engine's hidden state")
     # 2. End to end against the oracle's own chain, for every sequence whose oracle result
-    # is stable under fp64 sums (helpers.conditioned_rows): every logit within the bar.
-    # Sequences that are not (measured on B200 at batch 8: position 63, whose hidden
-    # state after layer 1 nearly cancels -- RMS 0.25 against ~40 for the others -- and
-    # whose logits then move by up to 0.2 between correct implementations) are held to
-    # the distribution check only: IRON's own app-level bound is a KL bound
-    # (iron/applications/llama_3.2_1b/test.py:77-113).
+    # is stable under fp64 sums (helpers.conditioned_rows) and whose residual stream does
+    # not cancel: every logit within the bar. The others (measured on B200 at batch 8:
+    # position 63, whose hidden state after layer 1 nearly cancels -- RMS 0.25 against ~40
+    # for the others -- and whose logits then move by up to 0.2 between correct
+    # implementations) are held to the distribution check only: IRON's own app-level bound
+    # is a KL bound (iron/applications/llama_3.2_1b/test.py:77-113).
     d = (eng.logits.cpu().float() - logits.float()).abs()
     bad = d >= torch.maximum(torch.full_like(d, 1e-2), 2e-2 * (eng.logits.cpu().float().abs() + logits.float().abs()))
     print(f"batch {batch} {fuse}: per sequence (pos, well-conditioned, outside 2e-2 / 1e-2, max |diff|): "
@@ -96,6 +107,11 @@ def test_decode_step_matches_oracle(batch, prefix, fuse):
     kl = (lp.exp() * (lp - torch.log_softmax(eng.logits.cpu().float(), -1))).sum(-1)
     assert float(kl[well].max()) < 1e-3, kl
     assert float(kl.max()) <= 0.05, kl
+    if fold:  # and the distributions against IRON's operator order (rms_norm, then the GEMV)
+        iron_order = oracle_step(fold_=False)
+        lp = torch.log_softmax(iron_order.float(), -1)
+        kl2 = (lp.exp() * (lp - torch.log_softmax(eng.logits.cpu().float(), -1))).sum(-1)
+        assert float(kl2[well].max()) < 1e-3, kl2
     # caches got the new rows, positions advanced, greedy token consistent
     # (layer 0's rows for every sequence; deeper rows for the well-conditioned ones)
     for li in range(shape.n_layers):

@@ -50,10 +50,11 @@ def test_q4nx_gemv_matches_oracle(case, n_vec):
     res = torch.randn(n_vec, N, generator=g).to(torch.bfloat16)
     y = torch.empty(n_vec, N, dtype=torch.bfloat16, device="cuda")
     yr = torch.empty_like(y)
+    xd, rd = x.cuda(), res.cuda()  # held: the kernels read them after the calls return
     op = GEMV(M=N, K=K, weight_dtype="q4nx", n_vec=n_vec)
-    op.get_callable()(packed, x.cuda(), y)
-    _lib.call("iron_gemv_q4g32", packed.data_ptr(), x.cuda().data_ptr(), yr.data_ptr(), N, K, n_vec,
-              res.cuda().data_ptr(), 0, _lib.current_stream())
+    op.get_callable()(packed, xd, y)
+    _lib.call("iron_gemv_q4g32", packed.data_ptr(), xd.data_ptr(), yr.data_ptr(), N, K, n_vec, rd.data_ptr(), 0,
+              _lib.current_stream())
     torch.cuda.synchronize()
     assert torch.equal(got_w.cpu().view(torch.int16), wb.view(torch.int16)), "dequantized q4nx weights differ"
     ref = ops.gemv_multi(wb, x)
