@@ -29,6 +29,13 @@ namespace cg = cooperative_groups;
 // Head dims: 64 (Llama-3.2-1B; IRON's MHA supports d = 64 only, mha/op.py:39-41) and
 // 128 (the Llama-3-8B block).
 constexpr int kAWarps = 4;
+// warps per CTA in the cluster form at head_dim 64: one 16-token block per warp, every
+// block of a split of up to 192 tokens requested before the wait (B200, batch 1 at 2048
+// tokens: the 4-warp CTA walked 3 blocks per warp, two of them after the wait -- 2.6 us
+// of a 5.7 us attention). head_dim 128 keeps 4 warps (registers and shared memory).
+constexpr int kAClusterWarps = 12;
+template <int kAD>
+constexpr int attn_cluster_warps() { return kAD == 64 ? kAClusterWarps : kAWarps; }
 constexpr int kABlk = 16;     // tokens per warp step
 constexpr int kAMinChunk = 64;   // tokens per split at least
 constexpr int kAMaxSplits = 64;  // splits per sequence at most (the combine holds one value per split)
@@ -78,17 +85,19 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void *smem
 // shared memory and rank 0 merges them in rank order after one cluster barrier -- no
 // workspace, no second kernel.
 template <int kAD, bool kFused = false, int kCS = 1>
-__global__ void __launch_bounds__(32 * kAWarps)
+__global__ void __launch_bounds__(32 * ((kCS > 1 && kAD == 64) ? kAClusterWarps : kAWarps))
 attn_decode_kernel(AttnArgs a) {
+  constexpr int kW = (kCS > 1 && kAD == 64) ? kAClusterWarps : kAWarps;  // warps of this CTA
+  constexpr int kG = kCS > 1 ? 4 : 16;                    // query-head rows kept per warp (the cluster form: g <= 4)
   constexpr int kAVStride = kAD + 8;  // padded V tile row: an odd number of 16-byte chunks
-  constexpr int kVBytes = kAWarps * kABlk * kAVStride * 2;
-  constexpr int kOBytes = kAWarps * 16 * kAD * 4;
+  constexpr int kVBytes = kW * kABlk * kAVStride * 2;
+  constexpr int kOBytes = kW * kG * kAD * 4;
   // the V tiles (loop) and the warp-merge buffer (after it) share the storage
   __shared__ __align__(16) uint8_t smem[kVBytes > kOBytes ? kVBytes : kOBytes];
-  __shared__ float red_m[kAWarps][16], red_l[kAWarps][16];
+  __shared__ float red_m[kW][16], red_l[kW][16];
   extern __shared__ __align__(16) float cbuf[];  // kCS > 1 (rank 0): [kCS][g][2 + kAD]
   uint16_t (*vtile)[kABlk * kAVStride] = reinterpret_cast<uint16_t (*)[kABlk * kAVStride]>(smem);
-  float (*red_o)[16][kAD] = reinterpret_cast<float (*)[16][kAD]>(smem);
+  float (*red_o)[kG][kAD] = reinterpret_cast<float (*)[kG][kAD]>(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tid = lane & 3;
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -154,7 +163,7 @@ attn_decode_kernel(AttnArgs a) {
   if (blk < t_end) load_block(blk, kr, vr, false);
   if constexpr (kFused) {
     // the split's further cached rows into L2, then wait for the QKV projection
-    const int r0 = t_begin + kAWarps * kABlk, r1 = min(t_end, p);
+    const int r0 = t_begin + kW * kABlk, r1 = min(t_end, p);
     if (a.l2_prefetch && threadIdx.x == 0 && r1 > r0) {
       const uint32_t bytes = static_cast<uint32_t>(r1 - r0) * kAD * 2;
       asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(kb + static_cast<int64_t>(r0) * kAD), "r"(bytes)
@@ -175,11 +184,11 @@ attn_decode_kernel(AttnArgs a) {
     const float *ang = a.lut + static_cast<int64_t>(p) * kAD;
     const bool owner = valid && t_begin <= p && p < t_begin + a.chunk;
     // zero rows g..15 of the q tile (no loads)
-    for (int i = g * kAD + threadIdx.x * 8; i < 16 * kAD; i += 32 * kAWarps * 8)
+    for (int i = g * kAD + threadIdx.x * 8; i < 16 * kAD; i += 32 * kW * 8)
       *reinterpret_cast<uint4 *>(qbuf + i) = make_uint4(0u, 0u, 0u, 0u);
     // one pass: every thread issues the loads of its q pair and (the first `half`
     // threads) of its new k / v pair before using any of them -- one L2 round trip
-    for (int i0 = 0; i0 < g * half || i0 < half; i0 += 32 * kAWarps) {
+    for (int i0 = 0; i0 < g * half || i0 < half; i0 += 32 * kW) {
       const int i = i0 + threadIdx.x;
       const bool hq_ = i < g * half, hk_ = i < half;
       const int r = hq_ ? i / half : 0, jq = hq_ ? i % half : 0;
@@ -253,7 +262,7 @@ attn_decode_kernel(AttnArgs a) {
   float l_lo = 0.f, l_hi = 0.f;              // this lane's share of the running sums
   uint16_t *vs = vtile[warp];
 
-  for (; blk < t_end; blk += kAWarps * kABlk) {
+  for (; blk < t_end; blk += kW * kABlk) {
     // stage V, then prefetch the next block while this one computes
 #pragma unroll
     for (int i = 0; i < kVR; ++i) {
@@ -265,7 +274,7 @@ attn_decode_kernel(AttnArgs a) {
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int db = 0; db < kDB; ++db) kc[nt][db] = kr[nt][db];
-    const int nxt = blk + kAWarps * kABlk;
+    const int nxt = blk + kW * kABlk;
     if (nxt < t_end) load_block(nxt, kr, vr, true);
 
     // S = Q K^T for the two 8-token halves
@@ -338,7 +347,7 @@ attn_decode_kernel(AttnArgs a) {
     l_lo += __shfl_xor_sync(0xffffffffu, l_lo, o_);
     l_hi += __shfl_xor_sync(0xffffffffu, l_hi, o_);
   }
-  // merge the four warps (red_o reuses the V tiles: every warp must be done with them)
+  // merge the warps (red_o reuses the V tiles: every warp must be done with them)
   __syncthreads();
   if (tid == 0) {
     red_m[warp][gid] = m_lo; red_m[warp][gid + 8] = m_hi;
@@ -346,21 +355,25 @@ attn_decode_kernel(AttnArgs a) {
   }
 #pragma unroll
   for (int j = 0; j < kAD / 8; ++j) {
-    red_o[warp][gid][8 * j + 2 * tid] = o[j][0];
-    red_o[warp][gid][8 * j + 2 * tid + 1] = o[j][1];
-    red_o[warp][gid + 8][8 * j + 2 * tid] = o[j][2];
-    red_o[warp][gid + 8][8 * j + 2 * tid + 1] = o[j][3];
+    if (gid < kG) {
+      red_o[warp][gid][8 * j + 2 * tid] = o[j][0];
+      red_o[warp][gid][8 * j + 2 * tid + 1] = o[j][1];
+    }
+    if (gid + 8 < kG) {
+      red_o[warp][gid + 8 < kG ? gid + 8 : 0][8 * j + 2 * tid] = o[j][2];
+      red_o[warp][gid + 8 < kG ? gid + 8 : 0][8 * j + 2 * tid + 1] = o[j][3];
+    }
   }
   __syncthreads();
   for (int idx = threadIdx.x; idx < g * kAD; idx += blockDim.x) {
     const int r = idx / kAD, d = idx % kAD;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kAWarps; ++w) M = fmaxf(M, red_m[w][r]);
+    for (int w = 0; w < kW; ++w) M = fmaxf(M, red_m[w][r]);
     float L = 0.f, O = 0.f;
     if (M != -INFINITY) {
 #pragma unroll
-      for (int w = 0; w < kAWarps; ++w) {
+      for (int w = 0; w < kW; ++w) {
         const float f = exp2f(red_m[w][r] - M);
         L += red_l[w][r] * f;
         O += red_o[w][r][d] * f;
@@ -558,11 +571,11 @@ static int launch_attn_cluster_cs(AttnArgs a, int B, int Hkv, int Lmax, bool pdl
   });
   if (cst != IRON_OK) return cst;
   a.splits = kCS;
-  a.chunk = ((Lmax + kCS - 1) / kCS + kAWarps * kABlk - 1) / (kAWarps * kABlk) * (kAWarps * kABlk);
+  a.chunk = ((Lmax + kCS - 1) / kCS + kABlk - 1) / kABlk * kABlk;  // whole 16-token blocks
   a.ws = nullptr;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(kCS, Hkv, B);
-  cfg.blockDim = dim3(32 * kAWarps);
+  cfg.blockDim = dim3(32 * attn_cluster_warps<kAD>());
   cfg.dynamicSmemBytes = static_cast<size_t>(kCS) * (a.Hq / a.Hkv) * (2 + kAD) * sizeof(float);
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
