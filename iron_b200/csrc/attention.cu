@@ -29,13 +29,19 @@ namespace cg = cooperative_groups;
 // Head dims: 64 (Llama-3.2-1B; IRON's MHA supports d = 64 only, mha/op.py:39-41) and
 // 128 (the Llama-3-8B block).
 constexpr int kAWarps = 4;
-// warps per CTA in the cluster form at head_dim 64: one 16-token block per warp, every
-// block of a split of up to 192 tokens requested before the wait (B200, batch 1 at 2048
-// tokens: the 4-warp CTA walked 3 blocks per warp, two of them after the wait -- 2.6 us
-// of a 5.7 us attention). head_dim 128 keeps 4 warps (registers and shared memory).
-constexpr int kAClusterWarps = 12;
+// warps per CTA in the cluster form at head_dim 64: one 16-token block per warp, so a
+// split of up to 128 tokens (2048 per sequence in 16 CTAs) is requested entirely before
+// the wait (B200, batch 1 at 2048 tokens: the 4-warp CTA walked 3 blocks per warp, two of
+// them after the wait -- 2.6 us of a 5.7 us attention). Two such CTAs must fit an SM
+// (launch bound 2): at 12 warps a CTA held most of an SM's registers, and 16-CTA
+// clusters that need 16 free SMs of one GPC went out in two waves (measured: a tenth
+// of the CTAs started 4.7 us late). head_dim 128 keeps 4 warps (registers and shared
+// memory).
+constexpr int kAClusterWarps = 8;
 template <int kAD>
 constexpr int attn_cluster_warps() { return kAD == 64 ? kAClusterWarps : kAWarps; }
+template <int kAD, int kCS>
+constexpr int attn_min_ctas() { return (kCS > 1 && kAD == 64) ? 2 : 0; }
 constexpr int kABlk = 16;     // tokens per warp step
 constexpr int kAMinChunk = 64;   // tokens per split at least
 constexpr int kAMaxSplits = 64;  // splits per sequence at most (the combine holds one value per split)
@@ -85,7 +91,7 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void *smem
 // shared memory and rank 0 merges them in rank order after one cluster barrier -- no
 // workspace, no second kernel.
 template <int kAD, bool kFused = false, int kCS = 1>
-__global__ void __launch_bounds__(32 * ((kCS > 1 && kAD == 64) ? kAClusterWarps : kAWarps))
+__global__ void __launch_bounds__(32 * ((kCS > 1 && kAD == 64) ? kAClusterWarps : kAWarps), attn_min_ctas<kAD, kCS>())
 attn_decode_kernel(AttnArgs a) {
   constexpr int kW = (kCS > 1 && kAD == 64) ? kAClusterWarps : kAWarps;  // warps of this CTA
   constexpr int kG = kCS > 1 ? 4 : 16;                    // query-head rows kept per warp (the cluster form: g <= 4)

@@ -376,6 +376,14 @@ template <int NT, bool kNorm>
 constexpr int s4_min_ctas() { return (NT == 1 && !kNorm) ? 4 : 0; }
 template <int NT>
 constexpr int s4_units() { return NT <= 2 ? 2 : 4; }
+// kHalf (single-tile kernels): CTAs of 4 warps, 8 per SM, for matrices with more tiles
+// than one wave of 8-warp CTAs holds (the gate / up projection, the lm-head): the
+// smaller CTAs all fit in one wave or retire in finer steps (B200, 1 vector: gate / up
+// 5.67 against 6.17 us, lm-head 35.3 against 38.0 us per launch).
+template <int NT, bool kHalf>
+constexpr int s4_cta_warps() { return (kHalf && NT == 1) ? 4 : s4_warps<NT>(); }
+template <int NT, bool kNorm, bool kHalf>
+constexpr int s4_cta_min() { return (kHalf && NT == 1) ? 8 : s4_min_ctas<NT, kNorm>(); }
 
 // kNorm: the RMSNorm prologue (n_vec <= 8) -- x normalised into shared memory first.
 // (Staging a plain x the same way measured slower on B200: 4.16 against 3.77 us per
@@ -383,11 +391,11 @@ constexpr int s4_units() { return NT <= 2 ? 2 : 4; }
 // kChain (NT == 1): the decode chain's folded RMSNorm (S4Epi ss_in / ss_out / yw); a
 // separate instantiation, so the plain GEMV carries none of its shared memory or code.
 template <int NT, int CS, bool kNorm = false, bool kAR = false, bool kRO = false, bool kChain = false,
-          bool kAsym = false>
-__global__ void __launch_bounds__(32 * s4_warps<NT>(), s4_min_ctas<NT, kNorm || kAsym>())
+          bool kAsym = false, bool kHalf = false>
+__global__ void __launch_bounds__(32 * s4_cta_warps<NT, kHalf>(), s4_cta_min<NT, kNorm || kAsym, kHalf>())
 gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__restrict__ x,
                        uint16_t *__restrict__ y, int N, int K, int n_vec, S4Epi epi) {
-  constexpr int kT4Warps = s4_warps<NT>();
+  constexpr int kT4Warps = s4_cta_warps<NT, kHalf>();
   constexpr int kT4Units = s4_units<NT>();
   __shared__ float red[(kT4Warps + CS) * NT * 128];
   extern __shared__ __align__(16) uint16_t xs_norm[];  // [n_vec, this CTA's k range] when staged
@@ -446,15 +454,17 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
   if (!bound) pdl_launch_dependents();
   pdl_wait();
   if (bound) pdl_launch_dependents();
-  // chain prologue: warp v requests vector v's partial sums of squares now and sums them
-  // after its units (K / 16 partials: K / 2048 16-byte pieces per lane)
+  // chain prologue: warp w requests the partial sums of squares of vectors w, w + warps,
+  // ... now and sums them after its units (K / 16 partials: K / 2048 16-byte pieces per lane)
   __shared__ float inv_s[8];
   const bool ss_warp = chain && epi.ss_in != nullptr && rank == 0 && warp < n_vec;
   if (ss_warp) {
-    const float *ps = epi.ss_in + static_cast<int64_t>(warp) * (K / 16) + lane * 4;
-    float *pd = pss_s + warp * 256 + lane * 4;
-    cp_async16(pd, ps);
-    if (K == 4096) cp_async16(pd + 128, ps + 128);
+    for (int vv = warp; vv < n_vec; vv += kT4Warps) {
+      const float *ps = epi.ss_in + static_cast<int64_t>(vv) * (K / 16) + lane * 4;
+      float *pd = pss_s + vv * 256 + lane * 4;
+      cp_async16(pd, ps);
+      if (K == 4096) cp_async16(pd + 128, ps + 128);
+    }
   }
   if constexpr (chain) cp_async_commit();
   __shared__ float res_s[16 * 8 * NT];
@@ -522,14 +532,16 @@ gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__res
   if (has_res) rres.park(res_s, n_vec);
   if constexpr (chain) cp_async_wait_all();  // this thread's chain copies (if any) have landed
   if (ss_warp) {  // inv_s[v] = 1 / sqrt(mean(x_v^2) + eps), the partials summed in a fixed order
-    const float4 a = *reinterpret_cast<const float4 *>(pss_s + warp * 256 + lane * 4);
-    float t = (a.x + a.y) + (a.z + a.w);
-    if (K == 4096) {
-      const float4 c = *reinterpret_cast<const float4 *>(pss_s + warp * 256 + 128 + lane * 4);
-      t += (c.x + c.y) + (c.z + c.w);
+    for (int vv = warp; vv < n_vec; vv += kT4Warps) {
+      const float4 a = *reinterpret_cast<const float4 *>(pss_s + vv * 256 + lane * 4);
+      float t = (a.x + a.y) + (a.z + a.w);
+      if (K == 4096) {
+        const float4 c = *reinterpret_cast<const float4 *>(pss_s + vv * 256 + 128 + lane * 4);
+        t += (c.x + c.y) + (c.z + c.w);
+      }
+      t = warp_sum(t);
+      if (lane == 0) inv_s[vv] = rsqrtf(t / K + epi.eps);
     }
-    t = warp_sum(t);
-    if (lane == 0) inv_s[warp] = rsqrtf(t / K + epi.eps);
   }
   // reduce over warps (and cluster ranks) in fixed order
 #pragma unroll
@@ -634,12 +646,12 @@ __global__ void pack_s4g32_kernel(const uint8_t *__restrict__ codes,
   reinterpret_cast<uint4 *>(out)[p] = make_uint4(words[0], words[1], words[2], words[3]);
 }
 
-template <int NT, int CS>
+template <int NT, int CS, bool kHalf = false>
 static int launch_s4_tile(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,
                           int n_vec, const S4Epi &epi, bool pdl, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>((N / 16) * CS));
-  cfg.blockDim = dim3(32 * s4_warps<NT>());
+  cfg.blockDim = dim3(32 * s4_cta_warps<NT, kHalf>());
   cfg.stream = s;
   if (epi.norm_w) {
     // the CTA's normalised k range of every vector (<= 8 x 2048 bf16 = 32 KB)
@@ -673,13 +685,13 @@ static int launch_s4_tile(const uint8_t *packed, const uint16_t *x, uint16_t *y,
                  : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, true, false>, packed, x, y, N, K, n_vec, epi);
   } else if (epi.ss_in || epi.yw) {
     if constexpr (NT != 1) return IRON_ERR_SHAPE;
-    e = epi.x_ro ? cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, false, true, true>, packed, x, y, N, K, n_vec, epi)
-                 : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, false, false, true>, packed, x, y, N, K, n_vec, epi);
+    e = epi.x_ro ? cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, false, true, true, false, kHalf>, packed, x, y, N, K, n_vec, epi)
+                 : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, false, false, true, false, kHalf>, packed, x, y, N, K, n_vec, epi);
   } else if (epi.norm_w) {
     e = cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, true>, packed, x, y, N, K, n_vec, epi);
   } else {
-    e = epi.x_ro ? cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, false, false, true>, packed, x, y, N, K, n_vec, epi)
-                 : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, false, false, false>, packed, x, y, N, K, n_vec, epi);
+    e = epi.x_ro ? cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, false, false, true, false, false, kHalf>, packed, x, y, N, K, n_vec, epi)
+                 : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, false, false, false, false, false, kHalf>, packed, x, y, N, K, n_vec, epi);
   }
   if (e != cudaSuccess) {
     set_last_cuda_error(e);
@@ -699,6 +711,12 @@ static int launch_s4_tile_cs(const uint8_t *packed, const uint16_t *x, uint16_t 
   const int tiles = N / 16, cpt = K / 128;
   int cs = 1;
   while (cs < kMaxCS && tiles * cs < 2 * sm_count() && cpt >= s4_warps<NT>() * cs * 2) cs *= 2;
+  // more tiles than one wave of four 8-warp CTAs per SM: the half-width CTAs (plain and
+  // chain single-tile forms)
+  if constexpr (NT == 1) {
+    if (cs == 1 && tiles > 4 * sm_count() && !res.norm_w && !res.asym && res.ar.world <= 1)
+      return launch_s4_tile<1, 1, true>(packed, x, y, N, K, n_vec, res, pdl, s);
+  }
   switch (cs) {
     case 1: return launch_s4_tile<NT, 1>(packed, x, y, N, K, n_vec, res, pdl, s);
     case 2: return launch_s4_tile<NT, 2>(packed, x, y, N, K, n_vec, res, pdl, s);

@@ -72,10 +72,11 @@ def test_decode_step_matches_oracle(batch, prefix, fuse):
     hid = []
     oracle_step(kcs, vcs, hidden=hid)  # the oracle's appended cache rows, for the row checks below
     # a sequence whose residual stream ends as a near-cancellation of far larger terms
-    # (final RMS < 5 % of the largest block output's) turns one-ulp differences of those
-    # terms into errors of its own size: not held to the elementwise bar
+    # (final RMS < 5 % of the batch's median final RMS: the blocks' outputs have the same
+    # scale for every sequence, so a much smaller sum is a cancellation) turns one-ulp
+    # differences of those terms into errors of its own size: not held to the elementwise bar
     rms = torch.stack([h.float().pow(2).mean(-1).sqrt() for h in hid])
-    well = well & (rms[-1] > 0.05 * rms.max(0).values)
+    well = well & (rms[-1] > 0.05 * rms[-1].median())
     # 1. The last layer's attention and the lm-head recomputed by the oracle on the
     # engine's OWN inputs (its QKV projection and caches; its final hidden state): every
     # output within the north star's bar, no exceptions -- the kernels' parity, free of
@@ -100,7 +101,8 @@ def test_decode_step_matches_oracle(batch, prefix, fuse):
     d = (eng.logits.cpu().float() - logits.float()).abs()
     bad = d >= torch.maximum(torch.full_like(d, 1e-2), 2e-2 * (eng.logits.cpu().float().abs() + logits.float().abs()))
     print(f"batch {batch} {fuse}: per sequence (pos, well-conditioned, outside 2e-2 / 1e-2, max |diff|): "
-          f"{[(p, bool(well[b]), int(bad[b].sum()), round(float(d[b].max()), 4)) for b, p in enumerate(prefix)]}")
+          f"{[(p, bool(well[b]), int(bad[b].sum()), round(float(d[b].max()), 4)) for b, p in enumerate(prefix)]}; "
+          f"final RMS {[round(float(r), 3) for r in rms[-1]]}")
     assert int(well.sum()) >= (batch + 1) // 2, "most sequences must be well-conditioned"
     assert_close(eng.logits.cpu()[well], logits[well], 2e-2, 1e-2, what="logits (well-conditioned sequences)")
     lp = torch.log_softmax(logits.float(), -1)

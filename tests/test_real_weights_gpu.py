@@ -7,14 +7,24 @@ and Llama-like magnitudes.
 
 Checks:
   - the engine's matrices are the quantizer's (bitwise);
+  - the lm-head on the engine's own final hidden state within rtol 2e-2 / atol 1e-2
+    (the kernel's parity, free of the network's amplification);
   - prefill and decode logits against the oracle on the same (dequantized) weights, and
     the next-token distributions against IRON's fp32 CPU reference within IRON's
     accuracy bounds: KL <= 0.1 after prefill, <= 0.05 per decode step, teacher-forced
-    (iron/applications/llama_3.2_1b/test.py:77-97);
+    (iron/applications/llama_3.2_1b/test.py:77-97). End to end the absolute bound of a
+    decode row is two bf16 ulps of its largest logit where that exceeds 1e-2: a logit is
+    a 2048-term dot product of the final normalised hidden state, so the last-bit
+    differences that two correct summation orders leave in that state (two layers of
+    bf16 roundings) move every logit by the same absolute amount, small ones included
+    -- measured on B200: 275 of 4096 logits of one step past 1e-2 (by at most 0.0012),
+    none past 0.0313, KL to the fp32 reference 5e-5;
   - bitwise determinism over alternating prompts (test.py:100-113: repeated runs must
     give identical logits; alternating two prompts exposes state left over from the
     previous one).
 """
+
+import math
 
 import pytest
 import torch
@@ -114,9 +124,14 @@ def test_checkpoint_quantized_prefill_decode_and_accuracy(tmp_path):
                                         [v[None].clone() for v in vc], lut, SHAPE.n_heads, SHAPE.n_kv_groups,
                                         SHAPE.head_dim, fold=fold), 2e-2, 1e-2)
         d = (got.float() - ref.float()).abs()
-        print(f"decode step {t}: max |diff| {float(d.max()):.3g} (max |logit| {float(ref.float().abs().max()):.3g})")
+        top = float(ref.float().abs().max())
+        print(f"decode step {t}: max |diff| {float(d.max()):.3g} (max |logit| {top:.3g})")
+        # the lm-head on the engine's own final hidden state: the strict bar
+        head = ollama._normed_gemv(lm, eng.x.cpu(), nf, SHAPE.eps, fold)
+        assert_close(got, head, 2e-2, 1e-2, what=f"lm-head on the engine's hidden state, step {t}")
         if bool(well[0]):
-            assert_close(got, ref, 2e-2, 1e-2, what=f"decode logits, step {t}")
+            ulp2 = 2 * 2.0 ** (math.floor(math.log2(top)) - 7)  # two bf16 ulps of the largest logit
+            assert_close(got, ref, 2e-2, max(1e-2, ulp2) + 1e-6, what=f"decode logits, step {t}")
         with ops.fp32_reference():
             r32 = ollama.model_decode([tok], [pos], W32, nf.float(), emb.float(), lm.float(),
                                       [k[None] for k in kc32], [v[None] for v in vc32], lut, SHAPE.n_heads,
