@@ -10,9 +10,10 @@
 // Persistent and warp-specialised: one CTA per SM walks 128 x BN output tiles
 // with a ring of shared-memory stages (TMA loads of 64-wide k-blocks, 128-byte
 // swizzle) and two TMEM accumulators, so the drain of one tile overlaps the
-// mainloop of the next. Every mbarrier wait gives up after 2 s without
-// progress; a timeout sets the status word and the CTA leaves after freeing
-// its TMEM.
+// mainloop of the next. The drain stages each warp's 32 x 32 output block in
+// shared memory (swizzled, conflict-free) and writes it with one TMA bulk store.
+// Every mbarrier wait gives up after 2 s without progress; a timeout sets the
+// status word and the CTA leaves after freeing its TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -66,14 +67,26 @@ __device__ __forceinline__ uint32_t add_res2(uint32_t packed, uint32_t res) {
   return pack_bf16x2(bf16_lo(packed) + bf16_lo(res), bf16_hi(packed) + bf16_hi(res));
 }
 
+// Output staging: per epilogue warp two buffers of 32 rows x 32 columns of bf16 (64-byte
+// rows; the SwiGLU form's 16 output columns use 32-byte rows of the same buffers),
+// written in the TMA store's swizzled order (64B / 32B swizzle) so that the 32 lanes'
+// 16-byte stores are free of bank conflicts.
+constexpr int kStgBytes = 32 * 64;
+
 template <int BN>
 struct Cfg {
   static constexpr int kStageA = BM * BK * 2;
   static constexpr int kStageB = BN * BK * 2;
   static constexpr int kStage = kStageA + kStageB;
   static constexpr int kStages = (192 * 1024) / kStage;
-  static constexpr int kSmem = 1024 + kStages * kStage + 256;
+  static constexpr int kBars = 1024;  // mbarriers and the TMEM slot
+  static constexpr int kSmem = 1024 + kStages * kStage + kBars + kEpiWarps * 2 * kStgBytes;
 };
+
+// Byte offset of 16-byte chunk g of row r in a staging buffer (TMA 64B / 32B swizzle:
+// chunk bits 4-5 (4) XORed with address bits 7-8 (7)).
+__device__ __forceinline__ uint32_t stg64(int r, int g) { return r * 64 + ((g ^ ((r >> 1) & 3)) << 4); }
+__device__ __forceinline__ uint32_t stg32(int r, int g) { return r * 32 + ((g ^ ((r >> 2) & 1)) << 4); }
 
 // Persistent, warp-specialised kernel. Each CTA walks the output tiles
 // blockIdx.x, blockIdx.x + gridDim.x, ... with two TMEM accumulators, so the
@@ -86,7 +99,7 @@ struct Cfg {
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   uint16_t *__restrict__ C, int M, int N, int K, int64_t ldc,
+                   const __grid_constant__ CUtensorMap tmC, int M, int N, int K,
                    const uint16_t *__restrict__ R, int64_t ldr, Epi epi) {
   using G = Cfg<BN>;
   constexpr int S = G::kStages;
@@ -100,6 +113,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tfull0 = bars + 16 * S, tempty0 = tfull0 + 16;  // [2] each
   const uint32_t tslot = tempty0 + 16;
   uint32_t *tslot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tslot - raw));
+  const uint32_t stg0 = bars + G::kBars;  // 1024-byte aligned
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kb_count = (K + BK - 1) / BK;
@@ -109,6 +123,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     tc::prefetch_tmap(&tmA);
     tc::prefetch_tmap(&tmB);
+    tc::prefetch_tmap(&tmC);
     for (int s = 0; s < S; ++s) {
       tc::mbar_init_u32(full0 + 8 * s, 1);
       tc::mbar_init_u32(empty0 + 8 * s, 1);
@@ -187,9 +202,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) atomicCAS(&g_gemm_status, 0u, 2u);
     }
   } else {
-    // ---- epilogue: TMEM -> registers -> bf16 -> HBM ----
+    // ---- epilogue: TMEM -> registers -> bf16 -> shared staging -> TMA store ----
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    int i = 0;
+    const uint32_t stg = stg0 + q * 2 * kStgBytes;
+    uint8_t *stg_ptr = smem_raw + (stg - raw);
+    const int out_cols = epi.mode == 4 ? N / 2 : N;
+    // no activation, clamp or floor rounding: the drain is a plain conversion. (Per-value
+    // option branches made the drain instruction-bound: 25 us per 128 x 256 tile on
+    // B200, twice a K = 2048 tile's mainloop.)
+    const bool plain = epi.mode == 0 && !epi.floor && !epi.clamp;
+    int i = 0, nb = 0;  // nb: blocks this warp has stored (buffer nb & 1)
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
       const int acc = i & 1;
       const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
@@ -202,55 +224,68 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = m0 + q * 32 + lane;
       const uint32_t trow = tmem + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = 0; c < BN; c += 32, ++nb) {
         uint32_t r[32];
         tc::tmem_ld32(trow + c, r);
-        if (row < M && epi.mode == 4) {
+        const uint32_t buf = (nb & 1) * kStgBytes;
+        if (lane == 0) tc::bulk_wait_read<1>();  // this buffer's store (two blocks ago) has read it
+        __syncwarp();
+        if (epi.mode == 4) {
           // two 16-column groups: 8 gate then 8 up columns -> 8 outputs each
-          uint16_t *dst = C + static_cast<int64_t>(row) * ldc + (n0 + c) / 2;
 #pragma unroll
           for (int g = 0; g < 2; ++g) {
-            if (n0 + c + 16 * g + 16 <= N) {
-              const uint32_t *rg = r + 16 * g;
-              uint4 v;
-              v.x = pack_bf16x2(swiglu_pair(__uint_as_float(rg[0]), __uint_as_float(rg[8])),
-                                swiglu_pair(__uint_as_float(rg[1]), __uint_as_float(rg[9])));
-              v.y = pack_bf16x2(swiglu_pair(__uint_as_float(rg[2]), __uint_as_float(rg[10])),
-                                swiglu_pair(__uint_as_float(rg[3]), __uint_as_float(rg[11])));
-              v.z = pack_bf16x2(swiglu_pair(__uint_as_float(rg[4]), __uint_as_float(rg[12])),
-                                swiglu_pair(__uint_as_float(rg[5]), __uint_as_float(rg[13])));
-              v.w = pack_bf16x2(swiglu_pair(__uint_as_float(rg[6]), __uint_as_float(rg[14])),
-                                swiglu_pair(__uint_as_float(rg[7]), __uint_as_float(rg[15])));
-              *reinterpret_cast<uint4 *>(dst + 8 * g) = v;
-            }
+            const uint32_t *rg = r + 16 * g;
+            uint4 v;
+            v.x = pack_bf16x2(swiglu_pair(__uint_as_float(rg[0]), __uint_as_float(rg[8])),
+                              swiglu_pair(__uint_as_float(rg[1]), __uint_as_float(rg[9])));
+            v.y = pack_bf16x2(swiglu_pair(__uint_as_float(rg[2]), __uint_as_float(rg[10])),
+                              swiglu_pair(__uint_as_float(rg[3]), __uint_as_float(rg[11])));
+            v.z = pack_bf16x2(swiglu_pair(__uint_as_float(rg[4]), __uint_as_float(rg[12])),
+                              swiglu_pair(__uint_as_float(rg[5]), __uint_as_float(rg[13])));
+            v.w = pack_bf16x2(swiglu_pair(__uint_as_float(rg[6]), __uint_as_float(rg[14])),
+                              swiglu_pair(__uint_as_float(rg[7]), __uint_as_float(rg[15])));
+            *reinterpret_cast<uint4 *>(stg_ptr + buf + stg32(lane, g)) = v;
           }
-        } else if (row < M) {
-          uint16_t *dst = C + static_cast<int64_t>(row) * ldc + n0 + c;
-          const uint16_t *res = R ? R + static_cast<int64_t>(row) * ldr + n0 + c : nullptr;
+        } else {
+          const uint16_t *res = (R && row < M) ? R + static_cast<int64_t>(row) * ldr + n0 + c : nullptr;
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
-            if (n0 + c + 8 * g + 8 <= N) {
-              uint4 v;
+            uint4 v;
+            if (plain) {  // one rounding per value, two values per conversion
+              v.x = pack_bf16x2(__uint_as_float(r[8 * g + 0]), __uint_as_float(r[8 * g + 1]));
+              v.y = pack_bf16x2(__uint_as_float(r[8 * g + 2]), __uint_as_float(r[8 * g + 3]));
+              v.z = pack_bf16x2(__uint_as_float(r[8 * g + 4]), __uint_as_float(r[8 * g + 5]));
+              v.w = pack_bf16x2(__uint_as_float(r[8 * g + 6]), __uint_as_float(r[8 * g + 7]));
+            } else {
               v.x = pack_bf16x2(apply_epi(__uint_as_float(r[8 * g + 0]), epi), apply_epi(__uint_as_float(r[8 * g + 1]), epi));
               v.y = pack_bf16x2(apply_epi(__uint_as_float(r[8 * g + 2]), epi), apply_epi(__uint_as_float(r[8 * g + 3]), epi));
               v.z = pack_bf16x2(apply_epi(__uint_as_float(r[8 * g + 4]), epi), apply_epi(__uint_as_float(r[8 * g + 5]), epi));
               v.w = pack_bf16x2(apply_epi(__uint_as_float(r[8 * g + 6]), epi), apply_epi(__uint_as_float(r[8 * g + 7]), epi));
-              if (res) {
-                const uint4 rv = ld_act_v4(res + 8 * g);
-                v.x = add_res2(v.x, rv.x);
-                v.y = add_res2(v.y, rv.y);
-                v.z = add_res2(v.z, rv.z);
-                v.w = add_res2(v.w, rv.w);
-              }
-              *reinterpret_cast<uint4 *>(dst + 8 * g) = v;
             }
+            if (res && n0 + c + 8 * g + 8 <= N) {
+              const uint4 rv = ld_act_v4(res + 8 * g);
+              v.x = add_res2(v.x, rv.x);
+              v.y = add_res2(v.y, rv.y);
+              v.z = add_res2(v.z, rv.z);
+              v.w = add_res2(v.w, rv.w);
+            }
+            *reinterpret_cast<uint4 *>(stg_ptr + buf + stg64(lane, g)) = v;
           }
+        }
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        // rows past M and columns past the output's width are clipped by the store
+        const int x = epi.mode == 4 ? (n0 + c) / 2 : n0 + c;
+        if (lane == 0 && m0 + q * 32 < M && x < out_cols) {
+          tc::tma_store_2d(&tmC, stg + buf, x, m0 + q * 32);
+          tc::bulk_commit();
         }
       }
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tempty0 + 8 * acc) : "memory");
     }
+    if (lane == 0) tc::bulk_wait_all();  // the stores have written C (and read the staging)
   }
   __syncwarp();
   pdl_launch_dependents();
@@ -289,11 +324,30 @@ int make_tmap(CUtensorMap *m, const void *ptr, int rows, int K, int64_t ld, int 
   return r == CUDA_SUCCESS ? IRON_OK : IRON_ERR_ARG;
 }
 
+// The output C [rows, cols] (row pitch ld elements) as the epilogue's TMA store sees
+// it: boxes of 32 rows x box_cols columns, 64B swizzle for 32-column boxes (SwiGLU's
+// 16-column boxes: 32B), matching stg64 / stg32.
+int make_store_tmap(CUtensorMap *m, void *ptr, int rows, int cols, int64_t ld, int box_cols) {
+  auto fn = encode_fn();
+  if (!fn) return IRON_ERR_UNSUPPORTED;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), 32u};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  box_cols == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? IRON_OK : IRON_ERR_ARG;
+}
+
 // Pick the tile width: whole waves of 128 x BN tiles over the SMs, discounted for
-// the shared-memory operand traffic of narrow tiles.
+// the shared-memory operand traffic of narrow tiles (a 128 x 128 MMA reads its
+// operands from shared memory at the rate the SM supplies them; measured on B200 at
+// M = 2048, K = 2048, N = 2048 / 3072 / 8192: 128-wide tiles run 0.59-0.69 of the
+// 256-wide tile's rate per wave-slot, 64-wide ones about 0.35).
 int pick_bn(int M, int N, int sms) {
   const int cand[3] = {256, 128, 64};
-  const double smem_eff[3] = {1.0, 0.95, 0.66};
+  const double smem_eff[3] = {1.0, 0.62, 0.35};
   int best = 64;
   double best_e = -1;
   for (int i = 0; i < 3; ++i) {
@@ -312,7 +366,7 @@ int pick_bn(int M, int N, int sms) {
 }
 
 template <int BN>
-int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, uint16_t *C, int M, int N, int K, int64_t ldc,
+int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc, int M, int N, int K,
                 const uint16_t *R, int64_t ldr, Epi epi, cudaStream_t s, bool pdl) {
   using G = Cfg<BN>;
   static PerDeviceOnce attr_set;  // per instantiation and device: the shared memory opt-in
@@ -322,7 +376,7 @@ int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, uint16_t *C, int M
   if (ast != IRON_OK) return ast;
   const int64_t tiles = static_cast<int64_t>((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   dim3 grid(static_cast<unsigned>(tiles < sm_count() ? tiles : sm_count()));
-  return launch(gemm_tc_kernel<BN>, grid, dim3(kThreads), G::kSmem, s, pdl, ta, tb, C, M, N, K, ldc, R, ldr, epi);
+  return launch(gemm_tc_kernel<BN>, grid, dim3(kThreads), G::kSmem, s, pdl, ta, tb, tc, M, N, K, R, ldr, epi);
 }
 
 }  // namespace gemm
@@ -347,17 +401,18 @@ extern "C" int iron_gemm_bf16(const uint16_t *A, const uint16_t *B, uint16_t *C,
   if (residual && (ldr % 8 || !aligned16(residual))) return IRON_ERR_ALIGN;
   int bn = block_n ? block_n : pick_bn(M, N, sm_count());
   if (bn != 64 && bn != 128 && bn != 256) return IRON_ERR_ARG;
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tc;
   int st = make_tmap(&ta, A, M, K, lda, BM);
   if (st == IRON_OK) st = make_tmap(&tb, B, N, K, ldb, bn);
+  if (st == IRON_OK) st = make_store_tmap(&tc, C, M, static_cast<int>(out_cols), ldc, act == 4 ? 16 : 32);
   if (st != IRON_OK) return st;
   Epi epi{act, floor_rnd, clamp, clamp_lo, clamp_hi};
   auto s = static_cast<cudaStream_t>(stream);
   const bool pdl = (flags & IRON_FLAG_PDL) != 0;
   switch (bn) {
-    case 256: return launch_gemm<256>(ta, tb, C, M, N, K, ldc, residual, ldr, epi, s, pdl);
-    case 128: return launch_gemm<128>(ta, tb, C, M, N, K, ldc, residual, ldr, epi, s, pdl);
-    default: return launch_gemm<64>(ta, tb, C, M, N, K, ldc, residual, ldr, epi, s, pdl);
+    case 256: return launch_gemm<256>(ta, tb, tc, M, N, K, residual, ldr, epi, s, pdl);
+    case 128: return launch_gemm<128>(ta, tb, tc, M, N, K, residual, ldr, epi, s, pdl);
+    default: return launch_gemm<64>(ta, tb, tc, M, N, K, residual, ldr, epi, s, pdl);
   }
 }
 
