@@ -898,7 +898,8 @@ def run_gemm(args, world, rank, local):
             "config": {"workload": f"gemm M={M} K={K} N={N} (prefill projection shape)",
                        "l2": "operands L2-resident across steps (compute-bound)", "parallelism": f"dp{world}"},
             "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
-                         "frac": round(tf / peak, 4), "traffic": None, "peak_source": src},
+                         "frac": round(tf / peak, 4), "traffic": _profile_traffic(f"gemm:{M}x{K}x{N}"),
+                         "peak_source": src},
             "gpu_launches": args.steps, "clocks": clocks, "e2e": None}
     if rank == 0:
         print(json.dumps(line), flush=True)
