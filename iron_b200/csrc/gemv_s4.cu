@@ -376,14 +376,18 @@ template <int NT, bool kNorm>
 constexpr int s4_min_ctas() { return (NT == 1 && !kNorm) ? 4 : 0; }
 template <int NT>
 constexpr int s4_units() { return NT <= 2 ? 2 : 4; }
-// kHalf (single-tile kernels): CTAs of 4 warps, 8 per SM, for matrices with more tiles
+// kW (single-tile kernels; 0: the defaults above). kW = 4: CTAs of 4 warps, 8 per SM, for matrices with more tiles
 // than one wave of 8-warp CTAs holds (the gate / up projection, the lm-head): the
 // smaller CTAs all fit in one wave or retire in finer steps (B200, 1 vector: gate / up
 // 5.67 against 6.17 us, lm-head 35.3 against 38.0 us per launch).
-template <int NT, bool kHalf>
-constexpr int s4_cta_warps() { return (kHalf && NT == 1) ? 4 : s4_warps<NT>(); }
-template <int NT, bool kNorm, bool kHalf>
-constexpr int s4_cta_min() { return (kHalf && NT == 1) ? 8 : s4_min_ctas<NT, kNorm>(); }
+// kW = 16: CTAs of 16 warps, 2 per SM, in place of a 2-CTA cluster splitting K (the QKV and
+// O projections: one CTA per tile) -- the same warps per tile without the cluster barrier,
+// which with the skew between the two CTAs' SMs cost 0.6-1 us of a B200 decode GEMV
+// (decode step 0.4215 -> 0.4075 ms).
+template <int NT, int kW>
+constexpr int s4_cta_warps() { return (kW && NT == 1) ? kW : s4_warps<NT>(); }
+template <int NT, bool kNorm, int kW>
+constexpr int s4_cta_min() { return (kW == 4 && NT == 1) ? 8 : (kW == 16 && NT == 1) ? 2 : s4_min_ctas<NT, kNorm>(); }
 
 // kNorm: the RMSNorm prologue (n_vec <= 8) -- x normalised into shared memory first.
 // (Staging a plain x the same way measured slower on B200: 4.16 against 3.77 us per
@@ -391,11 +395,11 @@ constexpr int s4_cta_min() { return (kHalf && NT == 1) ? 8 : s4_min_ctas<NT, kNo
 // kChain (NT == 1): the decode chain's folded RMSNorm (S4Epi ss_in / ss_out / yw); a
 // separate instantiation, so the plain GEMV carries none of its shared memory or code.
 template <int NT, int CS, bool kNorm = false, bool kAR = false, bool kRO = false, bool kChain = false,
-          bool kAsym = false, bool kHalf = false>
-__global__ void __launch_bounds__(32 * s4_cta_warps<NT, kHalf>(), s4_cta_min<NT, kNorm || kAsym, kHalf>())
+          bool kAsym = false, int kW = 0>
+__global__ void __launch_bounds__(32 * s4_cta_warps<NT, kW>(), s4_cta_min<NT, kNorm || kAsym, kW>())
 gemv_s4g32_tile_kernel(const uint8_t *__restrict__ packed, const uint16_t *__restrict__ x,
                        uint16_t *__restrict__ y, int N, int K, int n_vec, S4Epi epi) {
-  constexpr int kT4Warps = s4_cta_warps<NT, kHalf>();
+  constexpr int kT4Warps = s4_cta_warps<NT, kW>();
   constexpr int kT4Units = s4_units<NT>();
   __shared__ float red[(kT4Warps + CS) * NT * 128];
   extern __shared__ __align__(16) uint16_t xs_norm[];  // [n_vec, this CTA's k range] when staged
@@ -646,12 +650,12 @@ __global__ void pack_s4g32_kernel(const uint8_t *__restrict__ codes,
   reinterpret_cast<uint4 *>(out)[p] = make_uint4(words[0], words[1], words[2], words[3]);
 }
 
-template <int NT, int CS, bool kHalf = false>
+template <int NT, int CS, int kW = 0>
 static int launch_s4_tile(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K,
                           int n_vec, const S4Epi &epi, bool pdl, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>((N / 16) * CS));
-  cfg.blockDim = dim3(32 * s4_cta_warps<NT, kHalf>());
+  cfg.blockDim = dim3(32 * s4_cta_warps<NT, kW>());
   cfg.stream = s;
   if (epi.norm_w) {
     // the CTA's normalised k range of every vector (<= 8 x 2048 bf16 = 32 KB)
@@ -685,13 +689,13 @@ static int launch_s4_tile(const uint8_t *packed, const uint16_t *x, uint16_t *y,
                  : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, true, false>, packed, x, y, N, K, n_vec, epi);
   } else if (epi.ss_in || epi.yw) {
     if constexpr (NT != 1) return IRON_ERR_SHAPE;
-    e = epi.x_ro ? cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, false, true, true, false, kHalf>, packed, x, y, N, K, n_vec, epi)
-                 : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, false, false, true, false, kHalf>, packed, x, y, N, K, n_vec, epi);
+    e = epi.x_ro ? cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, false, true, true, false, kW>, packed, x, y, N, K, n_vec, epi)
+                 : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<1, CS, false, false, false, true, false, kW>, packed, x, y, N, K, n_vec, epi);
   } else if (epi.norm_w) {
     e = cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, true>, packed, x, y, N, K, n_vec, epi);
   } else {
-    e = epi.x_ro ? cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, false, false, true, false, false, kHalf>, packed, x, y, N, K, n_vec, epi)
-                 : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, false, false, false, false, false, kHalf>, packed, x, y, N, K, n_vec, epi);
+    e = epi.x_ro ? cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, false, false, true, false, false, kW>, packed, x, y, N, K, n_vec, epi)
+                 : cudaLaunchKernelEx(&cfg, gemv_s4g32_tile_kernel<NT, CS, false, false, false, false, false, kW>, packed, x, y, N, K, n_vec, epi);
   }
   if (e != cudaSuccess) {
     set_last_cuda_error(e);
@@ -715,7 +719,12 @@ static int launch_s4_tile_cs(const uint8_t *packed, const uint16_t *x, uint16_t 
   // chain single-tile forms)
   if constexpr (NT == 1) {
     if (cs == 1 && tiles > 4 * sm_count() && !res.norm_w && !res.asym && res.ar.world <= 1)
-      return launch_s4_tile<1, 1, true>(packed, x, y, N, K, n_vec, res, pdl, s);
+      return launch_s4_tile<1, 1, 4>(packed, x, y, N, K, n_vec, res, pdl, s);
+    // a 2-CTA cluster splitting K: one 16-warp CTA per tile instead (each warp keeps >= 1
+    // unit). Clusters of 4 (the down projection) stay: halving them to 2 x 16 warps measured
+    // 404.5 against 402.8 us per B200 decode step.
+    if (cs == 2 && cpt >= 16 && !res.norm_w && !res.asym && res.ar.world <= 1)
+      return launch_s4_tile<1, 1, 16>(packed, x, y, N, K, n_vec, res, pdl, s);
   }
   switch (cs) {
     case 1: return launch_s4_tile<NT, 1>(packed, x, y, N, K, n_vec, res, pdl, s);
