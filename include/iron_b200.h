@@ -425,7 +425,7 @@ int iron_attn_prefill(const uint16_t *q, const uint16_t *k, const uint16_t *v, u
  * gate/up projection: B's rows come in groups of 16 (8 gate rows, then the 8 matching
  * up rows) and C [M, N/2] gets bf16(bf16(silu(bf16(gate))) * bf16(up)) per pair
  * (no residual, clamp or floor rounding with it; N a multiple of 16). K, N, lda, ldb, ldc multiples
- * of 8; pointers 16-byte aligned. block_n = 0 picks the tile width (64/128/256).
+ * of 8; pointers 16-byte aligned. block_n = 0 picks the tile width (64/128/192/256).
  * iron_gemm_status returns IRON_ERR_TIMEOUT if any GEMM since the last reset hit
  * its bounded-wait deadline (reset != 0 clears it); it synchronises the device.
  */

@@ -93,7 +93,7 @@ __device__ __forceinline__ uint32_t stg32(int r, int g) { return r * 32 + ((g ^ 
 // epilogue of one tile overlaps the mainloop of the next:
 //   warp 0, one thread : TMA producer (A and B k-blocks into the stage ring);
 //   warp 1, one thread : MMA issuer (accumulator i % 2 of the CTA's i-th tile);
-//   warp 2            : allocates / frees 2 * BN TMEM columns;
+//   warp 2            : allocates / frees the two accumulators' TMEM columns;
 //   warps 2..5        : epilogue, warp w draining TMEM lanes 32 (w % 4) ..
 //                       32 (w % 4) + 31 (the lane quarter that warp may access).
 template <int BN>
@@ -103,7 +103,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const uint16_t *__restrict__ R, int64_t ldr, Epi epi) {
   using G = Cfg<BN>;
   constexpr int S = G::kStages;
-  constexpr uint32_t kCols = 2 * BN;
+  // two accumulators of BN columns; TMEM is allocated in powers of two (BN = 192: 512)
+  constexpr uint32_t kCols = 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;  // 128-byte swizzle atoms need 1024-B alignment
@@ -343,14 +344,15 @@ int make_store_tmap(CUtensorMap *m, void *ptr, int rows, int cols, int64_t ld, i
 // Pick the tile width: whole waves of 128 x BN tiles over the SMs, discounted for
 // the shared-memory operand traffic of narrow tiles (a 128 x 128 MMA reads its
 // operands from shared memory at the rate the SM supplies them; measured on B200 at
-// M = 2048, K = 2048, N = 2048 / 3072 / 8192: 128-wide tiles run 0.59-0.69 of the
-// 256-wide tile's rate per wave-slot, 64-wide ones about 0.35).
+// M = 2048, K = 2048, N = 2048 / 3072 / 8192: per wave-slot 192-wide tiles run about
+// 0.8 of the 256-wide tile's rate, 128-wide 0.59-0.69, 64-wide about 0.35; 192 wins
+// where it fills the waves better, e.g. N = 3072: 970 against 917 TFLOP/s).
 int pick_bn(int M, int N, int sms) {
-  const int cand[3] = {256, 128, 64};
-  const double smem_eff[3] = {1.0, 0.62, 0.35};
+  const int cand[4] = {256, 192, 128, 64};
+  const double smem_eff[4] = {1.0, 0.8, 0.62, 0.35};
   int best = 64;
   double best_e = -1;
-  for (int i = 0; i < 3; ++i) {
+  for (int i = 0; i < 4; ++i) {
     const int bn = cand[i];
     if (N < bn && bn != 64) continue;
     const int64_t tiles = static_cast<int64_t>((M + BM - 1) / BM) * ((N + bn - 1) / bn);
@@ -400,7 +402,7 @@ extern "C" int iron_gemm_bf16(const uint16_t *A, const uint16_t *B, uint16_t *C,
   if (lda % 8 || ldb % 8 || ldc % 8 || !aligned16(A) || !aligned16(B) || !aligned16(C)) return IRON_ERR_ALIGN;
   if (residual && (ldr % 8 || !aligned16(residual))) return IRON_ERR_ALIGN;
   int bn = block_n ? block_n : pick_bn(M, N, sm_count());
-  if (bn != 64 && bn != 128 && bn != 256) return IRON_ERR_ARG;
+  if (bn != 64 && bn != 128 && bn != 192 && bn != 256) return IRON_ERR_ARG;
   CUtensorMap ta, tb, tc;
   int st = make_tmap(&ta, A, M, K, lda, BM);
   if (st == IRON_OK) st = make_tmap(&tb, B, N, K, ldb, bn);
@@ -411,6 +413,7 @@ extern "C" int iron_gemm_bf16(const uint16_t *A, const uint16_t *B, uint16_t *C,
   const bool pdl = (flags & IRON_FLAG_PDL) != 0;
   switch (bn) {
     case 256: return launch_gemm<256>(ta, tb, tc, M, N, K, residual, ldr, epi, s, pdl);
+    case 192: return launch_gemm<192>(ta, tb, tc, M, N, K, residual, ldr, epi, s, pdl);
     case 128: return launch_gemm<128>(ta, tb, tc, M, N, K, residual, ldr, epi, s, pdl);
     default: return launch_gemm<64>(ta, tb, tc, M, N, K, residual, ldr, epi, s, pdl);
   }

@@ -101,7 +101,7 @@ def test_gemm_golden_fixtures(name, bc, cc, M, K, N):
     assert not errors
 
 
-@pytest.mark.parametrize("block_n", [64, 128, 256])
+@pytest.mark.parametrize("block_n", [64, 128, 192, 256])
 def test_gemm_tile_widths_and_ragged_m(block_n):
     """Every tile width on shapes with partial tiles in M and N."""
     M, K, N = 200, 328, 376
@@ -200,8 +200,10 @@ def test_flm_gemm_golden_fixtures(epi, clamp):
     assert not errors
 
 
-def test_gemm_residual_epilogue():
-    """C = bf16(bf16(A B^T) + R): the o_proj / down_proj residual of a decoder block."""
+@pytest.mark.parametrize("block_n", [0, 192])
+def test_gemm_residual_epilogue(block_n):
+    """C = bf16(bf16(A B^T) + R): the o_proj / down_proj residual of a decoder block
+    (the chosen tile width, and 192-wide tiles with a partial last tile)."""
     M, K, N = 384, 1024, 768
     g = torch.Generator().manual_seed(11)
     A = torch.randn(M, K, generator=g).to(torch.bfloat16)
@@ -210,12 +212,13 @@ def test_gemm_residual_epilogue():
     Ad, Wd, Rd = A.cuda(), W.cuda(), R.cuda()
     C = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
     _lib.call("iron_gemm_bf16", Ad.data_ptr(), Wd.data_ptr(), C.data_ptr(), M, N, K, K, K, N, Rd.data_ptr(), N,
-              0, 0, 0.0, 0.0, 0, 0, _lib.current_stream())
+              0, 0, 0.0, 0.0, block_n, 0, _lib.current_stream())
     torch.cuda.synchronize()
     assert_close(C.cpu(), ops.add(R, ops.gemm(A, W, True, False)), 0.02, 0.01)
 
 
-def test_gemm_swiglu_epilogue():
+@pytest.mark.parametrize("block_n", [0, 192])
+def test_gemm_swiglu_epilogue(block_n):
     """Interleaved gate/up rows (8 + 8 per 16) -> silu(gate) * up, N/2 outputs."""
     M, K, H = 256, 512, 1024
     g = torch.Generator().manual_seed(12)
@@ -228,7 +231,7 @@ def test_gemm_swiglu_epilogue():
     Ad, Wd = A.cuda(), Wgu.cuda()
     C = torch.empty(M, H, dtype=torch.bfloat16, device="cuda")
     _lib.call("iron_gemm_bf16", Ad.data_ptr(), Wd.data_ptr(), C.data_ptr(), M, 2 * H, K, K, K, H, None, 0,
-              _lib.IRON_GEMM_EPI_SWIGLU, 0, 0.0, 0.0, 0, 0, _lib.current_stream())
+              _lib.IRON_GEMM_EPI_SWIGLU, 0, 0.0, 0.0, block_n, 0, _lib.current_stream())
     torch.cuda.synchronize()
     ref = ops.swiglu_act(ops.gemm(A, Wg, True, False), ops.gemm(A, Wu, True, False))
     assert_close(C.cpu(), ref, 0.04, 1e-3)
