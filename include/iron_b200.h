@@ -109,7 +109,10 @@ int iron_pack_int4g32(const uint8_t *codes, const uint16_t *scales, uint8_t *pac
  *             bf16 rounding) + residual[v, n] if residual != NULL -- the dequantized
  *   weights are exactly IRON Dequant's. x: bf16 [n_vec, K]; y: bf16 [n_vec, N]
  *   (N/2 with IRON_FLAG_SWIGLU); K % 128 == 0, N % 16 == 0, 1 <= n_vec <= 64.
- *   Needs no workspace.
+ *   Needs no workspace. From 33 vectors on (N % 128 == 0, no fused RMSNorm) the
+ *   product runs on the tcgen05 tensor cores (the same dequantized weights, fp32
+ *   accumulate, K split over a thread-block cluster and summed in a fixed order); a
+ *   bounded wait that runs out there is reported by iron_gemm_status.
  */
 /* iron_unpack_int4g32: the packed layout back to bf16 rows out [N, K], each weight
  * bf16(q * scale) exactly (bit-identical to iron_dequant_s4g32_rows on the natural

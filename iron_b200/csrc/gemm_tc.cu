@@ -19,7 +19,10 @@
 
 #include <mutex>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
+#include "s4.cuh"
 #include "tc.cuh"
 
 namespace iron {
@@ -295,6 +298,288 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 2) tc::tmem_free(tmem, kCols);
 }
 
+// ---- int4 g32 weights x a batch of vectors on the tensor cores -----------------------
+//
+// The int4 GEMV of iron_gemv_int4g32 for 33..64 vectors (decode batches), where the
+// mma.sync dot-product engine becomes compute-bound (B200, batch 64: 41-107 TFLOP/s).
+// A CTA owns a 128-row tile of the weights and a slice of K (a cluster of up to 8
+// CTAs splits K). Per 128-k stage:
+//   - the dequantising warps read their 16-row unit (or 8-row half) of the packed weights (the same
+//     1152-byte units as the GEMV, requested one stage ahead) and write the exact bf16
+//     values bf16(q * s) into shared memory in the 128-byte-swizzled K-major layout;
+//   - one thread loads the stage's activations [vectors, 128 k] by TMA;
+//   - one thread issues tcgen05.mma (M = 128 weight rows, N = vectors rounded up to 16)
+//     into a TMEM accumulator.
+// The weights never depend on the previous kernel, so the dequantising warps fill the
+// ring before the activations arrive; only the activation loads wait
+// (griddepcontrol.wait). The epilogue parks each CTA's fp32 partial tile in shared
+// memory; after a cluster barrier CTA r sums rows [r * 128 / CS, (r + 1) * 128 / CS) of
+// every rank's tile in rank order (bitwise deterministic) and applies the GEMV's
+// epilogue: plain, + residual, interleaved SwiGLU, or the greedy argmax keys.
+namespace s4tc {
+
+namespace cg = cooperative_groups;
+
+constexpr int kRows = 128;                        // weight rows per tile (MMA M)
+constexpr int kKB = 128;                          // k per stage: one packed unit
+constexpr int kStages = 4;
+constexpr int kDqWarps = 8;                       // 8: a 16-row unit each, 16: an 8-row half each
+constexpr int kHalves = kDqWarps / 8;             // warps per unit
+constexpr int kDrainWarps = 8;                    // the first 8 of them drain TMEM
+constexpr int kThreads = 32 * (2 + kDqWarps);     // warp 0: activation TMA, warp 1: MMA + TMEM
+constexpr int kMaxVec = 64;
+constexpr int kStageA = kRows * kKB * 2;          // two 64-k swizzle blocks of 16 KB
+constexpr int kStageB = kMaxVec * kKB * 2;        // two 64-k blocks of up to 8 KB
+constexpr int kStage = kStageA + kStageB;
+constexpr int kSmem = 1024 + kStages * kStage + 1024;
+constexpr int kUnitBytes = 1152;
+
+struct Args {
+  const uint8_t *packed;
+  uint16_t *y;
+  const uint16_t *residual;
+  unsigned long long *amax;
+  int N, K, n_vec, swiglu;
+};
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
+  unsigned u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  if (v != v) u = 0u;  // NaN never wins
+  return (static_cast<unsigned long long>(u) << 32) | static_cast<unsigned>(~row);
+}
+
+// Eight rows of a unit for this lane: rows row0 + gid, k 32 j + 8 tid + 0..7 of each
+// 32-k group j (words w, this row's group scales s01 = groups 0-1, s23 = groups 2-3), as
+// bf16(q * s) -- the GEMV's exact dequantisation -- stored at the rows' 16-byte chunks of
+// the stage's two swizzled 64-k blocks.
+__device__ __forceinline__ void dequant_rows(uint32_t stage_a, int row0, const uint4 &wv, uint32_t s01,
+                                             uint32_t s23) {
+  const int lane = threadIdx.x & 31, gid = lane >> 2, tid = lane & 3;
+  const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
+  const uint32_t sp[2] = {s01, s23};
+  const int r = row0 + gid;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t s2 = prmt_(sp[j >> 1], sp[j >> 1], (j & 1) ? 0x3232u : 0x1010u);
+    uint32_t p[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) p[q] = s4x2_dequant_(wd[j] >> (4 * q), s2);
+    const uint32_t blk = stage_a + (j >> 1) * (kRows * 128);
+    const int c16 = ((j & 1) << 2) | tid;  // 16-byte chunk of the 128-byte row
+    st_shared_v4(blk + r * 128 + ((c16 ^ (r & 7)) << 4), p[0], p[1], p[2], p[3]);
+  }
+}
+
+template <int CS>
+__global__ void __launch_bounds__(kThreads, 1)
+    s4tc_kernel(const __grid_constant__ CUtensorMap tmX, Args a, int nmma) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_addr(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;  // 128-byte swizzle atoms: 1024-B aligned
+  const uint32_t bars = base + kStages * kStage;
+  const uint32_t full0 = bars, empty0 = bars + 8 * kStages, accf = bars + 16 * kStages;
+  const uint32_t tslot = accf + 8;
+  uint32_t *tslot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tslot - raw));
+  float *P = reinterpret_cast<float *>(smem_raw + (base - raw));  // fp32 partial tile, after the mainloop
+  const int pstride = nmma + 1;                                   // [128][nmma + 1]: conflict-free columns
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rank = CS > 1 ? static_cast<int>(blockIdx.x % CS) : 0;
+  const int tile = blockIdx.x / CS;
+  const int cpt = a.K / kKB;
+  const int c0 = rank * cpt / CS, nkb = (rank + 1) * cpt / CS - c0;  // this CTA's k-blocks
+  const uint32_t cols = nmma <= 32 ? 32u : 64u;
+  constexpr uint64_t deadline = kDeadlineNs;
+
+  if (threadIdx.x == 0) {
+    tc::prefetch_tmap(&tmX);
+    for (int s = 0; s < kStages; ++s) {
+      tc::mbar_init_u32(full0 + 8 * s, kDqWarps + 1);  // the dequantising warps + the activation load
+      tc::mbar_init_u32(empty0 + 8 * s, 1);
+    }
+    tc::mbar_init_u32(accf, 1);
+    mbar_init_fence();
+  }
+  if (warp == 1) tc::tmem_alloc(tslot, cols);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tslot_ptr;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- activations: [vectors, 128 k] per stage, two 64-k boxes of nmma rows ----
+      pdl_wait();  // x is the previous kernel's output
+      bool ok = true;
+      int issued = 0;
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % kStages;
+        if (!tc::wait_until(empty0 + 8 * s, ((kb / kStages) & 1) ^ 1, deadline)) {
+          ok = false;
+          break;
+        }
+        const uint32_t sb = base + s * kStage + kStageA;
+        tc::expect_tx(full0 + 8 * s, static_cast<uint32_t>(nmma) * kKB * 2);
+        tc::tma_load_2d(sb, &tmX, (c0 + kb) * kKB, 0, full0 + 8 * s);
+        tc::tma_load_2d(sb + kStageB / 2, &tmX, (c0 + kb) * kKB + 64, 0, full0 + 8 * s);
+        issued = kb + 1;
+      }
+      if (!ok) {
+        atomicCAS(&g_gemm_status, 0u, 5u);
+        for (int j = (issued > kStages ? issued - kStages : 0); j < issued; ++j)  // copies in flight land
+          tc::wait_until(full0 + 8 * (j % kStages), (j / kStages) & 1, 100000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA: D[128 rows, nmma vectors] += W[128, 16] . X[nmma, 16]^T per 16 k ----
+      const uint32_t idesc = tc::idesc_bf16_f32(kRows, nmma);
+      bool ok = true;
+      for (int kb = 0; kb < nkb && ok; ++kb) {
+        const int s = kb % kStages;
+        if (!tc::wait_until(full0 + 8 * s, (kb / kStages) & 1, deadline)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        const uint32_t sa = base + s * kStage, sb = sa + kStageA;
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            tc::mma_bf16(tmem, tc::sdesc_kmajor_sw128(sa + h * (kRows * 128) + 32 * k),
+                         tc::sdesc_kmajor_sw128(sb + h * (kStageB / 2) + 32 * k), idesc, (kb | h | k) != 0);
+        tc::mma_commit(empty0 + 8 * s);  // the stage is free once these MMAs have read it
+      }
+      if (!ok) atomicCAS(&g_gemm_status, 0u, 6u);
+      tc::mma_commit(accf);  // accumulator ready (partial on error)
+    }
+  } else {
+    // ---- dequantising warps: unit u (rows 16 u .. 16 u + 15) of each k-block, or one of
+    // its 8-row halves (kHalves == 2) ----
+    const int w = warp - 2, gid = lane >> 2, u = w / kHalves, hsel = kHalves == 2 ? (w & 1) : 0;
+    const uint8_t *ub = a.packed + (static_cast<int64_t>(tile) * 8 + u) * cpt * kUnitBytes;
+    auto load = [&](int kb, uint4 &lo, uint4 &hi, uint4 &sc) {
+      const uint8_t *p = ub + static_cast<int64_t>(c0 + kb) * kUnitBytes;
+      if (kHalves == 1 || hsel == 0) lo = ld_stream_v4(p + lane * 16);
+      if (kHalves == 1 || hsel == 1) hi = ld_stream_v4(p + 512 + lane * 16);
+      sc = ld_stream_v4(p + 1024 + gid * 16);
+    };
+    bool ok = true;
+    auto put = [&](int kb, const uint4 &lo, const uint4 &hi, const uint4 &sc) {
+      const int s = kb % kStages;
+      if (ok && !tc::wait_until(empty0 + 8 * s, ((kb / kStages) & 1) ^ 1, deadline)) ok = false;
+      if (ok) {
+        if (kHalves == 1 || hsel == 0) dequant_rows(base + s * kStage, u * 16, lo, sc.x, sc.y);
+        if (kHalves == 1 || hsel == 1) dequant_rows(base + s * kStage, u * 16 + 8, hi, sc.z, sc.w);
+      }
+      tc::fence_proxy_async_smem();  // the tensor core reads these stores through the async proxy
+      __syncwarp();
+      if (lane == 0) mbar_arrive(full0 + 8 * s);
+    };
+    uint4 l0 = {}, h0 = {}, s0 = {}, l1 = {}, h1 = {}, s1 = {};
+    if (nkb > 0) load(0, l0, h0, s0);
+    for (int kb = 0; kb < nkb; kb += 2) {  // two register sets: the next unit in flight
+      if (kb + 1 < nkb) load(kb + 1, l1, h1, s1);
+      put(kb, l0, h0, s0);
+      if (kb + 1 >= nkb) break;
+      if (kb + 2 < nkb) load(kb + 2, l0, h0, s0);
+      put(kb + 1, l1, h1, s1);
+    }
+    if (!ok && lane == 0) atomicCAS(&g_gemm_status, 0u, 7u);
+  }
+
+  // ---- epilogue ----
+  pdl_wait();  // every thread: the previous kernel's outputs (the residual) are visible
+  pdl_launch_dependents();
+  if (warp >= 2 && warp < 2 + kDrainWarps) {
+    // TMEM lane quarter (warp % 4) = rows 32 q .. 32 q + 31; two warps per quarter split the columns
+    const bool have = __all_sync(0xffffffffu, tc::wait_until(accf, 0, deadline));
+    if (!have && lane == 0) atomicCAS(&g_gemm_status, 0u, 8u);
+    tc::fence_after_sync();
+    const int q = warp & 3, part = (warp - 2) >> 2, nh = nmma / 2;
+    const int row = q * 32 + lane;
+    for (int c = part * nh; c < (part + 1) * nh; c += 8) {
+      uint32_t r[8];
+      tc::tmem_ld8(tmem + (static_cast<uint32_t>(q * 32) << 16) + c, r);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) P[row * pstride + c + e] = __uint_as_float(r[e]);
+    }
+  }
+  tc::fence_before_sync();
+  if constexpr (CS > 1) cg::this_cluster().sync();
+  else __syncthreads();
+  // rows [r0, r0 + rows_r) of the tile: every rank's partial, summed in rank order
+  const int rows_r = kRows / CS, r0 = rank * rows_r;
+  const int row_base = tile * kRows + r0;
+  if (threadIdx.x < 256) {
+    const float *parts[CS];
+#pragma unroll
+    for (int qq = 0; qq < CS; ++qq) {
+      if constexpr (CS > 1) parts[qq] = cg::this_cluster().map_shared_rank(P, qq);
+      else parts[qq] = P;
+    }
+    if (a.swiglu) {
+      const int H = a.N / 2, half_r = rows_r / 2, items = a.n_vec * half_r;
+      for (int it = threadIdx.x; it < items; it += 256) {
+        const int t = it / half_r, o = it % half_r;
+        const int rg = r0 + (o >> 3) * 16 + (o & 7), ru = rg + 8;
+        float g = 0.f, u = 0.f;
+#pragma unroll
+        for (int qq = 0; qq < CS; ++qq) {
+          g += parts[qq][rg * pstride + t];
+          u += parts[qq][ru * pstride + t];
+        }
+        const float gte = __bfloat162float(__float2bfloat16_rn(g));
+        const float up = __bfloat162float(__float2bfloat16_rn(u));
+        const float sw = __bfloat162float(__float2bfloat16_rn(gte / (1.f + __expf(-gte))));
+        a.y[static_cast<int64_t>(t) * H + row_base / 2 + o] = float_to_bf16_bits(sw * up);
+      }
+    } else {
+      const int items = a.n_vec * rows_r;
+      const int seg = rows_r < 32 ? rows_r : 32;  // lanes of one vector in a warp (argmax)
+      for (int b0 = 0; b0 < items; b0 += 256) {
+        const int it = b0 + threadIdx.x;
+        const bool valid = it < items;
+        const int t = valid ? it / rows_r : 0, i = valid ? it % rows_r : 0;
+        const int grow = row_base + i;
+        uint16_t yb = 0;
+        if (valid) {
+          float v = 0.f;
+#pragma unroll
+          for (int qq = 0; qq < CS; ++qq) v += parts[qq][(r0 + i) * pstride + t];
+          const int64_t o = static_cast<int64_t>(t) * a.N + grow;
+          // the residual is added to the bf16-rounded projection (IRON adds two bf16 buffers)
+          if (a.residual) v = __bfloat162float(__float2bfloat16_rn(v)) + bf16_bits_to_float(ld_act_u16(a.residual + o));
+          yb = float_to_bf16_bits(v);
+          a.y[o] = yb;
+        }
+        if (a.amax) {
+          unsigned long long key = valid ? argmax_key(bf16_bits_to_float(yb), grow) : 0ull;
+          for (int x = 1; x < seg; x <<= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, x);
+            key = other > key ? other : key;
+          }
+          if (valid && (lane % seg) == 0) atomicMax(a.amax + t * 32 + ((grow >> 4) & 31), key);
+        }
+      }
+    }
+  }
+  if constexpr (CS > 1) cg::this_cluster().sync();  // the other ranks have read this CTA's partial
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) tc::tmem_free(tmem, cols);
+}
+
+}  // namespace s4tc
+
 // ---- host side ---------------------------------------------------------------------
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -381,7 +666,73 @@ int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap 
   return launch(gemm_tc_kernel<BN>, grid, dim3(kThreads), G::kSmem, s, pdl, ta, tb, tc, M, N, K, R, ldr, epi);
 }
 
+namespace s4tc {
+template <int CS>
+static int launch_cs(const CUtensorMap &tx, const Args &a, int nmma, int tiles, bool pdl, cudaStream_t s) {
+  static PerDeviceOnce attr_set;  // per instantiation and device: the shared memory opt-in
+  const int ast = attr_set.run([]() {
+    return call_status(cudaFuncSetAttribute(s4tc_kernel<CS>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+  });
+  if (ast != IRON_OK) return ast;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(tiles * CS));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (CS > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = CS;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, s4tc_kernel<CS>, tx, a, nmma);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    (void)cudaGetLastError();
+    return IRON_ERR_CUDA;
+  }
+  return IRON_OK;
+}
+}  // namespace s4tc
 }  // namespace gemm
+
+// The tensor-core form of the int4 g32 GEMV for 33..64 vectors (declared in s4.cuh).
+// IRON_ERR_UNSUPPORTED: not this form's shape (N % 128, vector count); the caller then
+// runs the mma.sync GEMV.
+int launch_s4_tc(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K, int n_vec,
+                 const uint16_t *residual, int swiglu, unsigned long long *amax, bool pdl, cudaStream_t s) {
+  using namespace gemm::s4tc;
+  // from 33 vectors on (B200 decode, ms per step with / without this form: 64 vectors
+  // 2.29 / 2.93; 32: 1.66 / 1.54; 16: 1.28 / 0.95)
+  if (n_vec <= 32 || n_vec > kMaxVec || N % kRows || K % kKB) return IRON_ERR_UNSUPPORTED;
+  const int nmma = (n_vec + 15) / 16 * 16;
+  CUtensorMap tx;
+  const int st = gemm::make_tmap(&tx, x, n_vec, K, K, nmma);
+  if (st != IRON_OK) return st;
+  const Args a{packed, y, residual, amax, N, K, n_vec, swiglu};
+  const int tiles = N / kRows, cpt = K / kKB;
+  // split K over a cluster while the doubled grid still fits one wave (and every CTA
+  // keeps at least two k-blocks)
+  int cs = 1;
+  while (cs < 8 && tiles * cs * 2 <= sm_count() && cpt >= cs * 4) cs *= 2;
+  switch (cs) {
+    case 1: return gemm::s4tc::launch_cs<1>(tx, a, nmma, tiles, pdl, s);
+    case 2: return gemm::s4tc::launch_cs<2>(tx, a, nmma, tiles, pdl, s);
+    case 4: return gemm::s4tc::launch_cs<4>(tx, a, nmma, tiles, pdl, s);
+    default: return gemm::s4tc::launch_cs<8>(tx, a, nmma, tiles, pdl, s);
+  }
+}
+
 }  // namespace iron
 
 using namespace iron;

@@ -866,6 +866,10 @@ extern "C" int iron_gemv_int4g32_ex(const uint8_t *packed, const uint16_t *x, ui
   epi.ar.world = 1;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (n_vec <= 8) return launch_s4_tile_cs<1>(packed, x, y, N, K, n_vec, epi, pdl, s);
+  if (!norm_weight) {  // 33..64 vectors: the tensor-core form where it takes the shape
+    const int st = launch_s4_tc(packed, x, y, N, K, n_vec, residual, swiglu, argmax_keys, pdl, s);
+    if (st != IRON_ERR_UNSUPPORTED) return st;
+  }
 #ifdef IRON_S4_ONLY_NT1
   return IRON_ERR_SHAPE;
 #else

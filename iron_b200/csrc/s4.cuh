@@ -58,4 +58,10 @@ __device__ __forceinline__ uint32_t s4_word_nibble(uint32_t packed, int i) {
   return (packed >> ((i & 1) ? 16 + 4 * (i >> 1) : 4 * (i >> 1))) & 0xfu;
 }
 
+// The tensor-core form of the int4 g32 GEMV for 33..64 vectors (gemm_tc.cu): the same
+// packed units and epilogues (residual, interleaved SwiGLU, argmax keys). Returns
+// IRON_ERR_UNSUPPORTED for shapes it does not take (N % 128, 32 vectors or fewer).
+int launch_s4_tc(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, int K, int n_vec,
+                 const uint16_t *residual, int swiglu, unsigned long long *amax, bool pdl, cudaStream_t s);
+
 }  // namespace iron

@@ -117,9 +117,11 @@ def test_full_model_decode_matches_oracle(batch):
     # rounding an ulp apart): measured on B200, 3 of sequence 0's 512 k entries at layer
     # 15 (batch 64) fell outside 2e-2 / 1e-2, the worst 0.113 against 0.102 in a row of
     # RMS ~2.5 -- 0.4 % of the row's scale, while every logit stayed within tolerance.
-    # So there: at most 1 % of the entries outside, and no error above 2 % of the row RMS.
+    # With the tensor-core GEMV at batch 64 (another summation order) 6 of sequence 2's
+    # 512 entries, the worst 0.1016 against 0.1118 (0.4 % of the row RMS). So there: at
+    # most 2 % of the entries outside, and no error above 2 % of the row RMS.
     for li in (0, shape.n_layers - 1):
-        frac = 0.0 if li == 0 else 1e-2
+        frac = 0.0 if li == 0 else 2e-2
         for b in range(min(batch, 8)):
             p = pos0[b] + STEPS - 1
             for name, got_c, ref_c in (("k", eng.kc, kc), ("v", eng.vc, vc)):
