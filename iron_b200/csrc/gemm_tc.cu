@@ -304,13 +304,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 // mma.sync dot-product engine becomes compute-bound (B200, batch 64: 41-107 TFLOP/s).
 // A CTA owns a 128-row tile of the weights and a slice of K (a cluster of up to 8
 // CTAs splits K). Per 128-k stage:
-//   - one thread streams the k-block's eight packed 1152-byte units (the GEMV's units)
-//     into a raw ring six k-blocks ahead by bulk copies -- before the wait, as the
-//     weights never depend on the previous kernel (requested one unit ahead by the
-//     dequantising warps themselves, every k-block waited a DRAM round trip: 22 us per
-//     B200 batch-64 projection);
-//   - eight dequantising warps turn their unit into the exact bf16 values bf16(q * s) in
-//     the stage, in the 128-byte-swizzled K-major layout;
+//   - eight dequantising warps read their 16-row unit of the packed weights (the same
+//     1152-byte units as the GEMV, requested one stage ahead) and write the exact bf16
+//     values bf16(q * s) into shared memory in the 128-byte-swizzled K-major layout
+//     (streaming the units into a shared ring by bulk copies instead, which left room
+//     for 3 stages rather than 4, measured 2.04 against 1.82 ms per B200 batch-64
+//     decode step);
 //   - one thread loads the stage's activations [vectors, 128 k] by TMA;
 //   - one thread issues tcgen05.mma (M = 128 weight rows, N = vectors rounded up to 16)
 //     into a TMEM accumulator.
@@ -326,19 +325,16 @@ namespace cg = cooperative_groups;
 
 constexpr int kRows = 128;                        // weight rows per tile (MMA M)
 constexpr int kKB = 128;                          // k per stage: one packed unit
-constexpr int kStages = 3;                        // bf16 weight + activation stages
-constexpr int kRaw = 6;                           // raw-weight stages (8 packed units each)
+constexpr int kStages = 4;
 constexpr int kDqWarps = 8;                       // a 16-row unit each; also the TMEM drain
 constexpr int kDrainWarps = 8;
-// warp 0: raw-weight bulk copies, warp 1: MMA + TMEM, warp 2: activation TMA, 3..10: dequantise
-constexpr int kThreads = 32 * (3 + kDqWarps);
+constexpr int kThreads = 32 * (2 + kDqWarps);     // warp 0: activation TMA, warp 1: MMA + TMEM
 constexpr int kMaxVec = 64;
 constexpr int kStageA = kRows * kKB * 2;          // two 64-k swizzle blocks of 16 KB
 constexpr int kStageB = kMaxVec * kKB * 2;        // two 64-k blocks of up to 8 KB
 constexpr int kStage = kStageA + kStageB;
+constexpr int kSmem = 1024 + kStages * kStage + 1024;
 constexpr int kUnitBytes = 1152;
-constexpr int kRawStage = 8 * kUnitBytes;
-constexpr int kSmem = 1024 + kStages * kStage + kRaw * kRawStage + 1024;
 
 struct Args {
   const uint8_t *packed;
@@ -350,12 +346,6 @@ struct Args {
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
-__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
-               : "memory");
-  return v;
 }
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
@@ -395,11 +385,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;  // 128-byte swizzle atoms: 1024-B aligned
-  const uint32_t wraw0 = base + kStages * kStage;  // raw-weight ring: kRaw x 8 packed units
-  const uint32_t bars = wraw0 + kRaw * kRawStage;
-  const uint32_t full0 = bars, empty0 = bars + 8 * kStages;
-  const uint32_t rfull0 = bars + 16 * kStages, rempty0 = rfull0 + 8 * kRaw;
-  const uint32_t accf = rempty0 + 8 * kRaw;
+  const uint32_t bars = base + kStages * kStage;
+  const uint32_t full0 = bars, empty0 = bars + 8 * kStages, accf = bars + 16 * kStages;
   const uint32_t tslot = accf + 8;
   uint32_t *tslot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tslot - raw));
   float *P = reinterpret_cast<float *>(smem_raw + (base - raw));  // fp32 partial tile, after the mainloop
@@ -419,10 +406,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::mbar_init_u32(full0 + 8 * s, kDqWarps + 1);  // the dequantising warps + the activation load
       tc::mbar_init_u32(empty0 + 8 * s, 1);
     }
-    for (int r = 0; r < kRaw; ++r) {
-      tc::mbar_init_u32(rfull0 + 8 * r, 1);
-      tc::mbar_init_u32(rempty0 + 8 * r, kDqWarps);
-    }
     tc::mbar_init_u32(accf, 1);
     mbar_init_fence();
   }
@@ -434,29 +417,26 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---- raw weights: each k-block's 8 packed units (1152 B each, rows 16 u .. 16 u + 15)
-      // into the raw ring, kRaw k-blocks ahead. They never depend on the previous kernel:
-      // no wait here. ----
-      const uint8_t *tb = a.packed + static_cast<int64_t>(tile) * 8 * cpt * kUnitBytes;
+      // ---- activations: [vectors, 128 k] per stage, two 64-k boxes of nmma rows ----
+      pdl_wait();  // x is the previous kernel's output
       bool ok = true;
       int issued = 0;
       for (int kb = 0; kb < nkb; ++kb) {
-        const int r = kb % kRaw;
-        if (!tc::wait_until(rempty0 + 8 * r, ((kb / kRaw) & 1) ^ 1, deadline)) {
+        const int s = kb % kStages;
+        if (!tc::wait_until(empty0 + 8 * s, ((kb / kStages) & 1) ^ 1, deadline)) {
           ok = false;
           break;
         }
-        tc::expect_tx(rfull0 + 8 * r, kRawStage);
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          tc::bulk_load(wraw0 + r * kRawStage + u * kUnitBytes,
-                        tb + (static_cast<int64_t>(u) * cpt + c0 + kb) * kUnitBytes, kUnitBytes, rfull0 + 8 * r);
+        const uint32_t sb = base + s * kStage + kStageA;
+        tc::expect_tx(full0 + 8 * s, static_cast<uint32_t>(nmma) * kKB * 2);
+        tc::tma_load_2d(sb, &tmX, (c0 + kb) * kKB, 0, full0 + 8 * s);
+        tc::tma_load_2d(sb + kStageB / 2, &tmX, (c0 + kb) * kKB + 64, 0, full0 + 8 * s);
         issued = kb + 1;
       }
       if (!ok) {
-        atomicCAS(&g_gemm_status, 0u, 9u);
-        for (int j = (issued > kRaw ? issued - kRaw : 0); j < issued; ++j)  // copies in flight land
-          tc::wait_until(rfull0 + 8 * (j % kRaw), (j / kRaw) & 1, 100000000ull);
+        atomicCAS(&g_gemm_status, 0u, 5u);
+        for (int j = (issued > kStages ? issued - kStages : 0); j < issued; ++j)  // copies in flight land
+          tc::wait_until(full0 + 8 * (j % kStages), (j / kStages) & 1, 100000000ull);
       }
     }
   } else if (warp == 1) {
@@ -483,47 +463,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) atomicCAS(&g_gemm_status, 0u, 6u);
       tc::mma_commit(accf);  // accumulator ready (partial on error)
     }
-  } else if (warp == 2) {
-    if (lane == 0) {
-      // ---- activations: [vectors, 128 k] per stage, two 64-k boxes of nmma rows ----
-      pdl_wait();  // x is the previous kernel's output
-      bool ok = true;
-      int issued = 0;
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % kStages;
-        if (!tc::wait_until(empty0 + 8 * s, ((kb / kStages) & 1) ^ 1, deadline)) {
-          ok = false;
-          break;
-        }
-        const uint32_t sb = base + s * kStage + kStageA;
-        tc::expect_tx(full0 + 8 * s, static_cast<uint32_t>(nmma) * kKB * 2);
-        tc::tma_load_2d(sb, &tmX, (c0 + kb) * kKB, 0, full0 + 8 * s);
-        tc::tma_load_2d(sb + kStageB / 2, &tmX, (c0 + kb) * kKB + 64, 0, full0 + 8 * s);
-        issued = kb + 1;
-      }
-      if (!ok) {
-        atomicCAS(&g_gemm_status, 0u, 5u);
-        for (int j = (issued > kStages ? issued - kStages : 0); j < issued; ++j)  // copies in flight land
-          tc::wait_until(full0 + 8 * (j % kStages), (j / kStages) & 1, 100000000ull);
-      }
-    }
   } else {
-    // ---- dequantising warps: unit u (rows 16 u .. 16 u + 15) of each k-block, read from
-    // the raw ring, written as bf16 into the stage ----
-    const int u = warp - 3, gid = lane >> 2;
+    // ---- dequantising warps: unit u (rows 16 u .. 16 u + 15) of each k-block (16
+    // warps on 8-row halves measured slower) ----
+    const int u = warp - 2, gid = lane >> 2;
+    const uint8_t *ub = a.packed + (static_cast<int64_t>(tile) * 8 + u) * cpt * kUnitBytes;
+    auto load = [&](int kb, uint4 &lo, uint4 &hi, uint4 &sc) {
+      const uint8_t *p = ub + static_cast<int64_t>(c0 + kb) * kUnitBytes;
+      lo = ld_stream_v4(p + lane * 16);
+      hi = ld_stream_v4(p + 512 + lane * 16);
+      sc = ld_stream_v4(p + 1024 + gid * 16);
+    };
     bool ok = true;
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int r = kb % kRaw, s = kb % kStages;
-      uint4 lo = {}, hi = {}, sc = {};
-      if (ok && !tc::wait_until(rfull0 + 8 * r, (kb / kRaw) & 1, deadline)) ok = false;
-      if (ok) {
-        const uint32_t p = wraw0 + r * kRawStage + u * kUnitBytes;
-        lo = ld_shared_v4(p + lane * 16);
-        hi = ld_shared_v4(p + 512 + lane * 16);
-        sc = ld_shared_v4(p + 1024 + gid * 16);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(rempty0 + 8 * r);  // this warp's unit of the raw stage is read
+    auto put = [&](int kb, const uint4 &lo, const uint4 &hi, const uint4 &sc) {
+      const int s = kb % kStages;
       if (ok && !tc::wait_until(empty0 + 8 * s, ((kb / kStages) & 1) ^ 1, deadline)) ok = false;
       if (ok) {
         dequant_rows(base + s * kStage, u * 16, lo, sc.x, sc.y);
@@ -532,6 +485,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_proxy_async_smem();  // the tensor core reads these stores through the async proxy
       __syncwarp();
       if (lane == 0) mbar_arrive(full0 + 8 * s);
+    };
+    uint4 l0 = {}, h0 = {}, s0 = {}, l1 = {}, h1 = {}, s1 = {};
+    if (nkb > 0) load(0, l0, h0, s0);
+    for (int kb = 0; kb < nkb; kb += 2) {  // two register sets: the next unit in flight
+      if (kb + 1 < nkb) load(kb + 1, l1, h1, s1);
+      put(kb, l0, h0, s0);
+      if (kb + 1 >= nkb) break;
+      if (kb + 2 < nkb) load(kb + 2, l0, h0, s0);
+      put(kb + 1, l1, h1, s1);
     }
     if (!ok && lane == 0) atomicCAS(&g_gemm_status, 0u, 7u);
   }
@@ -539,12 +501,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---- epilogue ----
   pdl_wait();  // every thread: the previous kernel's outputs (the residual) are visible
   pdl_launch_dependents();
-  if (warp >= 3 && warp < 3 + kDrainWarps) {
+  if (warp >= 2 && warp < 2 + kDrainWarps) {
     // TMEM lane quarter (warp % 4) = rows 32 q .. 32 q + 31; two warps per quarter split the columns
     const bool have = __all_sync(0xffffffffu, tc::wait_until(accf, 0, deadline));
     if (!have && lane == 0) atomicCAS(&g_gemm_status, 0u, 8u);
     tc::fence_after_sync();
-    const int q = warp & 3, part = (warp - 3) >> 2, nh = nmma / 2;
+    const int q = warp & 3, part = (warp - 2) >> 2, nh = nmma / 2;
     const int row = q * 32 + lane;
     for (int c = part * nh; c < (part + 1) * nh; c += 8) {
       uint32_t r[8];
@@ -598,45 +560,48 @@ __global__ void __launch_bounds__(kThreads, 1)
             make_uint4(o[0], o[1], o[2], o[3]);
       }
     } else {
-      const int groups = rows_r / 8, items = a.n_vec * groups;  // groups: 2..16, divides 32
+      // 8 rows a thread (4 in 8-CTA clusters, to occupy all 256 threads, measured slower)
+      constexpr int kR = 8;
+      const int groups = rows_r / kR, items = a.n_vec * groups;  // groups: 2..16, divides 32
       for (int b0 = 0; b0 < items; b0 += 256) {
         const int it = b0 + threadIdx.x;
         const bool valid = it < items;
-        const int t = valid ? it / groups : 0, i0 = valid ? (it % groups) * 8 : 0;
+        const int t = valid ? it / groups : 0, i0 = valid ? (it % groups) * kR : 0;
         const int grow0 = row_base + i0;
         unsigned long long key = 0ull;
         if (valid) {
-          float v[8];
+          float v[kR];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] = 0.f;
+          for (int e = 0; e < kR; ++e) v[e] = 0.f;
 #pragma unroll
           for (int qq = 0; qq < CS; ++qq)
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] += parts[qq][(r0 + i0 + e) * pstride + t];
+            for (int e = 0; e < kR; ++e) v[e] += parts[qq][(r0 + i0 + e) * pstride + t];
           const int64_t o = static_cast<int64_t>(t) * a.N + grow0;
+          uint32_t rw[kR / 2];
           if (a.residual) {
             // the residual is added to the bf16-rounded projection (IRON adds two bf16 buffers)
             const uint4 rv = ld_act_v4(a.residual + o);
-            const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+            rw[0] = rv.x, rw[1] = rv.y, rw[2] = rv.z, rw[3] = rv.w;
 #pragma unroll
-            for (int e = 0; e < 8; e += 2) {
+            for (int e = 0; e < kR; e += 2) {
               v[e] = __bfloat162float(__float2bfloat16_rn(v[e])) + bf16_lo(rw[e / 2]);
               v[e + 1] = __bfloat162float(__float2bfloat16_rn(v[e + 1])) + bf16_hi(rw[e / 2]);
             }
           }
-          uint32_t w[4];
+          uint32_t w[kR / 2];
 #pragma unroll
-          for (int e = 0; e < 8; e += 2) w[e / 2] = pack_bf16x2(v[e], v[e + 1]);
+          for (int e = 0; e < kR; e += 2) w[e / 2] = pack_bf16x2(v[e], v[e + 1]);
           *reinterpret_cast<uint4 *>(a.y + o) = make_uint4(w[0], w[1], w[2], w[3]);
           if (a.amax) {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
+            for (int e = 0; e < kR; ++e) {
               const unsigned long long k = argmax_key((e & 1) ? bf16_hi(w[e / 2]) : bf16_lo(w[e / 2]), grow0 + e);
               key = k > key ? k : key;
             }
           }
         }
-        if (a.amax) {  // the vector's best over the tile's rows: one atomic per vector and tile
+        if (a.amax) {  // the vector's best over the CTA's rows: one atomic per vector and slice
           for (int x = 1; x < groups; x <<= 1) {
             const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, x);
             key = other > key ? other : key;
@@ -789,7 +754,7 @@ int launch_s4_tc(const uint8_t *packed, const uint16_t *x, uint16_t *y, int N, i
   // from 33 vectors on (B200 decode, ms per step with / without this form: 64 vectors
   // 2.29 / 2.93; 32: 1.66 / 1.54; 16: 1.28 / 0.95)
   if (n_vec <= 32 || n_vec > kMaxVec || N % kRows || K % kKB) return IRON_ERR_UNSUPPORTED;
-  if (!aligned16(y) || (residual && !aligned16(residual))) return IRON_ERR_UNSUPPORTED;  // 16-byte epilogue
+  if (!aligned16(y) || (residual && !aligned16(residual))) return IRON_ERR_UNSUPPORTED;
   const int nmma = (n_vec + 15) / 16 * 16;
   CUtensorMap tx;
   const int st = gemm::make_tmap(&tx, x, n_vec, K, K, nmma);

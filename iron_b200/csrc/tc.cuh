@@ -60,15 +60,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, int 
       : "memory");
 }
 
-// 1-D bulk copy global -> this CTA's own shared memory (no multicast), completing
-// `bytes` of transaction on the mbarrier. Both addresses 16-byte aligned, bytes a
-// multiple of 16.
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
-               : "memory");
-}
-
 // 2-D tiled TMA store this CTA's shared memory -> global, in a bulk async-group.
 // c0 (innermost, elements) * sizeof(elem) must be a multiple of 16 bytes and both
 // coordinates non-negative; rows / columns past the tensor's extent are not written.
