@@ -486,14 +486,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(full0 + 8 * s);
     };
-    uint4 l0 = {}, h0 = {}, s0 = {}, l1 = {}, h1 = {}, s1 = {};
+    // three register sets: two units in flight while one is dequantised
+    uint4 l0 = {}, h0 = {}, s0 = {}, l1 = {}, h1 = {}, s1 = {}, l2 = {}, h2 = {}, s2 = {};
     if (nkb > 0) load(0, l0, h0, s0);
-    for (int kb = 0; kb < nkb; kb += 2) {  // two register sets: the next unit in flight
-      if (kb + 1 < nkb) load(kb + 1, l1, h1, s1);
+    if (nkb > 1) load(1, l1, h1, s1);
+    for (int kb = 0; kb < nkb; kb += 3) {
+      if (kb + 2 < nkb) load(kb + 2, l2, h2, s2);
       put(kb, l0, h0, s0);
       if (kb + 1 >= nkb) break;
-      if (kb + 2 < nkb) load(kb + 2, l0, h0, s0);
+      if (kb + 3 < nkb) load(kb + 3, l0, h0, s0);
       put(kb + 1, l1, h1, s1);
+      if (kb + 2 >= nkb) break;
+      if (kb + 4 < nkb) load(kb + 4, l1, h1, s1);
+      put(kb + 2, l2, h2, s2);
     }
     if (!ok && lane == 0) atomicCAS(&g_gemm_status, 0u, 7u);
   }
