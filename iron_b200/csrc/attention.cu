@@ -282,6 +282,20 @@ attn_decode_kernel(AttnArgs a) {
       for (int db = 0; db < kDB; ++db) kc[nt][db] = kr[nt][db];
     const int nxt = blk + kW * kABlk;
     if (nxt < t_end) load_block(nxt, kr, vr, true);
+    // the stand-alone form (long, ragged caches): the block after the next one goes to L2
+    // now, so each warp has one block in registers and one in flight from DRAM without
+    // more registers (B200, config 4: 5.93 -> 6.46 TB/s, 353 -> 323 us; in the fused
+    // decode step it measured slightly slower: batch 64 1.815 against 1.806 ms per step)
+    if (!kFused && lane == 0) {
+      const int pf = nxt + kW * kABlk;
+      if (pf < t_end) {
+        const uint32_t bytes = static_cast<uint32_t>(min(kABlk, t_end - pf)) * kAD * 2;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(kb + static_cast<int64_t>(pf) * kAD), "r"(bytes)
+                     : "memory");
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(vb + static_cast<int64_t>(pf) * kAD), "r"(bytes)
+                     : "memory");
+      }
+    }
 
     // S = Q K^T for the two 8-token halves
     float s[2][4];
