@@ -640,6 +640,9 @@ def run_decode(args, world, rank, local):
     e2e = _decode_e2e(eng, B, e2e_steps)
     gemv = _int4_gemv_figure(not args.no_pdl)
     prefill = _prefill_figure(eng, PREFIX)
+    # BASELINE config 5 is quoted at batch 1 and 64: the default (batch-1, 1-GPU) line
+    # carries the batch-64 step beside it
+    batch64 = _batch_figure(64, not args.no_pdl) if (B == 1 and world == 1) else None
     line = {
         "metric": "Llama-3.2-1B-shape decode tok/s", "value": round(B * K * world / (ms_max * 1e-3), 1),
         "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_max / K,
@@ -656,6 +659,7 @@ def run_decode(args, world, rank, local):
                      else "fallback 6650 GB/s"},
         "int4_gemv": gemv,
         "prefill": prefill,
+        "batch64": batch64,
         "gpu_launches": eng.kernels_per_step() * K,
         "e2e": e2e,
         "clocks": clocks,
@@ -669,6 +673,46 @@ def run_decode(args, world, rank, local):
 
         eng.graph = None
         dist.destroy_process_group()
+
+
+def _batch_figure(B, pdl, steps=32):
+    """The decode step at batch B (context 2048, graph replays, CUDA events over `steps`
+    steps after 5 warm-up steps): ms per step, tok/s and the HBM roofline of its
+    algorithmic bytes. Each step reads >= 4 GB of weights and K / V at batch 64 (> L2)."""
+    from iron_b200.applications.llama_3_2_1b.decode import LlamaDecodeEngine, LlamaShape
+
+    shape = LlamaShape()
+    eng = LlamaDecodeEngine(shape, B, PREFIX + steps + 16, seed=4321, pdl=pdl)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(77)
+    for li in range(shape.n_layers):
+        eng.kc[li, :, :, :PREFIX].normal_(generator=g)
+        eng.vc[li, :, :, :PREFIX].normal_(generator=g)
+    eng.set_state(torch.randint(0, shape.vocab_size, (B,), device="cuda", generator=g, dtype=torch.int32),
+                  [PREFIX] * B)
+    eng.capture()
+    for _ in range(5):
+        eng.step()
+    eng.set_state(eng.tokens.clone(), [PREFIX] * B)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        eng.step()
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    bytes_per_step = sum(_decode_bytes(eng, [PREFIX + i] * B) for i in range(steps)) / steps
+    peak, _ = _peak_hbm()
+    achieved = bytes_per_step / (ms * 1e-3) / 1e9
+    eng.graph = None
+    del eng
+    torch.cuda.empty_cache()
+    return {"batch": B, "ms_per_step": round(ms, 4), "tok_s": round(B / (ms * 1e-3), 1), "steps": steps,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "algorithmic_bytes_per_step": int(bytes_per_step)},
+            "note": "int4 GEMVs on the tcgen05 tensor cores from 33 vectors on; context 2048"}
 
 
 def _peak_tensor():
