@@ -752,27 +752,31 @@ def _prefill_figure(eng, S, reps=3):
 def _decode_e2e(eng, B, steps):
     """tok/s through the engine API with host token ids, as IRON's decode loop runs
     (iron/common/sequence.py:721-730 reads the result back every token): each step
-    copies the batch's input tokens from pinned host memory, replays the decode graph,
-    reads the sampled tokens back to pinned host memory and waits for them on the host.
-    The same loop without the per-step host wait (steps pipelined) is reported beside it."""
-    host_in = eng.tokens.cpu().pin_memory()
-    host_out = torch.empty(B, dtype=torch.int32).pin_memory()
+    replays the engine's host-I/O graph (LlamaDecodeEngine.capture_host_io), which copies
+    the batch's input tokens from pinned host memory, decodes, and copies the sampled
+    tokens back to pinned host memory; the host waits for them and feeds them back as the
+    next step's input. The same loop without the per-step host wait (steps pipelined,
+    the same input every step) is reported beside it."""
+    eng.capture_host_io()
+    host_in, host_out = eng.host_tokens_in, eng.host_tokens_out
+    start = host_in.clone()
     stream = torch.cuda.current_stream()
 
     def loop(n, sync):
         for _ in range(n):
-            eng.tokens.copy_(host_in, non_blocking=True)
-            eng.step()
-            host_out.copy_(eng.tokens, non_blocking=True)
+            eng.step_host()
             if sync:
                 stream.synchronize()
+                host_in.copy_(host_out)
 
     res = {}
     for sync in (True, False):
-        eng.set_state(host_in, [PREFIX] * B)
+        host_in.copy_(start)
+        eng.set_state(start, [PREFIX] * B)
         loop(3, sync)
         torch.cuda.synchronize()
-        eng.set_state(host_in, [PREFIX] * B)
+        host_in.copy_(start)
+        eng.set_state(start, [PREFIX] * B)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -783,8 +787,8 @@ def _decode_e2e(eng, B, steps):
     ms, ms_pipe = res[True], res[False]
     return {"value": round(B * steps / (ms * 1e-3), 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
             "d2h_bytes_per_step": 4 * B, "steps": steps, "ms_per_step": ms / steps,
-            "path": "LlamaDecodeEngine.step (CUDA graph of C-ABI kernels), pinned host token ids in and out, "
-                    "host waits for each step's tokens",
+            "path": "LlamaDecodeEngine.step_host (one CUDA graph: pinned host token ids in, the decode step's "
+                    "C-ABI kernels, sampled token ids out), host waits for each step's tokens and feeds them back",
             "pipelined": {"value": round(B * steps / (ms_pipe * 1e-3), 1), "ms_per_step": ms_pipe / steps,
                           "note": "same loop without the per-step host wait"}}
 

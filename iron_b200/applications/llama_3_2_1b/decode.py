@@ -5,7 +5,8 @@ by llama_forward_pass_decode :1156-1195) is one fused OperatorSequence of ~40
 operators per layer. Here the same computation -- RMSNorm, q/k/v projections,
 RoPE, KV-cache append, GQA attention, o projection, residual, RMSNorm, SwiGLU
 MLP, residual; final norm and tied lm-head (llama_cpu.py:170-285) -- runs as
-nine kernels per layer with int4 group-32 weights, for a batch of sequences at
+five kernels per layer up to batch 8 (the RMSNorms folded into the GEMVs around
+them) and seven from batch 9 on, with int4 group-32 weights, for a batch of sequences at
 their own positions, captured once as a CUDA graph whose kernels are launched
 with programmatic dependent launch (each GEMV streams its weights while its
 predecessor finishes). Greedy argmax picks the next token on the device and
@@ -177,6 +178,7 @@ class LlamaDecodeEngine:
         self.attn_ws = torch.zeros(max(wsb, 16), dtype=torch.uint8, device=dev)
         self.amax = torch.zeros(B * 32, dtype=torch.int64, device=dev)  # fused argmax key slots
         self.graph = None
+        self.graph_io = None  # capture_host_io
         # where the RMSNorms run: "chain" (B <= 8) folds them into the GEMVs around them
         # (iron_gemv_int4g32_chain: the residual GEMVs write bf16(h * w) and per-16-row
         # sums of squares, the next GEMV scales its output by 1 / rms -- no norm kernels);
@@ -466,6 +468,37 @@ class LlamaDecodeEngine:
             self.graph.replay()
         else:
             self._launch_step(torch.cuda.current_stream().cuda_stream)
+
+    def capture_host_io(self):
+        """Capture a second decode step whose graph also moves the token ids between host
+        and device: it copies `host_tokens_in` (pinned, [B] int32) into the device before
+        the step and the step's tokens into `host_tokens_out` (pinned) after it, so a host
+        loop that feeds and reads token ids every step -- IRON's decode loop reads the
+        result back every token (iron/common/sequence.py:721-730) -- launches one graph
+        per token. `step_host` replays it; host_tokens_out is valid once the stream has
+        synchronised."""
+        B = self.B
+        self.host_tokens_in = torch.zeros(B, dtype=torch.int32).pin_memory()
+        self.host_tokens_out = torch.zeros(B, dtype=torch.int32).pin_memory()
+        self.host_tokens_in.copy_(self.tokens.cpu())
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        saved_tok, saved_pos = self.tokens.clone(), self.pos.clone()
+        torch.cuda.synchronize()
+        self.graph_io = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph_io, stream=s):
+            self.tokens.copy_(self.host_tokens_in, non_blocking=True)
+            self._launch_step(s.cuda_stream)
+            self.host_tokens_out.copy_(self.tokens, non_blocking=True)
+        torch.cuda.synchronize()
+        self.tokens.copy_(saved_tok)
+        self.pos.copy_(saved_pos)
+        torch.cuda.synchronize()
+
+    def step_host(self):
+        """One decode step of the host-I/O graph (capture_host_io): reads host_tokens_in,
+        writes host_tokens_out."""
+        self.graph_io.replay()
 
     def capture(self):
         """Capture one decode step as a CUDA graph (positions/tokens are device state)."""

@@ -148,6 +148,35 @@ def test_graph_replay_matches_eager_steps():
         assert torch.equal(ta, tb) and torch.equal(la, lb)
 
 
+def test_host_io_graph_matches_device_steps():
+    """capture_host_io / step_host: the step's graph with the token ids copied in from and
+    out to pinned host memory (the host feeding each read token back) gives bitwise the
+    tokens and logits of the device-state graph."""
+    shape = LlamaShape(n_layers=2, vocab_size=4096)
+    runs = []
+    for host in (False, True):
+        eng = LlamaDecodeEngine(shape, 2, 64, seed=3)
+        eng.set_state([11, 12], [4, 9])
+        eng.capture()
+        eng.capture_host_io()
+        outs = []
+        for _ in range(4):
+            if host:
+                eng.step_host()
+                torch.cuda.synchronize()
+                toks = eng.host_tokens_out.clone()
+                eng.host_tokens_in.copy_(toks)
+            else:
+                eng.step()
+                torch.cuda.synchronize()
+                toks = eng.tokens.cpu()
+            outs.append((toks, eng.logits.cpu()))
+        assert eng.pos.cpu().tolist() == [8, 13]
+        runs.append(outs)
+    for (ta, la), (tb, lb) in zip(*runs):
+        assert torch.equal(ta, tb) and torch.equal(la, lb)
+
+
 @pytest.mark.parametrize("S", [100, 192])
 def test_prefill_matches_oracle_then_decodes(S):
     """Prompt through the tensor-core prefill (int4 weights unpacked to bf16, tcgen05
