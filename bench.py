@@ -643,6 +643,7 @@ def run_decode(args, world, rank, local):
     # BASELINE config 5 is quoted at batch 1 and 64: the default (batch-1, 1-GPU) line
     # carries the batch-64 step beside it
     batch64 = _batch_figure(64, not args.no_pdl) if (B == 1 and world == 1) else None
+    gemm = _gemm_figure(not args.no_pdl) if (B == 1 and world == 1) else None
     line = {
         "metric": "Llama-3.2-1B-shape decode tok/s", "value": round(B * K * world / (ms_max * 1e-3), 1),
         "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_max / K,
@@ -660,6 +661,7 @@ def run_decode(args, world, rank, local):
         "int4_gemv": gemv,
         "prefill": prefill,
         "batch64": batch64,
+        "gemm": gemm,
         "gpu_launches": eng.kernels_per_step() * K,
         "e2e": e2e,
         "clocks": clocks,
@@ -673,6 +675,47 @@ def run_decode(args, world, rank, local):
 
         eng.graph = None
         dist.destroy_process_group()
+
+
+def _gemm_figure(pdl, shape=(2048, 2048, 8192), steps=50):
+    """The tcgen05 GEMM at a prefill projection shape (M, K, N), back-to-back launches,
+    CUDA events: TFLOP/s against the measured bf16 peak."""
+    from iron_b200 import _lib
+
+    M, K, N = shape
+    g = torch.Generator(device="cuda")
+    g.manual_seed(42)
+    A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    W = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    C = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    lib, stream = _lib.load(), torch.cuda.current_stream()
+    flags = _lib.IRON_FLAG_PDL if pdl else 0
+    lib.iron_gemm_status(1)
+
+    def launch():
+        st = lib.iron_gemm_bf16(A.data_ptr(), W.data_ptr(), C.data_ptr(), M, N, K, K, K, N, None, 0, 0, 0, 0.0, 0.0,
+                                0, flags, stream.cuda_stream)
+        if st != 0:
+            raise RuntimeError(_lib.strerror(st))
+
+    for _ in range(5):
+        launch()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        launch()
+    e1.record(stream)
+    e1.synchronize()
+    if lib.iron_gemm_status(1) != 0:
+        raise RuntimeError("a GEMM hit its bounded-wait deadline")
+    us = e0.elapsed_time(e1) / steps * 1e3
+    tf = 2 * M * N * K / (us * 1e-6) / 1e12
+    peak, src = _peak_tensor()
+    return {"shape_mkn": [M, K, N], "us_per_launch": round(us, 2), "tflops": round(tf, 1),
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(tf / peak, 4), "peak_source": src,
+                         "traffic": _profile_traffic(f"gemm:{M}x{K}x{N}")}}
 
 
 def _batch_figure(B, pdl, steps=32):
