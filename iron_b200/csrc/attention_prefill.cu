@@ -48,6 +48,13 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void *smem) {
 }
 }  // namespace
 
+// 2^x by the hardware approximation (ex2.approx.ftz.f32; x <= 0 here, results in (0, 1]).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __global__ void __launch_bounds__(kPThreads) attn_prefill_kernel(PrefillArgs a) {
   __shared__ __align__(16) uint16_t ks_[2][kPBlk * kPStride];
   __shared__ __align__(16) uint16_t vs_[2][kPBlk * kPStride];
@@ -127,40 +134,59 @@ __global__ void __launch_bounds__(kPThreads) attn_prefill_kernel(PrefillArgs a) 
         mma_bf16_16816(s[nt], qa[2 * half + 1], kb4[2], kb4[3]);
       }
     }
-    // scale, causal / length mask, running max
+    // running max of the raw scores (the scale is positive: max(s) * c = max(s * c));
+    // blocks wholly inside the valid, causal region skip the mask
     const int key0 = blk * kPBlk;
+    const float c = a.scale_log2;
+    const bool full = key0 + kPBlk <= a.S_kv && (!a.causal || key0 + kPBlk - 1 <= q0);
+    if (!full) {
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = key0 + nt * 8 + 2 * tid + (e & 1);
+          const int row = q0 + gid + ((e >> 1) << 3);
+          if (!(key < a.S_kv && (!a.causal || key <= row))) s[nt][e] = -INFINITY;
+        }
+    }
     float mx_lo = -INFINITY, mx_hi = -INFINITY;
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = key0 + nt * 8 + 2 * tid + (e & 1);
-        const int row = q0 + gid + ((e >> 1) << 3);
-        const bool ok = key < a.S_kv && (!a.causal || key <= row);
-        s[nt][e] = ok ? s[nt][e] * a.scale_log2 : -INFINITY;
-        if (e < 2) mx_lo = fmaxf(mx_lo, s[nt][e]);
-        else mx_hi = fmaxf(mx_hi, s[nt][e]);
-      }
+    for (int nt = 0; nt < 8; ++nt) {
+      mx_lo = fmaxf(mx_lo, fmaxf(s[nt][0], s[nt][1]));
+      mx_hi = fmaxf(mx_hi, fmaxf(s[nt][2], s[nt][3]));
+    }
 #pragma unroll
     for (int x = 1; x <= 2; x <<= 1) {
       mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, x));
       mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, x));
     }
-    const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
+    const float mn_lo = fmaxf(m_lo, mx_lo * c), mn_hi = fmaxf(m_hi, mx_hi * c);
     const float al_lo = mn_lo == -INFINITY ? 1.f : exp2f(m_lo - mn_lo);
     const float al_hi = mn_hi == -INFINITY ? 1.f : exp2f(m_hi - mn_hi);
     m_lo = mn_lo;
     m_hi = mn_hi;
+    // p = 2^(s c - m), one rounding (a fully masked row of a partial block: 0)
     float ps_lo = 0.f, ps_hi = 0.f;
+    if (full) {
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
+      for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float mr = e < 2 ? mn_lo : mn_hi;
-        s[nt][e] = mr == -INFINITY ? 0.f : exp2f(s[nt][e] - mr);
-        if (e < 2) ps_lo += s[nt][e];
-        else ps_hi += s[nt][e];
-      }
+        for (int e = 0; e < 4; ++e) {
+          s[nt][e] = ex2_approx(fmaf(s[nt][e], c, -(e < 2 ? mn_lo : mn_hi)));
+          if (e < 2) ps_lo += s[nt][e];
+          else ps_hi += s[nt][e];
+        }
+    } else {
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float mr = e < 2 ? mn_lo : mn_hi;
+          s[nt][e] = mr == -INFINITY ? 0.f : ex2_approx(fmaf(s[nt][e], c, -mr));
+          if (e < 2) ps_lo += s[nt][e];
+          else ps_hi += s[nt][e];
+        }
+    }
     l_lo = l_lo * al_lo + ps_lo;
     l_hi = l_hi * al_hi + ps_hi;
 #pragma unroll
