@@ -309,24 +309,38 @@ attn_decode_kernel(AttnArgs a) {
         mma_bf16_16816(s[nt], qa[ks], b0, b1);
       }
     }
-    // scale, mask, block max per row
+    // scale, mask (only the cache's ragged last block has tokens past t_end), block max
+    // per row
     float mx_lo = -INFINITY, mx_hi = -INFINITY;
+    if (blk + kABlk <= t_end) {
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int t = blk + nt * 8 + 2 * tid + (e & 1);
-        s[nt][e] = t < t_end ? s[nt][e] * a.scale_log2 : -INFINITY;
-        if (e < 2) mx_lo = fmaxf(mx_lo, s[nt][e]); else mx_hi = fmaxf(mx_hi, s[nt][e]);
-      }
+        for (int e = 0; e < 4; ++e) {
+          s[nt][e] *= a.scale_log2;
+          if (e < 2) mx_lo = fmaxf(mx_lo, s[nt][e]); else mx_hi = fmaxf(mx_hi, s[nt][e]);
+        }
+    } else {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int t = blk + nt * 8 + 2 * tid + (e & 1);
+          s[nt][e] = t < t_end ? s[nt][e] * a.scale_log2 : -INFINITY;
+          if (e < 2) mx_lo = fmaxf(mx_lo, s[nt][e]); else mx_hi = fmaxf(mx_hi, s[nt][e]);
+        }
+    }
 #pragma unroll
     for (int o_ = 1; o_ <= 2; o_ <<= 1) {
       mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, o_));
       mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, o_));
     }
+    // token blk is inside the cache, so both rows' maxima are finite from the first
+    // block on: the first rescale is ex2(-inf) = 0 and masked tokens give ex2(-inf) = 0,
+    // with no guards
     const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
-    const float al_lo = (mn_lo == -INFINITY) ? 1.f : exp2f(m_lo - mn_lo);
-    const float al_hi = (mn_hi == -INFINITY) ? 1.f : exp2f(m_hi - mn_hi);
+    const float al_lo = ex2_approx(m_lo - mn_lo);
+    const float al_hi = ex2_approx(m_hi - mn_hi);
     m_lo = mn_lo;
     m_hi = mn_hi;
     float p[2][4];
@@ -335,8 +349,7 @@ attn_decode_kernel(AttnArgs a) {
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float mr = (e < 2) ? mn_lo : mn_hi;
-        p[nt][e] = (mr == -INFINITY) ? 0.f : exp2f(s[nt][e] - mr);
+        p[nt][e] = ex2_approx(s[nt][e] - ((e < 2) ? mn_lo : mn_hi));
         if (e < 2) ps_lo += p[nt][e]; else ps_hi += p[nt][e];
       }
     l_lo = l_lo * al_lo + ps_lo;

@@ -48,13 +48,6 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void *smem) {
 }
 }  // namespace
 
-// 2^x by the hardware approximation (ex2.approx.ftz.f32; x <= 0 here, results in (0, 1]).
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 __global__ void __launch_bounds__(kPThreads) attn_prefill_kernel(PrefillArgs a) {
   __shared__ __align__(16) uint16_t ks_[2][kPBlk * kPStride];
   __shared__ __align__(16) uint16_t vs_[2][kPBlk * kPStride];

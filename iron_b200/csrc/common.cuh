@@ -171,6 +171,13 @@ __device__ __forceinline__ uint4 ld_stream_v4(const void *p) {
   return r;
 }
 
+// 2^x by the hardware approximation (ex2.approx.ftz.f32). The softmax loops call it
+// with x <= 0 (results in [0, 1], ex2(-inf) = 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
