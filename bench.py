@@ -14,7 +14,8 @@ Workloads:
       RoPE + KV append and its split merge (a cluster at batch <= 2, else a
       combine kernel), O GEMV+residual, RMSNorm, gate/up GEMV+SwiGLU, down
       GEMV+residual], final RMSNorm, lm-head GEMV, argmax). value = tokens/s.
-      The line also carries the config-2 int4 GEMV figure under "int4_gemv".
+      The line also carries the config-2 int4 GEMV figure under "int4_gemv",
+      and (1 GPU, batch 1) configs 1, 3 and 4 under "configs".
   int4_gemv (config 2): y = dequant(W) x, W [8192 x 2048] signed int4 with a
       bf16 scale per 32 k, x [V x 2048] bf16. One step = one GEMV call.
   bf16_gemv (config 1): W [2048 x 8192] bf16, x [8192].
@@ -644,6 +645,7 @@ def run_decode(args, world, rank, local):
     # carries the batch-64 step beside it
     batch64 = _batch_figure(64, not args.no_pdl) if (B == 1 and world == 1) else None
     gemm = _gemm_figure(not args.no_pdl) if (B == 1 and world == 1) else None
+    configs = _configs_figure(args) if (B == 1 and world == 1) else None
     line = {
         "metric": "Llama-3.2-1B-shape decode tok/s", "value": round(B * K * world / (ms_max * 1e-3), 1),
         "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_max / K,
@@ -662,6 +664,7 @@ def run_decode(args, world, rank, local):
         "prefill": prefill,
         "batch64": batch64,
         "gemm": gemm,
+        "configs": configs,
         "gpu_launches": eng.kernels_per_step() * K,
         "e2e": e2e,
         "clocks": clocks,
@@ -756,6 +759,83 @@ def _batch_figure(B, pdl, steps=32):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "algorithmic_bytes_per_step": int(bytes_per_step)},
             "note": "int4 GEMVs on the tcgen05 tensor cores from 33 vectors on; context 2048"}
+
+
+def _bf16_gemv_figure(pdl: bool, launches: int = 2048):
+    """Config-1 bf16 GEMV (W 2048 x 8192 ~ N(0, 0.02), one vector): device-timed graph of
+    launches over rotating weight copies (> 3x L2)."""
+    from iron_b200 import _lib
+
+    M, K = 2048, 8192
+    copies = max(2, -(-3 * L2_BYTES // (2 * M * K)))
+    g = torch.Generator(device="cuda")
+    g.manual_seed(42)
+    W = (torch.randn(copies, M, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    x = torch.randn(K, device="cuda", generator=g).to(torch.bfloat16)
+    y = torch.empty(M, dtype=torch.bfloat16, device="cuda")
+    lib, cap = _lib.load(), torch.cuda.Stream()
+    flags = (_lib.IRON_FLAG_PDL if pdl else 0) | _lib.IRON_FLAG_X_READONLY
+    per = copies * max(1, 256 // copies)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=cap):
+        for i in range(per):
+            st = lib.iron_gemv_bf16(W.data_ptr() + (i % copies) * M * K * 2, x.data_ptr(), y.data_ptr(), M, K, K,
+                                    1, 0, 0, 0, 1, None, 0, flags, torch.cuda.current_stream().cuda_stream)
+            if st != 0:
+                raise RuntimeError(_lib.strerror(st))
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    reps = max(1, launches // per)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * per)
+    nbytes = 2 * M * K + 2 * K + 2 * M
+    peak, _ = _peak_hbm()
+    gbs = nbytes / (us * 1e-6) / 1e9
+    del graph, W
+    torch.cuda.synchronize()
+    return {"metric": "bf16 GEMV achieved HBM GB/s (config 1)", "M": M, "K": K, "us_per_launch": round(us, 3),
+            "launches": reps * per, "value": round(gbs, 1), "unit": "GB/s", "peak": peak,
+            "frac": round(gbs / peak, 4), "algorithmic_bytes_per_launch": nbytes}
+
+
+def _configs_figure(args):
+    """BASELINE configs 1, 3 and 4 on the default (1-GPU, batch-1 decode) line, so that a
+    plain `bench.py` run records every config: the bf16 GEMV, the decoder block with bf16
+    weights at batch 1 and 16 (operator chain; the full block beside it), and the decode
+    attention's nine cases (each over rotating copies whose reads exceed 3x L2)."""
+    import argparse
+
+    pdl = not args.no_pdl
+    peak, _ = _peak_hbm()
+    out = {"bf16_gemv": _bf16_gemv_figure(pdl)}
+    blocks = []
+    for B in (1, 16):
+        pos = _block_positions(B)
+        ba = argparse.Namespace(batch=B, steps=300, warmup=30, no_pdl=args.no_pdl)
+        chain = _time_block_form(ba, 1, None, False, pos, 0)
+        full = _time_block_form(ba, 1, None, True, pos, 0)
+        gbs = chain["bytes_per_step"] / (chain["ms_per_step"] * 1e-3) / 1e9
+        blocks.append({"batch": B, "us_per_step": round(chain["ms_per_step"] * 1e3, 2), "achieved_gbs": round(gbs, 1),
+                       "frac": round(gbs / peak, 4), "algorithmic_bytes_per_step": chain["bytes_per_step"],
+                       "full_block_us": round(full["ms_per_step"] * 1e3, 2), "steps": chain["steps"]})
+    out["block"] = {"metric": "Llama-3.2-1B decoder block (bf16 weights) achieved HBM GB/s (config 3)",
+                    "ops": "RMSNorm, QKV GEMV, RoPE + KV append, gate GEMV, up GEMV, silu*mul, down GEMV",
+                    "cases": blocks}
+    cases = []
+    for B, L in ATTN_CASES:
+        c, _ = _time_attention(B, L, args)
+        c["frac"] = round(c["gbs"] / peak, 4)
+        cases.append(c)
+    out["attention"] = {"metric": "GQA decode attention achieved HBM GB/s (config 4)",
+                        "heads": "32 q / 8 kv, d 64", "cases": cases}
+    torch.cuda.empty_cache()
+    return out
 
 
 def _peak_tensor():
@@ -1203,7 +1283,7 @@ def _time_block_form(args, world, local, full: bool, pos, rank):
     for _ in range(max(1, args.warmup // len(blocks))):
         graph.replay()
     torch.cuda.synchronize()
-    sampler = ClockSampler(local) if (rank == 0 and not full) else None
+    sampler = ClockSampler(local) if (rank == 0 and not full and local is not None) else None
     if sampler:
         sampler.start()
         time.sleep(0.3)
